@@ -1,0 +1,416 @@
+#!/usr/bin/env python
+"""Paged-decode benchmark on the Llama-3.1-8B KV shape, batch 64 per GPU.
+
+One step = for each of 32 layers: append one new token per sequence into the
+paged pool (mz_kv_append_paged), then fused GQA decode attention over
+ctx + 1 tokens (mz_paged_decode).  Sequences: 64 with ctx ~ U[512, 8192]
+(seeded), block size 16, pools sized to the blocks needed + 10 %, random
+block tables, Q/K/V ~ N(0, 1) bf16.  Each step rewrites the same new-token
+slots, so every timed step does identical work.
+
+N > 1 GPUs (torchrun): weak scaling by KV-head sharding -- the global batch
+is 64 * N sequences, rank r holds KV heads [r*8/N, (r+1)*8/N) of every
+sequence (the same bytes per GPU as N = 1), and each layer's head-sharded
+output is all-gathered with NCCL.
+
+Printed value: KV bytes read per step (sum_b (ctx_b + 1) * 4096 B * 32
+layers, all ranks) / step time.  `--impl reference` times the reference's
+CPU algorithm (oracle port) instead.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+METRIC = ("paged-decode KV-read GB/s (% of HBM peak) and decode tok/s, 8B shape, batch 64")
+L, HQ, HKV, D, BS, B_PER_GPU = 32, 32, 8, 128, 16, 64
+CTX_LO, CTX_HI = 512, 8192
+FALLBACK_HBM_GBS = 6650.0
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="mlxz_b200", choices=["mlxz_b200", "reference"])
+    ap.add_argument("--layers", type=int, default=L)
+    ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=12.0,
+                    help="approximate CPU time budget of the cpu_baseline sample")
+    ap.add_argument("--num-warps", type=int, default=0)
+    ap.add_argument("--no-clocks", action="store_true")
+    return ap.parse_args()
+
+
+def workload_ctx(seed: int, n: int):
+    import numpy as np
+
+    return np.random.default_rng(seed).integers(CTX_LO, CTX_HI + 1, size=n).astype(np.int64)
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return FALLBACK_HBM_GBS, "fallback"
+
+
+def profile_traffic(name: str):
+    """traffic_bytes_per_launch from a committed ncu summary, or None."""
+    p = ROOT / "profiles" / name
+    if not p.exists():
+        return None
+    for line in p.read_text().splitlines():
+        if line.strip().startswith("traffic_bytes_per_launch:"):
+            try:
+                return float(line.split(":", 1)[1].strip().split()[0])
+            except ValueError:
+                return None
+    return None
+
+
+# ---------------------------------------------------------------------------
+# clocks sampling (nvidia-smi in the background during the timed region)
+# ---------------------------------------------------------------------------
+
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_uuid: str | None, enabled: bool = True):
+        self.proc = None
+        self.path = None
+        if not enabled:
+            return
+        try:
+            fd, self.path = tempfile.mkstemp(suffix=".csv")
+            os.close(fd)
+            cmd = ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                   "-lms", "200"]
+            if device_uuid:
+                cmd += ["-i", device_uuid]
+            self.proc = subprocess.Popen(cmd, stdout=open(self.path, "w"),
+                                         stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        rows = []
+        for line in Path(self.path).read_text().splitlines():
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                rows.append((float(parts[1]), float(parts[2]), float(parts[3]), parts[5:9]))
+            except ValueError:
+                continue
+        os.unlink(self.path)
+        if not rows:
+            return None
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i, v in enumerate(r[3]) if v == "Active"})
+        return {"sm_mhz": statistics.median(r[0] for r in rows), "sm_max_mhz": max(r[1] for r in rows),
+                "power_w_max": max(r[2] for r in rows), "samples": len(rows), "reasons": reasons}
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline: the reference's algorithm (oracle port) on the host cores
+# ---------------------------------------------------------------------------
+
+def cpu_sample(seed: int, budget_s: float, threads: int, n_seqs: int = 16):
+    """Times oracle.cpu_path.decode_layer (torch-CPU restatement of the
+    reference's get_kv + GQA attention) on one layer of `n_seqs` sequences
+    drawn from the workload's ctx distribution; repeats until ~budget_s."""
+    import numpy as np
+    import torch
+
+    from oracle import cpu_path
+
+    torch.set_num_threads(threads)
+    ctx = workload_ctx(seed + 17, n_seqs)
+    need = (ctx + 1 + BS - 1) // BS
+    n_blocks = int(need.sum())
+    g = torch.Generator().manual_seed(seed)
+    perm = torch.randperm(n_blocks, generator=g)
+    tables, used = [], 0
+    for n in need:
+        tables.append(perm[used:used + int(n)])
+        used += int(n)
+    kp = torch.randn((n_blocks, HKV, BS, D), generator=g).to(torch.bfloat16)
+    vp = torch.randn((n_blocks, HKV, BS, D), generator=g).to(torch.bfloat16)
+    q = torch.randn((n_seqs, HQ, D), generator=g).to(torch.bfloat16).float()
+    nk = torch.randn((n_seqs, HKV, D), generator=g).to(torch.bfloat16)
+    nv = torch.randn((n_seqs, HKV, D), generator=g).to(torch.bfloat16)
+    kv_bytes = float((ctx + 1).sum()) * HKV * D * 2 * 2
+    ctx_l = [int(c) for c in ctx]
+    cpu_path.decode_layer(q, kp, vp, tables, ctx_l, nk, nv, D ** -0.5)
+    times = []
+    t_end = time.perf_counter() + budget_s
+    while True:
+        t0 = time.perf_counter()
+        cpu_path.decode_layer(q, kp, vp, tables, ctx_l, nk, nv, D ** -0.5)
+        times.append(time.perf_counter() - t0)
+        if time.perf_counter() > t_end or len(times) >= 100:
+            break
+    t = statistics.median(times)
+    return {"gbs": kv_bytes / t / 1e9, "tok_s": n_seqs / (t * 32), "reps": len(times),
+            "layer_s": t, "n_seqs": n_seqs, "kv_bytes": kv_bytes}
+
+
+def run_reference(args, rank: int, world: int) -> None:
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    budget = max(2.0, 120.0 / max(1, args.steps + args.warmup))
+    vals = []
+    for i in range(args.warmup + args.steps):
+        r = cpu_sample(args.seed, budget, threads)
+        if i >= args.warmup:
+            vals.append(r)
+    v = statistics.median(x["gbs"] for x in vals)
+    ms = statistics.median(x["layer_s"] for x in vals) * 1000.0 * args.layers
+    sample = (f"1 of {args.layers} layers, {vals[0]['n_seqs']} of {B_PER_GPU} sequences "
+              f"(ctx ~ U[{CTX_LO},{CTX_HI}]), torch-CPU port of get_kv + GQA attention, "
+              f"{threads} threads; ms_per_step extrapolated to {args.layers} layers")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(v, 3), "unit": "GB/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(ms * B_PER_GPU / vals[0]["n_seqs"], 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded N(0,1) K/V/Q, random block tables)",
+        "config": {"workload": "8B KV shape decode step (CPU sample)", "layers": args.layers,
+                   "global_batch": B_PER_GPU, "seq_len": f"U[{CTX_LO},{CTX_HI}]",
+                   "parallelism": "host threads"},
+        "decode_tok_s": round(statistics.median(x["tok_s"] for x in vals) * (32 / args.layers), 3),
+        "cpu_baseline": {"value": round(v, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": round(v, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------
+# GPU benchmark
+# ---------------------------------------------------------------------------
+
+def run_gpu(args, rank: int, world: int, local_rank: int) -> None:
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    from mlxz_b200 import ops
+    from mlxz_b200.engine import PagedDecodeStep, PagedKVStore
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:
+        if HKV % world:
+            raise SystemExit(f"--gpus {world} must divide {HKV} KV heads")
+        import datetime
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=dev)
+    hkv, hq = HKV // world, HQ // world
+    nl = args.layers
+    B = B_PER_GPU * world
+    ctx = workload_ctx(args.seed, B)
+    need = (ctx + 1 + BS - 1) // BS
+    n_blocks = int(math.ceil(need.sum() * 1.1))
+    perm = np.random.default_rng(args.seed + 1).permutation(n_blocks)
+
+    torch.manual_seed(args.seed * 1000 + rank)
+    store = PagedKVStore(nl, n_blocks, hkv, D, BS, torch.bfloat16, dev, init="empty")
+    for l in range(nl):
+        store.pools[l].normal_()
+    used = 0
+    ids = []
+    for b in range(B):
+        sid = f"s{b}"
+        store.add_sequence(sid, int(ctx[b]), blocks=[int(x) for x in perm[used:used + need[b]]])
+        used += int(need[b])
+        ids.append(sid)
+    step = PagedDecodeStep(store, ids, hq)
+    q = torch.randn(nl, B, hq, D, device=dev).to(torch.bfloat16)
+    kn = torch.randn(nl, B, hkv, D, device=dev).to(torch.bfloat16)
+    vn = torch.randn(nl, B, hkv, D, device=dev).to(torch.bfloat16)
+    out = torch.empty_like(q)
+    gathered = torch.empty((nl, world, B, hq, D), dtype=torch.bfloat16, device=dev) if world > 1 else None
+
+    kv_bytes_rank = float((ctx + 1).sum()) * hkv * D * 2 * 2  # per layer, this rank
+    qo_bytes = 2.0 * B * hq * D * 2
+    table_bytes = float(need.sum()) * 4
+    decode_alg_bytes = kv_bytes_rank + qo_bytes + table_bytes
+
+    def one_step(ev=None):
+        for l in range(nl):
+            st = step.store
+            ops.kv_append_paged(st.k_pool(l), st.v_pool(l), kn[l], vn[l], step.tables, step.positions)
+            if ev is not None:
+                ev[l][0].record()
+            ops.paged_decode(q[l], st.k_pool(l), st.v_pool(l), step.tables, step.lengths,
+                             scale=step.scale, out=out[l], workspace=step.workspace,
+                             num_warps=args.num_warps)
+            if ev is not None:
+                ev[l][1].record()
+            if world > 1:
+                dist.all_gather_into_tensor(gathered[l], out[l])
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local_rank])
+
+    for _ in range(max(3, args.warmup)):
+        one_step()
+    torch.cuda.synchronize()
+    ops.check_device_errors(local_rank)
+
+    uuid = None
+    try:
+        uuid = "GPU-" + str(torch.cuda.get_device_properties(dev).uuid)
+    except Exception:
+        pass
+    evs = [[[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(nl)]
+           for _ in range(args.steps)]
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize()
+    clocks = ClockSampler(uuid, enabled=not args.no_clocks)
+    t0.record()
+    for k in range(args.steps):
+        one_step(evs[k])
+    t1.record()
+    torch.cuda.synchronize()
+    barrier()
+    clk = clocks.stop()
+    ms = t0.elapsed_time(t1) / args.steps
+    dec_ms = [evs[k][l][0].elapsed_time(evs[k][l][1]) for k in range(args.steps) for l in range(nl)]
+    dec_mean = sum(dec_ms) / len(dec_ms)
+    ops.check_device_errors(local_rank)
+
+    # End to end through the public step API: pinned host inputs/outputs.
+    qh = q.cpu().pin_memory()
+    kh = kn.cpu().pin_memory()
+    vh = vn.cpu().pin_memory()
+    oh = torch.empty(q.shape if world == 1 else (nl, world, B, hq, D), dtype=torch.bfloat16).pin_memory()
+    h2d = qh.numel() * 2 + kh.numel() * 2 + vh.numel() * 2
+    d2h = oh.numel() * 2
+
+    q_e, k_e, v_e = torch.empty_like(q), torch.empty_like(kn), torch.empty_like(vn)
+
+    def e2e_step():
+        if world == 1:
+            step.step_host(qh, kh, vh, oh)
+            return
+        q_e.copy_(qh, non_blocking=True)
+        k_e.copy_(kh, non_blocking=True)
+        v_e.copy_(vh, non_blocking=True)
+        step.step(q_e, k_e, v_e, out=out)
+        for l in range(nl):
+            dist.all_gather_into_tensor(gathered[l], out[l])
+        oh.copy_(gathered, non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
+    torch.cuda.synchronize()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        e2e_step()
+    e1.record()
+    torch.cuda.synchronize()
+    barrier()
+    e2e_ms = e0.elapsed_time(e1) / args.steps
+
+    if world > 1:
+        t = torch.tensor([ms, e2e_ms, dec_mean], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, e2e_ms, dec_mean = (float(x) for x in t.tolist())
+
+    kv_step_total = float((ctx + 1).sum()) * HKV * D * 2 * 2 * nl  # all heads, all ranks
+    value = kv_step_total / (ms / 1e3) / 1e9
+    peak, peak_kind = peaks()
+    achieved = decode_alg_bytes / (dec_mean / 1e3) / 1e9
+    result = None
+    if rank == 0:
+        cpu = None
+        if world == 1 and not args.no_cpu_baseline:
+            threads = os.cpu_count() or 1
+            r = cpu_sample(args.seed, args.cpu_seconds, threads)
+            cpu = {"value": round(r["gbs"], 3), "unit": "GB/s", "cores": threads, "kind": "port",
+                   "sample": (f"1 layer x {r['n_seqs']} sequences of the same ctx distribution, "
+                              f"{r['reps']} reps (median), torch-CPU port of get_kv + GQA attention")}
+        traffic = profile_traffic("paged_decode_c2.md")
+        result = {
+            "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
+            "steps": args.steps, "warmup": max(3, args.warmup), "ms_per_step": round(ms, 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded N(0,1) bf16 K/V/Q, random block tables)",
+            "config": {
+                "workload": (f"paged decode step, Llama-3.1-8B KV shape: {nl} layers, 32 q heads, "
+                             f"8 kv heads, head_dim 128, block 16; {B_PER_GPU} seqs per GPU, "
+                             f"ctx U[{CTX_LO},{CTX_HI}]; append 1 token + attention per layer"),
+                "layers": nl, "global_batch": B, "seq_len": f"U[{CTX_LO},{CTX_HI}]",
+                "mean_ctx": round(float(ctx.mean()), 1),
+                "parallelism": "1 GPU" if world == 1 else f"kv-head sharding x{world} + NCCL all-gather",
+                "l2": f"KV read per step {kv_step_total / world / 1e9:.1f} GB per GPU >> 126 MB L2",
+                "pool_blocks": n_blocks,
+            },
+            "decode_tok_s": round(B / (ms / 1e3), 1),
+            "hbm_frac": round(value / world / peak, 4),
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
+                         "unit": "GB/s", "frac": round(achieved / peak, 4),
+                         "traffic": traffic, "kernel": "paged_decode_kernel<128,bf16>",
+                         "peak_kind": peak_kind,
+                         "decode_ms_mean": round(dec_mean, 4),
+                         "alg_bytes_per_launch": decode_alg_bytes},
+            "cpu_baseline": cpu,
+            "e2e": {"value": round(kv_step_total / (e2e_ms / 1e3) / 1e9, 2), "unit": "GB/s",
+                    "ms_per_step": round(e2e_ms, 4), "h2d_bytes_per_step": int(h2d),
+                    "d2h_bytes_per_step": int(d2h)},
+            "gpu_launches": args.steps * nl * 2,
+            "clocks": clk,
+        }
+        print(json.dumps(result), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def main():
+    args = parse_args()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if world == 1 and args.gpus != 1 and rank == 0:
+        print(f"note: --gpus {args.gpus} without torchrun runs 1 rank", file=sys.stderr)
+    sys.path.insert(0, str(ROOT))
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+    else:
+        run_gpu(args, rank, world, local_rank)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,192 @@
+/*
+ * mlxz_b200.h -- C ABI of the B200 (sm_100a) KV-cache kernels.
+ *
+ * Every entry point takes plain device pointers, sizes and a CUDA stream.
+ * Nothing here allocates, frees or synchronises: launches are asynchronous on
+ * the given stream and the caller owns every buffer for the duration of the
+ * launch.  Functions return MZ_OK (0) or a negative MZ_ERR_* code; the text
+ * of the most recent error on the calling thread is read with mz_last_error.
+ *
+ * Data layout shared by all kernels (same as the reference's pool,
+ * src/mlxz/paged_attention/paged_kv.py:33-44):
+ *   K pool, V pool : [n_blocks][n_kv_heads][block_size][head_dim], row-major,
+ *                    element type `dtype` (MZ_DTYPE_*).
+ *   block tables   : int32 [n_seqs][max_blocks_per_seq]; entry j of sequence b
+ *                    is the physical block holding tokens [j*bs, (j+1)*bs).
+ *   slot           : block_id * block_size + position_in_block.
+ *
+ * Device error word: every kernel takes an optional `int32_t *dev_err`
+ * (device memory, may be NULL).  Instead of trapping, a kernel that meets an
+ * out-of-range block id, slot or context length skips that access and ORs an
+ * MZ_DEVERR_* bit into the word.  A bounded wait that gives up sets
+ * MZ_DEVERR_TIMEOUT.  The caller clears the word and reads it back when it
+ * wants to check.
+ */
+#ifndef MLXZ_B200_H
+#define MLXZ_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define MZ_API __attribute__((visibility("default")))
+#else
+#define MZ_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* A cudaStream_t (CUstream).  NULL selects the legacy default stream. */
+typedef void *mz_stream_t;
+
+enum mz_status {
+  MZ_OK = 0,
+  MZ_ERR_INVALID_ARG = -1, /* a size, stride or pointer argument is invalid  */
+  MZ_ERR_UNSUPPORTED = -2, /* valid, but outside what the kernels implement  */
+  MZ_ERR_ALIGNMENT = -3,   /* a pointer or stride breaks a stated alignment  */
+  MZ_ERR_CUDA = -4,        /* a CUDA runtime or driver call failed           */
+  MZ_ERR_WORKSPACE = -5,   /* workspace missing or smaller than required     */
+  MZ_ERR_TOO_LARGE = -6    /* problem larger than a fixed-capacity variant   */
+};
+
+enum mz_dtype { MZ_DTYPE_F16 = 0, MZ_DTYPE_BF16 = 1, MZ_DTYPE_F32 = 2 };
+
+enum mz_device_error {
+  MZ_DEVERR_BLOCK_ID = 1, /* block-table entry outside [0, n_blocks)          */
+  MZ_DEVERR_SLOT = 2,     /* slot outside [0, n_blocks * block_size)          */
+  MZ_DEVERR_CONTEXT = 4,  /* context length < 0 or > table capacity           */
+  MZ_DEVERR_TIMEOUT = 8   /* a bounded wait on an mbarrier or flag gave up    */
+};
+
+/* ABI version of this header (bumped on any signature change). */
+MZ_API int mz_abi_version(void);
+
+/* Copies the calling thread's last error message into buf (NUL-terminated,
+ * truncated to len).  Returns the status code that produced it. */
+MZ_API int mz_last_error(char *buf, size_t len);
+
+/* ------------------------------------------------------------------------ */
+/* KV append.                                                                */
+/* ------------------------------------------------------------------------ */
+
+/* Scatter n_tokens new K/V rows into the pools by slot.
+ * Replaces PagedKVCache.append_kv, src/mlxz/paged_attention/paged_kv.py:63-93
+ * (the per-token write `pool[blocks[pos // bs], :, pos % bs, :] = k[0, :, i, :]`
+ * at :85-91; block-table growth stays on the host).
+ * k_new/v_new element (token i, head h, dim d) sits at
+ *   base + i * new_tok_stride + h * new_head_stride + d        (elements).
+ * slot_mapping: int64 [n_tokens] device array; a negative slot skips the row.
+ * Bit-exact copy. */
+MZ_API int mz_kv_append(void *k_pool, void *v_pool, const void *k_new, const void *v_new,
+                 int64_t new_tok_stride, int64_t new_head_stride,
+                 const int64_t *slot_mapping, int64_t n_tokens, int32_t n_kv_heads,
+                 int32_t head_dim, int32_t block_size, int64_t n_blocks, int32_t dtype,
+                 int32_t *dev_err, mz_stream_t stream);
+
+/* Decode-step append: one new token per sequence, written at position
+ * positions[b] of sequence b through its block table (negative position skips).
+ * Replaces the per-request cache update inside the batched decode of
+ * ContinuousBatchingEngine._process_decodes, src/mlxz/engine/continuous.py:625-633,
+ * with one launch over ragged sequences.
+ * k_new/v_new element (seq b, head h, dim d) at base + b*new_seq_stride +
+ * h*new_head_stride + d.  Bit-exact copy. */
+MZ_API int mz_kv_append_paged(void *k_pool, void *v_pool, const void *k_new, const void *v_new,
+                       int64_t new_seq_stride, int64_t new_head_stride,
+                       const int32_t *block_tables, int32_t max_blocks_per_seq,
+                       const int32_t *positions, int32_t n_seqs, int32_t n_kv_heads,
+                       int32_t head_dim, int32_t block_size, int64_t n_blocks, int32_t dtype,
+                       int32_t *dev_err, mz_stream_t stream);
+
+/* ------------------------------------------------------------------------ */
+/* Block-table gather.                                                       */
+/* ------------------------------------------------------------------------ */
+
+/* Materialise contiguous K/V for n_seqs sequences.
+ * Replaces PagedKVCache.get_kv, src/mlxz/paged_attention/paged_kv.py:95-137.
+ * Sequence b is written as [n_kv_heads][ctx_lens[b]][head_dim] starting at
+ * element out_token_offsets[b] * n_kv_heads * head_dim of out_k / out_v
+ * (so one sequence gives the reference's (1, H, T, D) layout).
+ * max_ctx must be >= every ctx_lens[b] (it sizes the grid).  Bit-exact. */
+MZ_API int mz_kv_gather(void *out_k, void *out_v, const void *k_pool, const void *v_pool,
+                 const int32_t *block_tables, int32_t max_blocks_per_seq,
+                 const int32_t *ctx_lens, const int64_t *out_token_offsets, int32_t n_seqs,
+                 int64_t max_ctx, int32_t n_kv_heads, int32_t head_dim, int32_t block_size,
+                 int64_t n_blocks, int32_t dtype, int32_t *dev_err, mz_stream_t stream);
+
+/* ------------------------------------------------------------------------ */
+/* Fused GQA paged decode attention.                                         */
+/* ------------------------------------------------------------------------ */
+
+/* Bytes of workspace mz_paged_decode needs for these sizes on `device`
+ * (num_warps as passed to mz_paged_decode; 0 = the default grid).
+ * rows_per_kv_head = n_q_tokens * (n_heads / n_kv_heads), at most 16. */
+MZ_API int mz_paged_decode_workspace_size(int32_t n_seqs, int32_t n_kv_heads, int32_t rows_per_kv_head,
+                                   int32_t head_dim, int32_t num_warps, int32_t device,
+                                   size_t *bytes);
+
+/* out = softmax(q . K^T * scale) . V over each sequence's first ctx_lens[b]
+ * tokens, with query head hq reading KV head hq / (n_heads / n_kv_heads) and
+ * no mask, as in paged_attention_forward, src/mlxz/paged_attention/attention.py:9-49
+ * (get_kv + mx.repeat + mx.fast.scaled_dot_product_attention, :23-42), fused:
+ * no gather, no repeat.  Online softmax, fp32 accumulation.
+ * q element (seq b, query token i, head h, dim d) at
+ *   q + b*q_seq_stride + i*q_tok_stride + h*q_head_stride + d   (elements, dtype),
+ * out likewise with out_* strides and element type out_dtype (dtype or F32).
+ * Supported: dtype F16/BF16, head_dim 64 or 128, block_size a multiple of 16,
+ * n_q_tokens * (n_heads / n_kv_heads) <= 16.  K/V pools and q need 16-byte
+ * alignment.  A sequence with ctx_lens[b] == 0 gets zeros.
+ * workspace: >= mz_paged_decode_workspace_size bytes, zero-filled before its
+ * first use; every successful call leaves its counter region zeroed again.
+ * After a call that set a dev_err bit, zero the workspace before reuse.
+ * num_warps: persistent warps to launch (0 = one full wave of the device). */
+MZ_API int mz_paged_decode(void *out, int32_t out_dtype, int64_t out_seq_stride, int64_t out_tok_stride,
+                    int64_t out_head_stride, const void *q, int64_t q_seq_stride,
+                    int64_t q_tok_stride, int64_t q_head_stride, int32_t n_q_tokens,
+                    const void *k_pool, const void *v_pool, const int32_t *block_tables,
+                    int32_t max_blocks_per_seq, const int32_t *ctx_lens, int32_t n_seqs,
+                    int32_t n_heads, int32_t n_kv_heads, int32_t head_dim, int32_t block_size,
+                    int64_t n_blocks, float scale, int32_t dtype, int32_t num_warps,
+                    void *workspace, size_t workspace_bytes, int32_t *dev_err,
+                    mz_stream_t stream);
+
+/* ------------------------------------------------------------------------ */
+/* Prefix-cache block movement.                                              */
+/* ------------------------------------------------------------------------ */
+
+/* Copy whole blocks src_ids[i] -> dst_ids[i] in each of n_pools pools; pool p
+ * starts at pool_base + p * pool_stride_bytes and holds n_blocks blocks of
+ * block_bytes.  The data half of copy-on-write: BlockManager.copy_on_write,
+ * src/mlxz/paged_attention/block_manager.py:111-134, leaves the copy to the
+ * caller (:118).  It also replaces the prefix deep copies of
+ * src/mlxz/prefix_cache/memory.py:19-35 when a shared partial block is
+ * written.  dst ids must be distinct and must not appear in src_ids.
+ * block_bytes and pool_stride_bytes must be multiples of 16 and pool_base
+ * 16-byte aligned.  Bit-exact. */
+MZ_API int mz_block_copy(void *pool_base, int64_t pool_stride_bytes, int32_t n_pools, int64_t block_bytes,
+                  const int32_t *src_ids, const int32_t *dst_ids, int32_t n_copies,
+                  int64_t n_blocks, int32_t *dev_err, mz_stream_t stream);
+
+/* Gather blocks ids[0..n_ids) of every pool into a contiguous staging buffer
+ * laid out [n_ids][n_pools][block_bytes] (the device side of eviction to the
+ * pinned host tier; the caller then copies staging to host on a side stream).
+ * Replaces the eviction path of PrefixCacheMemory._evict_until_room,
+ * src/mlxz/prefix_cache/memory.py:181-192, which dropped entries instead of
+ * moving them to a slower tier.  Same alignment rules as mz_block_copy. */
+MZ_API int mz_block_pack(void *staging, const void *pool_base, int64_t pool_stride_bytes, int32_t n_pools,
+                  int64_t block_bytes, const int32_t *ids, int32_t n_ids, int64_t n_blocks,
+                  int32_t *dev_err, mz_stream_t stream);
+
+/* Inverse of mz_block_pack: scatter staging [n_ids][n_pools][block_bytes] into
+ * blocks ids[i] (the reload half: restore of an evicted prefix,
+ * src/mlxz/engine/continuous.py:258-259). */
+MZ_API int mz_block_unpack(void *pool_base, int64_t pool_stride_bytes, int32_t n_pools,
+                    int64_t block_bytes, const void *staging, const int32_t *ids, int32_t n_ids,
+                    int64_t n_blocks, int32_t *dev_err, mz_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MLXZ_B200_H */

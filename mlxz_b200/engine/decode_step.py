@@ -1,0 +1,184 @@
+"""Continuous-batching decode step over paged KV (the KV side of one step).
+
+The reference batches only requests whose caches have the same offset
+(ContinuousBatchingEngine._process_decodes, src/mlxz/engine/continuous.py:386-388),
+concatenates their per-layer caches along the batch axis before the forward
+and splits them back afterwards (_build_batched_cache / _scatter_batched_cache,
+:804-832): two full KV copies per step.  Here every live sequence of any
+length runs in one ragged launch per layer, straight from the block pools:
+
+    per layer l:  mz_kv_append_paged  (new token -> pool slot via block table)
+                  mz_paged_decode     (fused GQA attention over ctx + 1 tokens)
+
+``PagedKVStore`` holds all layers' pools with one block table per sequence
+(the paged form of the per-request cache list built at continuous.py:195-200).
+"""
+from __future__ import annotations
+
+import torch
+
+from .. import ops
+from ..paged_attention.block_manager import BlockManager
+
+
+class PagedKVStore:
+    """K/V pools of every layer, ``pools[l, 0]`` = K and ``pools[l, 1]`` = V,
+    each ``[n_blocks, n_kv_heads, block_size, head_dim]``, sharing one
+    BlockManager (one block id addresses the same slot range in every layer)."""
+
+    def __init__(self, n_layers: int, n_blocks: int, n_kv_heads: int, head_dim: int,
+                 block_size: int = 16, dtype: torch.dtype = torch.bfloat16, device=None,
+                 init: str = "zeros") -> None:
+        self.device = torch.device(device) if device is not None else torch.device(
+            "cuda", torch.cuda.current_device())
+        self.n_layers, self.n_blocks = n_layers, n_blocks
+        self.n_kv_heads, self.head_dim, self.block_size, self.dtype = (n_kv_heads, head_dim,
+                                                                       block_size, dtype)
+        shape = (n_layers, 2, n_blocks, n_kv_heads, block_size, head_dim)
+        if init == "zeros":
+            self.pools = torch.zeros(shape, dtype=dtype, device=self.device)
+        elif init == "empty":
+            self.pools = torch.empty(shape, dtype=dtype, device=self.device)
+        else:
+            raise ValueError(init)
+        self.bm = BlockManager(n_blocks, block_size)
+        self.tables: dict[str, list[int]] = {}
+        self.offsets: dict[str, int] = {}
+
+    def k_pool(self, layer: int) -> torch.Tensor:
+        return self.pools[layer, 0]
+
+    def v_pool(self, layer: int) -> torch.Tensor:
+        return self.pools[layer, 1]
+
+    @property
+    def block_bytes(self) -> int:
+        """Bytes of one block in one pool (one layer's K or V)."""
+        return self.n_kv_heads * self.block_size * self.head_dim * self.pools.element_size()
+
+    def pool_stack(self) -> torch.Tensor:
+        """All pools as one ``[2 * n_layers, n_blocks, ...]`` stack (block moves)."""
+        return self.pools.view(2 * self.n_layers, self.n_blocks, self.n_kv_heads,
+                               self.block_size, self.head_dim)
+
+    def add_sequence(self, seq_id: str, n_tokens: int = 0, blocks: list[int] | None = None) -> None:
+        """Register a sequence holding `n_tokens` tokens, allocating blocks from
+        the BlockManager unless an explicit block list is given."""
+        need = -(-n_tokens // self.block_size)
+        if blocks is None:
+            blocks = self.bm.allocate(need)
+        elif len(blocks) < need:
+            raise ValueError("block list too short for n_tokens")
+        self.tables[seq_id] = list(blocks)
+        self.offsets[seq_id] = n_tokens
+
+    def free_sequence(self, seq_id: str) -> None:
+        if seq_id in self.tables:
+            self.bm.free(self.tables.pop(seq_id))
+            self.offsets.pop(seq_id, None)
+
+    def ensure_capacity(self, seq_id: str, extra: int) -> bool:
+        """Grow the table for `extra` more tokens; True if it changed."""
+        t = self.tables[seq_id]
+        need = -(-(self.offsets[seq_id] + extra) // self.block_size)
+        grew = False
+        while len(t) < need:
+            t.extend(self.bm.allocate(1))
+            grew = True
+        return grew
+
+
+class PagedDecodeStep:
+    """One decode step for a fixed set of sequences.
+
+    Device state: int32 block tables ``[B, max_blocks]``, the write positions
+    (= current offsets) and the attended lengths (offset + 1).  ``step``
+    takes the step's per-layer q ``[L, B, Hq, D]`` and new K/V ``[L, B, Hkv, D]``
+    already on the device; ``step_host`` is the end-to-end form that copies
+    them from (pinned) host memory and copies the output back.
+    """
+
+    def __init__(self, store: PagedKVStore, seq_ids: list[str], n_heads: int,
+                 scale: float | None = None, max_blocks: int | None = None) -> None:
+        self.store = store
+        self.seq_ids = list(seq_ids)
+        self.n_heads = n_heads
+        self.scale = scale if scale is not None else store.head_dim ** -0.5
+        self.B = len(seq_ids)
+        for s in self.seq_ids:
+            store.ensure_capacity(s, 1)
+        width = max(len(store.tables[s]) for s in self.seq_ids)
+        self.max_blocks = max(width, max_blocks or 0)
+        dev = store.device
+        self.tables = torch.full((self.B, self.max_blocks), -1, dtype=torch.int32, device=dev)
+        self.positions = torch.zeros(self.B, dtype=torch.int32, device=dev)
+        self.lengths = torch.zeros(self.B, dtype=torch.int32, device=dev)
+        self.sync_metadata()
+        G = n_heads // store.n_kv_heads
+        self.workspace = ops.decode_workspace(self.B, store.n_kv_heads, G, store.head_dim,
+                                              dev.index if dev.index is not None else 0)
+        self._dev_in = None
+        self._graph = None
+
+    def sync_metadata(self) -> None:
+        """Upload block tables and offsets from the host mirror."""
+        host = torch.full((self.B, self.max_blocks), -1, dtype=torch.int32)
+        for i, s in enumerate(self.seq_ids):
+            t = self.store.tables[s]
+            if len(t) > self.max_blocks:
+                raise ValueError("a table outgrew max_blocks; rebuild the step")
+            if t:
+                host[i, : len(t)] = torch.tensor(t, dtype=torch.int32)
+        offs = torch.tensor([self.store.offsets[s] for s in self.seq_ids], dtype=torch.int32)
+        self.tables.copy_(host, non_blocking=False)
+        self.positions.copy_(offs)
+        self.lengths.copy_(offs + 1)
+
+    def layer(self, l: int, q: torch.Tensor, k_new: torch.Tensor, v_new: torch.Tensor,
+              out: torch.Tensor) -> None:
+        """Append this step's token of layer l, then attend (device tensors)."""
+        st = self.store
+        ops.kv_append_paged(st.k_pool(l), st.v_pool(l), k_new, v_new, self.tables, self.positions)
+        ops.paged_decode(q, st.k_pool(l), st.v_pool(l), self.tables, self.lengths,
+                         scale=self.scale, out=out, workspace=self.workspace)
+
+    def step(self, q: torch.Tensor, k_new: torch.Tensor, v_new: torch.Tensor,
+             out: torch.Tensor | None = None, advance: bool = False) -> torch.Tensor:
+        """All layers: q ``[L, B, Hq, D]``, k_new/v_new ``[L, B, Hkv, D]``."""
+        if out is None:
+            out = torch.empty_like(q)
+        for l in range(self.store.n_layers):
+            self.layer(l, q[l], k_new[l], v_new[l], out[l])
+        if advance:
+            self.advance()
+        return out
+
+    def advance(self) -> None:
+        """Commit the appended token: offsets += 1, growing tables as needed."""
+        grew = False
+        for s in self.seq_ids:
+            self.store.offsets[s] += 1
+            grew |= self.store.ensure_capacity(s, 1)
+        if grew:
+            self.sync_metadata()
+        else:
+            self.positions.add_(1)
+            self.lengths.add_(1)
+
+    def step_host(self, q_host: torch.Tensor, k_host: torch.Tensor, v_host: torch.Tensor,
+                  out_host: torch.Tensor, advance: bool = False) -> torch.Tensor:
+        """End-to-end step from host buffers (pinned for async copies): H2D of
+        the inputs, every layer's append + attention, D2H of the outputs."""
+        dev = self.store.device
+        if self._dev_in is None or self._dev_in[0].shape != q_host.shape:
+            self._dev_in = (torch.empty(q_host.shape, dtype=q_host.dtype, device=dev),
+                            torch.empty(k_host.shape, dtype=k_host.dtype, device=dev),
+                            torch.empty(v_host.shape, dtype=v_host.dtype, device=dev),
+                            torch.empty(q_host.shape, dtype=q_host.dtype, device=dev))
+        q, k, v, o = self._dev_in
+        q.copy_(q_host, non_blocking=True)
+        k.copy_(k_host, non_blocking=True)
+        v.copy_(v_host, non_blocking=True)
+        self.step(q, k, v, out=o, advance=advance)
+        out_host.copy_(o, non_blocking=True)
+        return out_host

@@ -1,0 +1,334 @@
+"""Torch-tensor front end of the C-ABI kernels.
+
+Each function validates shapes on the host, passes raw device pointers and the
+current CUDA stream to libmlxz_b200.so, and returns without synchronising.
+Kernels report out-of-range block ids, slots and context lengths through a
+per-device int32 error word instead of trapping; ``check_device_errors`` reads
+and clears it (``MLXZ_B200_DEBUG=1`` makes every call check it).
+"""
+from __future__ import annotations
+
+import ctypes
+import math
+import os
+
+import torch
+
+from . import _native as nat
+
+_DTYPES = {torch.float16: nat.MZ_DTYPE_F16, torch.bfloat16: nat.MZ_DTYPE_BF16,
+           torch.float32: nat.MZ_DTYPE_F32}
+_DEBUG = os.environ.get("MLXZ_B200_DEBUG", "0") not in ("", "0")
+
+_err_words: dict[int, torch.Tensor] = {}
+_workspaces: dict[tuple[int, int], torch.Tensor] = {}
+
+
+def dtype_code(dt: torch.dtype) -> int:
+    try:
+        return _DTYPES[dt]
+    except KeyError:
+        raise ValueError(f"unsupported dtype {dt}") from None
+
+
+def _dev_index(t: torch.Tensor) -> int:
+    if t.device.type != "cuda":
+        raise ValueError(f"expected a CUDA tensor, got one on {t.device}")
+    return t.device.index if t.device.index is not None else torch.cuda.current_device()
+
+
+def _stream(device: int) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def error_word(device: int) -> torch.Tensor:
+    """The int32 device error word kernels on `device` report into."""
+    w = _err_words.get(device)
+    if w is None:
+        w = torch.zeros(1, dtype=torch.int32, device=f"cuda:{device}")
+        _err_words[device] = w
+    return w
+
+
+def check_device_errors(device: int | None = None, clear: bool = True) -> int:
+    """Synchronise with `device`'s error word; raise DeviceError if a bit is set."""
+    device = torch.cuda.current_device() if device is None else device
+    w = _err_words.get(device)
+    if w is None:
+        return 0
+    bits = int(w.item())
+    if bits and clear:
+        w.zero_()
+    if bits:
+        raise nat.DeviceError(bits)
+    return 0
+
+
+def _after(device: int) -> None:
+    if _DEBUG:
+        check_device_errors(device)
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def _check_pools(k_pool: torch.Tensor, v_pool: torch.Tensor) -> tuple[int, int, int, int]:
+    if k_pool.shape != v_pool.shape or k_pool.dtype != v_pool.dtype:
+        raise ValueError("k_pool and v_pool must have the same shape and dtype")
+    if k_pool.dim() != 4 or not k_pool.is_contiguous() or not v_pool.is_contiguous():
+        raise ValueError("pools must be contiguous [n_blocks, n_kv_heads, block_size, head_dim]")
+    if k_pool.device != v_pool.device:
+        raise ValueError("pools must be on the same device")
+    n, h, bs, d = k_pool.shape
+    return n, h, bs, d
+
+
+def _as_i32(t: torch.Tensor, device: torch.device, name: str) -> torch.Tensor:
+    if t.dtype != torch.int32 or t.device != device or not t.is_contiguous():
+        raise ValueError(f"{name} must be a contiguous int32 tensor on {device}")
+    return t
+
+
+# ---------------------------------------------------------------------------
+# Append / gather
+# ---------------------------------------------------------------------------
+
+def kv_append(k_pool: torch.Tensor, v_pool: torch.Tensor, keys: torch.Tensor,
+              values: torch.Tensor, slot_mapping: torch.Tensor) -> None:
+    """Write keys/values ``(1, H, n, D)`` (or ``(H, n, D)``) to pool slots.
+
+    slot_mapping: int64 ``[n]`` on the pools' device; a negative slot skips.
+    """
+    n_blocks, H, bs, D = _check_pools(k_pool, v_pool)
+    if keys.shape != values.shape or keys.dtype != k_pool.dtype or values.dtype != k_pool.dtype:
+        raise ValueError("keys/values must match each other and the pool dtype")
+    kk, vv = keys, values
+    if kk.dim() == 4:
+        if kk.shape[0] != 1:
+            raise ValueError("keys must have batch size 1: (1, H, n, D)")
+        kk, vv = kk[0], vv[0]
+    if kk.dim() != 3 or kk.shape[0] != H or kk.shape[2] != D:
+        raise ValueError(f"keys must be (1, {H}, n, {D}), got {tuple(keys.shape)}")
+    if kk.stride(2) != 1 or vv.stride(2) != 1 or kk.stride() != vv.stride():
+        kk, vv = kk.contiguous(), vv.contiguous()
+    n = kk.shape[1]
+    if slot_mapping.dtype != torch.int64 or slot_mapping.numel() != n or \
+            slot_mapping.device != k_pool.device:
+        raise ValueError("slot_mapping must be int64 [n] on the pool device")
+    if n == 0:
+        return
+    dev = _dev_index(k_pool)
+    nat.call("mz_kv_append", k_pool.data_ptr(), v_pool.data_ptr(), kk.data_ptr(), vv.data_ptr(),
+             kk.stride(1), kk.stride(0), slot_mapping.data_ptr(), n, H, D, bs, n_blocks,
+             dtype_code(k_pool.dtype), error_word(dev).data_ptr(), _stream(dev))
+    _after(dev)
+
+
+def kv_append_paged(k_pool: torch.Tensor, v_pool: torch.Tensor, keys: torch.Tensor,
+                    values: torch.Tensor, block_tables: torch.Tensor,
+                    positions: torch.Tensor) -> None:
+    """Decode-step append: keys/values ``[B, H, D]`` (or ``[B, H, 1, D]``), one
+    token per sequence at ``positions[b]`` through ``block_tables[b]``."""
+    n_blocks, H, bs, D = _check_pools(k_pool, v_pool)
+    kk, vv = keys, values
+    if kk.dim() == 4:
+        kk, vv = kk[:, :, 0, :], vv[:, :, 0, :]
+    if kk.dim() != 3 or kk.shape[1:] != (H, D) or kk.shape != vv.shape:
+        raise ValueError(f"keys must be [B, {H}, D={D}], got {tuple(keys.shape)}")
+    if kk.dtype != k_pool.dtype or vv.dtype != k_pool.dtype:
+        raise ValueError("keys/values dtype must match the pool")
+    if kk.stride(2) != 1 or vv.stride(2) != 1 or kk.stride() != vv.stride():
+        kk, vv = kk.contiguous(), vv.contiguous()
+    B = kk.shape[0]
+    _as_i32(block_tables, k_pool.device, "block_tables")
+    _as_i32(positions, k_pool.device, "positions")
+    if block_tables.dim() != 2 or block_tables.shape[0] < B or positions.numel() < B:
+        raise ValueError("block_tables must be [>=B, max_blocks] and positions [>=B]")
+    if B == 0:
+        return
+    dev = _dev_index(k_pool)
+    nat.call("mz_kv_append_paged", k_pool.data_ptr(), v_pool.data_ptr(), kk.data_ptr(),
+             vv.data_ptr(), kk.stride(0), kk.stride(1), block_tables.data_ptr(),
+             block_tables.shape[1], positions.data_ptr(), B, H, D, bs, n_blocks,
+             dtype_code(k_pool.dtype), error_word(dev).data_ptr(), _stream(dev))
+    _after(dev)
+
+
+def kv_gather(k_pool: torch.Tensor, v_pool: torch.Tensor, block_tables: torch.Tensor,
+              ctx_lens: torch.Tensor, ctx_lens_host: list[int]) -> tuple[torch.Tensor, torch.Tensor]:
+    """Gather each sequence's KV into contiguous ``[H, ctx_b, D]`` pieces.
+
+    Returns (K, V) as flat tensors ``[sum_b H*ctx_b*D]`` viewed per sequence by
+    the caller; with one sequence they are shaped ``(1, H, T, D)``.
+    """
+    n_blocks, H, bs, D = _check_pools(k_pool, v_pool)
+    _as_i32(block_tables, k_pool.device, "block_tables")
+    _as_i32(ctx_lens, k_pool.device, "ctx_lens")
+    B = len(ctx_lens_host)
+    offs = [0] * B
+    tot = 0
+    for i, c in enumerate(ctx_lens_host):
+        offs[i] = tot
+        tot += c
+    out_k = torch.empty(tot * H * D, dtype=k_pool.dtype, device=k_pool.device)
+    out_v = torch.empty_like(out_k)
+    if B == 1:
+        out_k = out_k.view(1, H, tot, D)
+        out_v = out_v.view(1, H, tot, D)
+    if B == 0 or tot == 0:
+        return out_k, out_v
+    off_t = torch.tensor(offs, dtype=torch.int64).to(k_pool.device, non_blocking=True)
+    dev = _dev_index(k_pool)
+    nat.call("mz_kv_gather", out_k.data_ptr(), out_v.data_ptr(), k_pool.data_ptr(),
+             v_pool.data_ptr(), block_tables.data_ptr(), block_tables.shape[1],
+             ctx_lens.data_ptr(), off_t.data_ptr(), B, max(ctx_lens_host), H, D, bs, n_blocks,
+             dtype_code(k_pool.dtype), error_word(dev).data_ptr(), _stream(dev))
+    _after(dev)
+    return out_k, out_v
+
+
+# ---------------------------------------------------------------------------
+# Decode attention
+# ---------------------------------------------------------------------------
+
+def decode_workspace(n_seqs: int, n_kv_heads: int, rows: int, head_dim: int, device: int,
+                     num_warps: int = 0) -> torch.Tensor:
+    """A zero-initialised workspace big enough for these sizes (cached, grows)."""
+    size = ctypes.c_size_t(0)
+    nat.call("mz_paged_decode_workspace_size", n_seqs, n_kv_heads, rows, head_dim, num_warps,
+             device, ctypes.byref(size))
+    need = int(size.value)
+    key = (device, 0)
+    ws = _workspaces.get(key)
+    if ws is None or ws.numel() < need:
+        ws = torch.zeros(max(need, 1 << 20), dtype=torch.uint8, device=f"cuda:{device}")
+        _workspaces[key] = ws
+    return ws
+
+
+def reset_workspaces() -> None:
+    """Zero every cached workspace (needed after a call that reported an error)."""
+    for ws in _workspaces.values():
+        ws.zero_()
+
+
+def paged_decode(q: torch.Tensor, k_pool: torch.Tensor, v_pool: torch.Tensor,
+                 block_tables: torch.Tensor, ctx_lens: torch.Tensor, scale: float | None = None,
+                 out: torch.Tensor | None = None, out_dtype: torch.dtype | None = None,
+                 num_warps: int = 0, workspace: torch.Tensor | None = None) -> torch.Tensor:
+    """Fused GQA paged decode attention.
+
+    q: ``[B, Hq, D]`` (one query token per sequence) or ``[B, n_q, Hq, D]``.
+    Returns ``out`` with q's shape, dtype ``out_dtype`` (default q.dtype).
+    """
+    n_blocks, Hkv, bs, D = _check_pools(k_pool, v_pool)
+    if q.dtype != k_pool.dtype:
+        raise ValueError("q dtype must match the pools")
+    if q.dim() == 3:
+        B, Hq, Dq = q.shape
+        nq = 1
+        q_sb, q_st, q_sh = q.stride(0), 0, q.stride(1)
+    elif q.dim() == 4:
+        B, nq, Hq, Dq = q.shape
+        q_sb, q_st, q_sh = q.stride(0), q.stride(1), q.stride(2)
+    else:
+        raise ValueError("q must be [B, Hq, D] or [B, n_q, Hq, D]")
+    if Dq != D or q.stride(-1) != 1:
+        raise ValueError(f"q head_dim must be {D} with unit stride")
+    if Hq % Hkv:
+        raise ValueError(f"n_heads {Hq} is not a multiple of n_kv_heads {Hkv}")
+    _as_i32(block_tables, k_pool.device, "block_tables")
+    _as_i32(ctx_lens, k_pool.device, "ctx_lens")
+    if block_tables.dim() != 2 or block_tables.shape[0] < B or ctx_lens.numel() < B:
+        raise ValueError("block_tables must be [>=B, max_blocks] and ctx_lens [>=B]")
+    out_dtype = out_dtype or q.dtype
+    if out is None:
+        out = torch.empty(q.shape, dtype=out_dtype, device=q.device)
+    if out.shape != q.shape or out.dtype != out_dtype or out.stride(-1) != 1:
+        raise ValueError("out must match q's shape with unit last stride")
+    if q.dim() == 3:
+        o_sb, o_st, o_sh = out.stride(0), 0, out.stride(1)
+    else:
+        o_sb, o_st, o_sh = out.stride(0), out.stride(1), out.stride(2)
+    if scale is None:
+        scale = D ** -0.5
+    if B == 0:
+        return out
+    dev = _dev_index(q)
+    rows = nq * (Hq // Hkv)
+    if workspace is None:
+        workspace = decode_workspace(B, Hkv, rows, D, dev, num_warps)
+    nat.call("mz_paged_decode", out.data_ptr(), dtype_code(out_dtype), o_sb, o_st, o_sh,
+             q.data_ptr(), q_sb, q_st, q_sh, nq, k_pool.data_ptr(), v_pool.data_ptr(),
+             block_tables.data_ptr(), block_tables.shape[1], ctx_lens.data_ptr(), B, Hq, Hkv,
+             D, bs, n_blocks, float(scale), dtype_code(q.dtype), num_warps,
+             workspace.data_ptr(), workspace.numel(), error_word(dev).data_ptr(), _stream(dev))
+    _after(dev)
+    return out
+
+
+# ---------------------------------------------------------------------------
+# Block movement
+# ---------------------------------------------------------------------------
+
+def _pool_geometry(pools: torch.Tensor) -> tuple[int, int, int]:
+    """(n_pools, n_blocks, block_bytes) of a contiguous ``[P, n_blocks, ...]``
+    stack of pools (or a single pool ``[n_blocks, ...]``)."""
+    if not pools.is_contiguous():
+        raise ValueError("pools must be contiguous")
+    return pools.shape[0], pools.shape[1], pools[0, 0].numel() * pools.element_size()
+
+
+def block_copy(pools: torch.Tensor, src_ids: torch.Tensor, dst_ids: torch.Tensor) -> None:
+    """Copy block src_ids[i] -> dst_ids[i] in every pool of ``pools``
+    (a contiguous ``[P, n_blocks, ...]`` stack)."""
+    P, N, bb = _pool_geometry(pools)
+    _as_i32(src_ids, pools.device, "src_ids")
+    _as_i32(dst_ids, pools.device, "dst_ids")
+    if src_ids.numel() != dst_ids.numel():
+        raise ValueError("src_ids and dst_ids must have the same length")
+    n = src_ids.numel()
+    if n == 0:
+        return
+    dev = _dev_index(pools)
+    nat.call("mz_block_copy", pools.data_ptr(), N * bb, P, bb, src_ids.data_ptr(),
+             dst_ids.data_ptr(), n, N, error_word(dev).data_ptr(), _stream(dev))
+    _after(dev)
+
+
+def block_pack(pools: torch.Tensor, ids: torch.Tensor, staging: torch.Tensor | None = None
+               ) -> torch.Tensor:
+    """Gather blocks ``ids`` of every pool into ``staging[n, P, block_bytes]`` (uint8)."""
+    P, N, bb = _pool_geometry(pools)
+    _as_i32(ids, pools.device, "ids")
+    n = ids.numel()
+    if staging is None:
+        staging = torch.empty((n, P, bb), dtype=torch.uint8, device=pools.device)
+    if staging.numel() < n * P * bb or not staging.is_contiguous():
+        raise ValueError("staging too small or not contiguous")
+    if n:
+        dev = _dev_index(pools)
+        nat.call("mz_block_pack", staging.data_ptr(), pools.data_ptr(), N * bb, P, bb,
+                 ids.data_ptr(), n, N, error_word(dev).data_ptr(), _stream(dev))
+        _after(dev)
+    return staging
+
+
+def block_unpack(pools: torch.Tensor, ids: torch.Tensor, staging: torch.Tensor) -> None:
+    """Scatter ``staging[n, P, block_bytes]`` into blocks ``ids`` of every pool."""
+    P, N, bb = _pool_geometry(pools)
+    _as_i32(ids, pools.device, "ids")
+    n = ids.numel()
+    if staging.numel() < n * P * bb or not staging.is_contiguous() or \
+            staging.device != pools.device:
+        raise ValueError("staging must be a contiguous device buffer of n*P*block_bytes")
+    if n:
+        dev = _dev_index(pools)
+        nat.call("mz_block_unpack", pools.data_ptr(), N * bb, P, bb, staging.data_ptr(),
+                 ids.data_ptr(), n, N, error_word(dev).data_ptr(), _stream(dev))
+        _after(dev)
+
+
+def default_scale(head_dim: int) -> float:
+    return 1.0 / math.sqrt(head_dim)

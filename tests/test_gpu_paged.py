@@ -1,0 +1,313 @@
+"""GPU parity: append / gather / decode attention / block moves through the
+C ABI, against the golden fixtures (the reference's own outputs) and the CPU
+oracle on the same seeded inputs.
+
+Tolerances: data movement is bit-exact (SHA-256 or array equality).
+Attention: max|out - ref| / max|ref| <= 2e-3 against the fp32/float64 oracle.
+"""
+import hashlib
+import json
+
+import numpy as np
+import pytest
+import torch
+
+from mlxz_b200 import ops
+from mlxz_b200._native import DeviceError
+from mlxz_b200.paged_attention import (BlockManager, OutOfBlocksError, PagedKVCache,
+                                       paged_attention_forward)
+from oracle import paged as opaged
+from oracle import rng
+from tests.conftest import GOLDEN
+from tests.gpu_util import TORCH, random_paged_case, rel_err, sha_t, to_bits, to_dev
+from tests.test_oracle_golden import c1_inputs
+
+pytestmark = pytest.mark.gpu
+ATOL_REL = 2e-3
+
+
+def test_c1_golden_through_reference_api(cuda):
+    """C1 (1B shape, fp16, 4 ragged sequences, random block tables): append,
+    gather and attention through PagedKVCache / paged_attention_forward."""
+    g = json.loads((GOLDEN / "c1_layer.json").read_text())
+    gold_attn = np.load(GOLDEN / "c1_layer_attn.npy")
+    inp = c1_inputs()
+    bm = BlockManager(inp["n_blocks"], inp["bs"])
+    cache = PagedKVCache(bm, inp["H"], inp["D"], dtype=torch.float16, device=cuda)
+    for b in range(4):
+        sid = f"seq{b}"
+        cache._block_tables[sid] = list(inp["tables"][b])  # injected, as in the fixture
+        cache._offsets[sid] = 0
+        cache.append_kv(sid, to_dev(inp["pre_k"][b], "f16", cuda)[None],
+                        to_dev(inp["pre_v"][b], "f16", cuda)[None])
+    for b in range(4):
+        sid = f"seq{b}"
+        cache.append_kv(sid, to_dev(inp["new_k"][b], "f16", cuda)[None],
+                        to_dev(inp["new_v"][b], "f16", cuda)[None])
+    torch.cuda.synchronize()
+    ops.check_device_errors(0)
+    assert sha_t(cache.k_pool) == g["k_pool_sha256"]
+    assert sha_t(cache.v_pool) == g["v_pool_sha256"]
+    for b in range(4):
+        sid = f"seq{b}"
+        k, v = cache.get_kv(sid)
+        assert list(k.shape) == g["seqs"][b]["shape"]
+        assert sha_t(k) == g["seqs"][b]["k_sha256"]
+        assert sha_t(v) == g["seqs"][b]["v_sha256"]
+        q = to_dev(inp["q"][b], "f16", cuda)[None]
+        out = paged_attention_forward(q, cache, sid, scale=g["scale"])
+        assert out.shape == (1, 32, 1, 64) and out.dtype == torch.float16
+        assert rel_err(out[0].float().cpu().numpy(), gold_attn[b]) <= ATOL_REL
+        # fp32 output path of the same kernel
+        out32 = ops.paged_decode(q[:, :, 0, :], cache.k_pool, cache.v_pool,
+                                 cache.block_table_tensor([sid]), cache.ctx_tensor([sid]),
+                                 scale=g["scale"], out_dtype=torch.float32)
+        assert rel_err(out32[0].cpu().numpy(), gold_attn[b][:, 0, :]) <= ATOL_REL
+    ops.check_device_errors(0)
+
+
+def test_bm_paged_replay_through_api(cuda):
+    """The reference's BlockManager-driven scenario (block growth, free,
+    reuse of freed blocks) replayed through the product API: identical block
+    tables, offsets, stats and pool bytes after every operation."""
+    g = json.loads((GOLDEN / "bm_paged.json").read_text())
+    c = g["config"]
+    dt = TORCH[c["dtype"]]
+    bm = BlockManager(c["n_blocks"], c["bs"])
+    cache = PagedKVCache(bm, c["H"], c["D"], dtype=dt, device=cuda)
+    for rec in g["ops"]:
+        sid = rec["seq"]
+        if rec["op"] == "alloc":
+            cache.allocate_sequence(sid, rec["n"])
+        elif rec["op"] == "free":
+            cache.free_sequence(sid)
+        else:
+            n = rec["n"]
+            k = rng.normal(g["seeds"]["k"], (c["H"], n, c["D"]), c["dtype"], stream=rec["k_stream"])
+            v = rng.normal(g["seeds"]["v"], (c["H"], n, c["D"]), c["dtype"], stream=rec["k_stream"])
+            cache.append_kv(sid, to_dev(k, c["dtype"], cuda)[None], to_dev(v, c["dtype"], cuda)[None])
+        assert {s: cache.get_block_table(s) for s in sorted(cache._block_tables)} == rec["tables"]
+        assert {s: cache.get_offset(s) for s in sorted(cache._offsets)} == rec["offsets"]
+        assert cache.stats == rec["stats"]
+        assert sha_t(cache.k_pool) == rec["k_pool_sha256"]
+        assert sha_t(cache.v_pool) == rec["v_pool_sha256"]
+    attn = np.load(GOLDEN / "bm_paged_attn.npy")
+    for i, sid in enumerate(g["attn_order"]):
+        k, v = cache.get_kv(sid)
+        gg = g["gathers"][sid]
+        assert sha_t(k) == gg["k_sha256"] and sha_t(v) == gg["v_sha256"]
+        q = rng.normal(g["seeds"]["q"], (c["Hq"], 1, c["D"]), c["dtype"], stream=gg["q_stream"])
+        out = paged_attention_forward(to_dev(q, c["dtype"], cuda)[None], cache, sid)
+        assert rel_err(out[0].float().cpu().numpy(), attn[i]) <= ATOL_REL
+    ops.check_device_errors(0)
+
+
+def test_append_out_of_blocks_partial_effect(cuda):
+    """Running out of blocks mid-append: earlier rows written, offset kept,
+    OutOfBlocksError raised (reference loop semantics)."""
+    bm = BlockManager(2, 16)
+    cache = PagedKVCache(bm, 2, 64, dtype=torch.bfloat16, device=cuda)
+    cache.allocate_sequence("s", 1)
+    k = torch.randn(1, 2, 40, 64, device=cuda).to(torch.bfloat16)
+    with pytest.raises(OutOfBlocksError):
+        cache.append_kv("s", k, k)
+    assert cache.get_offset("s") == 0
+    tab = cache.get_block_table("s")
+    assert len(tab) == 2
+    torch.cuda.synchronize()
+    got = cache.k_pool[tab].permute(1, 0, 2, 3).reshape(2, 32, 64)
+    assert torch.equal(got, k[0, :, :32])
+
+
+DECODE_CASES = [
+    # dtype, D, G, bs, ctx list, num_warps
+    ("bf16", 128, 4, 16, [513, 1, 15, 16, 17, 100, 2048, 777], 0),
+    ("bf16", 128, 4, 16, [513, 1, 15, 16, 17, 100, 2048, 777], 8),
+    ("bf16", 128, 4, 16, [513, 1, 15, 16, 17, 100, 2048, 777], 12),
+    ("bf16", 128, 8, 16, [300, 4096, 5, 0, 33], 0),
+    ("bf16", 128, 1, 32, [300, 64, 5, 1000], 4),
+    ("bf16", 128, 2, 64, [129, 64, 1], 0),
+    ("f16", 64, 4, 16, [38, 129, 301, 512], 0),
+    ("f16", 64, 4, 16, [38, 129, 301, 512], 4),
+    ("f16", 128, 16, 16, [70, 3], 0),
+    ("bf16", 64, 8, 16, [0, 0, 45], 0),
+]
+
+
+@pytest.mark.parametrize("dtype,D,G,bs,ctx,nw", DECODE_CASES)
+@pytest.mark.parametrize("out32", [False, True])
+def test_paged_decode_vs_oracle(cuda, dtype, D, G, bs, ctx, nw, out32):
+    Hkv = 2 if G == 16 else 4
+    case = random_paged_case(7 + len(ctx) + D + G, len(ctx), Hkv, D, bs, ctx, dtype, G=G)
+    kp, vp = to_dev(case["kp"], dtype, cuda), to_dev(case["vp"], dtype, cuda)
+    q = to_dev(case["q"][:, 0], dtype, cuda)
+    tables = torch.from_numpy(case["tables"]).to(cuda)
+    ctx_t = torch.from_numpy(case["ctx"]).to(cuda)
+    out = ops.paged_decode(q, kp, vp, tables, ctx_t, num_warps=nw,
+                           out_dtype=torch.float32 if out32 else None)
+    torch.cuda.synchronize()
+    ops.check_device_errors(0)
+    ref = opaged.paged_decode(case["q"][:, 0], case["kp"], case["vp"], case["tables"], case["ctx"],
+                              dtype)
+    assert rel_err(out.float().cpu().numpy(), ref) <= ATOL_REL
+    # zero-context sequences produce exact zeros
+    for b, c in enumerate(ctx):
+        if c == 0:
+            assert torch.count_nonzero(out[b]) == 0
+
+
+def test_paged_decode_multi_query_rows(cuda):
+    """n_q query tokens per sequence (no mask) and the 16-row chunking of
+    paged_attention_forward."""
+    dtype, D, G, Hkv = "bf16", 128, 4, 2
+    case = random_paged_case(99, 3, Hkv, D, 16, [40, 200, 7], dtype, nq=3, G=G)
+    kp, vp = to_dev(case["kp"], dtype, cuda), to_dev(case["vp"], dtype, cuda)
+    q = to_dev(case["q"], dtype, cuda)  # [B, 3, Hq, D]
+    out = ops.paged_decode(q, kp, vp, torch.from_numpy(case["tables"]).to(cuda),
+                           torch.from_numpy(case["ctx"]).to(cuda), out_dtype=torch.float32)
+    ref = opaged.paged_decode(case["q"], case["kp"], case["vp"], case["tables"], case["ctx"], dtype)
+    assert rel_err(out.cpu().numpy(), ref) <= ATOL_REL
+    # through the reference-shaped API with 5 query tokens (G=4 -> chunks of 4)
+    bm = BlockManager(64, 16)
+    cache = PagedKVCache(bm, Hkv, D, dtype=torch.bfloat16, device=cuda)
+    cache.allocate_sequence("x")
+    kk = torch.randn(1, Hkv, 150, D, device=cuda).to(torch.bfloat16)
+    vv = torch.randn(1, Hkv, 150, D, device=cuda).to(torch.bfloat16)
+    cache.append_kv("x", kk, vv)
+    qq = torch.randn(1, Hkv * G, 5, D, device=cuda).to(torch.bfloat16)
+    o = paged_attention_forward(qq, cache, "x")
+    r = opaged.attention(qq[0].float().cpu().numpy(), kk[0].float().cpu().numpy(),
+                         vv[0].float().cpu().numpy())
+    assert rel_err(o[0].float().cpu().numpy(), r) <= ATOL_REL
+
+
+@pytest.mark.parametrize("dtype,H,D,bs", [("bf16", 8, 128, 16), ("f16", 8, 64, 16),
+                                          ("bf16", 3, 24, 8), ("f16", 2, 7, 5)])
+def test_batched_append_and_gather_bit_exact(cuda, dtype, H, D, bs):
+    ctx = [0, 1, 15, 16, 33, 100]
+    B = len(ctx)
+    case = random_paged_case(31 + D, B, H, D, bs, [c + 1 for c in ctx], dtype, G=1)
+    kp, vp = to_dev(case["kp"], dtype, cuda), to_dev(case["vp"], dtype, cuda)
+    newk = rng.normal(41, (B, H, D), dtype, stream=1)
+    newv = rng.normal(41, (B, H, D), dtype, stream=2)
+    tables = torch.from_numpy(case["tables"]).to(cuda)
+    pos = torch.tensor(ctx, dtype=torch.int32, device=cuda)
+    ops.kv_append_paged(kp, vp, to_dev(newk, dtype, cuda), to_dev(newv, dtype, cuda), tables, pos)
+    # oracle
+    okp, ovp = case["kp"].copy(), case["vp"].copy()
+    for b in range(B):
+        blk = case["tables"][b][ctx[b] // bs]
+        okp[blk, :, ctx[b] % bs] = newk[b]
+        ovp[blk, :, ctx[b] % bs] = newv[b]
+    torch.cuda.synchronize()
+    ops.check_device_errors(0)
+    assert np.array_equal(to_bits(kp), okp) and np.array_equal(to_bits(vp), ovp)
+    lens = [c + 1 for c in ctx]
+    ok, ov = ops.kv_gather(kp, vp, tables, torch.tensor(lens, dtype=torch.int32, device=cuda), lens)
+    ok, ov = to_bits(ok).reshape(-1), to_bits(ov).reshape(-1)
+    off = 0
+    for b in range(B):
+        gk, gv = opaged.gather(okp, ovp, list(case["tables"][b]), lens[b], bs)
+        n = gk.size
+        assert np.array_equal(ok[off:off + n], gk.reshape(-1))
+        assert np.array_equal(ov[off:off + n], gv.reshape(-1))
+        off += n
+
+
+def test_slot_append_strided_input(cuda):
+    """mz_kv_append with a non-contiguous (1, H, n, D) view and skipped slots."""
+    H, D, bs, N = 4, 64, 16, 10
+    kp = torch.zeros(N, H, bs, D, dtype=torch.float16, device=cuda)
+    vp = torch.zeros_like(kp)
+    big = torch.randn(1, 2 * H, 12, D, device=cuda).half()
+    k = big[:, ::2]  # strided head axis
+    v = big[:, 1::2]
+    slots = torch.tensor([5, 17, -1, 40, 41, 159, 0, 1, 2, 3, 100, 101], dtype=torch.int64,
+                         device=cuda)
+    ops.kv_append(kp, vp, k, v, slots)
+    torch.cuda.synchronize()
+    okp = np.zeros((N, H, bs, D), dtype=np.uint16)
+    okv = okp.copy()
+    kb, vb = to_bits(k[0]), to_bits(v[0])
+    for i, s in enumerate(slots.tolist()):
+        if s >= 0:
+            okp[s // bs, :, s % bs] = kb[:, i]
+            okv[s // bs, :, s % bs] = vb[:, i]
+    assert np.array_equal(to_bits(kp), okp) and np.array_equal(to_bits(vp), okv)
+
+
+def test_block_copy_pack_unpack_bit_exact(cuda):
+    pools_np = rng.normal(3, (6, 20, 8, 16, 128), "bf16")  # 3 layers x (K, V)
+    pools = to_dev(pools_np, "bf16", cuda)
+    src = torch.tensor([1, 2, 3, 19], dtype=torch.int32, device=cuda)
+    dst = torch.tensor([10, 11, 0, 12], dtype=torch.int32, device=cuda)
+    ops.block_copy(pools, src, dst)
+    opaged.block_copy(pools_np, [1, 2, 3, 19], [10, 11, 0, 12])
+    torch.cuda.synchronize()
+    assert np.array_equal(to_bits(pools), pools_np)
+    ids = torch.tensor([4, 0, 17], dtype=torch.int32, device=cuda)
+    st = ops.block_pack(pools, ids)
+    torch.cuda.synchronize()
+    assert np.array_equal(st.cpu().numpy(), opaged.block_pack(pools_np, [4, 0, 17]))
+    fresh = torch.zeros_like(pools)
+    ops.block_unpack(fresh, ids, st)
+    torch.cuda.synchronize()
+    for b in (4, 0, 17):
+        assert torch.equal(fresh[:, b], pools[:, b])
+    ops.check_device_errors(0)
+
+
+def test_device_error_word_reports_bad_block_ids(cuda):
+    """Out-of-range table entries are skipped by the kernels' own bounds
+    checks and reported in the device error word (no trap)."""
+    kp = torch.zeros(4, 2, 16, 64, dtype=torch.bfloat16, device=cuda)
+    vp = torch.zeros_like(kp)
+    tables = torch.tensor([[0, 9]], dtype=torch.int32, device=cuda)
+    ctx = torch.tensor([20], dtype=torch.int32, device=cuda)
+    q = torch.randn(1, 8, 64, device=cuda).to(torch.bfloat16)
+    ops.paged_decode(q, kp, vp, tables, ctx)
+    torch.cuda.synchronize()
+    with pytest.raises(DeviceError):
+        ops.check_device_errors(0)
+    ops.reset_workspaces()
+    pos = torch.tensor([200], dtype=torch.int32, device=cuda)
+    ops.kv_append_paged(kp, vp, q[:, :2], q[:, :2], tables, pos)
+    torch.cuda.synchronize()
+    with pytest.raises(DeviceError):
+        ops.check_device_errors(0)
+    ops.check_device_errors(0)  # cleared
+
+
+def test_decode_full_size_properties(cuda):
+    """8B-shape layer at the benchmark batch (64 sequences, ctx in [512, 8192]):
+    constant V gives exactly that constant; a sample of sequences matches a
+    torch fp32 reference gathered through torch indexing."""
+    B, Hkv, G, D, bs = 64, 8, 4, 128, 16
+    gen = torch.Generator().manual_seed(0)
+    ctx = torch.randint(512, 8193, (B,), generator=gen)
+    need = (ctx + bs - 1) // bs
+    n_blocks = int(need.sum().item() * 1.1)
+    perm = torch.randperm(n_blocks, generator=gen)
+    tables = torch.full((B, int(need.max())), -1, dtype=torch.int32)
+    used = 0
+    for b in range(B):
+        tables[b, : need[b]] = perm[used:used + need[b]].int()
+        used += int(need[b])
+    kp = torch.randn(n_blocks, Hkv, bs, D, device=cuda).to(torch.bfloat16)
+    vp = torch.full_like(kp, 0.375)
+    q = torch.randn(B, Hkv * G, D, device=cuda).to(torch.bfloat16)
+    tab_d, ctx_d = tables.to(cuda), ctx.int().to(cuda)
+    out = ops.paged_decode(q, kp, vp, tab_d, ctx_d, out_dtype=torch.float32)
+    assert torch.allclose(out, torch.full_like(out, 0.375), rtol=0, atol=1e-6)
+    vp.normal_()
+    out = ops.paged_decode(q, kp, vp, tab_d, ctx_d, out_dtype=torch.float32)
+    torch.cuda.synchronize()
+    ops.check_device_errors(0)
+    for b in (0, 17, 63):
+        blocks = tables[b, : need[b]].long().to(cuda)
+        K = kp[blocks].permute(1, 0, 2, 3).reshape(Hkv, -1, D)[:, : ctx[b]].float()
+        V = vp[blocks].permute(1, 0, 2, 3).reshape(Hkv, -1, D)[:, : ctx[b]].float()
+        Kr, Vr = K.repeat_interleave(G, 0), V.repeat_interleave(G, 0)
+        s = torch.einsum("hd,htd->ht", q[b].float(), Kr) * D ** -0.5
+        ref = torch.einsum("ht,htd->hd", torch.softmax(s, -1), Vr)
+        assert rel_err(out[b].cpu().numpy(), ref.cpu().numpy()) <= ATOL_REL
