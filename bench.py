@@ -40,8 +40,8 @@ FALLBACK_HBM_GBS = 6650.0
 def parse_args():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=10)
-    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--steps", type=int, default=300)
+    ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="mlxz_b200", choices=["mlxz_b200", "reference"])
     ap.add_argument("--layers", type=int, default=L)
     ap.add_argument("--seed", type=int, default=0)

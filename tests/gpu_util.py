@@ -29,6 +29,22 @@ def rel_err(out, ref) -> float:
     return float(np.abs(out - ref).max() / max(np.abs(ref).max(), 1e-30))
 
 
+# Unit roundoff of the output element type: storing a result in bf16 (8-bit
+# significand) or fp16 (11-bit) alone moves it by up to this fraction of its
+# magnitude, so the 2e-3 attention bar is applied to the error beyond that.
+UNIT_ROUNDOFF = {torch.bfloat16: 2.0 ** -8, torch.float16: 2.0 ** -11, torch.float32: 0.0}
+
+
+def attn_err(out: torch.Tensor, ref) -> float:
+    """Attention error metric: max(|out - ref| - u*|ref|, 0) / max|ref|, with u
+    the unit roundoff of out's dtype (0 for float32 outputs)."""
+    u = UNIT_ROUNDOFF[out.dtype]
+    o = out.detach().float().cpu().numpy().astype(np.float64)
+    r = np.asarray(ref, dtype=np.float64)
+    excess = np.maximum(np.abs(o - r) - u * np.abs(r), 0.0)
+    return float(excess.max() / max(np.abs(r).max(), 1e-30))
+
+
 def random_paged_case(seed, B, Hkv, D, bs, ctx, dtype, n_blocks=None, nq=1, G=4):
     """Seeded pools/tables/q for a ragged batch (oracle-side uint16 bits)."""
     need = [(c + bs - 1) // bs for c in ctx]
