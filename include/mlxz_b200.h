@@ -151,6 +151,34 @@ MZ_API int mz_paged_decode(void *out, int32_t out_dtype, int64_t out_seq_stride,
                     void *workspace, size_t workspace_bytes, int32_t *dev_err,
                     mz_stream_t stream);
 
+/* mz_paged_decode without a workspace argument: it allocates nothing.
+ * No counterpart in the reference (which has no device memory management);
+ * it exists for callers that cannot allocate device memory when they call in,
+ * e.g. a host whose own memory pool already owns the GPU, an FFI binding with
+ * no device allocator of its own, or a latency-bound path where cudaMalloc's
+ * implicit synchronisation is not allowed.
+ * Scratch: a fixed 16 MiB array built into the library (a file-scope
+ * __device__ array), held by every GPU that loads the library until the
+ * process exits.  Sizes whose scratch would exceed it (see
+ * mz_paged_decode_workspace_size) return MZ_ERR_TOO_LARGE; for the 8B-shape
+ * batch of 64 sequences it needs about 3.5 MiB.
+ * The first call on each device looks the array's address up with
+ * cudaGetSymbolAddress (with that device current); make that first call before
+ * any stream capture.  Each call clears the array's counters on `stream`
+ * before its kernel.  All calls on a device share the one array, so calls that
+ * overlap on the GPU (other streams, other host threads) race: serialise them.
+ * Arguments and results are otherwise those of mz_paged_decode. */
+MZ_API int mz_paged_decode_noalloc(void *out, int32_t out_dtype, int64_t out_seq_stride,
+                                   int64_t out_tok_stride, int64_t out_head_stride, const void *q,
+                                   int64_t q_seq_stride, int64_t q_tok_stride,
+                                   int64_t q_head_stride, int32_t n_q_tokens, const void *k_pool,
+                                   const void *v_pool, const int32_t *block_tables,
+                                   int32_t max_blocks_per_seq, const int32_t *ctx_lens,
+                                   int32_t n_seqs, int32_t n_heads, int32_t n_kv_heads,
+                                   int32_t head_dim, int32_t block_size, int64_t n_blocks,
+                                   float scale, int32_t dtype, int32_t num_warps,
+                                   int32_t *dev_err, mz_stream_t stream);
+
 /* ------------------------------------------------------------------------ */
 /* Prefix-cache block movement.                                              */
 /* ------------------------------------------------------------------------ */

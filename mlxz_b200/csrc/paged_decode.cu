@@ -697,3 +697,156 @@ extern "C" int mz_paged_decode(void *out, int32_t out_dtype, int64_t out_seq_str
   MZ_CHECK_LAUNCH("mz_paged_decode");
   return MZ_OK;
 }
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant: the same kernel, with its scratch (split-piece
+// partials and per-pair arrival counters) in a fixed array built into the
+// library instead of a caller-supplied workspace.  For callers that cannot
+// allocate device memory when they call in: a host whose own pool already
+// owns the GPU's memory, an FFI binding with no device allocator of its own,
+// or a latency-bound path where cudaMalloc's implicit device synchronisation
+// is not allowed.  The array is loaded with the library's device code, so
+// every GPU that runs this code holds it until the process exits.
+// ---------------------------------------------------------------------------
+namespace mz {
+namespace decode {
+
+constexpr size_t kStaticScratchBytes = size_t(16) << 20;  // 16 MiB per device
+static __device__ __align__(256) uint8_t g_static_scratch[kStaticScratchBytes];
+
+struct StaticScratchSlot {
+  std::once_flag once;
+  void *ptr = nullptr;
+  cudaError_t err = cudaSuccess;
+};
+constexpr int kMaxStaticDevices = 64;
+StaticScratchSlot g_static_slots[kMaxStaticDevices];
+
+// Device address of g_static_scratch on `device`, which must be the current
+// device.  Host code cannot use the symbol's name as a device pointer, so the
+// address is looked up once per device with cudaGetSymbolAddress.
+int static_scratch_ptr(int device, void **ptr) {
+  if (device < 0 || device >= kMaxStaticDevices)
+    return fail(MZ_ERR_CUDA, "no usable current device (%d)", device);
+  StaticScratchSlot &s = g_static_slots[device];
+  std::call_once(s.once, [&s]() { s.err = cudaGetSymbolAddress(&s.ptr, g_static_scratch); });
+  if (s.err != cudaSuccess) return cuda_fail(s.err, "cudaGetSymbolAddress(decode scratch)");
+  if (!s.ptr) return fail(MZ_ERR_CUDA, "decode scratch has no device address");
+  *ptr = s.ptr;
+  return MZ_OK;
+}
+
+}  // namespace decode
+}  // namespace mz
+
+extern "C" int mz_paged_decode_noalloc(void *out, int32_t out_dtype, int64_t out_seq_stride,
+                                       int64_t out_tok_stride, int64_t out_head_stride,
+                                       const void *q, int64_t q_seq_stride, int64_t q_tok_stride,
+                                       int64_t q_head_stride, int32_t n_q_tokens,
+                                       const void *k_pool, const void *v_pool,
+                                       const int32_t *block_tables, int32_t max_blocks_per_seq,
+                                       const int32_t *ctx_lens, int32_t n_seqs, int32_t n_heads,
+                                       int32_t n_kv_heads, int32_t head_dim, int32_t block_size,
+                                       int64_t n_blocks, float scale, int32_t dtype,
+                                       int32_t num_warps, int32_t *dev_err, mz_stream_t stream) {
+  if (dtype != MZ_DTYPE_F16 && dtype != MZ_DTYPE_BF16)
+    return fail(MZ_ERR_UNSUPPORTED, "mz_paged_decode_noalloc: dtype must be F16 or BF16");
+  if (out_dtype != dtype && out_dtype != MZ_DTYPE_F32)
+    return fail(MZ_ERR_UNSUPPORTED, "mz_paged_decode_noalloc: out_dtype must equal dtype or be F32");
+  if (head_dim != 64 && head_dim != 128)
+    return fail(MZ_ERR_UNSUPPORTED, "mz_paged_decode_noalloc: head_dim %d (supported: 64, 128)",
+                head_dim);
+  if (block_size <= 0 || block_size % kTileTok)
+    return fail(MZ_ERR_UNSUPPORTED,
+                "mz_paged_decode_noalloc: block_size %d is not a multiple of 16", block_size);
+  if (n_seqs < 0 || n_kv_heads <= 0 || n_heads <= 0 || n_heads % n_kv_heads || n_q_tokens <= 0 ||
+      max_blocks_per_seq <= 0 || n_blocks <= 0)
+    return fail(MZ_ERR_INVALID_ARG, "mz_paged_decode_noalloc: bad sizes");
+  const int G = n_heads / n_kv_heads;
+  const int rows = n_q_tokens * G;
+  if (rows > 16)
+    return fail(MZ_ERR_UNSUPPORTED,
+                "mz_paged_decode_noalloc: n_q_tokens * (n_heads / n_kv_heads) = %d exceeds 16", rows);
+  if (!std::isfinite(scale))
+    return fail(MZ_ERR_INVALID_ARG, "mz_paged_decode_noalloc: scale not finite");
+  if (n_seqs == 0) return MZ_OK;
+  if (!out || !q || !k_pool || !v_pool || !block_tables || !ctx_lens)
+    return fail(MZ_ERR_INVALID_ARG, "mz_paged_decode_noalloc: null pointer");
+  if (!aligned(k_pool, 16) || !aligned(v_pool, 16) || !aligned(q, 4) || (q_seq_stride & 1) ||
+      (q_tok_stride & 1) || (q_head_stride & 1))
+    return fail(MZ_ERR_ALIGNMENT,
+                "mz_paged_decode_noalloc: pools need 16-byte alignment, q 4-byte alignment and "
+                "even strides");
+  const int ob = out_dtype == MZ_DTYPE_F32 ? 8 : 4;
+  if (!aligned(out, ob) || (out_seq_stride & 1) || (out_tok_stride & 1) || (out_head_stride & 1))
+    return fail(MZ_ERR_ALIGNMENT,
+                "mz_paged_decode_noalloc: out needs %d-byte alignment and even strides", ob);
+  const int64_t rows_total = n_blocks * n_kv_heads * block_size;
+  if (rows_total >= (int64_t(1) << 31))
+    return fail(MZ_ERR_UNSUPPORTED, "mz_paged_decode_noalloc: pool has >= 2^31 rows");
+  const bool bf16 = dtype == MZ_DTYPE_BF16;
+  const int device = current_device();
+  int64_t warps = 0;
+  if (int rc = resolve_warps(head_dim, bf16, num_warps, device, &warps)) return rc;
+  const int64_t n_pairs = (int64_t)n_seqs * n_kv_heads;
+  const WsLayout ws = ws_layout(n_pairs, warps, rows, head_dim);
+  if (ws.total > kStaticScratchBytes)
+    return fail(MZ_ERR_TOO_LARGE,
+                "mz_paged_decode_noalloc: these sizes need %zu bytes of scratch but the built-in "
+                "area holds %zu; lower n_seqs * n_kv_heads, rows or num_warps, or call "
+                "mz_paged_decode with a workspace",
+                ws.total, kStaticScratchBytes);
+  void *scratch = nullptr;
+  if (int rc = static_scratch_ptr(device, &scratch)) return rc;
+
+  CUtensorMap tk, tv;
+  if (int rc = make_pool_map(&tk, k_pool, rows_total, head_dim, bf16)) return rc;
+  if (int rc = make_pool_map(&tv, v_pool, rows_total, head_dim, bf16)) return rc;
+
+  Params p;
+  p.out = out;
+  p.o_sb = out_seq_stride;
+  p.o_st = out_tok_stride;
+  p.o_sh = out_head_stride;
+  p.out_f32 = out_dtype == MZ_DTYPE_F32;
+  p.q = q;
+  p.q_sb = q_seq_stride;
+  p.q_st = q_tok_stride;
+  p.q_sh = q_head_stride;
+  p.n_q = n_q_tokens;
+  p.G = G;
+  p.rows = rows;
+  p.tables = block_tables;
+  p.max_blocks = max_blocks_per_seq;
+  p.ctx = ctx_lens;
+  p.B = n_seqs;
+  p.Hkv = n_kv_heads;
+  p.bs = block_size;
+  p.tpb = block_size / kTileTok;
+  p.n_blocks = n_blocks;
+  p.scale_log2 = static_cast<float>(static_cast<double>(scale) * 1.4426950408889634);
+  auto *w8 = static_cast<uint8_t *>(scratch);
+  p.counters = reinterpret_cast<int32_t *>(w8 + ws.counters);
+  p.ml = reinterpret_cast<float *>(w8 + ws.ml);
+  p.part = reinterpret_cast<float *>(w8 + ws.part);
+  p.err = dev_err;
+
+  int per_sm = 0;
+  if (int rc = ctas_per_sm(head_dim, bf16, &per_sm)) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // The area keeps whatever the previous call left; the arrival counters
+  // must start at zero, so clear them on this stream first.
+  cudaError_t e = cudaMemsetAsync(p.counters, 0, n_pairs * sizeof(int32_t), s);
+  if (e != cudaSuccess) return cuda_fail(e, "mz_paged_decode_noalloc: clearing counters");
+  const unsigned grid = static_cast<unsigned>(warps / kWarps);
+#define MZ_LAUNCH(D_, BF_)                                                               \
+  paged_decode_kernel<D_, BF_><<<grid, kWarps * 32, Cfg<D_>::kSmemBytes, s>>>(tk, tv, p)
+  if (head_dim == 128) {
+    if (bf16) MZ_LAUNCH(128, true); else MZ_LAUNCH(128, false);
+  } else {
+    if (bf16) MZ_LAUNCH(64, true); else MZ_LAUNCH(64, false);
+  }
+#undef MZ_LAUNCH
+  MZ_CHECK_LAUNCH("mz_paged_decode_noalloc");
+  return MZ_OK;
+}
