@@ -1,9 +1,9 @@
 #!/usr/bin/env python
 """Paged-decode benchmark on the Llama-3.1-8B KV shape, batch 64 per GPU.
 
-One step = for each of 32 layers: append one new token per sequence into the
-paged pool (mz_kv_append_paged), then fused GQA decode attention over
-ctx + 1 tokens (mz_paged_decode).  Sequences: 64 with ctx ~ U[512, 8192]
+One step = for each of 32 layers, one launch of mz_paged_append_decode: append
+one new token per sequence into the paged pool, then fused GQA decode
+attention over ctx + 1 tokens.  Sequences: 64 with ctx ~ U[512, 8192]
 (seeded), block size 16, pools sized to the blocks needed + 10 %, random
 block tables, Q/K/V ~ N(0, 1) bf16.  Each step rewrites the same new-token
 slots, so every timed step does identical work.
@@ -50,6 +50,9 @@ def parse_args():
                     help="approximate CPU time budget of the cpu_baseline sample")
     ap.add_argument("--num-warps", type=int, default=0)
     ap.add_argument("--no-clocks", action="store_true")
+    ap.add_argument("--separate-append", action="store_true",
+                    help="append with mz_kv_append_paged, then mz_paged_decode (two launches)")
+    ap.add_argument("--no-e2e", action="store_true")
     return ap.parse_args()
 
 
@@ -266,12 +269,17 @@ def run_gpu(args, rank: int, world: int, local_rank: int) -> None:
     def one_step(ev=None):
         for l in range(nl):
             st = step.store
-            ops.kv_append_paged(st.k_pool(l), st.v_pool(l), kn[l], vn[l], step.tables, step.positions)
+            if args.separate_append:
+                ops.kv_append_paged(st.k_pool(l), st.v_pool(l), kn[l], vn[l], step.tables,
+                                    step.positions)
             if ev is not None:
                 ev[l][0].record()
-            ops.paged_decode(q[l], st.k_pool(l), st.v_pool(l), step.tables, step.lengths,
-                             scale=step.scale, out=out[l], workspace=step.workspace,
-                             num_warps=args.num_warps)
+            if args.separate_append:
+                ops.paged_decode(q[l], st.k_pool(l), st.v_pool(l), step.tables, step.lengths,
+                                 scale=step.scale, out=out[l], workspace=step.workspace,
+                                 num_warps=args.num_warps)
+            else:
+                step.layer(l, q[l], kn[l], vn[l], out[l], num_warps=args.num_warps)
             if ev is not None:
                 ev[l][1].record()
             if world > 1:
@@ -309,40 +317,43 @@ def run_gpu(args, rank: int, world: int, local_rank: int) -> None:
     dec_mean = sum(dec_ms) / len(dec_ms)
     ops.check_device_errors(local_rank)
 
-    # End to end through the public step API: pinned host inputs/outputs.
-    qh = q.cpu().pin_memory()
-    kh = kn.cpu().pin_memory()
-    vh = vn.cpu().pin_memory()
-    oh = torch.empty(q.shape if world == 1 else (nl, world, B, hq, D), dtype=torch.bfloat16).pin_memory()
-    h2d = qh.numel() * 2 + kh.numel() * 2 + vh.numel() * 2
-    d2h = oh.numel() * 2
+    e2e_ms, h2d, d2h = float('nan'), 0, 0
+    if not args.no_e2e:
+        # End to end through the public step API: pinned host inputs/outputs.
+        qh = q.cpu().pin_memory()
+        kh = kn.cpu().pin_memory()
+        vh = vn.cpu().pin_memory()
+        oh = torch.empty(q.shape if world == 1 else (nl, world, B, hq, D), dtype=torch.bfloat16).pin_memory()
+        h2d = qh.numel() * 2 + kh.numel() * 2 + vh.numel() * 2
+        d2h = oh.numel() * 2
 
-    q_e, k_e, v_e = torch.empty_like(q), torch.empty_like(kn), torch.empty_like(vn)
+        q_e, k_e, v_e = torch.empty_like(q), torch.empty_like(kn), torch.empty_like(vn)
 
-    def e2e_step():
-        if world == 1:
-            step.step_host(qh, kh, vh, oh)
-            return
-        q_e.copy_(qh, non_blocking=True)
-        k_e.copy_(kh, non_blocking=True)
-        v_e.copy_(vh, non_blocking=True)
-        step.step(q_e, k_e, v_e, out=out)
-        for l in range(nl):
-            dist.all_gather_into_tensor(gathered[l], out[l])
-        oh.copy_(gathered, non_blocking=True)
+        def e2e_step():
+            if world == 1:
+                step.step_host(qh, kh, vh, oh)
+                return
+            q_e.copy_(qh, non_blocking=True)
+            k_e.copy_(kh, non_blocking=True)
+            v_e.copy_(vh, non_blocking=True)
+            step.step(q_e, k_e, v_e, out=out)
+            for l in range(nl):
+                dist.all_gather_into_tensor(gathered[l], out[l])
+            oh.copy_(gathered, non_blocking=True)
 
-    for _ in range(2):
-        e2e_step()
-    torch.cuda.synchronize()
-    barrier()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(args.steps):
-        e2e_step()
-    e1.record()
-    torch.cuda.synchronize()
-    barrier()
-    e2e_ms = e0.elapsed_time(e1) / args.steps
+        for _ in range(2):
+            e2e_step()
+        torch.cuda.synchronize()
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            e2e_step()
+        e1.record()
+        torch.cuda.synchronize()
+        barrier()
+        e2e_ms = e0.elapsed_time(e1) / args.steps
+
 
     if world > 1:
         t = torch.tensor([ms, e2e_ms, dec_mean], device=dev)
@@ -382,15 +393,16 @@ def run_gpu(args, rank: int, world: int, local_rank: int) -> None:
             "hbm_frac": round(value / world / peak, 4),
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
                          "unit": "GB/s", "frac": round(achieved / peak, 4),
-                         "traffic": traffic, "kernel": "paged_decode_kernel<128,bf16>",
+                         "traffic": traffic, "kernel": "paged_decode_kernel<128,bf16> (fused append + decode)",
                          "peak_kind": peak_kind,
                          "decode_ms_mean": round(dec_mean, 4),
                          "alg_bytes_per_launch": decode_alg_bytes},
             "cpu_baseline": cpu,
-            "e2e": {"value": round(kv_step_total / (e2e_ms / 1e3) / 1e9, 2), "unit": "GB/s",
-                    "ms_per_step": round(e2e_ms, 4), "h2d_bytes_per_step": int(h2d),
-                    "d2h_bytes_per_step": int(d2h)},
-            "gpu_launches": args.steps * nl * 2,
+            "e2e": None if args.no_e2e else {
+                "value": round(kv_step_total / (e2e_ms / 1e3) / 1e9, 2), "unit": "GB/s",
+                "ms_per_step": round(e2e_ms, 4), "h2d_bytes_per_step": int(h2d),
+                "d2h_bytes_per_step": int(d2h)},
+            "gpu_launches": args.steps * nl * (2 if args.separate_append else 1),
             "clocks": clk,
         }
         print(json.dumps(result), flush=True)

@@ -135,8 +135,9 @@ MZ_API int mz_paged_decode_workspace_size(int32_t n_seqs, int32_t n_kv_heads, in
  *   q + b*q_seq_stride + i*q_tok_stride + h*q_head_stride + d   (elements, dtype),
  * out likewise with out_* strides and element type out_dtype (dtype or F32).
  * Supported: dtype F16/BF16, head_dim 64 or 128, block_size a multiple of 16,
- * n_q_tokens * (n_heads / n_kv_heads) <= 16.  K/V pools and q need 16-byte
- * alignment.  A sequence with ctx_lens[b] == 0 gets zeros.
+ * n_q_tokens * (n_heads / n_kv_heads) <= 16.  K/V pools need 16-byte
+ * alignment, q and out 4-byte (8-byte for F32 out) alignment and even strides.
+ * A sequence with ctx_lens[b] == 0 gets zeros.
  * workspace: >= mz_paged_decode_workspace_size bytes, zero-filled before its
  * first use; every successful call leaves its counter region zeroed again.
  * After a call that set a dev_err bit, zero the workspace before reuse.
@@ -151,6 +152,28 @@ MZ_API int mz_paged_decode(void *out, int32_t out_dtype, int64_t out_seq_stride,
                     void *workspace, size_t workspace_bytes, int32_t *dev_err,
                     mz_stream_t stream);
 
+/* Fused decode step: append one new token per sequence, then attend.
+ * The new token of sequence b is the last attended one (position
+ * ctx_lens[b] - 1): its K/V rows, k_new/v_new element (b, h, d) at
+ * base + b*new_seq_stride + h*new_head_stride + d, are written to that slot of
+ * the pools through the block table (bit-exact, as mz_kv_append_paged) and used
+ * by the attention in the same launch.  Replaces the per-layer pair
+ * cache.update_and_fetch + SDPA of the reference's batched decode
+ * (src/mlxz/engine/continuous.py:625-633) for one layer.  q/out are
+ * [n_seqs][n_heads][head_dim] with the given strides (one query token).
+ * k_new/v_new need 16-byte alignment and strides that are multiples of 8.
+ * Workspace and the other rules as mz_paged_decode. */
+MZ_API int mz_paged_append_decode(void *out, int32_t out_dtype, int64_t out_seq_stride,
+                                  int64_t out_head_stride, const void *q, int64_t q_seq_stride,
+                                  int64_t q_head_stride, void *k_pool, void *v_pool,
+                                  const void *k_new, const void *v_new, int64_t new_seq_stride,
+                                  int64_t new_head_stride, const int32_t *block_tables,
+                                  int32_t max_blocks_per_seq, const int32_t *ctx_lens,
+                                  int32_t n_seqs, int32_t n_heads, int32_t n_kv_heads,
+                                  int32_t head_dim, int32_t block_size, int64_t n_blocks,
+                                  float scale, int32_t dtype, int32_t num_warps, void *workspace,
+                                  size_t workspace_bytes, int32_t *dev_err, mz_stream_t stream);
+
 /* mz_paged_decode without a workspace argument: it allocates nothing.
  * No counterpart in the reference (which has no device memory management);
  * it exists for callers that cannot allocate device memory when they call in,
@@ -161,7 +184,7 @@ MZ_API int mz_paged_decode(void *out, int32_t out_dtype, int64_t out_seq_stride,
  * __device__ array), held by every GPU that loads the library until the
  * process exits.  Sizes whose scratch would exceed it (see
  * mz_paged_decode_workspace_size) return MZ_ERR_TOO_LARGE; for the 8B-shape
- * batch of 64 sequences it needs about 3.5 MiB.
+ * batch of 64 sequences it needs about 8.5 MiB.
  * The first call on each device looks the array's address up with
  * cudaGetSymbolAddress (with that device current); make that first call before
  * any stream capture.  Each call clears the array's counters on `stream`

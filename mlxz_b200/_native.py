@@ -82,6 +82,9 @@ _SIGNATURES: dict[str, list] = {
     "mz_paged_decode": [_vp, _i32, _i64, _i64, _i64, _vp, _i64, _i64, _i64, _i32, _vp, _vp,
                         _vp, _i32, _vp, _i32, _i32, _i32, _i32, _i32, _i64, _f32, _i32, _i32,
                         _vp, _sz, _vp, _vp],
+    "mz_paged_append_decode": [_vp, _i32, _i64, _i64, _vp, _i64, _i64, _vp, _vp, _vp, _vp, _i64,
+                               _i64, _vp, _i32, _vp, _i32, _i32, _i32, _i32, _i32, _i64, _f32,
+                               _i32, _i32, _vp, _sz, _vp, _vp],
     "mz_paged_decode_noalloc": [_vp, _i32, _i64, _i64, _i64, _vp, _i64, _i64, _i64, _i32, _vp,
                                 _vp, _vp, _i32, _vp, _i32, _i32, _i32, _i32, _i32, _i64, _f32,
                                 _i32, _i32, _vp, _vp],

@@ -1,15 +1,23 @@
 // Fused GQA paged decode attention for sm_100a.
 //
-// Work decomposition.  The KV of every (sequence b, kv head h) is a list of
-// 16-token tiles (a block of block_size tokens is block_size/16 tiles).  All
-// tiles of all (b, h) pairs, in (b, h, t) order, form one flat sequence of T
-// tiles.  The grid is a persistent set of W warps; warp w owns the contiguous
-// share [w*per, (w+1)*per) with per = ceil(T / W), so every warp streams the
-// same number of tiles whatever the context lengths are (no tail from ragged
-// sequences).  A (b, h) pair that lies inside one warp's share is finished by
-// that warp.  A pair cut by share boundaries leaves one partial (running max
-// m, running sum l, unnormalised O) per piece in the workspace; the warp that
-// finishes the last piece (per-pair arrival counter) merges them.
+// Work decomposition.  The KV of every (sequence b, kv head h) -- a "pair" --
+// is a list of 16-token tiles (a block of block_size tokens is block_size/16
+// tiles).  All tiles of all pairs, in (b, h, t) order, form one flat sequence
+// of T tiles, cut into units:
+//   * static units: the first T_s tiles (MLXZ_B200_DECODE_STATIC_PCT percent
+//     of T, all of it by default), one contiguous share of per_s = ceil(T_s / W)
+//     tiles per warp (W persistent warps);
+//   * dynamic units: the rest, if any, in chunks of C tiles that warps claim
+//     with an atomic ticket once their static share is done.
+// Measured on B200 at the 8B shape, the per-warp tile rate is uniform to a
+// few percent, and a dynamic chunk is too coarse (one warp streams a 16-tile
+// chunk in ~23 us) to shorten the tail, so the default hands out everything
+// statically; the dynamic path stays for tuning and is tested.
+// A pair that lies inside one unit is finished by the warp that runs the unit.
+// A pair cut by unit boundaries leaves one partial (running max m, running sum
+// l, unnormalised O) per piece in the workspace at slot (unit + pair); the
+// warp that finishes the pair's last piece (per-pair arrival counter) merges
+// them.  Counters clean themselves up, so a zeroed workspace stays reusable.
 //
 // Per warp, a STAGES-deep ring of shared-memory stages is filled by 2-D bulk
 // tensor copies (cp.async.bulk.tensor, 128-byte swizzle, no multicast) that
@@ -19,6 +27,10 @@
 // the exp2 domain, then O += P.V (D/8 n-tiles).  For bf16, P is split into
 // hi + lo bf16 parts so P.V carries ~16 mantissa bits of P.
 //
+// Optional fused append (decode step): the new token of each sequence, the
+// last one attended, is written into its pool slot and patched into the staged
+// tile before use, so no separate append launch is needed.
+//
 // Roofline: each tile moves 2 * 16 * D * 2 bytes (K and V) and needs
 // 4 * rows * 16 * D flops; with rows = 4 (GQA group 4) that is 2 flop/byte,
 // so the kernel is HBM-bound and the bulk-copy pipeline depth is what matters.
@@ -26,6 +38,7 @@
 #include <cudaTypedefs.h>
 
 #include <cmath>
+#include <cstdlib>
 #include <mutex>
 
 #include "common.cuh"
@@ -35,15 +48,21 @@ namespace decode {
 
 constexpr int kWarps = 4;
 constexpr int kTileTok = 16;
+#ifndef MZ_DECODE_STAGES_D128
+#define MZ_DECODE_STAGES_D128 3
+#endif
+constexpr int kUnitQ = 8;  // per-warp ring of unit descriptors
 constexpr uint64_t kTimeoutNs = 2000000000ull;  // 2 s bound on any single wait
 
 template <int D>
 struct Cfg {
-  static constexpr int kStages = (D == 64) ? 6 : 3;
+  static constexpr int kStages = (D == 64) ? 6 : MZ_DECODE_STAGES_D128;
   static constexpr int kTileBytes = kTileTok * D * 2;        // one of K or V
   static constexpr int kStageBytes = 2 * kTileBytes;         // K + V
   static constexpr int kSmemTiles = kWarps * kStages * kStageBytes;
-  static constexpr int kSmemBytes = kSmemTiles + kWarps * kStages * 8 + 1024;  // + barriers + align
+  static constexpr int kSmemBars = kWarps * kStages * 8;
+  static constexpr int kSmemUnits = kWarps * kUnitQ * 32;
+  static constexpr int kSmemBytes = kSmemTiles + kSmemBars + kSmemUnits + 1024;  // + align
 };
 
 struct Params {
@@ -60,15 +79,28 @@ struct Params {
   int bs, tpb;  // block size, tiles per block
   int64_t n_blocks;
   float scale_log2;
-  int32_t *counters;  // [B * Hkv]
+  // fused append (kn == nullptr: none)
+  const uint16_t *kn, *vn;
+  int64_t kn_sb, kn_sh;
+  uint16_t *k_pool, *v_pool;
+  // workspace
+  int32_t *counters;  // [n_pairs] arrival counters, then [2] = ticket, exited
   float *ml;          // [slots][rows][2]
   float *part;        // [slots][rows][D]
+  int max_chunks;
+  int static_pct;  // share of tiles handed out statically (1..100)
+  int min_chunk;   // smallest dynamic chunk (tiles)
   int32_t *err;
 };
 
 struct Cursor {
   int b, h, t, n, ctx;
-  int64_t pos;
+  int pos;
+};
+
+// A unit descriptor (32 bytes), passed from the producer to the consumer.
+struct Unit {
+  int start, end, u, b, h, t, n, ctx;
 };
 
 __device__ __forceinline__ int ntiles_of(int ctx) { return (ctx + kTileTok - 1) / kTileTok; }
@@ -102,6 +134,38 @@ __device__ __forceinline__ void advance(Cursor &c, const Params &p) {
   }
 }
 
+// Cursor at flat tile x (0 <= x < T), found with a warp scan over sequences.
+__device__ Cursor locate(const Params &p, int x, int lane) {
+  int base = 0, bf = 0;
+  for (int b0 = 0; b0 < p.B; b0 += 32) {
+    const int b = b0 + lane;
+    const int c = (b < p.B) ? ntiles_of(clamped_ctx(p, b)) * p.Hkv : 0;
+    int incl = c;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += y;
+    }
+    const unsigned m = __ballot_sync(0xffffffffu, base + incl > x);
+    if (m) {
+      const int L = __ffs(m) - 1;
+      base += __shfl_sync(0xffffffffu, incl - c, L);
+      bf = b0 + L;
+      break;
+    }
+    base += __shfl_sync(0xffffffffu, incl, 31);
+  }
+  Cursor cur;
+  cur.b = bf;
+  cur.ctx = clamped_ctx(p, bf);
+  cur.n = ntiles_of(cur.ctx);
+  const int r = x - base;
+  cur.h = r / cur.n;
+  cur.t = r - cur.h * cur.n;
+  cur.pos = x;
+  return cur;
+}
+
 // Address of output (or q) element row r of pair (b, h), dim 0.
 __device__ __forceinline__ int64_t row_offset(int64_t sb, int64_t st, int64_t sh, int b, int h,
                                               int r, int G) {
@@ -119,6 +183,13 @@ __device__ __forceinline__ void store_pair(const Params &p, int64_t off, float x
   } else {
     *reinterpret_cast<__half2 *>(static_cast<__half *>(p.out) + off) = __floats2half2_rn(x, y);
   }
+}
+
+// 128-byte swizzle of a [16 tok][64 dim] 2-KiB box: 16-byte unit u of line
+// `tok` lives at unit u ^ (tok & 7).  D = 128 uses two boxes (dims 0-63, 64-127).
+__device__ __forceinline__ uint32_t smem_off(int tok, int d) {
+  const int box = d >> 6, u = (d & 63) >> 3;
+  return box * 2048 + tok * 128 + ((u ^ (tok & 7)) << 4);
 }
 
 template <int D, bool BF16>
@@ -140,6 +211,7 @@ __global__ void __launch_bounds__(kWarps * 32, 2)
 
   uint8_t *stages = smem + warp * S * C::kStageBytes;
   uint64_t *bars = reinterpret_cast<uint64_t *>(smem + C::kSmemTiles) + warp * S;
+  Unit *uq = reinterpret_cast<Unit *>(smem + C::kSmemTiles + C::kSmemBars) + warp * kUnitQ;
   const uint32_t bar0 = smem_u32(bars);
   const uint32_t stage0 = smem_u32(stages);
 
@@ -159,51 +231,81 @@ __global__ void __launch_bounds__(kWarps * 32, 2)
       }
   }
 
-  // Total tiles T and this warp's share.
-  int64_t tot = 0;
+  // Total tiles T, the static share per warp and the dynamic chunking.
+  int tot = 0;
   for (int b = lane; b < p.B; b += 32) tot += ntiles_of(clamped_ctx(p, b));
 #pragma unroll
   for (int o = 16; o; o >>= 1) tot += __shfl_xor_sync(0xffffffffu, tot, o);
   tot *= p.Hkv;
-  if (tot == 0) return;
-  const int64_t per = (tot + W - 1) / W;
-  const int64_t p0 = (int64_t)wid * per;
-  if (p0 >= tot) return;
-  const int my_n = static_cast<int>(min(per, tot - p0));
+  if (tot == 0) return;  // every warp leaves here: no counter is touched
+  // static share: ceil(T * pct / 100 / W) tiles per warp (the last shares may
+  // be short or empty), so with pct = 100 warps differ by at most one tile
+  const int64_t t_target = (int64_t)tot * p.static_pct / 100;
+  const int per_s = static_cast<int>((t_target + W - 1) / W);
+  const int t_s = static_cast<int>(min((int64_t)per_s * W, (int64_t)tot));
+  const int dyn = tot - t_s;
+  int chunk = (dyn + p.max_chunks - 1) / p.max_chunks;
+  if (chunk < p.min_chunk) chunk = p.min_chunk;
+  const int n_chunks = (dyn + chunk - 1) / chunk;
+  int32_t *ticket = p.counters + (int64_t)p.B * p.Hkv;
+  // unit index of flat tile x
+  auto unit_of = [&](int x) -> int { return x < t_s ? x / per_s : W + (x - t_s) / chunk; };
 
-  // Locate tile p0: find b with prefix(b) <= p0 < prefix(b+1), prefix in tiles*Hkv.
-  Cursor start;
-  {
-    int64_t base = 0;
-    int bf = 0;
-    for (int b0 = 0; b0 < p.B; b0 += 32) {
-      const int b = b0 + lane;
-      const int64_t c = (b < p.B) ? (int64_t)ntiles_of(clamped_ctx(p, b)) * p.Hkv : 0;
-      int64_t incl = c;
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const int64_t y = __shfl_up_sync(0xffffffffu, incl, o);
-        if (lane >= o) incl += y;
-      }
-      const unsigned m = __ballot_sync(0xffffffffu, base + incl > p0);
-      if (m) {
-        const int L = __ffs(m) - 1;
-        base += __shfl_sync(0xffffffffu, incl - c, L);
-        bf = b0 + L;
-        break;
-      }
-      base += __shfl_sync(0xffffffffu, incl, 31);
-    }
-    start.b = bf;
-    start.ctx = clamped_ctx(p, bf);
-    start.n = ntiles_of(start.ctx);
-    const int64_t r = p0 - base;
-    start.h = static_cast<int>(r / start.n);
-    start.t = static_cast<int>(r - (int64_t)start.h * start.n);
-    start.pos = p0;
-  }
-
+  // ---- producer state (warp-uniform; lane 0 issues) ----
+  Cursor pc;
+  int p_left = 0, pushed = 0, issued = 0;
+  bool p_done = false, static_taken = false;
   const uint64_t pol = l2_policy_evict_first();
+
+  auto next_unit = [&]() -> bool {
+    int start = 0, end = 0, u = 0;
+    bool ok = false;
+    if (!static_taken) {
+      static_taken = true;
+      if (per_s > 0 && (int64_t)wid * per_s < t_s) {
+        start = wid * per_s;
+        end = min(start + per_s, t_s);
+        u = wid;
+        ok = true;
+      }
+    }
+    if (!ok) {
+      int tk = 0;
+      if (lane == 0) tk = atomicAdd(ticket, 1);
+      tk = __shfl_sync(0xffffffffu, tk, 0);
+      if (tk >= n_chunks) {
+        // Out of work.  The last warp out resets the ticket for the next call.
+        if (lane == 0) {
+          const int out_n = atomicAdd(ticket + 1, 1);
+          if (out_n == W - 1) {
+            ticket[0] = 0;
+            ticket[1] = 0;
+          }
+        }
+        return false;
+      }
+      start = t_s + tk * chunk;
+      end = min(start + chunk, tot);
+      u = W + tk;
+    }
+    pc = locate(p, start, lane);
+    if (lane == 0) {
+      Unit un;
+      un.start = start;
+      un.end = end;
+      un.u = u;
+      un.b = pc.b;
+      un.h = pc.h;
+      un.t = pc.t;
+      un.n = pc.n;
+      un.ctx = pc.ctx;
+      uq[pushed % kUnitQ] = un;
+    }
+    ++pushed;
+    p_left = end - start;
+    return true;
+  };
+
   auto issue = [&](int s, const Cursor &c) {
     if (lane == 0) {
       int32_t blk = p.tables[(int64_t)c.b * p.max_blocks + c.t / p.tpb];
@@ -223,42 +325,59 @@ __global__ void __launch_bounds__(kWarps * 32, 2)
     }
   };
 
-  // Per-lane ldmatrix geometry (see the swizzle note at smem_off).
+  // Keep S tiles in flight.
+  auto refill = [&](int consumed) {
+    while (!p_done && issued - consumed < S) {
+      if (p_left == 0 && !next_unit()) {
+        p_done = true;
+        break;
+      }
+      if (lane == 0 && issued >= S) fence_proxy_async_smem();
+      issue(issued % S, pc);
+      advance(pc, p);
+      --p_left;
+      ++issued;
+    }
+  };
+
+  // Per-lane ldmatrix geometry.
   const int mi = lane >> 3, r8 = lane & 7;
   const int tokK = r8 + 8 * (mi >> 1), subK = mi & 1;  // K: m0,m1 tok 0-7; m2,m3 tok 8-15
   const int tokV = r8 + 8 * (mi & 1), subV = mi >> 1;  // V: m0,m2 tok 0-7; m1,m3 tok 8-15
-  // 128-byte swizzle of a [16 tok][64 dim] 2-KiB box: 16-byte unit u of line
-  // `tok` lives at unit u ^ (tok & 7).  D = 128 uses two boxes (dims 0-63, 64-127).
-  auto smem_off = [](int tok, int d) -> uint32_t {
-    const int box = d >> 6, u = (d & 63) >> 3;
-    return box * 2048 + tok * 128 + ((u ^ (tok & 7)) << 4);
-  };
-
-  const int g = lane >> 2, cq = lane & 3;  // mma fragment row / column-pair
-
-  Cursor pc = start, cc = start;
-  int issued = 0;
-  {
-    const int pro = my_n < S ? my_n : S;
-    for (; issued < pro; ++issued) {
-      issue(issued, pc);
-      advance(pc, p);
-    }
-  }
+  const int g = lane >> 2, cq = lane & 3;              // mma fragment row / column-pair
 
   uint32_t qa[KS][4];
   float oacc[NT][4];
   float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
-  int seg_t0 = 0;
   const bool two_groups = p.rows > 8;
 
-  for (int i = 0; i < my_n; ++i) {
+  Cursor cc;
+  int c_left = 0, c_unit = 0, popped = 0;
+  bool seg_first = true;
+
+  refill(0);
+  for (int i = 0; i < issued; ++i) {
     const int s = i % S;
     const uint32_t ph = (i / S) & 1;
 
-    if (i == 0 || cc.t == 0) {
-      // New (b, h) segment: load the grouped query rows as A fragments.
-      seg_t0 = cc.t;
+    if (c_left == 0) {
+      __syncwarp();
+      const Unit un = uq[popped % kUnitQ];
+      ++popped;
+      cc.b = un.b;
+      cc.h = un.h;
+      cc.t = un.t;
+      cc.n = un.n;
+      cc.ctx = un.ctx;
+      cc.pos = un.start;
+      c_left = un.end - un.start;
+      c_unit = un.u;
+      seg_first = true;
+    }
+
+    if (seg_first || cc.t == 0) {
+      // New piece: load the grouped query rows as A fragments.
+      seg_first = false;
       m0 = m1 = -INFINITY;
       l0 = l1 = 0.f;
 #pragma unroll
@@ -285,13 +404,37 @@ __global__ void __launch_bounds__(kWarps * 32, 2)
       return;
     }
 
+    uint8_t *kt = stages + s * C::kStageBytes;
+    uint8_t *vt = kt + C::kTileBytes;
     const uint32_t kb = stage0 + s * C::kStageBytes;
     const uint32_t vb = kb + C::kTileBytes;
     const int nvalid = min(kTileTok, cc.ctx - cc.t * kTileTok);
+    const bool last_tile = (cc.t == cc.n - 1);
+    if (p.kn != nullptr && last_tile) {
+      // Fused append: the sequence's new token is its last attended one.  Write
+      // it to its pool slot and into the staged tile (which may predate it).
+      const int pos = cc.ctx - 1;
+      const int row = pos & (kTileTok - 1);
+      constexpr int U = D / 8;  // 16-byte units per row
+      if (lane < 2 * U) {
+        const bool is_v = lane >= U;
+        const int d = (lane - (is_v ? U : 0)) * 8;
+        const uint16_t *src =
+            (is_v ? p.vn : p.kn) + (int64_t)cc.b * p.kn_sb + (int64_t)cc.h * p.kn_sh + d;
+        const uint4 val = *reinterpret_cast<const uint4 *>(src);
+        *reinterpret_cast<uint4 *>((is_v ? vt : kt) + smem_off(row, d)) = val;
+        const int32_t blk = p.tables[(int64_t)cc.b * p.max_blocks + pos / p.bs];
+        if (blk >= 0 && blk < p.n_blocks) {
+          uint16_t *dst = (is_v ? p.v_pool : p.k_pool) +
+                          ((((int64_t)blk * p.Hkv + cc.h) * p.bs + pos % p.bs) * D + d);
+          *reinterpret_cast<uint4 *>(dst) = val;
+        }
+      }
+      __syncwarp();
+    }
     if (nvalid < kTileTok) {
       // Rows past the context may hold stale data; make them exact zeros so
       // that 0 * V stays 0 in P.V.
-      uint8_t *vt = stages + s * C::kStageBytes + C::kTileBytes;
       for (int e = lane; e < (kTileTok - nvalid) * (D / 8); e += 32) {
         const int tok = nvalid + e / (D / 8), d = (e % (D / 8)) * 8;
         *reinterpret_cast<uint4 *>(vt + smem_off(tok, d)) = make_uint4(0, 0, 0, 0);
@@ -352,12 +495,14 @@ __global__ void __launch_bounds__(kWarps * 32, 2)
     }
     l0 = l0 * a0 + rs0;
     l1 = l1 * a1 + rs1;
+    if (__any_sync(0xffffffffu, a0 != 1.f || a1 != 1.f)) {
 #pragma unroll
-    for (int n = 0; n < NT; ++n) {
-      oacc[n][0] *= a0;
-      oacc[n][1] *= a0;
-      oacc[n][2] *= a1;
-      oacc[n][3] *= a1;
+      for (int n = 0; n < NT; ++n) {
+        oacc[n][0] *= a0;
+        oacc[n][1] *= a0;
+        oacc[n][2] *= a1;
+        oacc[n][3] *= a1;
+      }
     }
 
     // P as A fragments (hi, and lo for bf16).
@@ -393,15 +538,17 @@ __global__ void __launch_bounds__(kWarps * 32, 2)
       }
     }
 
-    // Segment end: last tile of the pair, or last tile of this warp's share.
-    if (cc.t == cc.n - 1 || i == my_n - 1) {
+    // Piece end: last tile of the pair, or last tile of the unit.
+    if (last_tile || c_left == 1) {
       float L0 = l0, L1 = l1;
       L0 += __shfl_xor_sync(0xffffffffu, L0, 1);
       L0 += __shfl_xor_sync(0xffffffffu, L0, 2);
       L1 += __shfl_xor_sync(0xffffffffu, L1, 1);
       L1 += __shfl_xor_sync(0xffffffffu, L1, 2);
       const int bh = cc.b * p.Hkv + cc.h;
-      if (seg_t0 == 0 && cc.t == cc.n - 1) {
+      const int pbh = cc.pos - cc.t;  // flat index of tile 0 of this pair
+      const int uf = unit_of(pbh), ul = unit_of(pbh + cc.n - 1);
+      if (uf == ul) {
         const float i0 = 1.f / L0, i1 = two_groups ? 1.f / L1 : 0.f;
         if (g < p.rows) {
           const int64_t o = row_offset(p.o_sb, p.o_st, p.o_sh, cc.b, cc.h, g, p.G);
@@ -416,7 +563,7 @@ __global__ void __launch_bounds__(kWarps * 32, 2)
             store_pair(p, o + n * 8 + 2 * cq, oacc[n][2] * i1, oacc[n][3] * i1, BF16);
         }
       } else {
-        const int64_t slot = (int64_t)wid + bh;
+        const int64_t slot = (int64_t)c_unit + bh;
         float *pr = p.part + slot * p.rows * D;
         float *mlr = p.ml + slot * p.rows * 2;
         if (g < p.rows) {
@@ -438,9 +585,7 @@ __global__ void __launch_bounds__(kWarps * 32, 2)
         int old = 0;
         if (lane == 0) old = atomicAdd(p.counters + bh, 1);
         old = __shfl_sync(0xffffffffu, old, 0);
-        const int64_t pbh = cc.pos - cc.t;  // flat index of tile 0 of this pair
-        const int64_t wf = pbh / per, wl = (pbh + cc.n - 1) / per;
-        const int nparts = static_cast<int>(wl - wf + 1);
+        const int nparts = ul - uf + 1;
         if (old == nparts - 1) {
           // Last piece: merge every piece's (m, l, O) and write the output.
           __threadfence();
@@ -450,7 +595,7 @@ __global__ void __launch_bounds__(kWarps * 32, 2)
             float M = -INFINITY, Ls = 0.f;
             float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
             for (int k = 0; k < nparts; ++k) {
-              const int64_t sl = wf + k + bh;
+              const int64_t sl = (int64_t)uf + k + bh;
               const float2 mlk = __ldcg(reinterpret_cast<const float2 *>(p.ml + (sl * p.rows + r) * 2));
               const float4 ok = __ldcg(reinterpret_cast<const float4 *>(p.part + (sl * p.rows + r) * D + d));
               const float Mn = fmaxf(M, mlk.x);
@@ -470,16 +615,13 @@ __global__ void __launch_bounds__(kWarps * 32, 2)
           if (lane == 0) p.counters[bh] = 0;
         }
       }
+      seg_first = true;  // the next tile starts a new piece
     }
 
     __syncwarp();
-    if (issued < my_n) {
-      if (lane == 0) fence_proxy_async_smem();
-      issue(s, pc);
-      advance(pc, p);
-      ++issued;
-    }
+    --c_left;
     advance(cc, p);
+    refill(i + 1);
   }
 }
 
@@ -542,15 +684,22 @@ int ctas_per_sm(int D, bool bf16, int *out) {
 
 struct WsLayout {
   size_t counters, ml, part, total;
+  int64_t counter_words;
+  int max_chunks;
 };
 
 inline size_t align256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
 
+// Workspace for W warps: per-pair counters + 2 scheduler words, then (m, l)
+// and O partials for W static units + max_chunks dynamic units + one extra
+// slot per pair (slot = unit + pair).
 WsLayout ws_layout(int64_t n_pairs, int64_t warps, int rows, int D) {
   WsLayout w;
-  const int64_t slots = warps + n_pairs;
+  w.max_chunks = static_cast<int>(2 * warps);
+  const int64_t slots = warps + w.max_chunks + n_pairs;
+  w.counter_words = n_pairs + 2;
   w.counters = 0;
-  w.ml = align256(n_pairs * sizeof(int32_t));
+  w.ml = align256(w.counter_words * sizeof(int32_t));
   w.part = w.ml + align256(slots * rows * 2 * sizeof(float));
   w.total = w.part + align256(slots * rows * D * sizeof(float));
   return w;
@@ -575,6 +724,190 @@ int resolve_warps(int D, bool bf16, int num_warps, int device, int64_t *warps) {
   return MZ_OK;
 }
 
+// Scheduler tuning knob from the environment (read at each launch), clamped.
+int env_int(const char *name, int dflt, int lo, int hi) {
+  const char *v = getenv(name);
+  if (!v || !*v) return dflt;
+  long x = strtol(v, nullptr, 10);
+  return static_cast<int>(x < lo ? lo : (x > hi ? hi : x));
+}
+
+// Everything a decode launch needs besides its scratch.
+struct DecodeArgs {
+  void *out;
+  int32_t out_dtype;
+  int64_t o_sb, o_st, o_sh;
+  const void *q;
+  int64_t q_sb, q_st, q_sh;
+  int32_t n_q;
+  const void *k_pool, *v_pool;
+  const int32_t *tables;
+  int32_t max_blocks;
+  const int32_t *ctx;
+  int32_t B, Hq, Hkv, D, bs;
+  int64_t n_blocks;
+  float scale;
+  int32_t dtype, num_warps;
+  const void *kn, *vn;
+  int64_t kn_sb, kn_sh;
+  int32_t *err;
+  cudaStream_t stream;
+};
+
+// Host-side checks shared by the entry points; fills the resolved warp count
+// and workspace layout.
+int validate(const DecodeArgs &a, const char *fn, int64_t *warps, WsLayout *ws) {
+  if (a.dtype != MZ_DTYPE_F16 && a.dtype != MZ_DTYPE_BF16)
+    return fail(MZ_ERR_UNSUPPORTED, "%s: dtype must be F16 or BF16", fn);
+  if (a.out_dtype != a.dtype && a.out_dtype != MZ_DTYPE_F32)
+    return fail(MZ_ERR_UNSUPPORTED, "%s: out_dtype must equal dtype or be F32", fn);
+  if (a.D != 64 && a.D != 128)
+    return fail(MZ_ERR_UNSUPPORTED, "%s: head_dim %d (supported: 64, 128)", fn, a.D);
+  if (a.bs <= 0 || a.bs % kTileTok)
+    return fail(MZ_ERR_UNSUPPORTED, "%s: block_size %d is not a multiple of 16", fn, a.bs);
+  if (a.B < 0 || a.Hkv <= 0 || a.Hq <= 0 || a.Hq % a.Hkv || a.n_q <= 0 || a.max_blocks <= 0 ||
+      a.n_blocks <= 0)
+    return fail(MZ_ERR_INVALID_ARG, "%s: bad sizes", fn);
+  const int rows = a.n_q * (a.Hq / a.Hkv);
+  if (rows > 16)
+    return fail(MZ_ERR_UNSUPPORTED, "%s: n_q_tokens * (n_heads / n_kv_heads) = %d exceeds 16", fn,
+                rows);
+  if (!std::isfinite(a.scale)) return fail(MZ_ERR_INVALID_ARG, "%s: scale not finite", fn);
+  if (a.B == 0) return MZ_OK;
+  if (!a.out || !a.q || !a.k_pool || !a.v_pool || !a.tables || !a.ctx)
+    return fail(MZ_ERR_INVALID_ARG, "%s: null pointer", fn);
+  if (!aligned(a.k_pool, 16) || !aligned(a.v_pool, 16) || !aligned(a.q, 4) || (a.q_sb & 1) ||
+      (a.q_st & 1) || (a.q_sh & 1))
+    return fail(MZ_ERR_ALIGNMENT,
+                "%s: pools need 16-byte alignment, q 4-byte alignment and even strides", fn);
+  const int ob = a.out_dtype == MZ_DTYPE_F32 ? 8 : 4;
+  if (!aligned(a.out, ob) || (a.o_sb & 1) || (a.o_st & 1) || (a.o_sh & 1))
+    return fail(MZ_ERR_ALIGNMENT, "%s: out needs %d-byte alignment and even strides", fn, ob);
+  if (a.kn || a.vn) {
+    if (!a.kn || !a.vn || !aligned(a.kn, 16) || !aligned(a.vn, 16) || (a.kn_sb % 8) ||
+        (a.kn_sh % 8))
+      return fail(MZ_ERR_ALIGNMENT,
+                  "%s: k_new/v_new need 16-byte alignment and strides that are multiples of 8", fn);
+    if (a.n_q != 1) return fail(MZ_ERR_UNSUPPORTED, "%s: fused append needs n_q_tokens == 1", fn);
+  }
+  const int64_t rows_total = a.n_blocks * a.Hkv * a.bs;
+  if (rows_total >= (int64_t(1) << 31))
+    return fail(MZ_ERR_UNSUPPORTED, "%s: pool has >= 2^31 rows", fn);
+  if ((int64_t)a.B * a.Hkv * a.max_blocks * (a.bs / kTileTok) >= (int64_t(1) << 30))
+    return fail(MZ_ERR_UNSUPPORTED, "%s: more than 2^30 tiles of context", fn);
+  const int device = current_device();
+  if (int rc = resolve_warps(a.D, a.dtype == MZ_DTYPE_BF16, a.num_warps, device, warps)) return rc;
+  *ws = ws_layout((int64_t)a.B * a.Hkv, *warps, rows, a.D);
+  return MZ_OK;
+}
+
+// Launch with scratch at `scratch`; `clear_counters` zeroes the counter words
+// on the stream first (for scratch that does not start zeroed).
+int launch(const DecodeArgs &a, int64_t warps, const WsLayout &ws, void *scratch,
+           bool clear_counters, const char *fn) {
+  if (!aligned(scratch, 256)) return fail(MZ_ERR_ALIGNMENT, "%s: workspace must be 256-byte aligned", fn);
+  const bool bf16 = a.dtype == MZ_DTYPE_BF16;
+  const int64_t rows_total = a.n_blocks * a.Hkv * a.bs;
+  CUtensorMap tk, tv;
+  if (int rc = make_pool_map(&tk, a.k_pool, rows_total, a.D, bf16)) return rc;
+  if (int rc = make_pool_map(&tv, a.v_pool, rows_total, a.D, bf16)) return rc;
+
+  Params p;
+  p.out = a.out;
+  p.o_sb = a.o_sb;
+  p.o_st = a.o_st;
+  p.o_sh = a.o_sh;
+  p.out_f32 = a.out_dtype == MZ_DTYPE_F32;
+  p.q = a.q;
+  p.q_sb = a.q_sb;
+  p.q_st = a.q_st;
+  p.q_sh = a.q_sh;
+  p.n_q = a.n_q;
+  p.G = a.Hq / a.Hkv;
+  p.rows = a.n_q * p.G;
+  p.tables = a.tables;
+  p.max_blocks = a.max_blocks;
+  p.ctx = a.ctx;
+  p.B = a.B;
+  p.Hkv = a.Hkv;
+  p.bs = a.bs;
+  p.tpb = a.bs / kTileTok;
+  p.n_blocks = a.n_blocks;
+  p.scale_log2 = static_cast<float>(static_cast<double>(a.scale) * 1.4426950408889634);
+  p.kn = static_cast<const uint16_t *>(a.kn);
+  p.vn = static_cast<const uint16_t *>(a.vn);
+  p.kn_sb = a.kn_sb;
+  p.kn_sh = a.kn_sh;
+  p.k_pool = static_cast<uint16_t *>(const_cast<void *>(a.k_pool));
+  p.v_pool = static_cast<uint16_t *>(const_cast<void *>(a.v_pool));
+  auto *w8 = static_cast<uint8_t *>(scratch);
+  p.counters = reinterpret_cast<int32_t *>(w8 + ws.counters);
+  p.ml = reinterpret_cast<float *>(w8 + ws.ml);
+  p.part = reinterpret_cast<float *>(w8 + ws.part);
+  p.max_chunks = ws.max_chunks;
+  p.static_pct = env_int("MLXZ_B200_DECODE_STATIC_PCT", 100, 1, 100);
+  p.min_chunk = env_int("MLXZ_B200_DECODE_MIN_CHUNK", 16, 1, 1 << 20);
+  p.err = a.err;
+
+  int per_sm = 0;  // also sets the kernel's shared-memory attribute (once)
+  if (int rc = ctas_per_sm(a.D, bf16, &per_sm)) return rc;
+  if (clear_counters) {
+    cudaError_t e = cudaMemsetAsync(p.counters, 0, ws.counter_words * sizeof(int32_t), a.stream);
+    if (e != cudaSuccess) return cuda_fail(e, "clearing decode counters");
+  }
+  const unsigned grid = static_cast<unsigned>(warps / kWarps);
+#define MZ_LAUNCH(D_, BF_)                                                                   \
+  paged_decode_kernel<D_, BF_><<<grid, kWarps * 32, Cfg<D_>::kSmemBytes, a.stream>>>(tk, tv, p)
+  if (a.D == 128) {
+    if (bf16) MZ_LAUNCH(128, true); else MZ_LAUNCH(128, false);
+  } else {
+    if (bf16) MZ_LAUNCH(64, true); else MZ_LAUNCH(64, false);
+  }
+#undef MZ_LAUNCH
+  MZ_CHECK_LAUNCH(fn);
+  return MZ_OK;
+}
+
+DecodeArgs make_args(void *out, int32_t out_dtype, int64_t out_seq_stride, int64_t out_tok_stride,
+                     int64_t out_head_stride, const void *q, int64_t q_seq_stride,
+                     int64_t q_tok_stride, int64_t q_head_stride, int32_t n_q_tokens,
+                     const void *k_pool, const void *v_pool, const int32_t *block_tables,
+                     int32_t max_blocks_per_seq, const int32_t *ctx_lens, int32_t n_seqs,
+                     int32_t n_heads, int32_t n_kv_heads, int32_t head_dim, int32_t block_size,
+                     int64_t n_blocks, float scale, int32_t dtype, int32_t num_warps,
+                     int32_t *dev_err, mz_stream_t stream) {
+  DecodeArgs a;
+  a.out = out;
+  a.out_dtype = out_dtype;
+  a.o_sb = out_seq_stride;
+  a.o_st = out_tok_stride;
+  a.o_sh = out_head_stride;
+  a.q = q;
+  a.q_sb = q_seq_stride;
+  a.q_st = q_tok_stride;
+  a.q_sh = q_head_stride;
+  a.n_q = n_q_tokens;
+  a.k_pool = k_pool;
+  a.v_pool = v_pool;
+  a.tables = block_tables;
+  a.max_blocks = max_blocks_per_seq;
+  a.ctx = ctx_lens;
+  a.B = n_seqs;
+  a.Hq = n_heads;
+  a.Hkv = n_kv_heads;
+  a.D = head_dim;
+  a.bs = block_size;
+  a.n_blocks = n_blocks;
+  a.scale = scale;
+  a.dtype = dtype;
+  a.num_warps = num_warps;
+  a.kn = a.vn = nullptr;
+  a.kn_sb = a.kn_sh = 0;
+  a.err = dev_err;
+  a.stream = static_cast<cudaStream_t>(stream);
+  return a;
+}
+
 }  // namespace decode
 }  // namespace mz
 
@@ -591,7 +924,6 @@ extern "C" int mz_paged_decode_workspace_size(int32_t n_seqs, int32_t n_kv_heads
     return fail(MZ_ERR_UNSUPPORTED, "head_dim %d (supported: 64, 128)", head_dim);
   int64_t warps = 0;
   if (device < 0) device = current_device();
-  // Occupancy is the same for bf16 and fp16 instantiations.
   if (int rc = resolve_warps(head_dim, true, num_warps, device, &warps)) return rc;
   *bytes = ws_layout((int64_t)n_seqs * n_kv_heads, warps, rows_per_kv_head, head_dim).total;
   return MZ_OK;
@@ -607,106 +939,61 @@ extern "C" int mz_paged_decode(void *out, int32_t out_dtype, int64_t out_seq_str
                                int64_t n_blocks, float scale, int32_t dtype, int32_t num_warps,
                                void *workspace, size_t workspace_bytes, int32_t *dev_err,
                                mz_stream_t stream) {
-  if (dtype != MZ_DTYPE_F16 && dtype != MZ_DTYPE_BF16)
-    return fail(MZ_ERR_UNSUPPORTED, "mz_paged_decode: dtype must be F16 or BF16");
-  if (out_dtype != dtype && out_dtype != MZ_DTYPE_F32)
-    return fail(MZ_ERR_UNSUPPORTED, "mz_paged_decode: out_dtype must equal dtype or be F32");
-  if (head_dim != 64 && head_dim != 128)
-    return fail(MZ_ERR_UNSUPPORTED, "mz_paged_decode: head_dim %d (supported: 64, 128)", head_dim);
-  if (block_size <= 0 || block_size % kTileTok)
-    return fail(MZ_ERR_UNSUPPORTED, "mz_paged_decode: block_size %d is not a multiple of 16",
-                block_size);
-  if (n_seqs < 0 || n_kv_heads <= 0 || n_heads <= 0 || n_heads % n_kv_heads || n_q_tokens <= 0 ||
-      max_blocks_per_seq <= 0 || n_blocks <= 0)
-    return fail(MZ_ERR_INVALID_ARG, "mz_paged_decode: bad sizes");
-  const int G = n_heads / n_kv_heads;
-  const int rows = n_q_tokens * G;
-  if (rows > 16)
-    return fail(MZ_ERR_UNSUPPORTED,
-                "mz_paged_decode: n_q_tokens * (n_heads / n_kv_heads) = %d exceeds 16", rows);
-  if (!std::isfinite(scale)) return fail(MZ_ERR_INVALID_ARG, "mz_paged_decode: scale not finite");
-  if (n_seqs == 0) return MZ_OK;
-  if (!out || !q || !k_pool || !v_pool || !block_tables || !ctx_lens || !workspace)
-    return fail(workspace ? MZ_ERR_INVALID_ARG : MZ_ERR_WORKSPACE, "mz_paged_decode: null pointer");
-  if (!aligned(k_pool, 16) || !aligned(v_pool, 16) || !aligned(q, 4) || (q_seq_stride & 1) ||
-      (q_tok_stride & 1) || (q_head_stride & 1))
-    return fail(MZ_ERR_ALIGNMENT,
-                "mz_paged_decode: pools need 16-byte alignment, q 4-byte alignment and even strides");
-  const int ob = out_dtype == MZ_DTYPE_F32 ? 8 : 4;
-  if (!aligned(out, ob) || (out_seq_stride & 1) || (out_tok_stride & 1) || (out_head_stride & 1))
-    return fail(MZ_ERR_ALIGNMENT, "mz_paged_decode: out needs %d-byte alignment and even strides",
-                ob);
-  const int64_t rows_total = n_blocks * n_kv_heads * block_size;
-  if (rows_total >= (int64_t(1) << 31))
-    return fail(MZ_ERR_UNSUPPORTED, "mz_paged_decode: pool has >= 2^31 rows");
-  const bool bf16 = dtype == MZ_DTYPE_BF16;
-  const int device = current_device();
+  const DecodeArgs a = make_args(out, out_dtype, out_seq_stride, out_tok_stride, out_head_stride,
+                                 q, q_seq_stride, q_tok_stride, q_head_stride, n_q_tokens, k_pool,
+                                 v_pool, block_tables, max_blocks_per_seq, ctx_lens, n_seqs,
+                                 n_heads, n_kv_heads, head_dim, block_size, n_blocks, scale,
+                                 dtype, num_warps, dev_err, stream);
   int64_t warps = 0;
-  if (int rc = resolve_warps(head_dim, bf16, num_warps, device, &warps)) return rc;
-  const WsLayout ws = ws_layout((int64_t)n_seqs * n_kv_heads, warps, rows, head_dim);
+  WsLayout ws;
+  if (int rc = validate(a, "mz_paged_decode", &warps, &ws)) return rc;
+  if (n_seqs == 0) return MZ_OK;
+  if (!workspace) return fail(MZ_ERR_WORKSPACE, "mz_paged_decode: workspace is null");
   if (workspace_bytes < ws.total)
     return fail(MZ_ERR_WORKSPACE, "mz_paged_decode: workspace %zu bytes < required %zu",
                 workspace_bytes, ws.total);
-  if (!aligned(workspace, 256)) return fail(MZ_ERR_ALIGNMENT, "workspace must be 256-byte aligned");
+  return launch(a, warps, ws, workspace, false, "mz_paged_decode");
+}
 
-  CUtensorMap tk, tv;
-  if (int rc = make_pool_map(&tk, k_pool, rows_total, head_dim, bf16)) return rc;
-  if (int rc = make_pool_map(&tv, v_pool, rows_total, head_dim, bf16)) return rc;
-
-  Params p;
-  p.out = out;
-  p.o_sb = out_seq_stride;
-  p.o_st = out_tok_stride;
-  p.o_sh = out_head_stride;
-  p.out_f32 = out_dtype == MZ_DTYPE_F32;
-  p.q = q;
-  p.q_sb = q_seq_stride;
-  p.q_st = q_tok_stride;
-  p.q_sh = q_head_stride;
-  p.n_q = n_q_tokens;
-  p.G = G;
-  p.rows = rows;
-  p.tables = block_tables;
-  p.max_blocks = max_blocks_per_seq;
-  p.ctx = ctx_lens;
-  p.B = n_seqs;
-  p.Hkv = n_kv_heads;
-  p.bs = block_size;
-  p.tpb = block_size / kTileTok;
-  p.n_blocks = n_blocks;
-  p.scale_log2 = static_cast<float>(static_cast<double>(scale) * 1.4426950408889634);
-  auto *w8 = static_cast<uint8_t *>(workspace);
-  p.counters = reinterpret_cast<int32_t *>(w8 + ws.counters);
-  p.ml = reinterpret_cast<float *>(w8 + ws.ml);
-  p.part = reinterpret_cast<float *>(w8 + ws.part);
-  p.err = dev_err;
-
-  // Make sure the instantiation's smem attribute is set (cached per kernel).
-  int per_sm = 0;
-  if (int rc = ctas_per_sm(head_dim, bf16, &per_sm)) return rc;
-  const unsigned grid = static_cast<unsigned>(warps / kWarps);
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-#define MZ_LAUNCH(D_, BF_)                                                               \
-  paged_decode_kernel<D_, BF_><<<grid, kWarps * 32, Cfg<D_>::kSmemBytes, s>>>(tk, tv, p)
-  if (head_dim == 128) {
-    if (bf16) MZ_LAUNCH(128, true); else MZ_LAUNCH(128, false);
-  } else {
-    if (bf16) MZ_LAUNCH(64, true); else MZ_LAUNCH(64, false);
-  }
-#undef MZ_LAUNCH
-  MZ_CHECK_LAUNCH("mz_paged_decode");
-  return MZ_OK;
+extern "C" int mz_paged_append_decode(
+    void *out, int32_t out_dtype, int64_t out_seq_stride, int64_t out_head_stride, const void *q,
+    int64_t q_seq_stride, int64_t q_head_stride, void *k_pool, void *v_pool, const void *k_new,
+    const void *v_new, int64_t new_seq_stride, int64_t new_head_stride,
+    const int32_t *block_tables, int32_t max_blocks_per_seq, const int32_t *ctx_lens,
+    int32_t n_seqs, int32_t n_heads, int32_t n_kv_heads, int32_t head_dim, int32_t block_size,
+    int64_t n_blocks, float scale, int32_t dtype, int32_t num_warps, void *workspace,
+    size_t workspace_bytes, int32_t *dev_err, mz_stream_t stream) {
+  DecodeArgs a = make_args(out, out_dtype, out_seq_stride, 0, out_head_stride, q, q_seq_stride, 0,
+                           q_head_stride, 1, k_pool, v_pool, block_tables, max_blocks_per_seq,
+                           ctx_lens, n_seqs, n_heads, n_kv_heads, head_dim, block_size, n_blocks,
+                           scale, dtype, num_warps, dev_err, stream);
+  a.kn = k_new;
+  a.vn = v_new;
+  a.kn_sb = new_seq_stride;
+  a.kn_sh = new_head_stride;
+  if (!k_new || !v_new)
+    return fail(MZ_ERR_INVALID_ARG, "mz_paged_append_decode: null k_new / v_new");
+  int64_t warps = 0;
+  WsLayout ws;
+  if (int rc = validate(a, "mz_paged_append_decode", &warps, &ws)) return rc;
+  if (n_seqs == 0) return MZ_OK;
+  if (!workspace) return fail(MZ_ERR_WORKSPACE, "mz_paged_append_decode: workspace is null");
+  if (workspace_bytes < ws.total)
+    return fail(MZ_ERR_WORKSPACE, "mz_paged_append_decode: workspace %zu bytes < required %zu",
+                workspace_bytes, ws.total);
+  return launch(a, warps, ws, workspace, false, "mz_paged_append_decode");
 }
 
 // ---------------------------------------------------------------------------
 // Allocation-free variant: the same kernel, with its scratch (split-piece
-// partials and per-pair arrival counters) in a fixed array built into the
-// library instead of a caller-supplied workspace.  For callers that cannot
-// allocate device memory when they call in: a host whose own pool already
-// owns the GPU's memory, an FFI binding with no device allocator of its own,
-// or a latency-bound path where cudaMalloc's implicit device synchronisation
-// is not allowed.  The array is loaded with the library's device code, so
-// every GPU that runs this code holds it until the process exits.
+// partials, per-pair arrival counters and the chunk ticket) in a fixed array
+// built into the library instead of a caller-supplied workspace.  For callers
+// that cannot allocate device memory when they call in: a host whose own pool
+// already owns the GPU's memory, an FFI binding with no device allocator of
+// its own, or a latency-bound path where cudaMalloc's implicit device
+// synchronisation is not allowed.  The array is loaded with the library's
+// device code, so every GPU that runs this code holds it until the process
+// exits.
 // ---------------------------------------------------------------------------
 namespace mz {
 namespace decode {
@@ -749,47 +1036,15 @@ extern "C" int mz_paged_decode_noalloc(void *out, int32_t out_dtype, int64_t out
                                        int32_t n_kv_heads, int32_t head_dim, int32_t block_size,
                                        int64_t n_blocks, float scale, int32_t dtype,
                                        int32_t num_warps, int32_t *dev_err, mz_stream_t stream) {
-  if (dtype != MZ_DTYPE_F16 && dtype != MZ_DTYPE_BF16)
-    return fail(MZ_ERR_UNSUPPORTED, "mz_paged_decode_noalloc: dtype must be F16 or BF16");
-  if (out_dtype != dtype && out_dtype != MZ_DTYPE_F32)
-    return fail(MZ_ERR_UNSUPPORTED, "mz_paged_decode_noalloc: out_dtype must equal dtype or be F32");
-  if (head_dim != 64 && head_dim != 128)
-    return fail(MZ_ERR_UNSUPPORTED, "mz_paged_decode_noalloc: head_dim %d (supported: 64, 128)",
-                head_dim);
-  if (block_size <= 0 || block_size % kTileTok)
-    return fail(MZ_ERR_UNSUPPORTED,
-                "mz_paged_decode_noalloc: block_size %d is not a multiple of 16", block_size);
-  if (n_seqs < 0 || n_kv_heads <= 0 || n_heads <= 0 || n_heads % n_kv_heads || n_q_tokens <= 0 ||
-      max_blocks_per_seq <= 0 || n_blocks <= 0)
-    return fail(MZ_ERR_INVALID_ARG, "mz_paged_decode_noalloc: bad sizes");
-  const int G = n_heads / n_kv_heads;
-  const int rows = n_q_tokens * G;
-  if (rows > 16)
-    return fail(MZ_ERR_UNSUPPORTED,
-                "mz_paged_decode_noalloc: n_q_tokens * (n_heads / n_kv_heads) = %d exceeds 16", rows);
-  if (!std::isfinite(scale))
-    return fail(MZ_ERR_INVALID_ARG, "mz_paged_decode_noalloc: scale not finite");
-  if (n_seqs == 0) return MZ_OK;
-  if (!out || !q || !k_pool || !v_pool || !block_tables || !ctx_lens)
-    return fail(MZ_ERR_INVALID_ARG, "mz_paged_decode_noalloc: null pointer");
-  if (!aligned(k_pool, 16) || !aligned(v_pool, 16) || !aligned(q, 4) || (q_seq_stride & 1) ||
-      (q_tok_stride & 1) || (q_head_stride & 1))
-    return fail(MZ_ERR_ALIGNMENT,
-                "mz_paged_decode_noalloc: pools need 16-byte alignment, q 4-byte alignment and "
-                "even strides");
-  const int ob = out_dtype == MZ_DTYPE_F32 ? 8 : 4;
-  if (!aligned(out, ob) || (out_seq_stride & 1) || (out_tok_stride & 1) || (out_head_stride & 1))
-    return fail(MZ_ERR_ALIGNMENT,
-                "mz_paged_decode_noalloc: out needs %d-byte alignment and even strides", ob);
-  const int64_t rows_total = n_blocks * n_kv_heads * block_size;
-  if (rows_total >= (int64_t(1) << 31))
-    return fail(MZ_ERR_UNSUPPORTED, "mz_paged_decode_noalloc: pool has >= 2^31 rows");
-  const bool bf16 = dtype == MZ_DTYPE_BF16;
-  const int device = current_device();
+  const DecodeArgs a = make_args(out, out_dtype, out_seq_stride, out_tok_stride, out_head_stride,
+                                 q, q_seq_stride, q_tok_stride, q_head_stride, n_q_tokens, k_pool,
+                                 v_pool, block_tables, max_blocks_per_seq, ctx_lens, n_seqs,
+                                 n_heads, n_kv_heads, head_dim, block_size, n_blocks, scale,
+                                 dtype, num_warps, dev_err, stream);
   int64_t warps = 0;
-  if (int rc = resolve_warps(head_dim, bf16, num_warps, device, &warps)) return rc;
-  const int64_t n_pairs = (int64_t)n_seqs * n_kv_heads;
-  const WsLayout ws = ws_layout(n_pairs, warps, rows, head_dim);
+  WsLayout ws;
+  if (int rc = validate(a, "mz_paged_decode_noalloc", &warps, &ws)) return rc;
+  if (n_seqs == 0) return MZ_OK;
   if (ws.total > kStaticScratchBytes)
     return fail(MZ_ERR_TOO_LARGE,
                 "mz_paged_decode_noalloc: these sizes need %zu bytes of scratch but the built-in "
@@ -797,56 +1052,8 @@ extern "C" int mz_paged_decode_noalloc(void *out, int32_t out_dtype, int64_t out
                 "mz_paged_decode with a workspace",
                 ws.total, kStaticScratchBytes);
   void *scratch = nullptr;
-  if (int rc = static_scratch_ptr(device, &scratch)) return rc;
-
-  CUtensorMap tk, tv;
-  if (int rc = make_pool_map(&tk, k_pool, rows_total, head_dim, bf16)) return rc;
-  if (int rc = make_pool_map(&tv, v_pool, rows_total, head_dim, bf16)) return rc;
-
-  Params p;
-  p.out = out;
-  p.o_sb = out_seq_stride;
-  p.o_st = out_tok_stride;
-  p.o_sh = out_head_stride;
-  p.out_f32 = out_dtype == MZ_DTYPE_F32;
-  p.q = q;
-  p.q_sb = q_seq_stride;
-  p.q_st = q_tok_stride;
-  p.q_sh = q_head_stride;
-  p.n_q = n_q_tokens;
-  p.G = G;
-  p.rows = rows;
-  p.tables = block_tables;
-  p.max_blocks = max_blocks_per_seq;
-  p.ctx = ctx_lens;
-  p.B = n_seqs;
-  p.Hkv = n_kv_heads;
-  p.bs = block_size;
-  p.tpb = block_size / kTileTok;
-  p.n_blocks = n_blocks;
-  p.scale_log2 = static_cast<float>(static_cast<double>(scale) * 1.4426950408889634);
-  auto *w8 = static_cast<uint8_t *>(scratch);
-  p.counters = reinterpret_cast<int32_t *>(w8 + ws.counters);
-  p.ml = reinterpret_cast<float *>(w8 + ws.ml);
-  p.part = reinterpret_cast<float *>(w8 + ws.part);
-  p.err = dev_err;
-
-  int per_sm = 0;
-  if (int rc = ctas_per_sm(head_dim, bf16, &per_sm)) return rc;
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  // The area keeps whatever the previous call left; the arrival counters
-  // must start at zero, so clear them on this stream first.
-  cudaError_t e = cudaMemsetAsync(p.counters, 0, n_pairs * sizeof(int32_t), s);
-  if (e != cudaSuccess) return cuda_fail(e, "mz_paged_decode_noalloc: clearing counters");
-  const unsigned grid = static_cast<unsigned>(warps / kWarps);
-#define MZ_LAUNCH(D_, BF_)                                                               \
-  paged_decode_kernel<D_, BF_><<<grid, kWarps * 32, Cfg<D_>::kSmemBytes, s>>>(tk, tv, p)
-  if (head_dim == 128) {
-    if (bf16) MZ_LAUNCH(128, true); else MZ_LAUNCH(128, false);
-  } else {
-    if (bf16) MZ_LAUNCH(64, true); else MZ_LAUNCH(64, false);
-  }
-#undef MZ_LAUNCH
-  MZ_CHECK_LAUNCH("mz_paged_decode_noalloc");
-  return MZ_OK;
+  if (int rc = static_scratch_ptr(current_device(), &scratch)) return rc;
+  // The area keeps whatever the previous call left; the counters must start
+  // at zero, so launch() clears them on this stream first.
+  return launch(a, warps, ws, scratch, true, "mz_paged_decode_noalloc");
 }

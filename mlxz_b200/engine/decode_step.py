@@ -7,8 +7,9 @@ and splits them back afterwards (_build_batched_cache / _scatter_batched_cache,
 :804-832): two full KV copies per step.  Here every live sequence of any
 length runs in one ragged launch per layer, straight from the block pools:
 
-    per layer l:  mz_kv_append_paged  (new token -> pool slot via block table)
-                  mz_paged_decode     (fused GQA attention over ctx + 1 tokens)
+    per layer l:  mz_paged_append_decode  (new token -> its pool slot through
+                  the block table, then fused GQA attention over ctx + 1 tokens,
+                  in one launch)
 
 ``PagedKVStore`` holds all layers' pools with one block table per sequence
 (the paged form of the per-request cache list built at continuous.py:195-200).
@@ -135,12 +136,12 @@ class PagedDecodeStep:
         self.lengths.copy_(offs + 1)
 
     def layer(self, l: int, q: torch.Tensor, k_new: torch.Tensor, v_new: torch.Tensor,
-              out: torch.Tensor) -> None:
-        """Append this step's token of layer l, then attend (device tensors)."""
+              out: torch.Tensor, num_warps: int = 0) -> None:
+        """Append this step's token of layer l and attend, one launch (device tensors)."""
         st = self.store
-        ops.kv_append_paged(st.k_pool(l), st.v_pool(l), k_new, v_new, self.tables, self.positions)
-        ops.paged_decode(q, st.k_pool(l), st.v_pool(l), self.tables, self.lengths,
-                         scale=self.scale, out=out, workspace=self.workspace)
+        ops.paged_append_decode(q, st.k_pool(l), st.v_pool(l), k_new, v_new, self.tables,
+                                self.lengths, scale=self.scale, out=out,
+                                workspace=self.workspace, num_warps=num_warps)
 
     def step(self, q: torch.Tensor, k_new: torch.Tensor, v_new: torch.Tensor,
              out: torch.Tensor | None = None, advance: bool = False) -> torch.Tensor:

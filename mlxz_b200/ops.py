@@ -268,6 +268,49 @@ def paged_decode(q: torch.Tensor, k_pool: torch.Tensor, v_pool: torch.Tensor,
     return out
 
 
+def paged_append_decode(q: torch.Tensor, k_pool: torch.Tensor, v_pool: torch.Tensor,
+                        k_new: torch.Tensor, v_new: torch.Tensor, block_tables: torch.Tensor,
+                        ctx_lens: torch.Tensor, scale: float | None = None,
+                        out: torch.Tensor | None = None, out_dtype: torch.dtype | None = None,
+                        num_warps: int = 0, workspace: torch.Tensor | None = None) -> torch.Tensor:
+    """Fused decode step for one layer: write ``k_new/v_new [B, Hkv, D]`` at
+    position ``ctx_lens[b] - 1`` of each sequence, then attend ``q [B, Hq, D]``
+    over the first ``ctx_lens[b]`` tokens (one launch)."""
+    n_blocks, Hkv, bs, D = _check_pools(k_pool, v_pool)
+    if q.dim() != 3 or q.shape[2] != D or q.stride(-1) != 1 or q.dtype != k_pool.dtype:
+        raise ValueError(f"q must be [B, Hq, {D}] of the pool dtype with unit last stride")
+    B, Hq, _ = q.shape
+    if k_new.shape != (B, Hkv, D) or v_new.shape != (B, Hkv, D):
+        raise ValueError(f"k_new/v_new must be [{B}, {Hkv}, {D}]")
+    if k_new.dtype != k_pool.dtype or v_new.dtype != k_pool.dtype:
+        raise ValueError("k_new/v_new dtype must match the pools")
+    if k_new.stride() != v_new.stride() or k_new.stride(2) != 1:
+        k_new, v_new = k_new.contiguous(), v_new.contiguous()
+    _as_i32(block_tables, k_pool.device, "block_tables")
+    _as_i32(ctx_lens, k_pool.device, "ctx_lens")
+    out_dtype = out_dtype or q.dtype
+    if out is None:
+        out = torch.empty(q.shape, dtype=out_dtype, device=q.device)
+    if out.shape != q.shape or out.dtype != out_dtype or out.stride(-1) != 1:
+        raise ValueError("out must match q's shape with unit last stride")
+    if scale is None:
+        scale = D ** -0.5
+    if B == 0:
+        return out
+    dev = _dev_index(q)
+    if workspace is None:
+        workspace = decode_workspace(B, Hkv, Hq // Hkv, D, dev, num_warps)
+    nat.call("mz_paged_append_decode", out.data_ptr(), dtype_code(out_dtype), out.stride(0),
+             out.stride(1), q.data_ptr(), q.stride(0), q.stride(1), k_pool.data_ptr(),
+             v_pool.data_ptr(), k_new.data_ptr(), v_new.data_ptr(), k_new.stride(0),
+             k_new.stride(1), block_tables.data_ptr(), block_tables.shape[1],
+             ctx_lens.data_ptr(), B, Hq, Hkv, D, bs, n_blocks, float(scale),
+             dtype_code(q.dtype), num_warps, workspace.data_ptr(), workspace.numel(),
+             error_word(dev).data_ptr(), _stream(dev))
+    _after(dev)
+    return out
+
+
 # ---------------------------------------------------------------------------
 # Block movement
 # ---------------------------------------------------------------------------

@@ -316,3 +316,106 @@ def test_decode_full_size_properties(cuda):
         s = torch.einsum("hd,htd->ht", q[b].float(), Kr) * D ** -0.5
         ref = torch.einsum("ht,htd->hd", torch.softmax(s, -1), Vr)
         assert attn_err(out[b], ref.cpu().numpy()) <= ATOL_REL
+
+
+@pytest.mark.parametrize("nw", [0, 4, 40, 400])
+def test_fused_append_decode_matches_separate_launches(cuda, nw):
+    """mz_paged_append_decode = mz_kv_append_paged then mz_paged_decode:
+    identical pools (bit-exact) and attention within tolerance, for warp
+    counts that make the schedule all-static, mixed, or all-dynamic."""
+    B, Hkv, G, D, bs = 12, 8, 4, 128, 16
+    lengths = [1, 15, 16, 17, 100, 511, 512, 513, 2000, 33, 7, 4095]
+    case = random_paged_case(77, B, Hkv, D, bs, lengths, "bf16", G=G)
+    kp, vp = to_dev(case["kp"], "bf16", cuda), to_dev(case["vp"], "bf16", cuda)
+    kp2, vp2 = kp.clone(), vp.clone()
+    nk_bits = rng.normal(78, (B, Hkv, D), "bf16", stream=1)
+    nv_bits = rng.normal(78, (B, Hkv, D), "bf16", stream=2)
+    nk, nv = to_dev(nk_bits, "bf16", cuda), to_dev(nv_bits, "bf16", cuda)
+    q = to_dev(case["q"][:, 0], "bf16", cuda)
+    tables = torch.from_numpy(case["tables"]).to(cuda)
+    lens = torch.tensor(lengths, dtype=torch.int32, device=cuda)
+    out = ops.paged_append_decode(q, kp, vp, nk, nv, tables, lens, num_warps=nw,
+                                  out_dtype=torch.float32)
+    ops.kv_append_paged(kp2, vp2, nk, nv, tables, lens - 1)
+    out2 = ops.paged_decode(q, kp2, vp2, tables, lens, num_warps=nw, out_dtype=torch.float32)
+    torch.cuda.synchronize()
+    ops.check_device_errors(0)
+    assert torch.equal(kp, kp2) and torch.equal(vp, vp2)
+    assert attn_err(out, out2.cpu().numpy()) <= ATOL_REL
+    okp, ovp = case["kp"].copy(), case["vp"].copy()
+    for b in range(B):
+        pos = lengths[b] - 1
+        blk = case["tables"][b][pos // bs]
+        okp[blk, :, pos % bs] = nk_bits[b]
+        ovp[blk, :, pos % bs] = nv_bits[b]
+    ref = opaged.paged_decode(case["q"][:, 0], okp, ovp, case["tables"], np.array(lengths), "bf16")
+    assert attn_err(out, ref) <= ATOL_REL
+
+
+@pytest.mark.parametrize("nw,static_pct,min_chunk", [(0, 100, 16), (0, 85, 16), (8, 60, 4),
+                                                     (1000, 70, 1), (40, 1, 16)])
+def test_decode_many_ragged_sequences_dynamic_schedule(cuda, monkeypatch, nw, static_pct,
+                                                       min_chunk):
+    """Many short and long sequences (pairs cut by static shares and dynamic
+    chunks claimed by ticket) against the oracle, twice in a row on the same
+    workspace so the self-resetting counters are exercised."""
+    monkeypatch.setenv("MLXZ_B200_DECODE_STATIC_PCT", str(static_pct))
+    monkeypatch.setenv("MLXZ_B200_DECODE_MIN_CHUNK", str(min_chunk))
+    dtype, D, G, Hkv, bs = "bf16", 128, 4, 2, 16
+    ctx = [int(x) for x in rng.randint(21, 150, 0, 1200)]
+    ctx[3] = 0
+    ctx[10] = 1
+    case = random_paged_case(21, len(ctx), Hkv, D, bs, ctx, dtype, G=G)
+    kp, vp = to_dev(case["kp"], dtype, cuda), to_dev(case["vp"], dtype, cuda)
+    q = to_dev(case["q"][:, 0], dtype, cuda)
+    tables = torch.from_numpy(case["tables"]).to(cuda)
+    ctx_t = torch.from_numpy(case["ctx"]).to(cuda)
+    ref = opaged.paged_decode(case["q"][:, 0], case["kp"], case["vp"], case["tables"], case["ctx"],
+                              dtype)
+    for _ in range(2):
+        out = ops.paged_decode(q, kp, vp, tables, ctx_t, num_warps=nw, out_dtype=torch.float32)
+        torch.cuda.synchronize()
+        ops.check_device_errors(0)
+        assert attn_err(out, ref) <= ATOL_REL
+
+
+def test_decode_step_multi_layer_with_table_growth(cuda):
+    """PagedDecodeStep over 2 layers for 20 steps with advance(): appends cross
+    block boundaries (tables grow through the BlockManager) and every step's
+    output matches the oracle replaying the same appends."""
+    from mlxz_b200.engine import PagedDecodeStep, PagedKVStore
+
+    L, Hkv, G, D, bs = 2, 2, 4, 128, 16
+    Hq = Hkv * G
+    offsets = [0, 15, 16, 31, 100, 5]
+    store = PagedKVStore(L, 64, Hkv, D, bs, torch.bfloat16, cuda, init="zeros")
+    init = rng.normal(61, tuple(store.pools.shape), "bf16")
+    store.pools.copy_(to_dev(init, "bf16", cuda))
+    for i, o in enumerate(offsets):
+        store.add_sequence(f"r{i}", o)
+    ids = [f"r{i}" for i in range(len(offsets))]
+    step = PagedDecodeStep(store, ids, Hq, max_blocks=16)
+    mirror = init.copy()
+    B = len(ids)
+    for it in range(20):
+        qb = rng.normal(62, (L, B, Hq, D), "bf16", stream=it)
+        kb = rng.normal(63, (L, B, Hkv, D), "bf16", stream=it)
+        vb = rng.normal(64, (L, B, Hkv, D), "bf16", stream=it)
+        out = step.step(to_dev(qb, "bf16", cuda), to_dev(kb, "bf16", cuda),
+                        to_dev(vb, "bf16", cuda))
+        torch.cuda.synchronize()
+        ops.check_device_errors(0)
+        tabs = np.full((B, 16), -1, dtype=np.int32)
+        for b, s in enumerate(ids):
+            t = store.tables[s]
+            tabs[b, : len(t)] = t
+            pos = store.offsets[s]
+            for l in range(L):
+                mirror[l, 0, t[pos // bs], :, pos % bs] = kb[l, b]
+                mirror[l, 1, t[pos // bs], :, pos % bs] = vb[l, b]
+        lens = np.array([store.offsets[s] + 1 for s in ids])
+        for l in range(L):
+            ref = opaged.paged_decode(qb[l], mirror[l, 0], mirror[l, 1], tabs, lens, "bf16")
+            assert attn_err(out[l], ref) <= ATOL_REL, (it, l)
+        step.advance()
+    assert np.array_equal(to_bits(store.pools), mirror)
