@@ -78,6 +78,50 @@ class PagedKVStore:
             self.bm.free(self.tables.pop(seq_id))
             self.offsets.pop(seq_id, None)
 
+    def make_writable(self, seq_id: str, position: int) -> tuple[int, int] | None:
+        """Copy-on-write the block that will hold `position` if another table
+        or the prefix cache shares it: the sequence gets a fresh block
+        (BlockManager.copy_on_write) and the caller must copy the data.
+        Returns (old, new) block ids, or None when the block is private."""
+        t = self.tables[seq_id]
+        bi = position // self.block_size
+        if bi >= len(t):
+            return None
+        blk = t[bi]
+        if self.bm.get_refcount(blk) <= 1:
+            return None
+        new = self.bm.copy_on_write(blk)
+        t[bi] = new
+        return blk, new
+
+    def copy_blocks(self, pairs: list[tuple[int, int]]) -> None:
+        """Copy block src -> dst in every layer's K and V (one mz_block_copy)."""
+        if not pairs:
+            return
+        src = torch.tensor([a for a, _ in pairs], dtype=torch.int32).to(self.device, non_blocking=True)
+        dst = torch.tensor([b for _, b in pairs], dtype=torch.int32).to(self.device, non_blocking=True)
+        ops.block_copy(self.pool_stack(), src, dst)
+
+    def append_tokens(self, seq_id: str, keys: torch.Tensor, values: torch.Tensor) -> None:
+        """Prefill-style append of n tokens to every layer: keys/values
+        ``[L, H, n, D]``.  Grows the table, copy-on-writes a shared first
+        block, then one mz_kv_append per layer with the slots of the new tokens."""
+        n = keys.shape[2]
+        if n == 0:
+            return
+        off = self.offsets[seq_id]
+        self.ensure_capacity(seq_id, n)
+        cow = self.make_writable(seq_id, off)
+        if cow:
+            self.copy_blocks([cow])
+        t = self.tables[seq_id]
+        bs = self.block_size
+        slots = torch.tensor([t[(off + i) // bs] * bs + (off + i) % bs for i in range(n)],
+                             dtype=torch.int64).to(self.device, non_blocking=True)
+        for l in range(self.n_layers):
+            ops.kv_append(self.k_pool(l), self.v_pool(l), keys[l], values[l], slots)
+        self.offsets[seq_id] = off + n
+
     def ensure_capacity(self, seq_id: str, extra: int) -> bool:
         """Grow the table for `extra` more tokens; True if it changed."""
         t = self.tables[seq_id]
@@ -143,11 +187,26 @@ class PagedDecodeStep:
                                 self.lengths, scale=self.scale, out=out,
                                 workspace=self.workspace, num_warps=num_warps)
 
+    def prepare_writes(self) -> int:
+        """Copy-on-write every block this step will write that is shared (a
+        restored prefix's partial last block, say); one batched block copy.
+        Returns the number of blocks copied."""
+        pairs = []
+        for s in self.seq_ids:
+            cow = self.store.make_writable(s, self.store.offsets[s])
+            if cow:
+                pairs.append(cow)
+        if pairs:
+            self.store.copy_blocks(pairs)
+            self.sync_metadata()
+        return len(pairs)
+
     def step(self, q: torch.Tensor, k_new: torch.Tensor, v_new: torch.Tensor,
              out: torch.Tensor | None = None, advance: bool = False) -> torch.Tensor:
         """All layers: q ``[L, B, Hq, D]``, k_new/v_new ``[L, B, Hkv, D]``."""
         if out is None:
             out = torch.empty_like(q)
+        self.prepare_writes()
         for l in range(self.store.n_layers):
             self.layer(l, q[l], k_new[l], v_new[l], out[l])
         if advance:
