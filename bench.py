@@ -53,6 +53,9 @@ def parse_args():
     ap.add_argument("--separate-append", action="store_true",
                     help="append with mz_kv_append_paged, then mz_paged_decode (two launches)")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--config", default="decode", choices=["decode", "prefix"],
+                    help="decode: the paged decode step (headline); prefix: prefix-cache "
+                         "restore / copy-on-write / host-tier eviction and reload")
     return ap.parse_args()
 
 
@@ -410,6 +413,172 @@ def run_gpu(args, rank: int, world: int, local_rank: int) -> None:
         dist.destroy_process_group()
 
 
+def run_prefix(args, local_rank: int) -> None:
+    """Prefix-cache workload, 8B KV shape (32 layers, 8 KV heads, head_dim 128,
+    bf16, block 16): a 2048-token shared prefix cached once; 32 requests
+    restore it (zero-copy) and write a U[64, 512]-token suffix; each request's
+    full prompt is cached; then the least recently used 25 % of the pool's
+    blocks go to the pinned host tier and are reloaded.  Copy-on-write is
+    timed as the reference's full-hit path triggers it (re-running the last
+    prompt token writes into the shared last prefix block), and as a bulk
+    block copy of 25 % of the pool."""
+    import numpy as np
+    import torch
+
+    from mlxz_b200 import ops
+    from mlxz_b200.engine import PagedKVStore
+    from mlxz_b200.prefix_cache import PagedPrefixCache, PinnedHostTier, RollingPrefixHasher
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    nl, prefix, n_req = args.layers, 2048, 32
+    g = np.random.default_rng(args.seed)
+    suffix = g.integers(64, 513, size=n_req)
+    need = prefix // BS + int(sum((int(x) + BS - 1) // BS for x in suffix))
+    n_blocks = int(math.ceil(need * 1.1))
+    store = PagedKVStore(nl, n_blocks, HKV, D, BS, torch.bfloat16, dev, init="zeros")
+    bb_all = 2 * nl * store.block_bytes  # one block across every layer's K and V
+    tier = PinnedHostTier(n_blocks, 2 * nl, store.block_bytes, dev)
+    cache = PagedPrefixCache(store, memory_budget_bytes=1 << 40, host_tier=tier)
+    hasher = RollingPrefixHasher(BS)
+    torch.manual_seed(args.seed)
+
+    def kv(n):
+        return (torch.randn(nl, HKV, n, D, device=dev).to(torch.bfloat16),
+                torch.randn(nl, HKV, n, D, device=dev).to(torch.bfloat16))
+
+    prompt0 = list(range(prefix))
+    store.add_sequence("p", 0)
+    store.append_tokens("p", *kv(prefix))
+    cache.store_sync(hasher.hash_chunks(prompt0), "p", block_size=BS)
+    store.free_sequence("p")
+    torch.cuda.synchronize()
+
+    # restore + suffix write per request
+    restore_s, write_s, cow_blocks = [], [], 0
+    suffix_kv = [kv(int(n)) for n in suffix]
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+    ev[0].record()
+    for r in range(n_req):
+        prompt = prompt0 + [100000 + 1000 * r + i for i in range(int(suffix[r]))]
+        hashes = hasher.hash_chunks(prompt)
+        t0 = time.perf_counter()
+        n, state, _ = cache.lookup_sync(hashes)
+        cache.restore(f"r{r}", state)
+        restore_s.append(time.perf_counter() - t0)
+        store.append_tokens(f"r{r}", *suffix_kv[r])
+        cache.store_sync(hashes, f"r{r}", block_size=BS)
+    ev[1].record()
+    torch.cuda.synchronize()
+    write_ms = ev[0].elapsed_time(ev[1])
+    suffix_bytes = float(suffix.sum()) * 2 * nl * HKV * D * 2
+
+    # copy-on-write as the full-hit path triggers it: each of the 32 requests
+    # re-runs the last prefix token, writing into the shared block 127
+    pairs = []
+    for r in range(n_req):
+        store.add_sequence(f"h{r}", 0)
+        n, state, _ = cache.lookup_sync(hasher.hash_chunks(prompt0))
+        cache.restore(f"h{r}", state)
+        store.offsets[f"h{r}"] = prefix - 1
+        pairs.append(store.make_writable(f"h{r}", prefix - 1))
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    store.copy_blocks(pairs)
+    e1.record()
+    torch.cuda.synchronize()
+    cow_ms = e0.elapsed_time(e1)
+    cow_blocks = len(pairs)
+    for r in range(n_req):
+        store.free_sequence(f"h{r}")
+
+    # bulk block copy of 25 % of the pool (HBM roofline of mz_block_copy)
+    nb_bulk = max(1, n_blocks // 4)
+    free_now = store.bm.free_blocks
+    nb_bulk = min(nb_bulk, free_now // 2)
+    srcs = store.bm.allocate(nb_bulk)
+    dsts = store.bm.allocate(nb_bulk)
+    src_t = torch.tensor(srcs, dtype=torch.int32, device=dev)
+    dst_t = torch.tensor(dsts, dtype=torch.int32, device=dev)
+    for _ in range(3):
+        ops.block_copy(store.pool_stack(), src_t, dst_t)
+    reps = 20
+    e0.record()
+    for _ in range(reps):
+        ops.block_copy(store.pool_stack(), src_t, dst_t)
+    e1.record()
+    torch.cuda.synchronize()
+    bulk_ms = e0.elapsed_time(e1) / reps
+    store.bm.free(srcs + dsts)
+    peak, peak_kind = peaks()
+    bulk_gbs = 2.0 * nb_bulk * bb_all / (bulk_ms / 1e3) / 1e9
+
+    # host link peaks (pinned, 1 GiB each way)
+    big_h = torch.empty(1 << 30, dtype=torch.uint8, pin_memory=True)
+    big_d = torch.empty(1 << 30, dtype=torch.uint8, device=dev)
+    big_d.copy_(big_h, non_blocking=True)
+    torch.cuda.synchronize()
+    e0.record()
+    big_d.copy_(big_h, non_blocking=True)
+    e1.record()
+    torch.cuda.synchronize()
+    h2d_peak = (1 << 30) / (e0.elapsed_time(e1) / 1e3) / 1e9
+    e0.record()
+    big_h.copy_(big_d, non_blocking=True)
+    e1.record()
+    torch.cuda.synchronize()
+    d2h_peak = (1 << 30) / (e0.elapsed_time(e1) / 1e3) / 1e9
+    del big_h, big_d
+
+    # LRU eviction of 25 % of the pool to the host tier, then reload
+    for r in range(n_req):
+        store.free_sequence(f"r{r}")
+    n_evict = n_blocks // 4
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    moved = cache.evict_to_host(n_evict)
+    tier.sync()
+    evict_s = time.perf_counter() - t0
+    lookups = [hasher.hash_chunks(prompt0 + [100000 + 1000 * r + i for i in range(int(suffix[r]))])
+               for r in range(n_req)]
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    reloaded = 0
+    for r in range(n_req):
+        n, state, _ = cache.lookup_sync(lookups[r])
+        reloaded += cache.reload(state)
+    tier.sync()
+    reload_s = time.perf_counter() - t0
+    ops.check_device_errors(local_rank)
+    line = {
+        "metric": "prefix-cache restore + copy-on-write + host-tier evict/reload, 8B KV shape",
+        "value": round(moved * bb_all / evict_s / 1e9, 3), "unit": "GB/s (evict to pinned host)",
+        "higher_is_better": True, "n_gpus": 1, "dtype": "bf16",
+        "data": "synthetic (seeded N(0,1) bf16 K/V)",
+        "config": {"workload": (f"prefix cache: {prefix}-token shared prefix, {n_req} requests, "
+                                f"suffix U[64,512]; {nl} layers, 8 kv heads, head_dim 128, "
+                                f"block 16"), "layers": nl, "pool_blocks": n_blocks,
+                   "block_bytes_all_layers": bb_all},
+        "restore_us_per_request": round(1e6 * statistics.median(restore_s), 1),
+        "restore_blocks_per_request": prefix // BS,
+        "suffix_write_gbs": round(suffix_bytes / (write_ms / 1e3) / 1e9, 2),
+        "cow_full_hit": {"blocks": cow_blocks, "ms": round(cow_ms, 4),
+                         "gbs": round(2.0 * cow_blocks * bb_all / (cow_ms / 1e3) / 1e9, 1)},
+        "block_copy_bulk": {"blocks": nb_bulk, "ms": round(bulk_ms, 4), "gbs": round(bulk_gbs, 1),
+                            "roofline_frac": round(bulk_gbs / peak, 4), "peak": peak,
+                            "peak_kind": peak_kind},
+        "evict": {"blocks": moved, "bytes": moved * bb_all, "s": round(evict_s, 5),
+                  "gbs": round(moved * bb_all / evict_s / 1e9, 2),
+                  "frac_of_d2h_peak": round(moved * bb_all / evict_s / 1e9 / d2h_peak, 3)},
+        "reload": {"blocks": reloaded, "bytes": reloaded * bb_all, "s": round(reload_s, 5),
+                   "gbs": round(reloaded * bb_all / reload_s / 1e9, 2),
+                   "frac_of_h2d_peak": round(reloaded * bb_all / reload_s / 1e9 / h2d_peak, 3)},
+        "host_link": {"h2d_gbs": round(h2d_peak, 2), "d2h_gbs": round(d2h_peak, 2)},
+        "stats": cache.stats().__repr__(),
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse_args()
     rank = int(os.environ.get("RANK", "0"))
@@ -420,6 +589,9 @@ def main():
     sys.path.insert(0, str(ROOT))
     if args.impl == "reference":
         run_reference(args, rank, world)
+    elif args.config == "prefix":
+        if rank == 0:
+            run_prefix(args, local_rank)
     else:
         run_gpu(args, rank, world, local_rank)
 
