@@ -1,0 +1,454 @@
+// Pieces shared by the paged decode kernels (bf16/fp16 K/V and quantised K/V):
+// launch parameters, the flat tile cursor, the per-warp unit scheduler and
+// the merge of split pieces.
+//
+// Work decomposition.  The KV of every (sequence b, kv head h) -- a "pair" --
+// is a list of 16-token tiles (a block of block_size tokens is block_size/16
+// tiles).  All tiles of all pairs, in (b, h, t) order, form one flat sequence
+// of T tiles, cut into units:
+//   * static units: the first T_s tiles (MLXZ_B200_DECODE_STATIC_PCT percent
+//     of T, all of it by default), one contiguous share of per_s = ceil(T_s / W)
+//     tiles per warp (W persistent warps);
+//   * dynamic units: the rest, if any, in chunks of C tiles that warps claim
+//     with an atomic ticket once their static share is done.
+// A pair that lies inside one unit is finished by the warp that runs the unit.
+// A pair cut by unit boundaries leaves one partial (running max m, running sum
+// l, unnormalised O) per piece in the workspace at slot (unit + pair); the
+// warp that finishes the pair's last piece (per-pair arrival counter) merges
+// them.  Counters clean themselves up, so a zeroed workspace stays reusable.
+#pragma once
+
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <cmath>
+#include <cstdlib>
+#include <mutex>
+
+#include "common.cuh"
+
+namespace mz {
+namespace decode {
+
+constexpr int kWarps = 4;           // warps per CTA, each an independent tile stream
+constexpr int kTileTok = 16;        // tokens per tile
+constexpr int kUnitQ = 8;           // per-warp ring of unit descriptors
+constexpr uint64_t kTimeoutNs = 2000000000ull;  // 2 s bound on any single wait
+
+struct Params {
+  void *out;
+  int64_t o_sb, o_st, o_sh;
+  int out_f32;
+  const void *q;
+  int64_t q_sb, q_st, q_sh;
+  int q_bf16;  // element type of q (and of out unless out_f32)
+  int n_q, G, rows;
+  const int32_t *tables;
+  int max_blocks;
+  const int32_t *ctx;
+  int B, Hkv;
+  int bs, tpb;  // block size, tiles per block
+  int64_t n_blocks;
+  float scale_log2;
+  // fused append (kn == nullptr: none) -- bf16/fp16 pools only
+  const uint16_t *kn, *vn;
+  int64_t kn_sb, kn_sh;
+  uint16_t *k_pool, *v_pool;
+  // quantised pools: per-token group scales and biases (fp16)
+  const __half *k_scales, *k_biases, *v_scales, *v_biases;
+  // workspace
+  int32_t *counters;  // [n_pairs] arrival counters, then [2] = ticket, exited
+  float *ml;          // [slots][rows][2]
+  float *part;        // [slots][rows][D]
+  int max_chunks;
+  int static_pct;  // share of tiles handed out statically (1..100)
+  int min_chunk;   // smallest dynamic chunk (tiles)
+  int32_t *err;
+};
+
+struct Cursor {
+  int b, h, t, n, ctx;
+  int pos;
+};
+
+// A unit descriptor (32 bytes), passed from the producer to the consumer.
+struct Unit {
+  int start, end, u, b, h, t, n, ctx;
+};
+
+__device__ __forceinline__ int ntiles_of(int ctx) { return (ctx + kTileTok - 1) / kTileTok; }
+
+__device__ __forceinline__ int clamped_ctx(const Params &p, int b) {
+  int c = p.ctx[b];
+  const int cap = p.max_blocks * p.bs;
+  if (c < 0 || c > cap) {
+    dev_error(p.err, MZ_DEVERR_CONTEXT);
+    c = c < 0 ? 0 : cap;
+  }
+  return c;
+}
+
+__device__ __forceinline__ void advance(Cursor &c, const Params &p) {
+  ++c.pos;
+  if (++c.t == c.n) {
+    c.t = 0;
+    if (++c.h == p.Hkv) {
+      c.h = 0;
+      for (;;) {
+        if (++c.b >= p.B) {
+          c.n = 0;
+          break;
+        }
+        c.ctx = clamped_ctx(p, c.b);
+        c.n = ntiles_of(c.ctx);
+        if (c.n > 0) break;
+      }
+    }
+  }
+}
+
+// Cursor at flat tile x (0 <= x < T), found with a warp scan over sequences.
+__device__ __forceinline__ Cursor locate(const Params &p, int x, int lane) {
+  int base = 0, bf = 0;
+  for (int b0 = 0; b0 < p.B; b0 += 32) {
+    const int b = b0 + lane;
+    const int c = (b < p.B) ? ntiles_of(clamped_ctx(p, b)) * p.Hkv : 0;
+    int incl = c;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += y;
+    }
+    const unsigned m = __ballot_sync(0xffffffffu, base + incl > x);
+    if (m) {
+      const int L = __ffs(m) - 1;
+      base += __shfl_sync(0xffffffffu, incl - c, L);
+      bf = b0 + L;
+      break;
+    }
+    base += __shfl_sync(0xffffffffu, incl, 31);
+  }
+  Cursor cur;
+  cur.b = bf;
+  cur.ctx = clamped_ctx(p, bf);
+  cur.n = ntiles_of(cur.ctx);
+  const int r = x - base;
+  cur.h = r / cur.n;
+  cur.t = r - cur.h * cur.n;
+  cur.pos = x;
+  return cur;
+}
+
+// Element offset of query/output row r (query token r / G, head h*G + r % G)
+// of pair (b, h), dim 0.
+__device__ __forceinline__ int64_t row_offset(int64_t sb, int64_t st, int64_t sh, int b, int h,
+                                              int r, int G) {
+  const int i = r / G, g = r - (r / G) * G;
+  return (int64_t)b * sb + (int64_t)i * st + (int64_t)(h * G + g) * sh;
+}
+
+__device__ __forceinline__ void store_pair(const Params &p, int64_t off, float x, float y) {
+  if (p.out_f32) {
+    *reinterpret_cast<float2 *>(static_cast<float *>(p.out) + off) = make_float2(x, y);
+  } else if (p.q_bf16) {
+    *reinterpret_cast<__nv_bfloat162 *>(static_cast<__nv_bfloat16 *>(p.out) + off) =
+        __floats2bfloat162_rn(x, y);
+  } else {
+    *reinterpret_cast<__half2 *>(static_cast<__half *>(p.out) + off) = __floats2half2_rn(x, y);
+  }
+}
+
+// 128-byte swizzle of a [16 rows][128 bytes] box (what a bulk tensor copy with
+// CU_TENSOR_MAP_SWIZZLE_128B writes): 16-byte unit u of row r lives at unit
+// u ^ (r & 7).  Rows wider than 128 bytes are split into 2-KiB boxes.
+__device__ __forceinline__ uint32_t swz128(int row, int byte) {
+  const int box = byte >> 7, u = (byte & 127) >> 4;
+  return box * 2048 + row * 128 + ((u ^ (row & 7)) << 4) + (byte & 15);
+}
+
+// Sequences with no context produce zeros (every warp takes b = wid mod W).
+template <int D>
+__device__ __forceinline__ void zero_empty_outputs(const Params &p, int wid, int W, int lane) {
+  for (int b = wid; b < p.B; b += W) {
+    if (clamped_ctx(p, b) != 0) continue;
+    for (int h = 0; h < p.Hkv; ++h)
+      for (int r = 0; r < p.rows; ++r) {
+        const int64_t o = row_offset(p.o_sb, p.o_st, p.o_sh, b, h, r, p.G);
+        for (int d = 2 * lane; d < D; d += 64) store_pair(p, o + d, 0.f, 0.f);
+      }
+  }
+}
+
+// Per-warp scheduler: static share first, then dynamic chunks by ticket.  All
+// lanes run it in lockstep (the values are warp-uniform); lane 0 does the
+// atomics and writes the unit ring, which the consumer reads after a
+// __syncwarp.
+struct Sched {
+  int lane, wid, W;
+  int tot, per_s, t_s, chunk, n_chunks;
+  int32_t *ticket;
+  Unit *uq;
+  Cursor pc;
+  int p_left, pushed, issued;
+  bool p_done, static_taken;
+
+  // Returns false (nothing to do, no counter touched) when T == 0.
+  __device__ bool init(const Params &p, int lane_, int wid_, int W_, Unit *uq_) {
+    lane = lane_;
+    wid = wid_;
+    W = W_;
+    uq = uq_;
+    int t = 0;
+    for (int b = lane; b < p.B; b += 32) t += ntiles_of(clamped_ctx(p, b));
+#pragma unroll
+    for (int o = 16; o; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+    tot = t * p.Hkv;
+    if (tot == 0) return false;
+    // static share: ceil(T * pct / 100 / W) tiles per warp (the last shares
+    // may be short or empty), so with pct = 100 warps differ by <= one tile
+    const int64_t target = (int64_t)tot * p.static_pct / 100;
+    per_s = static_cast<int>((target + W - 1) / W);
+    t_s = static_cast<int>(min((int64_t)per_s * W, (int64_t)tot));
+    const int dyn = tot - t_s;
+    chunk = (dyn + p.max_chunks - 1) / p.max_chunks;
+    if (chunk < p.min_chunk) chunk = p.min_chunk;
+    n_chunks = (dyn + chunk - 1) / chunk;
+    ticket = p.counters + (int64_t)p.B * p.Hkv;
+    p_left = pushed = issued = 0;
+    p_done = static_taken = false;
+    return true;
+  }
+
+  __device__ __forceinline__ int unit_of(int x) const {
+    return x < t_s ? x / per_s : W + (x - t_s) / chunk;
+  }
+
+  __device__ bool next_unit(const Params &p) {
+    int start = 0, end = 0, u = 0;
+    bool ok = false;
+    if (!static_taken) {
+      static_taken = true;
+      if (per_s > 0 && (int64_t)wid * per_s < t_s) {
+        start = wid * per_s;
+        end = min(start + per_s, t_s);
+        u = wid;
+        ok = true;
+      }
+    }
+    if (!ok) {
+      int tk = 0;
+      if (lane == 0) tk = atomicAdd(ticket, 1);
+      tk = __shfl_sync(0xffffffffu, tk, 0);
+      if (tk >= n_chunks) {
+        // Out of work.  The last warp out resets the ticket for the next call.
+        if (lane == 0) {
+          const int out_n = atomicAdd(ticket + 1, 1);
+          if (out_n == W - 1) {
+            ticket[0] = 0;
+            ticket[1] = 0;
+          }
+        }
+        return false;
+      }
+      start = t_s + tk * chunk;
+      end = min(start + chunk, tot);
+      u = W + tk;
+    }
+    pc = locate(p, start, lane);
+    if (lane == 0) {
+      Unit un;
+      un.start = start;
+      un.end = end;
+      un.u = u;
+      un.b = pc.b;
+      un.h = pc.h;
+      un.t = pc.t;
+      un.n = pc.n;
+      un.ctx = pc.ctx;
+      uq[pushed % kUnitQ] = un;
+    }
+    ++pushed;
+    p_left = end - start;
+    return true;
+  }
+
+  // Keep S tiles in flight; issue(stage, cursor) starts one tile's copies.
+  template <int S, class IssueFn>
+  __device__ __forceinline__ void refill(const Params &p, int consumed, IssueFn &&issue) {
+    while (!p_done && issued - consumed < S) {
+      if (p_left == 0 && !next_unit(p)) {
+        p_done = true;
+        break;
+      }
+      if (lane == 0 && issued >= S) fence_proxy_async_smem();
+      issue(issued % S, pc);
+      advance(pc, p);
+      --p_left;
+      ++issued;
+    }
+  }
+};
+
+// Consumer side of the unit ring.
+struct UnitReader {
+  Cursor cc;
+  int left = 0, unit = 0, popped = 0;
+
+  __device__ __forceinline__ bool need_pop() const { return left == 0; }
+  __device__ __forceinline__ void pop(const Unit *uq) {
+    __syncwarp();
+    const Unit un = uq[popped % kUnitQ];
+    ++popped;
+    cc.b = un.b;
+    cc.h = un.h;
+    cc.t = un.t;
+    cc.n = un.n;
+    cc.ctx = un.ctx;
+    cc.pos = un.start;
+    left = un.end - un.start;
+    unit = un.u;
+  }
+};
+
+// After this warp's piece of pair bh has been written to its slot: count the
+// arrival; the warp that brings the count to nparts merges every piece's
+// (m, l, O) (slots uf + bh .. uf + nparts - 1 + bh) into the output and resets
+// the counter.
+template <int D>
+__device__ __forceinline__ void arrive_and_merge(const Params &p, const Cursor &cc, int bh, int uf,
+                                                 int nparts, int lane) {
+  __threadfence();
+  __syncwarp();
+  int old = 0;
+  if (lane == 0) old = atomicAdd(p.counters + bh, 1);
+  old = __shfl_sync(0xffffffffu, old, 0);
+  if (old != nparts - 1) return;
+  __threadfence();
+  const int E = p.rows * D;
+  for (int e = 4 * lane; e < E; e += 128) {
+    const int r = e / D, d = e - (e / D) * D;
+    float M = -INFINITY, Ls = 0.f;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int k = 0; k < nparts; ++k) {
+      const int64_t sl = (int64_t)uf + k + bh;
+      const float2 mlk = __ldcg(reinterpret_cast<const float2 *>(p.ml + (sl * p.rows + r) * 2));
+      const float4 ok = __ldcg(reinterpret_cast<const float4 *>(p.part + (sl * p.rows + r) * D + d));
+      const float Mn = fmaxf(M, mlk.x);
+      const float sa = fast_exp2(M - Mn), sb = fast_exp2(mlk.x - Mn);
+      Ls = Ls * sa + mlk.y * sb;
+      acc.x = acc.x * sa + ok.x * sb;
+      acc.y = acc.y * sa + ok.y * sb;
+      acc.z = acc.z * sa + ok.z * sb;
+      acc.w = acc.w * sa + ok.w * sb;
+      M = Mn;
+    }
+    const float inv = 1.f / Ls;
+    const int64_t o = row_offset(p.o_sb, p.o_st, p.o_sh, cc.b, cc.h, r, p.G) + d;
+    store_pair(p, o, acc.x * inv, acc.y * inv);
+    store_pair(p, o + 2, acc.z * inv, acc.w * inv);
+  }
+  if (lane == 0) p.counters[bh] = 0;
+}
+
+// Bounded wait on a stage; on timeout, record it and let this warp's copies
+// in flight (tiles first..issued-1) land, bounded, before the caller returns.
+template <int S>
+__device__ __forceinline__ bool wait_stage(const Params &p, uint32_t bar0, int i, int issued,
+                                           int lane) {
+  if (mbar_wait_bounded(bar0 + 8 * (i % S), (i / S) & 1, kTimeoutNs)) return true;
+  if (lane == 0) dev_error(p.err, MZ_DEVERR_TIMEOUT);
+  for (int k = i; k < issued; ++k) (void)mbar_wait_bounded(bar0 + 8 * (k % S), (k / S) & 1, kTimeoutNs);
+  return false;
+}
+
+// ---------------------------------------------------------------------------
+// Host-side helpers.
+// ---------------------------------------------------------------------------
+
+inline PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, []() {
+    void *f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &f, 12000, cudaEnableDefault,
+                                         &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+  });
+  return fn;
+}
+
+// 2-D tensor map over `rows` rows of `row_elems` elements, box = box_elems x 16
+// rows, 128-byte swizzle.
+inline int make_row_map(CUtensorMap *m, const void *base, int64_t rows, int row_elems,
+                        CUtensorMapDataType type, int elem_bytes, int box_elems) {
+  auto fn = encode_fn();
+  if (!fn) return fail(MZ_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(row_elems), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(row_elems) * elem_bytes};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(box_elems), static_cast<cuuint32_t>(kTileTok)};
+  cuuint32_t es[2] = {1, 1};
+  CUresult r = fn(m, type, 2, const_cast<void *>(base), dims, strides, box, es,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(MZ_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return MZ_OK;
+}
+
+struct WsLayout {
+  size_t counters, ml, part, total;
+  int64_t counter_words;
+  int max_chunks;
+};
+
+inline size_t align256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
+
+// Workspace for W warps: per-pair counters + 2 scheduler words, then (m, l)
+// and O partials for W static units + max_chunks dynamic units + one extra
+// slot per pair (slot = unit + pair).
+inline WsLayout ws_layout(int64_t n_pairs, int64_t warps, int rows, int D) {
+  WsLayout w;
+  w.max_chunks = static_cast<int>(2 * warps);
+  const int64_t slots = warps + w.max_chunks + n_pairs;
+  w.counter_words = n_pairs + 2;
+  w.counters = 0;
+  w.ml = align256(w.counter_words * sizeof(int32_t));
+  w.part = w.ml + align256(slots * rows * 2 * sizeof(float));
+  w.total = w.part + align256(slots * rows * D * sizeof(float));
+  return w;
+}
+
+// Scheduler tuning knob from the environment (read at each launch), clamped.
+inline int env_int(const char *name, int dflt, int lo, int hi) {
+  const char *v = getenv(name);
+  if (!v || !*v) return dflt;
+  long x = strtol(v, nullptr, 10);
+  return static_cast<int>(x < lo ? lo : (x > hi ? hi : x));
+}
+
+inline void set_schedule(Params &p, const WsLayout &ws) {
+  p.max_chunks = ws.max_chunks;
+  p.static_pct = env_int("MLXZ_B200_DECODE_STATIC_PCT", 100, 1, 100);
+  p.min_chunk = env_int("MLXZ_B200_DECODE_MIN_CHUNK", 16, 1, 1 << 20);
+}
+
+// Occupancy of a decode kernel instantiation (cached; also sets its shared
+// memory attribute once).
+template <class KernelPtr>
+int kernel_occupancy(KernelPtr k, int smem_bytes, int *cache, std::once_flag *once,
+                     cudaError_t *err, int *out) {
+  std::call_once(*once, [&]() {
+    *err = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes);
+    if (*err != cudaSuccess) return;
+    int n = 0;
+    *err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k, kWarps * 32, smem_bytes);
+    *cache = n;
+  });
+  if (*err != cudaSuccess) return cuda_fail(*err, "paged decode: occupancy query");
+  *out = *cache;
+  return MZ_OK;
+}
+
+}  // namespace decode
+}  // namespace mz

@@ -1,31 +1,14 @@
-// Fused GQA paged decode attention for sm_100a.
+// Fused GQA paged decode attention for sm_100a, bf16 / fp16 K/V.
 //
-// Work decomposition.  The KV of every (sequence b, kv head h) -- a "pair" --
-// is a list of 16-token tiles (a block of block_size tokens is block_size/16
-// tiles).  All tiles of all pairs, in (b, h, t) order, form one flat sequence
-// of T tiles, cut into units:
-//   * static units: the first T_s tiles (MLXZ_B200_DECODE_STATIC_PCT percent
-//     of T, all of it by default), one contiguous share of per_s = ceil(T_s / W)
-//     tiles per warp (W persistent warps);
-//   * dynamic units: the rest, if any, in chunks of C tiles that warps claim
-//     with an atomic ticket once their static share is done.
-// Measured on B200 at the 8B shape, the per-warp tile rate is uniform to a
-// few percent, and a dynamic chunk is too coarse (one warp streams a 16-tile
-// chunk in ~23 us) to shorten the tail, so the default hands out everything
-// statically; the dynamic path stays for tuning and is tested.
-// A pair that lies inside one unit is finished by the warp that runs the unit.
-// A pair cut by unit boundaries leaves one partial (running max m, running sum
-// l, unnormalised O) per piece in the workspace at slot (unit + pair); the
-// warp that finishes the pair's last piece (per-pair arrival counter) merges
-// them.  Counters clean themselves up, so a zeroed workspace stays reusable.
-//
-// Per warp, a STAGES-deep ring of shared-memory stages is filled by 2-D bulk
-// tensor copies (cp.async.bulk.tensor, 128-byte swizzle, no multicast) that
-// complete on per-stage mbarriers; lane 0 issues, all lanes consume.  The
-// grouped query rows (n_q * G <= 16) form the M=16 side of mma.sync m16n8k16:
-// S = Q.K^T over the tile (2 n-tiles of 8 tokens), an fp32 online softmax in
-// the exp2 domain, then O += P.V (D/8 n-tiles).  For bf16, P is split into
-// hi + lo bf16 parts so P.V carries ~16 mantissa bits of P.
+// Scheduling (persistent warps, flat tile list, static shares + optional
+// dynamic chunks, merge of split pairs by the last-arriving piece) lives in
+// decode_common.cuh.  Per warp, a STAGES-deep ring of shared-memory stages is
+// filled by 2-D bulk tensor copies (cp.async.bulk.tensor, 128-byte swizzle, no
+// multicast) that complete on per-stage mbarriers; lane 0 issues, all lanes
+// consume.  The grouped query rows (n_q * G <= 16) form the M=16 side of
+// mma.sync m16n8k16: S = Q.K^T over the tile (2 n-tiles of 8 tokens), an fp32
+// online softmax in the exp2 domain, then O += P.V (D/8 n-tiles).  For bf16, P
+// is split into hi + lo bf16 parts so P.V carries ~16 mantissa bits of P.
 //
 // Optional fused append (decode step): the new token of each sequence, the
 // last one attended, is written into its pool slot and patched into the staged
@@ -34,25 +17,18 @@
 // Roofline: each tile moves 2 * 16 * D * 2 bytes (K and V) and needs
 // 4 * rows * 16 * D flops; with rows = 4 (GQA group 4) that is 2 flop/byte,
 // so the kernel is HBM-bound and the bulk-copy pipeline depth is what matters.
-#include <cuda.h>
-#include <cudaTypedefs.h>
+// Measured on B200 at the 8B shape, the per-warp tile rate is uniform to a
+// few percent, and a dynamic chunk is too coarse (one warp streams a 16-tile
+// chunk in ~23 us) to shorten the tail, so the default hands out everything
+// statically; the dynamic path stays for tuning and is tested.
+#include "decode_common.cuh"
 
-#include <cmath>
-#include <cstdlib>
-#include <mutex>
-
-#include "common.cuh"
-
-namespace mz {
-namespace decode {
-
-constexpr int kWarps = 4;
-constexpr int kTileTok = 16;
 #ifndef MZ_DECODE_STAGES_D128
 #define MZ_DECODE_STAGES_D128 3
 #endif
-constexpr int kUnitQ = 8;  // per-warp ring of unit descriptors
-constexpr uint64_t kTimeoutNs = 2000000000ull;  // 2 s bound on any single wait
+
+namespace mz {
+namespace decode {
 
 template <int D>
 struct Cfg {
@@ -64,133 +40,6 @@ struct Cfg {
   static constexpr int kSmemUnits = kWarps * kUnitQ * 32;
   static constexpr int kSmemBytes = kSmemTiles + kSmemBars + kSmemUnits + 1024;  // + align
 };
-
-struct Params {
-  void *out;
-  int64_t o_sb, o_st, o_sh;
-  int out_f32;
-  const void *q;
-  int64_t q_sb, q_st, q_sh;
-  int n_q, G, rows;
-  const int32_t *tables;
-  int max_blocks;
-  const int32_t *ctx;
-  int B, Hkv;
-  int bs, tpb;  // block size, tiles per block
-  int64_t n_blocks;
-  float scale_log2;
-  // fused append (kn == nullptr: none)
-  const uint16_t *kn, *vn;
-  int64_t kn_sb, kn_sh;
-  uint16_t *k_pool, *v_pool;
-  // workspace
-  int32_t *counters;  // [n_pairs] arrival counters, then [2] = ticket, exited
-  float *ml;          // [slots][rows][2]
-  float *part;        // [slots][rows][D]
-  int max_chunks;
-  int static_pct;  // share of tiles handed out statically (1..100)
-  int min_chunk;   // smallest dynamic chunk (tiles)
-  int32_t *err;
-};
-
-struct Cursor {
-  int b, h, t, n, ctx;
-  int pos;
-};
-
-// A unit descriptor (32 bytes), passed from the producer to the consumer.
-struct Unit {
-  int start, end, u, b, h, t, n, ctx;
-};
-
-__device__ __forceinline__ int ntiles_of(int ctx) { return (ctx + kTileTok - 1) / kTileTok; }
-
-__device__ __forceinline__ int clamped_ctx(const Params &p, int b) {
-  int c = p.ctx[b];
-  const int cap = p.max_blocks * p.bs;
-  if (c < 0 || c > cap) {
-    dev_error(p.err, MZ_DEVERR_CONTEXT);
-    c = c < 0 ? 0 : cap;
-  }
-  return c;
-}
-
-__device__ __forceinline__ void advance(Cursor &c, const Params &p) {
-  ++c.pos;
-  if (++c.t == c.n) {
-    c.t = 0;
-    if (++c.h == p.Hkv) {
-      c.h = 0;
-      for (;;) {
-        if (++c.b >= p.B) {
-          c.n = 0;
-          break;
-        }
-        c.ctx = clamped_ctx(p, c.b);
-        c.n = ntiles_of(c.ctx);
-        if (c.n > 0) break;
-      }
-    }
-  }
-}
-
-// Cursor at flat tile x (0 <= x < T), found with a warp scan over sequences.
-__device__ Cursor locate(const Params &p, int x, int lane) {
-  int base = 0, bf = 0;
-  for (int b0 = 0; b0 < p.B; b0 += 32) {
-    const int b = b0 + lane;
-    const int c = (b < p.B) ? ntiles_of(clamped_ctx(p, b)) * p.Hkv : 0;
-    int incl = c;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const int y = __shfl_up_sync(0xffffffffu, incl, o);
-      if (lane >= o) incl += y;
-    }
-    const unsigned m = __ballot_sync(0xffffffffu, base + incl > x);
-    if (m) {
-      const int L = __ffs(m) - 1;
-      base += __shfl_sync(0xffffffffu, incl - c, L);
-      bf = b0 + L;
-      break;
-    }
-    base += __shfl_sync(0xffffffffu, incl, 31);
-  }
-  Cursor cur;
-  cur.b = bf;
-  cur.ctx = clamped_ctx(p, bf);
-  cur.n = ntiles_of(cur.ctx);
-  const int r = x - base;
-  cur.h = r / cur.n;
-  cur.t = r - cur.h * cur.n;
-  cur.pos = x;
-  return cur;
-}
-
-// Address of output (or q) element row r of pair (b, h), dim 0.
-__device__ __forceinline__ int64_t row_offset(int64_t sb, int64_t st, int64_t sh, int b, int h,
-                                              int r, int G) {
-  const int i = r / G, g = r - (r / G) * G;
-  return (int64_t)b * sb + (int64_t)i * st + (int64_t)(h * G + g) * sh;
-}
-
-__device__ __forceinline__ void store_pair(const Params &p, int64_t off, float x, float y,
-                                           bool bf16) {
-  if (p.out_f32) {
-    *reinterpret_cast<float2 *>(static_cast<float *>(p.out) + off) = make_float2(x, y);
-  } else if (bf16) {
-    *reinterpret_cast<__nv_bfloat162 *>(static_cast<__nv_bfloat16 *>(p.out) + off) =
-        __floats2bfloat162_rn(x, y);
-  } else {
-    *reinterpret_cast<__half2 *>(static_cast<__half *>(p.out) + off) = __floats2half2_rn(x, y);
-  }
-}
-
-// 128-byte swizzle of a [16 tok][64 dim] 2-KiB box: 16-byte unit u of line
-// `tok` lives at unit u ^ (tok & 7).  D = 128 uses two boxes (dims 0-63, 64-127).
-__device__ __forceinline__ uint32_t smem_off(int tok, int d) {
-  const int box = d >> 6, u = (d & 63) >> 3;
-  return box * 2048 + tok * 128 + ((u ^ (tok & 7)) << 4);
-}
 
 template <int D, bool BF16>
 __global__ void __launch_bounds__(kWarps * 32, 2)
@@ -221,91 +70,11 @@ __global__ void __launch_bounds__(kWarps * 32, 2)
   }
   __syncwarp();
 
-  // Sequences with no context produce zeros.
-  for (int b = wid; b < p.B; b += W) {
-    if (clamped_ctx(p, b) != 0) continue;
-    for (int h = 0; h < p.Hkv; ++h)
-      for (int r = 0; r < p.rows; ++r) {
-        const int64_t o = row_offset(p.o_sb, p.o_st, p.o_sh, b, h, r, p.G);
-        for (int d = 2 * lane; d < D; d += 64) store_pair(p, o + d, 0.f, 0.f, BF16);
-      }
-  }
+  zero_empty_outputs<D>(p, wid, W, lane);
+  Sched sch;
+  if (!sch.init(p, lane, wid, W, uq)) return;  // T == 0: no counter is touched
 
-  // Total tiles T, the static share per warp and the dynamic chunking.
-  int tot = 0;
-  for (int b = lane; b < p.B; b += 32) tot += ntiles_of(clamped_ctx(p, b));
-#pragma unroll
-  for (int o = 16; o; o >>= 1) tot += __shfl_xor_sync(0xffffffffu, tot, o);
-  tot *= p.Hkv;
-  if (tot == 0) return;  // every warp leaves here: no counter is touched
-  // static share: ceil(T * pct / 100 / W) tiles per warp (the last shares may
-  // be short or empty), so with pct = 100 warps differ by at most one tile
-  const int64_t t_target = (int64_t)tot * p.static_pct / 100;
-  const int per_s = static_cast<int>((t_target + W - 1) / W);
-  const int t_s = static_cast<int>(min((int64_t)per_s * W, (int64_t)tot));
-  const int dyn = tot - t_s;
-  int chunk = (dyn + p.max_chunks - 1) / p.max_chunks;
-  if (chunk < p.min_chunk) chunk = p.min_chunk;
-  const int n_chunks = (dyn + chunk - 1) / chunk;
-  int32_t *ticket = p.counters + (int64_t)p.B * p.Hkv;
-  // unit index of flat tile x
-  auto unit_of = [&](int x) -> int { return x < t_s ? x / per_s : W + (x - t_s) / chunk; };
-
-  // ---- producer state (warp-uniform; lane 0 issues) ----
-  Cursor pc;
-  int p_left = 0, pushed = 0, issued = 0;
-  bool p_done = false, static_taken = false;
   const uint64_t pol = l2_policy_evict_first();
-
-  auto next_unit = [&]() -> bool {
-    int start = 0, end = 0, u = 0;
-    bool ok = false;
-    if (!static_taken) {
-      static_taken = true;
-      if (per_s > 0 && (int64_t)wid * per_s < t_s) {
-        start = wid * per_s;
-        end = min(start + per_s, t_s);
-        u = wid;
-        ok = true;
-      }
-    }
-    if (!ok) {
-      int tk = 0;
-      if (lane == 0) tk = atomicAdd(ticket, 1);
-      tk = __shfl_sync(0xffffffffu, tk, 0);
-      if (tk >= n_chunks) {
-        // Out of work.  The last warp out resets the ticket for the next call.
-        if (lane == 0) {
-          const int out_n = atomicAdd(ticket + 1, 1);
-          if (out_n == W - 1) {
-            ticket[0] = 0;
-            ticket[1] = 0;
-          }
-        }
-        return false;
-      }
-      start = t_s + tk * chunk;
-      end = min(start + chunk, tot);
-      u = W + tk;
-    }
-    pc = locate(p, start, lane);
-    if (lane == 0) {
-      Unit un;
-      un.start = start;
-      un.end = end;
-      un.u = u;
-      un.b = pc.b;
-      un.h = pc.h;
-      un.t = pc.t;
-      un.n = pc.n;
-      un.ctx = pc.ctx;
-      uq[pushed % kUnitQ] = un;
-    }
-    ++pushed;
-    p_left = end - start;
-    return true;
-  };
-
   auto issue = [&](int s, const Cursor &c) {
     if (lane == 0) {
       int32_t blk = p.tables[(int64_t)c.b * p.max_blocks + c.t / p.tpb];
@@ -325,21 +94,6 @@ __global__ void __launch_bounds__(kWarps * 32, 2)
     }
   };
 
-  // Keep S tiles in flight.
-  auto refill = [&](int consumed) {
-    while (!p_done && issued - consumed < S) {
-      if (p_left == 0 && !next_unit()) {
-        p_done = true;
-        break;
-      }
-      if (lane == 0 && issued >= S) fence_proxy_async_smem();
-      issue(issued % S, pc);
-      advance(pc, p);
-      --p_left;
-      ++issued;
-    }
-  };
-
   // Per-lane ldmatrix geometry.
   const int mi = lane >> 3, r8 = lane & 7;
   const int tokK = r8 + 8 * (mi >> 1), subK = mi & 1;  // K: m0,m1 tok 0-7; m2,m3 tok 8-15
@@ -351,29 +105,17 @@ __global__ void __launch_bounds__(kWarps * 32, 2)
   float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
   const bool two_groups = p.rows > 8;
 
-  Cursor cc;
-  int c_left = 0, c_unit = 0, popped = 0;
+  UnitReader ur;
   bool seg_first = true;
 
-  refill(0);
-  for (int i = 0; i < issued; ++i) {
+  sch.refill<S>(p, 0, issue);
+  for (int i = 0; i < sch.issued; ++i) {
     const int s = i % S;
-    const uint32_t ph = (i / S) & 1;
-
-    if (c_left == 0) {
-      __syncwarp();
-      const Unit un = uq[popped % kUnitQ];
-      ++popped;
-      cc.b = un.b;
-      cc.h = un.h;
-      cc.t = un.t;
-      cc.n = un.n;
-      cc.ctx = un.ctx;
-      cc.pos = un.start;
-      c_left = un.end - un.start;
-      c_unit = un.u;
+    if (ur.need_pop()) {
+      ur.pop(uq);
       seg_first = true;
     }
+    const Cursor &cc = ur.cc;
 
     if (seg_first || cc.t == 0) {
       // New piece: load the grouped query rows as A fragments.
@@ -396,13 +138,7 @@ __global__ void __launch_bounds__(kWarps * 32, 2)
       }
     }
 
-    if (!mbar_wait_bounded(bar0 + 8 * s, ph, kTimeoutNs)) {
-      // Give up: record it, let this warp's copies in flight land (bounded), return.
-      if (lane == 0) dev_error(p.err, MZ_DEVERR_TIMEOUT);
-      for (int k = i; k < issued; ++k)
-        (void)mbar_wait_bounded(bar0 + 8 * (k % S), (k / S) & 1, kTimeoutNs);
-      return;
-    }
+    if (!wait_stage<S>(p, bar0, i, sch.issued, lane)) return;
 
     uint8_t *kt = stages + s * C::kStageBytes;
     uint8_t *vt = kt + C::kTileBytes;
@@ -422,7 +158,7 @@ __global__ void __launch_bounds__(kWarps * 32, 2)
         const uint16_t *src =
             (is_v ? p.vn : p.kn) + (int64_t)cc.b * p.kn_sb + (int64_t)cc.h * p.kn_sh + d;
         const uint4 val = *reinterpret_cast<const uint4 *>(src);
-        *reinterpret_cast<uint4 *>((is_v ? vt : kt) + smem_off(row, d)) = val;
+        *reinterpret_cast<uint4 *>((is_v ? vt : kt) + swz128(row, 2 * d)) = val;
         const int32_t blk = p.tables[(int64_t)cc.b * p.max_blocks + pos / p.bs];
         if (blk >= 0 && blk < p.n_blocks) {
           uint16_t *dst = (is_v ? p.v_pool : p.k_pool) +
@@ -437,7 +173,7 @@ __global__ void __launch_bounds__(kWarps * 32, 2)
       // that 0 * V stays 0 in P.V.
       for (int e = lane; e < (kTileTok - nvalid) * (D / 8); e += 32) {
         const int tok = nvalid + e / (D / 8), d = (e % (D / 8)) * 8;
-        *reinterpret_cast<uint4 *>(vt + smem_off(tok, d)) = make_uint4(0, 0, 0, 0);
+        *reinterpret_cast<uint4 *>(vt + swz128(tok, 2 * d)) = make_uint4(0, 0, 0, 0);
       }
       __syncwarp();
     }
@@ -449,7 +185,7 @@ __global__ void __launch_bounds__(kWarps * 32, 2)
 #pragma unroll
     for (int j = 0; j < KS; ++j) {
       uint32_t b0, b1, b2, b3;
-      ldsm_x4(kb + smem_off(tokK, 16 * j + 8 * subK), b0, b1, b2, b3);
+      ldsm_x4(kb + swz128(tokK, 2 * (16 * j + 8 * subK)), b0, b1, b2, b3);
       mma_16816<BF16>(sacc[0], qa[j], b0, b1);
       mma_16816<BF16>(sacc[1], qa[j], b2, b3);
     }
@@ -529,7 +265,7 @@ __global__ void __launch_bounds__(kWarps * 32, 2)
 #pragma unroll
     for (int j = 0; j < KS; ++j) {
       uint32_t v0, v1, v2, v3;
-      ldsm_x4_trans(vb + smem_off(tokV, 16 * j + 8 * subV), v0, v1, v2, v3);
+      ldsm_x4_trans(vb + swz128(tokV, 2 * (16 * j + 8 * subV)), v0, v1, v2, v3);
       mma_16816<BF16>(oacc[2 * j], ph_, v0, v1);
       mma_16816<BF16>(oacc[2 * j + 1], ph_, v2, v3);
       if constexpr (BF16) {
@@ -539,7 +275,7 @@ __global__ void __launch_bounds__(kWarps * 32, 2)
     }
 
     // Piece end: last tile of the pair, or last tile of the unit.
-    if (last_tile || c_left == 1) {
+    if (last_tile || ur.left == 1) {
       float L0 = l0, L1 = l1;
       L0 += __shfl_xor_sync(0xffffffffu, L0, 1);
       L0 += __shfl_xor_sync(0xffffffffu, L0, 2);
@@ -547,23 +283,23 @@ __global__ void __launch_bounds__(kWarps * 32, 2)
       L1 += __shfl_xor_sync(0xffffffffu, L1, 2);
       const int bh = cc.b * p.Hkv + cc.h;
       const int pbh = cc.pos - cc.t;  // flat index of tile 0 of this pair
-      const int uf = unit_of(pbh), ul = unit_of(pbh + cc.n - 1);
+      const int uf = sch.unit_of(pbh), ul = sch.unit_of(pbh + cc.n - 1);
       if (uf == ul) {
         const float i0 = 1.f / L0, i1 = two_groups ? 1.f / L1 : 0.f;
         if (g < p.rows) {
           const int64_t o = row_offset(p.o_sb, p.o_st, p.o_sh, cc.b, cc.h, g, p.G);
 #pragma unroll
           for (int n = 0; n < NT; ++n)
-            store_pair(p, o + n * 8 + 2 * cq, oacc[n][0] * i0, oacc[n][1] * i0, BF16);
+            store_pair(p, o + n * 8 + 2 * cq, oacc[n][0] * i0, oacc[n][1] * i0);
         }
         if (g + 8 < p.rows) {
           const int64_t o = row_offset(p.o_sb, p.o_st, p.o_sh, cc.b, cc.h, g + 8, p.G);
 #pragma unroll
           for (int n = 0; n < NT; ++n)
-            store_pair(p, o + n * 8 + 2 * cq, oacc[n][2] * i1, oacc[n][3] * i1, BF16);
+            store_pair(p, o + n * 8 + 2 * cq, oacc[n][2] * i1, oacc[n][3] * i1);
         }
       } else {
-        const int64_t slot = (int64_t)c_unit + bh;
+        const int64_t slot = (int64_t)ur.unit + bh;
         float *pr = p.part + slot * p.rows * D;
         float *mlr = p.ml + slot * p.rows * 2;
         if (g < p.rows) {
@@ -580,48 +316,15 @@ __global__ void __launch_bounds__(kWarps * 32, 2)
                 make_float2(oacc[n][2], oacc[n][3]);
           if (cq == 0) *reinterpret_cast<float2 *>(mlr + 2 * (g + 8)) = make_float2(m1, L1);
         }
-        __threadfence();
-        __syncwarp();
-        int old = 0;
-        if (lane == 0) old = atomicAdd(p.counters + bh, 1);
-        old = __shfl_sync(0xffffffffu, old, 0);
-        const int nparts = ul - uf + 1;
-        if (old == nparts - 1) {
-          // Last piece: merge every piece's (m, l, O) and write the output.
-          __threadfence();
-          const int E = p.rows * D;
-          for (int e = 4 * lane; e < E; e += 128) {
-            const int r = e / D, d = e - (e / D) * D;
-            float M = -INFINITY, Ls = 0.f;
-            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-            for (int k = 0; k < nparts; ++k) {
-              const int64_t sl = (int64_t)uf + k + bh;
-              const float2 mlk = __ldcg(reinterpret_cast<const float2 *>(p.ml + (sl * p.rows + r) * 2));
-              const float4 ok = __ldcg(reinterpret_cast<const float4 *>(p.part + (sl * p.rows + r) * D + d));
-              const float Mn = fmaxf(M, mlk.x);
-              const float sa = fast_exp2(M - Mn), sb = fast_exp2(mlk.x - Mn);
-              Ls = Ls * sa + mlk.y * sb;
-              acc.x = acc.x * sa + ok.x * sb;
-              acc.y = acc.y * sa + ok.y * sb;
-              acc.z = acc.z * sa + ok.z * sb;
-              acc.w = acc.w * sa + ok.w * sb;
-              M = Mn;
-            }
-            const float inv = 1.f / Ls;
-            const int64_t o = row_offset(p.o_sb, p.o_st, p.o_sh, cc.b, cc.h, r, p.G) + d;
-            store_pair(p, o, acc.x * inv, acc.y * inv, BF16);
-            store_pair(p, o + 2, acc.z * inv, acc.w * inv, BF16);
-          }
-          if (lane == 0) p.counters[bh] = 0;
-        }
+        arrive_and_merge<D>(p, cc, bh, uf, ul - uf + 1, lane);
       }
       seg_first = true;  // the next tile starts a new piece
     }
 
     __syncwarp();
-    --c_left;
-    advance(cc, p);
-    refill(i + 1);
+    --ur.left;
+    advance(ur.cc, p);
+    sch.refill<S>(p, i + 1, issue);
   }
 }
 
@@ -629,34 +332,11 @@ __global__ void __launch_bounds__(kWarps * 32, 2)
 // Host side.
 // ---------------------------------------------------------------------------
 
-PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  static std::once_flag once;
-  std::call_once(once, []() {
-    void *f = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &f, 12000, cudaEnableDefault,
-                                         &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
-  });
-  return fn;
-}
-
 // Tensor map over a pool seen as rows of `D` 16-bit elements, box 64 x 16.
 int make_pool_map(CUtensorMap *m, const void *pool, int64_t rows, int D, bool bf16) {
-  auto fn = encode_fn();
-  if (!fn) return fail(MZ_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
-  cuuint64_t dims[2] = {static_cast<cuuint64_t>(D), static_cast<cuuint64_t>(rows)};
-  cuuint64_t strides[1] = {static_cast<cuuint64_t>(D) * 2};
-  cuuint32_t box[2] = {64, kTileTok};
-  cuuint32_t es[2] = {1, 1};
-  CUresult r = fn(m, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
-                  const_cast<void *>(pool), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) return fail(MZ_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
-  return MZ_OK;
+  return make_row_map(m, pool, rows, D,
+                      bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
+                      64);
 }
 
 template <int D, bool BF16>
@@ -664,45 +344,13 @@ int kernel_ctas_per_sm(int *out) {
   static int cached = -1;
   static std::once_flag once;
   static cudaError_t err = cudaSuccess;
-  std::call_once(once, []() {
-    auto k = paged_decode_kernel<D, BF16>;
-    err = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<D>::kSmemBytes);
-    if (err != cudaSuccess) return;
-    int n = 0;
-    err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k, kWarps * 32, Cfg<D>::kSmemBytes);
-    cached = n;
-  });
-  if (err != cudaSuccess) return cuda_fail(err, "paged_decode: occupancy query");
-  *out = cached;
-  return MZ_OK;
+  return kernel_occupancy(paged_decode_kernel<D, BF16>, Cfg<D>::kSmemBytes, &cached, &once, &err,
+                          out);
 }
 
 int ctas_per_sm(int D, bool bf16, int *out) {
   if (D == 128) return bf16 ? kernel_ctas_per_sm<128, true>(out) : kernel_ctas_per_sm<128, false>(out);
   return bf16 ? kernel_ctas_per_sm<64, true>(out) : kernel_ctas_per_sm<64, false>(out);
-}
-
-struct WsLayout {
-  size_t counters, ml, part, total;
-  int64_t counter_words;
-  int max_chunks;
-};
-
-inline size_t align256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
-
-// Workspace for W warps: per-pair counters + 2 scheduler words, then (m, l)
-// and O partials for W static units + max_chunks dynamic units + one extra
-// slot per pair (slot = unit + pair).
-WsLayout ws_layout(int64_t n_pairs, int64_t warps, int rows, int D) {
-  WsLayout w;
-  w.max_chunks = static_cast<int>(2 * warps);
-  const int64_t slots = warps + w.max_chunks + n_pairs;
-  w.counter_words = n_pairs + 2;
-  w.counters = 0;
-  w.ml = align256(w.counter_words * sizeof(int32_t));
-  w.part = w.ml + align256(slots * rows * 2 * sizeof(float));
-  w.total = w.part + align256(slots * rows * D * sizeof(float));
-  return w;
 }
 
 int resolve_warps(int D, bool bf16, int num_warps, int device, int64_t *warps) {
@@ -722,14 +370,6 @@ int resolve_warps(int D, bool bf16, int num_warps, int device, int64_t *warps) {
   if (sms <= 0) return fail(MZ_ERR_CUDA, "cannot query SM count of device %d", device);
   *warps = (int64_t)sms * per_sm * kWarps;
   return MZ_OK;
-}
-
-// Scheduler tuning knob from the environment (read at each launch), clamped.
-int env_int(const char *name, int dflt, int lo, int hi) {
-  const char *v = getenv(name);
-  if (!v || !*v) return dflt;
-  long x = strtol(v, nullptr, 10);
-  return static_cast<int>(x < lo ? lo : (x > hi ? hi : x));
 }
 
 // Everything a decode launch needs besides its scratch.
@@ -844,9 +484,9 @@ int launch(const DecodeArgs &a, int64_t warps, const WsLayout &ws, void *scratch
   p.counters = reinterpret_cast<int32_t *>(w8 + ws.counters);
   p.ml = reinterpret_cast<float *>(w8 + ws.ml);
   p.part = reinterpret_cast<float *>(w8 + ws.part);
-  p.max_chunks = ws.max_chunks;
-  p.static_pct = env_int("MLXZ_B200_DECODE_STATIC_PCT", 100, 1, 100);
-  p.min_chunk = env_int("MLXZ_B200_DECODE_MIN_CHUNK", 16, 1, 1 << 20);
+  set_schedule(p, ws);
+  p.q_bf16 = bf16;
+  p.k_scales = p.k_biases = p.v_scales = p.v_biases = nullptr;
   p.err = a.err;
 
   int per_sm = 0;  // also sets the kernel's shared-memory attribute (once)
