@@ -236,6 +236,75 @@ MZ_API int mz_block_unpack(void *pool_base, int64_t pool_stride_bytes, int32_t n
                     int64_t block_bytes, const void *staging, const int32_t *ids, int32_t n_ids,
                     int64_t n_blocks, int32_t *dev_err, mz_stream_t stream);
 
+/* ------------------------------------------------------------------------ */
+/* 4/8-bit affine group quantised KV.                                        */
+/* ------------------------------------------------------------------------ */
+
+/* Quantised pools, per layer and per K / V (the paged form of mlx_lm's
+ * quantised cache state ((data, scales, biases), used by the reference at
+ * src/mlxz/engine/cache_utils.py:12-92 and src/mlxz/prefix_cache/base.py:18)):
+ *   codes  uint32 [n_blocks][n_kv_heads][block_size][head_dim * bits / 32],
+ *          element i of a row at word i / (32/bits), bits (i % (32/bits))*bits
+ *          upward (least significant first);
+ *   scales fp16 [n_blocks][n_kv_heads][block_size][head_dim / 64], biases alike.
+ * Per 64-value group, in IEEE fp32 round-to-nearest-even:
+ *   scale = (max - min) / (2^bits - 1), s16 = fp16(scale), b16 = fp16(min),
+ *   q = clamp(rint((w - b16) / s16), 0, 2^bits - 1), q = 0 when s16 == 0;
+ *   dequantised value s16 * q + b16.  Inputs finite, |w| <= 65504.
+ * Supported: bits 4 or 8, group_size 64, head_dim 64 or 128. */
+
+/* Quantise-on-append by slot (the quantised form of mz_kv_append; replaces the
+ * quantisation inside QuantizedKVCache.update_and_fetch that the reference
+ * reaches through cache_utils.py:54-92).  k_new/v_new element (token i, head
+ * h, dim d) at base + i*new_tok_stride + h*new_head_stride + d (dtype F16 or
+ * BF16).  Negative slots skip.  Bit-exact to the rule above. */
+MZ_API int mz_kv_quant_append(void *k_codes, void *k_scales, void *k_biases, void *v_codes,
+                              void *v_scales, void *v_biases, const void *k_new, const void *v_new,
+                              int64_t new_tok_stride, int64_t new_head_stride,
+                              const int64_t *slot_mapping, int64_t n_tokens, int32_t n_kv_heads,
+                              int32_t head_dim, int32_t block_size, int64_t n_blocks, int32_t bits,
+                              int32_t group_size, int32_t dtype, int32_t *dev_err,
+                              mz_stream_t stream);
+
+/* Decode-step form: one token per sequence at positions[b] through the block
+ * table (the quantised form of mz_kv_append_paged). */
+MZ_API int mz_kv_quant_append_paged(void *k_codes, void *k_scales, void *k_biases, void *v_codes,
+                                    void *v_scales, void *v_biases, const void *k_new,
+                                    const void *v_new, int64_t new_seq_stride,
+                                    int64_t new_head_stride, const int32_t *block_tables,
+                                    int32_t max_blocks_per_seq, const int32_t *positions,
+                                    int32_t n_seqs, int32_t n_kv_heads, int32_t head_dim,
+                                    int32_t block_size, int64_t n_blocks, int32_t bits,
+                                    int32_t group_size, int32_t dtype, int32_t *dev_err,
+                                    mz_stream_t stream);
+
+/* Workspace bytes for mz_paged_decode_q (same layout rules as
+ * mz_paged_decode_workspace_size). */
+MZ_API int mz_paged_decode_q_workspace_size(int32_t n_seqs, int32_t n_kv_heads,
+                                            int32_t rows_per_kv_head, int32_t head_dim,
+                                            int32_t bits, int32_t num_warps, int32_t device,
+                                            size_t *bytes);
+
+/* Paged decode attention over quantised K/V with the dequantisation fused in
+ * (attention over the dequantised values s16 * q + b16; the reference attends
+ * over mlx_lm's quantised cache through mx.quantized_matmul).  Arguments as
+ * mz_paged_decode, with the six quantised pools in place of the K/V pools; q
+ * (and out unless F32) of element type `dtype`, converted to fp16 for the
+ * products (exact for bf16 values with fp16-representable magnitude).
+ * Pools need 16-byte alignment. */
+MZ_API int mz_paged_decode_q(void *out, int32_t out_dtype, int64_t out_seq_stride,
+                             int64_t out_tok_stride, int64_t out_head_stride, const void *q,
+                             int64_t q_seq_stride, int64_t q_tok_stride, int64_t q_head_stride,
+                             int32_t n_q_tokens, const void *k_codes, const void *k_scales,
+                             const void *k_biases, const void *v_codes, const void *v_scales,
+                             const void *v_biases, const int32_t *block_tables,
+                             int32_t max_blocks_per_seq, const int32_t *ctx_lens, int32_t n_seqs,
+                             int32_t n_heads, int32_t n_kv_heads, int32_t head_dim,
+                             int32_t block_size, int64_t n_blocks, int32_t bits,
+                             int32_t group_size, float scale, int32_t dtype, int32_t num_warps,
+                             void *workspace, size_t workspace_bytes, int32_t *dev_err,
+                             mz_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -89,6 +89,15 @@ _SIGNATURES: dict[str, list] = {
                                 _vp, _vp, _i32, _vp, _i32, _i32, _i32, _i32, _i32, _i64, _f32,
                                 _i32, _i32, _vp, _vp],
     "mz_block_copy": [_vp, _i64, _i32, _i64, _vp, _vp, _i32, _i64, _vp, _vp],
+    "mz_kv_quant_append": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _vp, _i64, _i32,
+                           _i32, _i32, _i64, _i32, _i32, _i32, _vp, _vp],
+    "mz_kv_quant_append_paged": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _vp, _i32,
+                                 _vp, _i32, _i32, _i32, _i32, _i64, _i32, _i32, _i32, _vp, _vp],
+    "mz_paged_decode_q_workspace_size": [_i32, _i32, _i32, _i32, _i32, _i32, _i32,
+                                         ctypes.POINTER(_sz)],
+    "mz_paged_decode_q": [_vp, _i32, _i64, _i64, _i64, _vp, _i64, _i64, _i64, _i32, _vp, _vp,
+                          _vp, _vp, _vp, _vp, _vp, _i32, _vp, _i32, _i32, _i32, _i32, _i32, _i64,
+                          _i32, _i32, _f32, _i32, _i32, _vp, _sz, _vp, _vp],
     "mz_block_pack": [_vp, _vp, _i64, _i32, _i64, _vp, _i32, _i64, _vp, _vp],
     "mz_block_unpack": [_vp, _i64, _i32, _i64, _vp, _vp, _i32, _i64, _vp, _vp],
 }

@@ -54,7 +54,8 @@ struct Params {
   const uint16_t *kn, *vn;
   int64_t kn_sb, kn_sh;
   uint16_t *k_pool, *v_pool;
-  // quantised pools: per-token group scales and biases (fp16)
+  // quantised pools: packed codes and per-token group scales and biases (fp16)
+  const uint8_t *kq, *vq;
   const __half *k_scales, *k_biases, *v_scales, *v_biases;
   // workspace
   int32_t *counters;  // [n_pairs] arrival counters, then [2] = ticket, exited

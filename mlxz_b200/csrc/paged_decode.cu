@@ -486,6 +486,7 @@ int launch(const DecodeArgs &a, int64_t warps, const WsLayout &ws, void *scratch
   p.part = reinterpret_cast<float *>(w8 + ws.part);
   set_schedule(p, ws);
   p.q_bf16 = bf16;
+  p.kq = p.vq = nullptr;
   p.k_scales = p.k_biases = p.v_scales = p.v_biases = nullptr;
   p.err = a.err;
 

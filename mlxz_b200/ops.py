@@ -209,7 +209,7 @@ def decode_workspace(n_seqs: int, n_kv_heads: int, rows: int, head_dim: int, dev
 
 def reset_workspaces() -> None:
     """Zero every cached workspace (needed after a call that reported an error)."""
-    for ws in _workspaces.values():
+    for ws in list(_workspaces.values()) + list(_qworkspaces.values()):
         ws.zero_()
 
 
@@ -307,6 +307,144 @@ def paged_append_decode(q: torch.Tensor, k_pool: torch.Tensor, v_pool: torch.Ten
              ctx_lens.data_ptr(), B, Hq, Hkv, D, bs, n_blocks, float(scale),
              dtype_code(q.dtype), num_warps, workspace.data_ptr(), workspace.numel(),
              error_word(dev).data_ptr(), _stream(dev))
+    _after(dev)
+    return out
+
+
+# ---------------------------------------------------------------------------
+# Quantised KV
+# ---------------------------------------------------------------------------
+
+def _check_qpools(pools) -> tuple[int, int, int, int, int]:
+    """(n_blocks, H, bs, D, bits) of a 6-tuple (k_codes, k_scales, k_biases,
+    v_codes, v_scales, v_biases): codes int32 [N, H, bs, D*bits/32], scales and
+    biases fp16 [N, H, bs, D/64]."""
+    if len(pools) != 6:
+        raise ValueError("quantised pools: (k_codes, k_scales, k_biases, v_codes, v_scales, v_biases)")
+    kc, ks, kb, vc, vs, vb = pools
+    for t in pools:
+        if not t.is_contiguous() or t.device != kc.device or t.dim() != 4:
+            raise ValueError("quantised pools must be contiguous 4-D tensors on one device")
+    if kc.dtype != torch.int32 or vc.dtype != torch.int32 or kc.shape != vc.shape:
+        raise ValueError("codes must be int32 [N, H, bs, words] (same for K and V)")
+    for t in (ks, kb, vs, vb):
+        if t.dtype != torch.float16 or t.shape != ks.shape:
+            raise ValueError("scales/biases must be fp16 [N, H, bs, D/64]")
+    n, h, bs, words = kc.shape
+    D = ks.shape[3] * 64
+    bits = words * 32 // D
+    if bits not in (4, 8) or ks.shape[:3] != kc.shape[:3]:
+        raise ValueError("codes/scales shapes do not describe 4- or 8-bit groups of 64")
+    return n, h, bs, D, bits
+
+
+def _qptrs(pools):
+    return [t.data_ptr() for t in pools]
+
+
+def kv_quant_append(pools, keys: torch.Tensor, values: torch.Tensor,
+                    slot_mapping: torch.Tensor) -> None:
+    """Quantise keys/values ``(1, H, n, D)`` (or ``(H, n, D)``) into pool slots."""
+    n_blocks, H, bs, D, bits = _check_qpools(pools)
+    kk, vv = (keys[0], values[0]) if keys.dim() == 4 else (keys, values)
+    if kk.shape != vv.shape or kk.dim() != 3 or kk.shape[0] != H or kk.shape[2] != D:
+        raise ValueError(f"keys must be (1, {H}, n, {D})")
+    if kk.stride(2) != 1 or vv.stride(2) != 1 or kk.stride() != vv.stride():
+        kk, vv = kk.contiguous(), vv.contiguous()
+    n = kk.shape[1]
+    if slot_mapping.dtype != torch.int64 or slot_mapping.numel() != n:
+        raise ValueError("slot_mapping must be int64 [n]")
+    if n == 0:
+        return
+    dev = _dev_index(pools[0])
+    nat.call("mz_kv_quant_append", *_qptrs(pools), kk.data_ptr(), vv.data_ptr(), kk.stride(1),
+             kk.stride(0), slot_mapping.data_ptr(), n, H, D, bs, n_blocks, bits, 64,
+             dtype_code(kk.dtype), error_word(dev).data_ptr(), _stream(dev))
+    _after(dev)
+
+
+def kv_quant_append_paged(pools, keys: torch.Tensor, values: torch.Tensor,
+                          block_tables: torch.Tensor, positions: torch.Tensor) -> None:
+    """Decode-step quantise-append: keys/values ``[B, H, D]``, one token per
+    sequence at ``positions[b]`` through ``block_tables[b]``."""
+    n_blocks, H, bs, D, bits = _check_qpools(pools)
+    kk, vv = keys, values
+    if kk.dim() == 4:
+        kk, vv = kk[:, :, 0, :], vv[:, :, 0, :]
+    if kk.dim() != 3 or kk.shape[1:] != (H, D) or kk.shape != vv.shape:
+        raise ValueError(f"keys must be [B, {H}, {D}]")
+    if kk.stride(2) != 1 or vv.stride(2) != 1 or kk.stride() != vv.stride():
+        kk, vv = kk.contiguous(), vv.contiguous()
+    _as_i32(block_tables, pools[0].device, "block_tables")
+    _as_i32(positions, pools[0].device, "positions")
+    B = kk.shape[0]
+    if B == 0:
+        return
+    dev = _dev_index(pools[0])
+    nat.call("mz_kv_quant_append_paged", *_qptrs(pools), kk.data_ptr(), vv.data_ptr(),
+             kk.stride(0), kk.stride(1), block_tables.data_ptr(), block_tables.shape[1],
+             positions.data_ptr(), B, H, D, bs, n_blocks, bits, 64, dtype_code(kk.dtype),
+             error_word(dev).data_ptr(), _stream(dev))
+    _after(dev)
+
+
+_qworkspaces: dict[int, torch.Tensor] = {}
+
+
+def decode_q_workspace(n_seqs: int, n_kv_heads: int, rows: int, head_dim: int, bits: int,
+                       device: int, num_warps: int = 0) -> torch.Tensor:
+    size = ctypes.c_size_t(0)
+    nat.call("mz_paged_decode_q_workspace_size", n_seqs, n_kv_heads, rows, head_dim, bits,
+             num_warps, device, ctypes.byref(size))
+    need = int(size.value)
+    ws = _qworkspaces.get(device)
+    if ws is None or ws.numel() < need:
+        ws = torch.zeros(max(need, 1 << 20), dtype=torch.uint8, device=f"cuda:{device}")
+        _qworkspaces[device] = ws
+    return ws
+
+
+def paged_decode_q(q: torch.Tensor, pools, block_tables: torch.Tensor, ctx_lens: torch.Tensor,
+                   scale: float | None = None, out: torch.Tensor | None = None,
+                   out_dtype: torch.dtype | None = None, num_warps: int = 0,
+                   workspace: torch.Tensor | None = None) -> torch.Tensor:
+    """Decode attention over quantised K/V (dequantisation fused in).
+    q: ``[B, Hq, D]`` or ``[B, n_q, Hq, D]`` (bf16/fp16)."""
+    n_blocks, Hkv, bs, D, bits = _check_qpools(pools)
+    if q.dtype not in (torch.float16, torch.bfloat16):
+        raise ValueError("q must be fp16 or bf16")
+    if q.dim() == 3:
+        B, Hq, Dq = q.shape
+        nq, q_sb, q_st, q_sh = 1, q.stride(0), 0, q.stride(1)
+    elif q.dim() == 4:
+        B, nq, Hq, Dq = q.shape
+        q_sb, q_st, q_sh = q.stride(0), q.stride(1), q.stride(2)
+    else:
+        raise ValueError("q must be [B, Hq, D] or [B, n_q, Hq, D]")
+    if Dq != D or q.stride(-1) != 1 or Hq % Hkv:
+        raise ValueError("q shape does not match the pools")
+    _as_i32(block_tables, q.device, "block_tables")
+    _as_i32(ctx_lens, q.device, "ctx_lens")
+    out_dtype = out_dtype or q.dtype
+    if out is None:
+        out = torch.empty(q.shape, dtype=out_dtype, device=q.device)
+    if q.dim() == 3:
+        o_sb, o_st, o_sh = out.stride(0), 0, out.stride(1)
+    else:
+        o_sb, o_st, o_sh = out.stride(0), out.stride(1), out.stride(2)
+    if scale is None:
+        scale = D ** -0.5
+    if B == 0:
+        return out
+    dev = _dev_index(q)
+    rows = nq * (Hq // Hkv)
+    if workspace is None:
+        workspace = decode_q_workspace(B, Hkv, rows, D, bits, dev, num_warps)
+    nat.call("mz_paged_decode_q", out.data_ptr(), dtype_code(out_dtype), o_sb, o_st, o_sh,
+             q.data_ptr(), q_sb, q_st, q_sh, nq, *_qptrs(pools), block_tables.data_ptr(),
+             block_tables.shape[1], ctx_lens.data_ptr(), B, Hq, Hkv, D, bs, n_blocks, bits, 64,
+             float(scale), dtype_code(q.dtype), num_warps, workspace.data_ptr(),
+             workspace.numel(), error_word(dev).data_ptr(), _stream(dev))
     _after(dev)
     return out
 
