@@ -53,9 +53,11 @@ def parse_args():
     ap.add_argument("--separate-append", action="store_true",
                     help="append with mz_kv_append_paged, then mz_paged_decode (two launches)")
     ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--config", default="decode", choices=["decode", "prefix"],
+    ap.add_argument("--config", default="decode", choices=["decode", "prefix", "quant"],
                     help="decode: the paged decode step (headline); prefix: prefix-cache "
-                         "restore / copy-on-write / host-tier eviction and reload")
+                         "restore / copy-on-write / host-tier eviction and reload; quant: "
+                         "4/8-bit quantised KV decode step")
+    ap.add_argument("--bits", type=int, default=8, choices=[4, 8])
     return ap.parse_args()
 
 
@@ -579,6 +581,112 @@ def run_prefix(args, local_rank: int) -> None:
     print(json.dumps(line), flush=True)
 
 
+def run_quant(args, local_rank: int) -> None:
+    """Quantised KV decode step, Llama-3.1-8B shape: 32 layers, 32 q heads, 8 KV
+    heads, head_dim 128, batch 32, ctx ~ U[4096, 16384], affine group-64
+    codes at `--bits`, fp16 scales and biases.  Pools are filled by quantising
+    seeded N(0,1) bf16 K/V with mz_kv_quant_append.  One step = per layer, the
+    quantise-on-append of one new token per sequence then attention with the
+    dequantisation fused in."""
+    import numpy as np
+    import torch
+
+    from mlxz_b200 import ops
+    from mlxz_b200.engine import QuantizedPagedDecodeStep, QuantizedPagedKVStore
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    nl, B, bits = args.layers, 32, args.bits
+    ctx = np.random.default_rng(args.seed).integers(4096, 16385, size=B).astype(np.int64)
+    need = (ctx + 1 + BS - 1) // BS
+    n_blocks = int(math.ceil(need.sum() * 1.1))
+    perm = np.random.default_rng(args.seed + 1).permutation(n_blocks)
+    store = QuantizedPagedKVStore(nl, n_blocks, HKV, D, BS, bits=bits, device=dev, init="empty")
+    ids, used = [], 0
+    for b in range(B):
+        store.add_sequence(f"s{b}", int(ctx[b]), blocks=[int(x) for x in perm[used:used + need[b]]])
+        used += int(need[b])
+        ids.append(f"s{b}")
+    # fill every block slot with quantised N(0,1) data, 8192 slots at a time
+    torch.manual_seed(args.seed)
+    all_slots = torch.arange(n_blocks * BS, dtype=torch.int64, device=dev)
+    for l in range(nl):
+        for lo in range(0, n_blocks * BS, 8192):
+            sl = all_slots[lo:lo + 8192]
+            k = torch.randn(1, HKV, sl.numel(), D, device=dev).to(torch.bfloat16)
+            v = torch.randn(1, HKV, sl.numel(), D, device=dev).to(torch.bfloat16)
+            ops.kv_quant_append(store.qpools(l), k, v, sl)
+    step = QuantizedPagedDecodeStep(store, ids, HQ)
+    q = torch.randn(nl, B, HQ, D, device=dev).to(torch.bfloat16)
+    kn = torch.randn(nl, B, HKV, D, device=dev).to(torch.bfloat16)
+    vn = torch.randn(nl, B, HKV, D, device=dev).to(torch.bfloat16)
+    out = torch.empty_like(q)
+    per_tok_layer = 2 * HKV * (D * bits // 8 + 2 * 2 * (D // 64))  # codes + scales + biases
+    kv_layer = float((ctx + 1).sum()) * per_tok_layer
+    alg = kv_layer + 2.0 * B * HQ * D * 2 + float(need.sum()) * 4
+    torch.cuda.synchronize()
+
+    def one_step(ev=None):
+        for l in range(nl):
+            pools = store.qpools(l)
+            ops.kv_quant_append_paged(pools, kn[l], vn[l], step.tables, step.positions)
+            if ev is not None:
+                ev[l][0].record()
+            ops.paged_decode_q(q[l], pools, step.tables, step.lengths, scale=step.scale,
+                               out=out[l], workspace=step.workspace, num_warps=args.num_warps)
+            if ev is not None:
+                ev[l][1].record()
+
+    for _ in range(max(3, args.warmup)):
+        one_step()
+    torch.cuda.synchronize()
+    ops.check_device_errors(local_rank)
+    steps = args.steps
+    evs = [[[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(nl)]
+           for _ in range(steps)]
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    uuid = None
+    try:
+        uuid = "GPU-" + str(torch.cuda.get_device_properties(dev).uuid)
+    except Exception:
+        pass
+    clocks = ClockSampler(uuid, enabled=not args.no_clocks)
+    t0.record()
+    for k in range(steps):
+        one_step(evs[k])
+    t1.record()
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    ops.check_device_errors(local_rank)
+    ms = t0.elapsed_time(t1) / steps
+    dec = [evs[k][l][0].elapsed_time(evs[k][l][1]) for k in range(steps) for l in range(nl)]
+    dec_ms = sum(dec) / len(dec)
+    peak, peak_kind = peaks()
+    value = kv_layer * nl / (ms / 1e3) / 1e9
+    line = {
+        "metric": f"quantised ({bits}-bit) paged-decode KV-read GB/s and decode tok/s, 8B shape, batch 32",
+        "value": round(value, 2), "unit": "GB/s", "n_gpus": 1, "steps": steps,
+        "warmup": max(3, args.warmup), "ms_per_step": round(ms, 4), "higher_is_better": True,
+        "dtype": f"u{bits} codes + fp16 scale/bias, bf16 q",
+        "data": "synthetic (seeded N(0,1) bf16 K/V quantised on the GPU, random block tables)",
+        "config": {"workload": (f"quantised decode step: {nl} layers, 32 q heads, 8 kv heads, "
+                                f"head_dim 128, block 16, group 64, {bits}-bit; 32 seqs, "
+                                f"ctx U[4096,16384]"), "layers": nl, "global_batch": B,
+                   "mean_ctx": round(float(ctx.mean()), 1), "pool_blocks": n_blocks,
+                   "kv_bytes_per_token_layer": per_tok_layer,
+                   "bf16_equivalent_step_bytes": float((ctx + 1).sum()) * 2 * HKV * D * 2 * nl},
+        "decode_tok_s": round(B / (ms / 1e3), 1),
+        "roofline": {"bound": "hbm", "achieved": round(alg / (dec_ms / 1e3) / 1e9, 1),
+                     "peak": peak, "unit": "GB/s",
+                     "frac": round(alg / (dec_ms / 1e3) / 1e9 / peak, 4),
+                     "kernel": f"paged_decode_q_kernel<128,{bits}>", "peak_kind": peak_kind,
+                     "decode_ms_mean": round(dec_ms, 4), "alg_bytes_per_launch": alg},
+        "gpu_launches": steps * nl * 2,
+        "clocks": clk,
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse_args()
     rank = int(os.environ.get("RANK", "0"))
@@ -592,6 +700,9 @@ def main():
     elif args.config == "prefix":
         if rank == 0:
             run_prefix(args, local_rank)
+    elif args.config == "quant":
+        if rank == 0:
+            run_quant(args, local_rank)
     else:
         run_gpu(args, rank, world, local_rank)
 

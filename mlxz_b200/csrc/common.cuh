@@ -156,6 +156,14 @@ __device__ __forceinline__ void mma_16816(float (&d)[4], const uint32_t (&a)[4],
   }
 }
 
+// Transpose an 8x8 matrix of 16-bit elements held one row-pair per lane in
+// mma C-fragment order (lane l holds row l/4, columns 2(l%4), 2(l%4)+1).
+__device__ __forceinline__ uint32_t movmatrix_trans(uint32_t x) {
+  uint32_t y;
+  asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(y) : "r"(x));
+  return y;
+}
+
 // 2^x with the hardware approximation (ex2.approx, flush-to-zero); 2^-inf = 0.
 __device__ __forceinline__ float fast_exp2(float x) {
   float y;

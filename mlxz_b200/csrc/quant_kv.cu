@@ -157,7 +157,7 @@ int quant_append(const QAppendParams &qp, int D, int bits, cudaStream_t s) {
 // Dequant-fused paged decode.
 // ---------------------------------------------------------------------------
 
-template <int D, int BITS>
+template <int D, int BITS, int NR>
 struct QCfg {
   static constexpr int RB = D * BITS / 8;   // code bytes per token row
   static constexpr int NG = D / 64;         // groups per row
@@ -165,7 +165,8 @@ struct QCfg {
   static constexpr int TS = kTileTok * NG * 2;  // scale (or bias) bytes per tile
   static constexpr int kTx = 2 * TD + 4 * TS;
   static constexpr int kStageBytes = (kTx + 127) / 128 * 128;
-  static constexpr int kStagesFit = (96 * 1024) / (kWarps * kStageBytes);
+  static constexpr int kCtas = NR == 1 ? 3 : 2;  // CTAs per SM the shared memory is sized for
+  static constexpr int kStagesFit = (210 * 1024 / kCtas) / (kWarps * kStageBytes);
   static constexpr int kStages = kStagesFit > 8 ? 8 : (kStagesFit < 3 ? 3 : kStagesFit);
   static constexpr int kSmemTiles = kWarps * kStages * kStageBytes;
   static constexpr int kSmemBars = kWarps * kStages * 8;
@@ -176,18 +177,16 @@ struct QCfg {
   static constexpr float kPScale = BITS == 8 ? 256.f : 16.f;
 };
 
+constexpr uint32_t kMagic = 0x64646464u;  // fp16 0x64xx = 1024 + xx
+
 __device__ __forceinline__ uint32_t h2_sub1024(uint32_t x) {
   __half2 h = *reinterpret_cast<__half2 *>(&x);
   h = __hsub2(h, __floats2half2_rn(1024.f, 1024.f));
   return *reinterpret_cast<uint32_t *>(&h);
 }
-// two bytes at positions 0 and 2 of x (after masking) -> half2 of their values
-__device__ __forceinline__ uint32_t u8pair_to_h2(uint32_t x) {
-  return h2_sub1024((x & 0x00FF00FFu) | 0x64006400u);
-}
-// two nibbles at bit 0 and bit 16 of x -> half2 of their values
-__device__ __forceinline__ uint32_t u4pair_to_h2(uint32_t x) {
-  return h2_sub1024((x & 0x000F000Fu) | 0x64006400u);
+// two nibbles at bit 0 and bit 16 of x -> half2 of (1024 + nibble)
+__device__ __forceinline__ uint32_t nib2_biased(uint32_t x) {
+  return (x & 0x000F000Fu) | 0x64006400u;
 }
 
 __device__ __forceinline__ float load_q16(const uint16_t *q, int64_t off, bool bf16) {
@@ -195,13 +194,19 @@ __device__ __forceinline__ float load_q16(const uint16_t *q, int64_t off, bool b
   return bf16 ? __uint_as_float(static_cast<uint32_t>(b) << 16) : __half2float(__ushort_as_half(b));
 }
 
-template <int D, int BITS>
-__global__ void __launch_bounds__(kWarps * 32, 2) paged_decode_q_kernel(const Params p) {
-  using C = QCfg<D, BITS>;
+// Transposed formulation: tokens (QK) and head dims (PV) are the M = 16 side
+// of mma.m16n8k16, the query rows of a KV head the N = 8 side (NR tiles of 8).
+//   QK:  S^T[tok][row] = sum_k A[tok][k] * B[k][row], A = K codes over a
+//        permutation pi of the head dim, B = Q with the same permutation;
+//   PV:  O^T[d][row] = sum_t A[d][t] * B[t][row], A = V codes (+1024, the
+//        fp16 magic bias, removed through sum_t P'), B = P'^T by movmatrix.
+template <int D, int BITS, int NR>
+__global__ void __launch_bounds__(kWarps * 32, QCfg<D, BITS, NR>::kCtas)
+    paged_decode_q_kernel(const Params p) {
+  using C = QCfg<D, BITS, NR>;
   constexpr int S = C::kStages;
   constexpr int NG = C::NG;
-  constexpr int KS = D / 16;   // k-steps of Q.K (4 per group)
-  constexpr int NT = D / 8;    // n-tiles of P.V (8 per group)
+  constexpr int MT = D / 16;  // m-tiles of P.V (4 per group)
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 127) &
@@ -249,13 +254,13 @@ __global__ void __launch_bounds__(kWarps * 32, 2) paged_decode_q_kernel(const Pa
   };
 
   const int g = lane >> 2, cq = lane & 3;
-  const bool two_groups = p.rows > 8;
 
-  uint32_t qa[KS][4];     // Q (fp16) A fragments over the permuted head dim
-  float qsum[2][NG];      // sum of Q over each group, rows g and g+8
-  float oacc[NT][4];      // 256/16-scaled P'.q_v accumulators
-  float rb[2][NG];        // sum_t p * b_v per row and group (lane partial)
-  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+  uint32_t qb[NR][NG][4][2];  // Q B-fragments: row 8*nr + g, k-step w of group G
+  float qs[NR][2][NG];        // sum of Q over group G, rows 8*nr + 2c + {0,1}
+  float oacc[NR][MT][4];      // O^T (biased by 1024 * sum P'), P-scaled
+  float rb[NR][2][NG];        // sum_t p * b_v (lane partial over its tokens g, g+8)
+  float cp[NR][2][NG];        // sum_t P' (lane partial) -- removes the +1024 bias
+  float mrow[NR][2], lrow[NR][2];
 
   UnitReader ur;
   bool seg_first = true;
@@ -271,51 +276,50 @@ __global__ void __launch_bounds__(kWarps * 32, 2) paged_decode_q_kernel(const Pa
 
     if (seg_first || cc.t == 0) {
       seg_first = false;
-      m0 = m1 = -INFINITY;
-      l0 = l1 = 0.f;
-#pragma unroll
-      for (int n = 0; n < NT; ++n) oacc[n][0] = oacc[n][1] = oacc[n][2] = oacc[n][3] = 0.f;
-#pragma unroll
-      for (int gg = 0; gg < NG; ++gg) rb[0][gg] = rb[1][gg] = qsum[0][gg] = qsum[1][gg] = 0.f;
       const auto *q16 = static_cast<const uint16_t *>(p.q);
-      const bool qb = p.q_bf16;
+      const bool qbf = p.q_bf16;
 #pragma unroll
-      for (int rs = 0; rs < 2; ++rs) {
-        const int row = g + 8 * rs;
+      for (int nr = 0; nr < NR; ++nr) {
+        const int row = 8 * nr + g;
         const bool live = row < p.rows;
         const int64_t qo = live ? row_offset(p.q_sb, p.q_st, p.q_sh, cc.b, cc.h, row, p.G) : 0;
+        float part[NG];
 #pragma unroll
-        for (int j = 0; j < KS; ++j) {
-          const int G = j / 4, w = j % 4;
-          int e0, e1, e2, e3;  // head-dim indices of k-slots 2c, 2c+1, 2c+8, 2c+9
-          if constexpr (BITS == 8) {
-            const int d0 = 64 * G + 16 * cq + 4 * w;
-            e0 = d0; e1 = d0 + 1; e2 = d0 + 2; e3 = d0 + 3;
-          } else {
-            const int base = 64 * G + 16 * cq + 8 * (w >> 1), j0 = 2 * (w & 1);
-            e0 = base + j0; e1 = base + j0 + 4; e2 = base + j0 + 1; e3 = base + j0 + 5;
+        for (int G = 0; G < NG; ++G) {
+          part[G] = 0.f;
+#pragma unroll
+          for (int w = 0; w < 4; ++w) {
+            int e0, e1, e2, e3;  // head dims of k-slots 2c, 2c+1, 2c+8, 2c+9
+            if constexpr (BITS == 8) {
+              const int d0 = 64 * G + 16 * cq + 4 * w;
+              e0 = d0; e1 = d0 + 1; e2 = d0 + 2; e3 = d0 + 3;
+            } else {
+              const int base = 64 * G + 16 * cq + 8 * (w >> 1), j0 = 2 * (w & 1);
+              e0 = base + j0; e1 = base + j0 + 4; e2 = base + j0 + 1; e3 = base + j0 + 5;
+            }
+            float f0 = 0.f, f1 = 0.f, f2 = 0.f, f3 = 0.f;
+            if (live) {
+              f0 = __half2float(__float2half_rn(load_q16(q16, qo + e0, qbf)));
+              f1 = __half2float(__float2half_rn(load_q16(q16, qo + e1, qbf)));
+              f2 = __half2float(__float2half_rn(load_q16(q16, qo + e2, qbf)));
+              f3 = __half2float(__float2half_rn(load_q16(q16, qo + e3, qbf)));
+            }
+            qb[nr][G][w][0] = pack2<false>(f0, f1);
+            qb[nr][G][w][1] = pack2<false>(f2, f3);
+            part[G] += (f0 + f1) + (f2 + f3);
           }
-          float f0 = 0.f, f1 = 0.f, f2 = 0.f, f3 = 0.f;
-          if (live) {
-            f0 = __half2float(__float2half_rn(load_q16(q16, qo + e0, qb)));
-            f1 = __half2float(__float2half_rn(load_q16(q16, qo + e1, qb)));
-            f2 = __half2float(__float2half_rn(load_q16(q16, qo + e2, qb)));
-            f3 = __half2float(__float2half_rn(load_q16(q16, qo + e3, qb)));
-          }
-          qa[j][rs] = pack2<false>(f0, f1);
-          qa[j][2 + rs] = pack2<false>(f2, f3);
-          qsum[rs][G] += (f0 + f1) + (f2 + f3);
+          part[G] += __shfl_xor_sync(0xffffffffu, part[G], 1);
+          part[G] += __shfl_xor_sync(0xffffffffu, part[G], 2);
+          // lanes 4r hold row 8*nr + r; this lane needs rows 2c and 2c+1
+          qs[nr][0][G] = __shfl_sync(0xffffffffu, part[G], 8 * cq);
+          qs[nr][1][G] = __shfl_sync(0xffffffffu, part[G], 8 * cq + 4);
+          rb[nr][0][G] = rb[nr][1][G] = cp[nr][0][G] = cp[nr][1][G] = 0.f;
         }
+#pragma unroll
+        for (int m = 0; m < MT; ++m) oacc[nr][m][0] = oacc[nr][m][1] = oacc[nr][m][2] = oacc[nr][m][3] = 0.f;
+        mrow[nr][0] = mrow[nr][1] = -INFINITY;
+        lrow[nr][0] = lrow[nr][1] = 0.f;
       }
-#pragma unroll
-      for (int rs = 0; rs < 2; ++rs)
-#pragma unroll
-        for (int gg = 0; gg < NG; ++gg) {
-          float v = qsum[rs][gg];
-          v += __shfl_xor_sync(0xffffffffu, v, 1);
-          v += __shfl_xor_sync(0xffffffffu, v, 2);
-          qsum[rs][gg] = v;
-        }
     }
 
     if (!wait_stage<S>(p, bar0, i, sch.issued, lane)) return;
@@ -329,210 +333,231 @@ __global__ void __launch_bounds__(kWarps * 32, 2) paged_decode_q_kernel(const Pa
     const int nvalid = min(kTileTok, cc.ctx - cc.t * kTileTok);
     const bool last_tile = (cc.t == cc.n - 1);
 
-    // ---- S = Q . K^T with K = s_k * q_k + b_k ----
-    float sacc[2][4];
-#pragma unroll
-    for (int nt = 0; nt < 2; ++nt) {
-      float acc[NG][4];
-#pragma unroll
-      for (int gg = 0; gg < NG; ++gg) acc[gg][0] = acc[gg][1] = acc[gg][2] = acc[gg][3] = 0.f;
-      const int tk = nt * 8 + g;
-#pragma unroll
-      for (int G = 0; G < NG; ++G) {
-        if constexpr (BITS == 8) {
-          const uint4 kw = *reinterpret_cast<const uint4 *>(kd + tk * C::RB + 64 * G + 16 * cq);
-          const uint32_t wv[4] = {kw.x, kw.y, kw.z, kw.w};
-#pragma unroll
-          for (int w = 0; w < 4; ++w) {
-            const uint32_t b0 = u8pair_to_h2(__byte_perm(wv[w], 0, 0x4140));
-            const uint32_t b1 = u8pair_to_h2(__byte_perm(wv[w], 0, 0x4342));
-            mma_16816<false>(acc[G], qa[4 * G + w], b0, b1);
-          }
-        } else {
-          const uint2 kw = *reinterpret_cast<const uint2 *>(kd + tk * C::RB + 32 * G + 8 * cq);
-#pragma unroll
-          for (int w = 0; w < 4; ++w) {
-            const uint32_t wx = (w >> 1) ? kw.y : kw.x;
-            const int j0 = 2 * (w & 1);
-            const uint32_t b0 = u4pair_to_h2(wx >> (4 * j0));
-            const uint32_t b1 = u4pair_to_h2(wx >> (4 * (j0 + 1)));
-            mma_16816<false>(acc[G], qa[4 * G + w], b0, b1);
-          }
-        }
-      }
-      // tokens nt*8 + 2c and +1 (C-fragment columns)
-      const int t0 = nt * 8 + 2 * cq;
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int tok = t0 + (e & 1), rs = e >> 1;
-        float x = 0.f;
-#pragma unroll
-        for (int G = 0; G < NG; ++G)
-          x += __half2float(ksc[tok * NG + G]) * acc[G][e] +
-               __half2float(kbi[tok * NG + G]) * qsum[rs][G];
-        x *= p.scale_log2;
-        if (tok >= nvalid) x = -INFINITY;
-        sacc[nt][e] = x;
-      }
-    }
-
-    // ---- online softmax (rows g: regs 0,1; g+8: regs 2,3) ----
-    float mx0 = fmaxf(fmaxf(sacc[0][0], sacc[0][1]), fmaxf(sacc[1][0], sacc[1][1]));
-    float mx1 = fmaxf(fmaxf(sacc[0][2], sacc[0][3]), fmaxf(sacc[1][2], sacc[1][3]));
-    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
-    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
-    const float mn0 = fmaxf(m0, mx0);
-    const float a0 = fast_exp2(m0 - mn0);
-    m0 = mn0;
-    float a1 = 1.f;
-    if (two_groups) {
-      mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
-      mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
-      const float mn1 = fmaxf(m1, mx1);
-      a1 = fast_exp2(m1 - mn1);
-      m1 = mn1;
-    }
-    float rs0 = 0.f, rs1 = 0.f;
-#pragma unroll
-    for (int nt = 0; nt < 2; ++nt) {
-      sacc[nt][0] = fast_exp2(sacc[nt][0] - m0);
-      sacc[nt][1] = fast_exp2(sacc[nt][1] - m0);
-      rs0 += sacc[nt][0] + sacc[nt][1];
-      if (two_groups) {
-        sacc[nt][2] = fast_exp2(sacc[nt][2] - m1);
-        sacc[nt][3] = fast_exp2(sacc[nt][3] - m1);
-        rs1 += sacc[nt][2] + sacc[nt][3];
-      } else {
-        sacc[nt][2] = sacc[nt][3] = 0.f;
-      }
-    }
-    l0 = l0 * a0 + rs0;
-    l1 = l1 * a1 + rs1;
-    if (__any_sync(0xffffffffu, a0 != 1.f || a1 != 1.f)) {
-#pragma unroll
-      for (int n = 0; n < NT; ++n) {
-        oacc[n][0] *= a0;
-        oacc[n][1] *= a0;
-        oacc[n][2] *= a1;
-        oacc[n][3] *= a1;
-      }
-#pragma unroll
-      for (int gg = 0; gg < NG; ++gg) {
-        rb[0][gg] *= a0;
-        rb[1][gg] *= a1;
-      }
-    }
-
-    // ---- O += (p * s_v) . q_v ;  rb += p * b_v ----
-    // this lane's tokens in the P fragments: 2c, 2c+1 (regs 0,1) and 8+2c, 9+2c (regs 2,3)
-    const int ta = 2 * cq, tb = 8 + 2 * cq;
-    float sv[4][NG], bv[4][NG];
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      const int tok = (k < 2 ? ta : tb) + (k & 1);
-      const bool ok = tok < nvalid;
-#pragma unroll
-      for (int G = 0; G < NG; ++G) {
-        sv[k][G] = ok ? __half2float(vsc[tok * NG + G]) * C::kPScale : 0.f;
-        bv[k][G] = ok ? __half2float(vbi[tok * NG + G]) : 0.f;
-      }
-    }
-    // P values by (row set, token slot k)
-    const float pv[2][4] = {{sacc[0][0], sacc[0][1], sacc[1][0], sacc[1][1]},
-                            {sacc[0][2], sacc[0][3], sacc[1][2], sacc[1][3]}};
+    // ---- S^T = K . Q^T per group (tokens g, g+8; rows 2c, 2c+1) ----
+    float acc[NR][NG][4];
 #pragma unroll
     for (int G = 0; G < NG; ++G) {
-      uint32_t pa[4];
-      pa[0] = pack2<false>(pv[0][0] * sv[0][G], pv[0][1] * sv[1][G]);
-      pa[1] = pack2<false>(pv[1][0] * sv[0][G], pv[1][1] * sv[1][G]);
-      pa[2] = pack2<false>(pv[0][2] * sv[2][G], pv[0][3] * sv[3][G]);
-      pa[3] = pack2<false>(pv[1][2] * sv[2][G], pv[1][3] * sv[3][G]);
 #pragma unroll
-      for (int rs = 0; rs < 2; ++rs)
-        rb[rs][G] += pv[rs][0] * bv[0][G] + pv[rs][1] * bv[1][G] + pv[rs][2] * bv[2][G] +
-                     pv[rs][3] * bv[3][G];
-      // V codes of tokens ta, ta+1, tb, tb+1 for head dims 64G + 8g + [0, 8)
+      for (int nr = 0; nr < NR; ++nr) acc[nr][G][0] = acc[nr][G][1] = acc[nr][G][2] = acc[nr][G][3] = 0.f;
       if constexpr (BITS == 8) {
-        const uint2 va0 = *reinterpret_cast<const uint2 *>(vd + (ta)*C::RB + 64 * G + 8 * g);
-        const uint2 va1 = *reinterpret_cast<const uint2 *>(vd + (ta + 1) * C::RB + 64 * G + 8 * g);
-        const uint2 vb0 = *reinterpret_cast<const uint2 *>(vd + (tb)*C::RB + 64 * G + 8 * g);
-        const uint2 vb1 = *reinterpret_cast<const uint2 *>(vd + (tb + 1) * C::RB + 64 * G + 8 * g);
+        const uint4 k0 = *reinterpret_cast<const uint4 *>(kd + g * C::RB + 64 * G + 16 * cq);
+        const uint4 k1 = *reinterpret_cast<const uint4 *>(kd + (g + 8) * C::RB + 64 * G + 16 * cq);
+        const uint32_t w0[4] = {k0.x, k0.y, k0.z, k0.w}, w1[4] = {k1.x, k1.y, k1.z, k1.w};
 #pragma unroll
-        for (int m = 0; m < 8; ++m) {
-          const uint32_t sel = static_cast<uint32_t>((m & 3) | ((4 + (m & 3)) << 8));
-          const uint32_t wa0 = m < 4 ? va0.x : va0.y, wa1 = m < 4 ? va1.x : va1.y;
-          const uint32_t wb0 = m < 4 ? vb0.x : vb0.y, wb1 = m < 4 ? vb1.x : vb1.y;
-          const uint32_t b0 = u8pair_to_h2(__byte_perm(wa0, wa1, sel));
-          const uint32_t b1 = u8pair_to_h2(__byte_perm(wb0, wb1, sel));
-          mma_16816<false>(oacc[8 * G + m], pa, b0, b1);
+        for (int w = 0; w < 4; ++w) {
+          uint32_t a[4];
+          a[0] = h2_sub1024(__byte_perm(w0[w], kMagic, 0x4140));
+          a[1] = h2_sub1024(__byte_perm(w1[w], kMagic, 0x4140));
+          a[2] = h2_sub1024(__byte_perm(w0[w], kMagic, 0x4342));
+          a[3] = h2_sub1024(__byte_perm(w1[w], kMagic, 0x4342));
+#pragma unroll
+          for (int nr = 0; nr < NR; ++nr) mma_16816<false>(acc[nr][G], a, qb[nr][G][w][0], qb[nr][G][w][1]);
         }
       } else {
-        const uint32_t va0 = *reinterpret_cast<const uint32_t *>(vd + (ta)*C::RB + 32 * G + 4 * g);
-        const uint32_t va1 = *reinterpret_cast<const uint32_t *>(vd + (ta + 1) * C::RB + 32 * G + 4 * g);
-        const uint32_t vb0 = *reinterpret_cast<const uint32_t *>(vd + (tb)*C::RB + 32 * G + 4 * g);
-        const uint32_t vb1 = *reinterpret_cast<const uint32_t *>(vd + (tb + 1) * C::RB + 32 * G + 4 * g);
+        const uint2 k0 = *reinterpret_cast<const uint2 *>(kd + g * C::RB + 32 * G + 8 * cq);
+        const uint2 k1 = *reinterpret_cast<const uint2 *>(kd + (g + 8) * C::RB + 32 * G + 8 * cq);
 #pragma unroll
-        for (int m = 0; m < 8; ++m) {
-          const uint32_t sel = static_cast<uint32_t>((m >> 1) | ((4 + (m >> 1)) << 8));
-          const int sh = 4 * (m & 1);
-          const uint32_t b0 = u4pair_to_h2(__byte_perm(va0, va1, sel) >> sh);
-          const uint32_t b1 = u4pair_to_h2(__byte_perm(vb0, vb1, sel) >> sh);
-          mma_16816<false>(oacc[8 * G + m], pa, b0, b1);
+        for (int w = 0; w < 4; ++w) {
+          const uint32_t x0 = (w >> 1) ? k0.y : k0.x, x1 = (w >> 1) ? k1.y : k1.x;
+          const int j0 = 2 * (w & 1);
+          uint32_t a[4];
+          a[0] = h2_sub1024(nib2_biased(x0 >> (4 * j0)));
+          a[1] = h2_sub1024(nib2_biased(x1 >> (4 * j0)));
+          a[2] = h2_sub1024(nib2_biased(x0 >> (4 * (j0 + 1))));
+          a[3] = h2_sub1024(nib2_biased(x1 >> (4 * (j0 + 1))));
+#pragma unroll
+          for (int nr = 0; nr < NR; ++nr) mma_16816<false>(acc[nr][G], a, qb[nr][G][w][0], qb[nr][G][w][1]);
+        }
+      }
+    }
+    // scores: reg 2*ts + rs <-> (token g + 8*ts, row 2c + rs)
+    float sc[NR][2][2];
+    {
+      float skv[2][NG], bkv[2][NG];
+#pragma unroll
+      for (int ts = 0; ts < 2; ++ts)
+#pragma unroll
+        for (int G = 0; G < NG; ++G) {
+          skv[ts][G] = __half2float(ksc[(g + 8 * ts) * NG + G]);
+          bkv[ts][G] = __half2float(kbi[(g + 8 * ts) * NG + G]);
+        }
+#pragma unroll
+      for (int nr = 0; nr < NR; ++nr)
+#pragma unroll
+        for (int ts = 0; ts < 2; ++ts)
+#pragma unroll
+          for (int rs = 0; rs < 2; ++rs) {
+            float x = 0.f;
+#pragma unroll
+            for (int G = 0; G < NG; ++G)
+              x += skv[ts][G] * acc[nr][G][2 * ts + rs] + bkv[ts][G] * qs[nr][rs][G];
+            x *= p.scale_log2;
+            if (g + 8 * ts >= nvalid) x = -INFINITY;
+            sc[nr][ts][rs] = x;
+          }
+    }
+
+    // ---- online softmax per query row (rows 2c, 2c+1 of each 8-row tile) ----
+    float alpha[NR][2];
+    bool moved = false;
+#pragma unroll
+    for (int nr = 0; nr < NR; ++nr)
+#pragma unroll
+      for (int rs = 0; rs < 2; ++rs) {
+        float mx = fmaxf(sc[nr][0][rs], sc[nr][1][rs]);
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+        const float mn = fmaxf(mrow[nr][rs], mx);
+        alpha[nr][rs] = fast_exp2(mrow[nr][rs] - mn);
+        moved |= alpha[nr][rs] != 1.f;
+        mrow[nr][rs] = mn;
+        sc[nr][0][rs] = fast_exp2(sc[nr][0][rs] - mn);
+        sc[nr][1][rs] = fast_exp2(sc[nr][1][rs] - mn);
+        lrow[nr][rs] = lrow[nr][rs] * alpha[nr][rs] + sc[nr][0][rs] + sc[nr][1][rs];
+      }
+    if (__any_sync(0xffffffffu, moved)) {
+#pragma unroll
+      for (int nr = 0; nr < NR; ++nr) {
+#pragma unroll
+        for (int m = 0; m < MT; ++m) {
+          oacc[nr][m][0] *= alpha[nr][0];
+          oacc[nr][m][1] *= alpha[nr][1];
+          oacc[nr][m][2] *= alpha[nr][0];
+          oacc[nr][m][3] *= alpha[nr][1];
+        }
+#pragma unroll
+        for (int G = 0; G < NG; ++G)
+#pragma unroll
+          for (int rs = 0; rs < 2; ++rs) {
+            rb[nr][rs][G] *= alpha[nr][rs];
+            cp[nr][rs][G] *= alpha[nr][rs];
+          }
+      }
+    }
+
+    // ---- O^T += (V codes + 1024) . (p * s_v)^T ; rb += p * b_v ; cp += P' ----
+#pragma unroll
+    for (int G = 0; G < NG; ++G) {
+      float sv[2], bv[2];
+#pragma unroll
+      for (int ts = 0; ts < 2; ++ts) {
+        const int tok = g + 8 * ts;
+        const bool ok = tok < nvalid;
+        sv[ts] = ok ? __half2float(vsc[tok * NG + G]) * C::kPScale : 0.f;
+        bv[ts] = ok ? __half2float(vbi[tok * NG + G]) : 0.f;
+      }
+      uint32_t pb[NR][2];
+#pragma unroll
+      for (int nr = 0; nr < NR; ++nr) {
+        const __half2 h0 = __floats2half2_rn(sc[nr][0][0] * sv[0], sc[nr][0][1] * sv[0]);
+        const __half2 h1 = __floats2half2_rn(sc[nr][1][0] * sv[1], sc[nr][1][1] * sv[1]);
+        const float2 r0 = __half22float2(h0), r1 = __half22float2(h1);
+        cp[nr][0][G] += r0.x + r1.x;
+        cp[nr][1][G] += r0.y + r1.y;
+#pragma unroll
+        for (int rs = 0; rs < 2; ++rs) rb[nr][rs][G] += sc[nr][0][rs] * bv[0] + sc[nr][1][rs] * bv[1];
+        pb[nr][0] = movmatrix_trans(*reinterpret_cast<const uint32_t *>(&h0));
+        pb[nr][1] = movmatrix_trans(*reinterpret_cast<const uint32_t *>(&h1));
+      }
+      // V codes of tokens 2c, 2c+1, 2c+8, 2c+9 for head dims 64G + 8g + [0, 8)
+      if constexpr (BITS == 8) {
+        const uint2 v0 = *reinterpret_cast<const uint2 *>(vd + (2 * cq) * C::RB + 64 * G + 8 * g);
+        const uint2 v1 = *reinterpret_cast<const uint2 *>(vd + (2 * cq + 1) * C::RB + 64 * G + 8 * g);
+        const uint2 v2 = *reinterpret_cast<const uint2 *>(vd + (2 * cq + 8) * C::RB + 64 * G + 8 * g);
+        const uint2 v3 = *reinterpret_cast<const uint2 *>(vd + (2 * cq + 9) * C::RB + 64 * G + 8 * g);
+        // byte interleaves: [ra.bk, rb.bk, ra.bk+1, rb.bk+1]
+        const uint32_t lo01a = __byte_perm(v0.x, v1.x, 0x5140), lo23a = __byte_perm(v0.x, v1.x, 0x7362);
+        const uint32_t hi01a = __byte_perm(v0.y, v1.y, 0x5140), hi23a = __byte_perm(v0.y, v1.y, 0x7362);
+        const uint32_t lo01b = __byte_perm(v2.x, v3.x, 0x5140), lo23b = __byte_perm(v2.x, v3.x, 0x7362);
+        const uint32_t hi01b = __byte_perm(v2.y, v3.y, 0x5140), hi23b = __byte_perm(v2.y, v3.y, 0x7362);
+#pragma unroll
+        for (int v = 0; v < 4; ++v) {
+          const uint32_t sel = (v & 1) ? 0x4342u : 0x4140u;
+          uint32_t a[4];
+          a[0] = __byte_perm((v < 2) ? lo01a : lo23a, kMagic, sel);  // d = 64G+8g+v, tokens 2c,2c+1
+          a[1] = __byte_perm((v < 2) ? hi01a : hi23a, kMagic, sel);  // d + 4
+          a[2] = __byte_perm((v < 2) ? lo01b : lo23b, kMagic, sel);  // tokens 2c+8, 2c+9
+          a[3] = __byte_perm((v < 2) ? hi01b : hi23b, kMagic, sel);
+#pragma unroll
+          for (int nr = 0; nr < NR; ++nr) mma_16816<false>(oacc[nr][4 * G + v], a, pb[nr][0], pb[nr][1]);
+        }
+      } else {
+        const uint32_t v0 = *reinterpret_cast<const uint32_t *>(vd + (2 * cq) * C::RB + 32 * G + 4 * g);
+        const uint32_t v1 = *reinterpret_cast<const uint32_t *>(vd + (2 * cq + 1) * C::RB + 32 * G + 4 * g);
+        const uint32_t v2 = *reinterpret_cast<const uint32_t *>(vd + (2 * cq + 8) * C::RB + 32 * G + 4 * g);
+        const uint32_t v3 = *reinterpret_cast<const uint32_t *>(vd + (2 * cq + 9) * C::RB + 32 * G + 4 * g);
+#pragma unroll
+        for (int v = 0; v < 4; ++v) {
+          // nibble v -> byte v/2 (low or high half); nibble 4 + v -> byte 2 + v/2
+          const uint32_t sl = static_cast<uint32_t>((v >> 1) | ((4 + (v >> 1)) << 8));
+          const uint32_t sh = static_cast<uint32_t>((2 + (v >> 1)) | ((6 + (v >> 1)) << 8));
+          const int sft = 4 * (v & 1);
+          uint32_t a[4];
+          a[0] = nib2_biased(__byte_perm(v0, v1, sl) >> sft);
+          a[1] = nib2_biased(__byte_perm(v0, v1, sh) >> sft);
+          a[2] = nib2_biased(__byte_perm(v2, v3, sl) >> sft);
+          a[3] = nib2_biased(__byte_perm(v2, v3, sh) >> sft);
+#pragma unroll
+          for (int nr = 0; nr < NR; ++nr) mma_16816<false>(oacc[nr][4 * G + v], a, pb[nr][0], pb[nr][1]);
         }
       }
     }
 
     // ---- piece end ----
     if (last_tile || ur.left == 1) {
-      float L0 = l0, L1 = l1;
-      L0 += __shfl_xor_sync(0xffffffffu, L0, 1);
-      L0 += __shfl_xor_sync(0xffffffffu, L0, 2);
-      L1 += __shfl_xor_sync(0xffffffffu, L1, 1);
-      L1 += __shfl_xor_sync(0xffffffffu, L1, 2);
-      float R[2][NG];
-#pragma unroll
-      for (int rs = 0; rs < 2; ++rs)
-#pragma unroll
-        for (int gg = 0; gg < NG; ++gg) {
-          float v = rb[rs][gg];
-          v += __shfl_xor_sync(0xffffffffu, v, 1);
-          v += __shfl_xor_sync(0xffffffffu, v, 2);
-          R[rs][gg] = v;
-        }
-      // value of C-fragment (n-tile 8G + m, reg e): row g + 8*(e >> 1),
-      // head dim 64G + 16c + 8*(e & 1) + m
-      constexpr float kInvP = 1.f / C::kPScale;
       const int bh = cc.b * p.Hkv + cc.h;
       const int pbh = cc.pos - cc.t;
       const int uf = sch.unit_of(pbh), ul = sch.unit_of(pbh + cc.n - 1);
       const bool full = uf == ul;
       const int64_t slot = (int64_t)ur.unit + bh;
+      constexpr float kInvP = 1.f / C::kPScale;
 #pragma unroll
-      for (int rs = 0; rs < 2; ++rs) {
-        const int row = g + 8 * rs;
-        if (row >= p.rows) continue;
-        const float inv = full ? 1.f / (rs ? L1 : L0) : 1.f;
-        const int64_t o = full ? row_offset(p.o_sb, p.o_st, p.o_sh, cc.b, cc.h, row, p.G) : 0;
-        float *pr = p.part + (slot * p.rows + row) * D;
+      for (int nr = 0; nr < NR; ++nr)
 #pragma unroll
-        for (int G = 0; G < NG; ++G)
+        for (int rs = 0; rs < 2; ++rs) {
+          float L = lrow[nr][rs];
+          L += __shfl_xor_sync(0xffffffffu, L, 4);
+          L += __shfl_xor_sync(0xffffffffu, L, 8);
+          L += __shfl_xor_sync(0xffffffffu, L, 16);
+          float Rg[NG], Cg[NG];
 #pragma unroll
-          for (int half = 0; half < 2; ++half)
+          for (int G = 0; G < NG; ++G) {
+            float r = rb[nr][rs][G], c = cp[nr][rs][G];
 #pragma unroll
-            for (int m = 0; m < 8; m += 2) {
-              const int e = 2 * rs + half;
-              const int d = 64 * G + 16 * cq + 8 * half + m;
-              const float x = (oacc[8 * G + m][e] * kInvP + R[rs][G]) * inv;
-              const float y = (oacc[8 * G + m + 1][e] * kInvP + R[rs][G]) * inv;
-              if (full)
-                store_pair(p, o + d, x, y);
-              else
-                *reinterpret_cast<float2 *>(pr + d) = make_float2(x, y);
+            for (int o = 4; o < 32; o <<= 1) {
+              r += __shfl_xor_sync(0xffffffffu, r, o);
+              c += __shfl_xor_sync(0xffffffffu, c, o);
             }
-        if (!full && cq == 0)
-          *reinterpret_cast<float2 *>(p.ml + (slot * p.rows + row) * 2) =
-              make_float2(rs ? m1 : m0, rs ? L1 : L0);
-      }
+            Rg[G] = r;
+            Cg[G] = c * 1024.f;
+          }
+          const int row = 8 * nr + 2 * cq + rs;
+          if (row >= p.rows) continue;
+          const float inv = full ? 1.f / L : 1.f;
+          const int64_t o = full ? row_offset(p.o_sb, p.o_st, p.o_sh, cc.b, cc.h, row, p.G) : 0;
+          float *pr = p.part + (slot * p.rows + row) * D;
+#pragma unroll
+          for (int G = 0; G < NG; ++G) {
+            float val[8];  // head dims 64G + 8g + j, j = 0..7
+#pragma unroll
+            for (int v = 0; v < 4; ++v) {
+              val[v] = ((oacc[nr][4 * G + v][rs] - Cg[G]) * kInvP + Rg[G]) * inv;
+              val[4 + v] = ((oacc[nr][4 * G + v][2 + rs] - Cg[G]) * kInvP + Rg[G]) * inv;
+            }
+            const int d0 = 64 * G + 8 * g;
+#pragma unroll
+            for (int j = 0; j < 8; j += 2) {
+              if (full)
+                store_pair(p, o + d0 + j, val[j], val[j + 1]);
+              else
+                *reinterpret_cast<float2 *>(pr + d0 + j) = make_float2(val[j], val[j + 1]);
+            }
+          }
+          if (!full && g == 0)
+            *reinterpret_cast<float2 *>(p.ml + (slot * p.rows + row) * 2) =
+                make_float2(mrow[nr][rs], L);
+        }
       if (!full) arrive_and_merge<D>(p, cc, bh, uf, ul - uf + 1, lane);
       seg_first = true;
     }
@@ -544,18 +569,30 @@ __global__ void __launch_bounds__(kWarps * 32, 2) paged_decode_q_kernel(const Pa
   }
 }
 
-template <int D, int BITS>
+template <int D, int BITS, int NR>
 int q_kernel_ctas_per_sm(int *out) {
   static int cached = -1;
   static std::once_flag once;
   static cudaError_t err = cudaSuccess;
-  return kernel_occupancy(paged_decode_q_kernel<D, BITS>, QCfg<D, BITS>::kSmemBytes, &cached,
-                          &once, &err, out);
+  return kernel_occupancy(paged_decode_q_kernel<D, BITS, NR>, QCfg<D, BITS, NR>::kSmemBytes,
+                          &cached, &once, &err, out);
 }
 
+template <int NR>
+int q_ctas_per_sm_nr(int D, int bits, int *out) {
+  if (D == 128)
+    return bits == 8 ? q_kernel_ctas_per_sm<128, 8, NR>(out) : q_kernel_ctas_per_sm<128, 4, NR>(out);
+  return bits == 8 ? q_kernel_ctas_per_sm<64, 8, NR>(out) : q_kernel_ctas_per_sm<64, 4, NR>(out);
+}
+
+// Occupancy used to size grids and workspaces: the larger of the two query-row
+// instantiations, so one workspace size fits both.
 int q_ctas_per_sm(int D, int bits, int *out) {
-  if (D == 128) return bits == 8 ? q_kernel_ctas_per_sm<128, 8>(out) : q_kernel_ctas_per_sm<128, 4>(out);
-  return bits == 8 ? q_kernel_ctas_per_sm<64, 8>(out) : q_kernel_ctas_per_sm<64, 4>(out);
+  int a = 0, b = 0;
+  if (int rc = q_ctas_per_sm_nr<1>(D, bits, &a)) return rc;
+  if (int rc = q_ctas_per_sm_nr<2>(D, bits, &b)) return rc;
+  *out = a > b ? a : b;
+  return MZ_OK;
 }
 
 int q_resolve_warps(int D, int bits, int num_warps, int device, int64_t *warps) {
@@ -767,16 +804,24 @@ extern "C" int mz_paged_decode_q(void *out, int32_t out_dtype, int64_t out_seq_s
   set_schedule(p, ws);
   p.err = dev_err;
 
-  int per_sm = 0;
+  int per_sm = 0;  // also sets the kernels' shared-memory attributes (once)
   if (int rc = q_ctas_per_sm(head_dim, bits, &per_sm)) return rc;
   const unsigned grid = static_cast<unsigned>(warps / kWarps);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-#define MZ_LQ(D_, B_)                                                                        \
-  paged_decode_q_kernel<D_, B_><<<grid, kWarps * 32, QCfg<D_, B_>::kSmemBytes, s>>>(p)
-  if (head_dim == 128) {
-    if (bits == 8) MZ_LQ(128, 8); else MZ_LQ(128, 4);
+#define MZ_LQ(D_, B_, NR_)                                                                    \
+  paged_decode_q_kernel<D_, B_, NR_><<<grid, kWarps * 32, QCfg<D_, B_, NR_>::kSmemBytes, s>>>(p)
+  if (rows <= 8) {
+    if (head_dim == 128) {
+      if (bits == 8) MZ_LQ(128, 8, 1); else MZ_LQ(128, 4, 1);
+    } else {
+      if (bits == 8) MZ_LQ(64, 8, 1); else MZ_LQ(64, 4, 1);
+    }
   } else {
-    if (bits == 8) MZ_LQ(64, 8); else MZ_LQ(64, 4);
+    if (head_dim == 128) {
+      if (bits == 8) MZ_LQ(128, 8, 2); else MZ_LQ(128, 4, 2);
+    } else {
+      if (bits == 8) MZ_LQ(64, 8, 2); else MZ_LQ(64, 4, 2);
+    }
   }
 #undef MZ_LQ
   MZ_CHECK_LAUNCH(fn);

@@ -57,10 +57,19 @@ class PagedKVStore:
         """Bytes of one block in one pool (one layer's K or V)."""
         return self.n_kv_heads * self.block_size * self.head_dim * self.pools.element_size()
 
+    @property
+    def bytes_per_token(self) -> int:
+        """Bytes of one token over all layers, K and V."""
+        return self.n_layers * 2 * self.n_kv_heads * self.head_dim * self.pools.element_size()
+
     def pool_stack(self) -> torch.Tensor:
         """All pools as one ``[2 * n_layers, n_blocks, ...]`` stack (block moves)."""
         return self.pools.view(2 * self.n_layers, self.n_blocks, self.n_kv_heads,
                                self.block_size, self.head_dim)
+
+    def pool_stacks(self) -> list[torch.Tensor]:
+        """Every tensor family a block lives in, as ``[P, n_blocks, ...]`` stacks."""
+        return [self.pool_stack()]
 
     def add_sequence(self, seq_id: str, n_tokens: int = 0, blocks: list[int] | None = None) -> None:
         """Register a sequence holding `n_tokens` tokens, allocating blocks from
@@ -100,7 +109,8 @@ class PagedKVStore:
             return
         src = torch.tensor([a for a, _ in pairs], dtype=torch.int32).to(self.device, non_blocking=True)
         dst = torch.tensor([b for _, b in pairs], dtype=torch.int32).to(self.device, non_blocking=True)
-        ops.block_copy(self.pool_stack(), src, dst)
+        for stack in self.pool_stacks():
+            ops.block_copy(stack, src, dst)
 
     def append_tokens(self, seq_id: str, keys: torch.Tensor, values: torch.Tensor) -> None:
         """Prefill-style append of n tokens to every layer: keys/values
@@ -119,8 +129,12 @@ class PagedKVStore:
         slots = torch.tensor([t[(off + i) // bs] * bs + (off + i) % bs for i in range(n)],
                              dtype=torch.int64).to(self.device, non_blocking=True)
         for l in range(self.n_layers):
-            ops.kv_append(self.k_pool(l), self.v_pool(l), keys[l], values[l], slots)
+            self._write_layer(l, keys[l], values[l], slots)
         self.offsets[seq_id] = off + n
+
+    def _write_layer(self, l: int, keys: torch.Tensor, values: torch.Tensor,
+                     slots: torch.Tensor) -> None:
+        ops.kv_append(self.k_pool(l), self.v_pool(l), keys, values, slots)
 
     def ensure_capacity(self, seq_id: str, extra: int) -> bool:
         """Grow the table for `extra` more tokens; True if it changed."""
@@ -242,3 +256,93 @@ class PagedDecodeStep:
         self.step(q, k, v, out=o, advance=advance)
         out_host.copy_(o, non_blocking=True)
         return out_host
+
+
+class QuantizedPagedKVStore(PagedKVStore):
+    """Paged KV store holding 4/8-bit group-64 quantised K/V: per layer and
+    per K/V, int32 codes ``[n_blocks, H, bs, D*bits/32]`` and fp16 scales and
+    biases ``[n_blocks, H, bs, D/64]`` (the layout of mz_kv_quant_append)."""
+
+    def __init__(self, n_layers: int, n_blocks: int, n_kv_heads: int, head_dim: int,
+                 block_size: int = 16, bits: int = 8, group_size: int = 64, device=None,
+                 init: str = "zeros") -> None:
+        if bits not in (4, 8) or group_size != 64 or head_dim % 64:
+            raise ValueError("quantised store: bits 4 or 8, group 64, head_dim a multiple of 64")
+        self.device = torch.device(device) if device is not None else torch.device(
+            "cuda", torch.cuda.current_device())
+        self.n_layers, self.n_blocks = n_layers, n_blocks
+        self.n_kv_heads, self.head_dim, self.block_size = n_kv_heads, head_dim, block_size
+        self.bits, self.group_size = bits, group_size
+        self.dtype = torch.float16
+        alloc = torch.zeros if init == "zeros" else torch.empty
+        base = (n_layers, 2, n_blocks, n_kv_heads, block_size)
+        self.codes = alloc(base + (head_dim * bits // 32,), dtype=torch.int32, device=self.device)
+        self.scales = alloc(base + (head_dim // 64,), dtype=torch.float16, device=self.device)
+        self.biases = alloc(base + (head_dim // 64,), dtype=torch.float16, device=self.device)
+        self.pools = self.codes  # element size used by callers that size per-token bytes
+        self.bm = BlockManager(n_blocks, block_size)
+        self.tables: dict[str, list[int]] = {}
+        self.offsets: dict[str, int] = {}
+
+    def qpools(self, layer: int) -> tuple[torch.Tensor, ...]:
+        """(k_codes, k_scales, k_biases, v_codes, v_scales, v_biases) of a layer."""
+        return (self.codes[layer, 0], self.scales[layer, 0], self.biases[layer, 0],
+                self.codes[layer, 1], self.scales[layer, 1], self.biases[layer, 1])
+
+    def k_pool(self, layer: int) -> torch.Tensor:
+        raise TypeError("quantised store: use qpools(layer)")
+
+    v_pool = k_pool
+
+    @property
+    def bytes_per_token(self) -> int:
+        """Bytes of one token over all layers, K and V (codes + scales + biases)."""
+        per_head = self.head_dim * self.bits // 8 + 2 * 2 * (self.head_dim // 64)
+        return self.n_layers * 2 * self.n_kv_heads * per_head
+
+    def pool_stack(self) -> torch.Tensor:
+        raise TypeError("quantised store: use pool_stacks()")
+
+    def pool_stacks(self) -> list[torch.Tensor]:
+        L2 = 2 * self.n_layers
+        return [t.view(L2, self.n_blocks, *t.shape[3:]) for t in (self.codes, self.scales,
+                                                                  self.biases)]
+
+    def _write_layer(self, l: int, keys: torch.Tensor, values: torch.Tensor,
+                     slots: torch.Tensor) -> None:
+        ops.kv_quant_append(self.qpools(l), keys, values, slots)
+
+
+class QuantizedPagedDecodeStep(PagedDecodeStep):
+    """Decode step over a QuantizedPagedKVStore: per layer, quantise-on-append
+    of the new token (mz_kv_quant_append_paged), then attention with the
+    dequantisation fused in (mz_paged_decode_q)."""
+
+    def __init__(self, store: QuantizedPagedKVStore, seq_ids: list[str], n_heads: int,
+                 scale: float | None = None, max_blocks: int | None = None) -> None:
+        self.store = store
+        self.seq_ids = list(seq_ids)
+        self.n_heads = n_heads
+        self.scale = scale if scale is not None else store.head_dim ** -0.5
+        self.B = len(seq_ids)
+        for s in self.seq_ids:
+            store.ensure_capacity(s, 1)
+        width = max(len(store.tables[s]) for s in self.seq_ids)
+        self.max_blocks = max(width, max_blocks or 0)
+        dev = store.device
+        self.tables = torch.full((self.B, self.max_blocks), -1, dtype=torch.int32, device=dev)
+        self.positions = torch.zeros(self.B, dtype=torch.int32, device=dev)
+        self.lengths = torch.zeros(self.B, dtype=torch.int32, device=dev)
+        self.sync_metadata()
+        G = n_heads // store.n_kv_heads
+        self.workspace = ops.decode_q_workspace(self.B, store.n_kv_heads, G, store.head_dim,
+                                                store.bits,
+                                                dev.index if dev.index is not None else 0)
+        self._dev_in = None
+
+    def layer(self, l: int, q: torch.Tensor, k_new: torch.Tensor, v_new: torch.Tensor,
+              out: torch.Tensor, num_warps: int = 0) -> None:
+        pools = self.store.qpools(l)
+        ops.kv_quant_append_paged(pools, k_new, v_new, self.tables, self.positions)
+        ops.paged_decode_q(q, pools, self.tables, self.lengths, scale=self.scale, out=out,
+                           workspace=self.workspace, num_warps=num_warps)

@@ -59,8 +59,11 @@ class PagedPrefixCache:
         self._users: dict[int, int] = {}             # logical block -> entries using it
         self._by_dev: dict[int, int] = {}            # device block -> logical block
         self._next_lb = 0
-        elem = store.pools.element_size()
-        self.bytes_per_token = store.n_layers * 2 * store.n_kv_heads * store.head_dim * elem
+        if hasattr(type(store), "bytes_per_token"):
+            self.bytes_per_token = store.bytes_per_token
+        else:
+            elem = store.pools.element_size()
+            self.bytes_per_token = store.n_layers * 2 * store.n_kv_heads * store.head_dim * elem
 
     # -- logical blocks ------------------------------------------------------
 
@@ -172,7 +175,7 @@ class PagedPrefixCache:
             return 0
         new = self.store.bm.allocate(len(host_lbs))
         slots = [self._loc[lb][1] for lb in host_lbs]
-        self.host_tier.reload(self.store.pool_stack(), slots, new)
+        self.host_tier.reload(self.store.pool_stacks(), slots, new)
         self.host_tier.release(slots)
         for lb, b in zip(host_lbs, new):
             self._loc[lb] = ("dev", b)
@@ -202,7 +205,7 @@ class PagedPrefixCache:
         if not chosen:
             return 0
         dev = [self._loc[lb][1] for lb in chosen]
-        slots = self.host_tier.evict(self.store.pool_stack(), dev)
+        slots = self.host_tier.evict(self.store.pool_stacks(), dev)
         for lb, b, s in zip(chosen, dev, slots):
             self._loc[lb] = ("host", s)
             del self._by_dev[b]
