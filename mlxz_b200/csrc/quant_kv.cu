@@ -163,19 +163,50 @@ struct QCfg {
   static constexpr int NG = D / 64;         // groups per row
   static constexpr int TD = kTileTok * RB;  // code bytes per tile (K or V)
   static constexpr int TS = kTileTok * NG * 2;  // scale (or bias) bytes per tile
+  // 128-byte code rows arrive by 2-D bulk tensor copies with the 128-byte
+  // swizzle (conflict-free fragment reads); narrower rows by 1-D bulk copies.
+  static constexpr bool kSwizzled = (RB == 128);
   static constexpr int kTx = 2 * TD + 4 * TS;
-  static constexpr int kStageBytes = (kTx + 127) / 128 * 128;
+  static constexpr int kCodeStage = 2 * TD;          // K + V codes (1024-aligned)
+  static constexpr int kScaleStage = 4 * TS;         // K/V scales and biases
+  static constexpr int kStageBytes = kCodeStage + kScaleStage;
   static constexpr int kCtas = NR == 1 ? 3 : 2;  // CTAs per SM the shared memory is sized for
   static constexpr int kStagesFit = (210 * 1024 / kCtas) / (kWarps * kStageBytes);
   static constexpr int kStages = kStagesFit > 8 ? 8 : (kStagesFit < 3 ? 3 : kStagesFit);
-  static constexpr int kSmemTiles = kWarps * kStages * kStageBytes;
+  static constexpr int kSmemCodes = kWarps * kStages * kCodeStage;
+  static constexpr int kSmemScales = kWarps * kStages * kScaleStage;
   static constexpr int kSmemBars = kWarps * kStages * 8;
   static constexpr int kSmemUnits = kWarps * kUnitQ * 32;
-  static constexpr int kSmemBytes = kSmemTiles + kSmemBars + kSmemUnits + 128;
+  static constexpr int kSmemBytes = kSmemCodes + kSmemScales + kSmemBars + kSmemUnits + 1024;
   // P' = p * s_v is stored in fp16 scaled by this power of two (keeps small
   // weights out of fp16 subnormals; removed exactly at the end).
   static constexpr float kPScale = BITS == 8 ? 256.f : 16.f;
 };
+
+// Byte offset of (row, byte) in a code tile: swizzled 128-byte rows, or plain.
+template <class C>
+__device__ __forceinline__ uint32_t code_off(int row, int byte) {
+  if constexpr (C::kSwizzled) {
+    return swz128(row, byte);
+  } else {
+    return row * C::RB + byte;
+  }
+}
+
+// Token of the tile held in mma row (or k index) m.  With swizzled rows the
+// odd rows are exchanged with their partner four rows away (m ^ 4), so that
+// the K reads (rows m, m+1 in one quarter-warp phase) and the V reads (rows
+// 2c or 2c+1 for c = 0..3 in one half-warp phase) fall in distinct bank
+// groups under the 128-byte swizzle.  Scores, masks, scales and V rows all go
+// through this map, so the order of the tokens inside a tile is immaterial.
+template <class C>
+__device__ __forceinline__ int tok_of(int m) {
+  if constexpr (C::kSwizzled) {
+    return m ^ ((m & 1) << 2);
+  } else {
+    return m;
+  }
+}
 
 constexpr uint32_t kMagic = 0x64646464u;  // fp16 0x64xx = 1024 + xx
 
@@ -202,25 +233,29 @@ __device__ __forceinline__ float load_q16(const uint16_t *q, int64_t off, bool b
 //        fp16 magic bias, removed through sum_t P'), B = P'^T by movmatrix.
 template <int D, int BITS, int NR>
 __global__ void __launch_bounds__(kWarps * 32, QCfg<D, BITS, NR>::kCtas)
-    paged_decode_q_kernel(const Params p) {
+    paged_decode_q_kernel(const __grid_constant__ CUtensorMap tmK,
+                          const __grid_constant__ CUtensorMap tmV, const Params p) {
   using C = QCfg<D, BITS, NR>;
   constexpr int S = C::kStages;
   constexpr int NG = C::NG;
   constexpr int MT = D / 16;  // m-tiles of P.V (4 per group)
 
   extern __shared__ uint8_t smem_raw[];
-  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 127) &
-                                              ~static_cast<uintptr_t>(127));
+  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                              ~static_cast<uintptr_t>(1023));
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int W = gridDim.x * kWarps;
   const int wid = blockIdx.x * kWarps + warp;
 
-  uint8_t *stages = smem + warp * S * C::kStageBytes;
-  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + C::kSmemTiles) + warp * S;
-  Unit *uq = reinterpret_cast<Unit *>(smem + C::kSmemTiles + C::kSmemBars) + warp * kUnitQ;
+  uint8_t *codes = smem + warp * S * C::kCodeStage;
+  uint8_t *scales = smem + C::kSmemCodes + warp * S * C::kScaleStage;
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + C::kSmemCodes + C::kSmemScales) + warp * S;
+  Unit *uq = reinterpret_cast<Unit *>(smem + C::kSmemCodes + C::kSmemScales + C::kSmemBars) +
+             warp * kUnitQ;
   const uint32_t bar0 = smem_u32(bars);
-  const uint32_t stage0 = smem_u32(stages);
+  const uint32_t code0 = smem_u32(codes);
+  const uint32_t scale0 = smem_u32(scales);
 
   if (lane == 0) {
     for (int s = 0; s < S; ++s) mbar_init(bar0 + 8 * s, 1);
@@ -242,14 +277,20 @@ __global__ void __launch_bounds__(kWarps * 32, QCfg<D, BITS, NR>::kCtas)
       }
       const int64_t row0 = ((int64_t)blk * p.Hkv + c.h) * p.bs + (c.t % p.tpb) * kTileTok;
       const uint32_t bar = bar0 + 8 * s;
-      const uint32_t st = stage0 + s * C::kStageBytes;
+      const uint32_t cs = code0 + s * C::kCodeStage;
+      const uint32_t ss = scale0 + s * C::kScaleStage;
       mbar_arrive_expect_tx(bar, C::kTx);
-      bulk_load(st, p.kq + row0 * C::RB, C::TD, bar, pol);
-      bulk_load(st + C::TD, p.vq + row0 * C::RB, C::TD, bar, pol);
-      bulk_load(st + 2 * C::TD, p.k_scales + row0 * NG, C::TS, bar, pol);
-      bulk_load(st + 2 * C::TD + C::TS, p.k_biases + row0 * NG, C::TS, bar, pol);
-      bulk_load(st + 2 * C::TD + 2 * C::TS, p.v_scales + row0 * NG, C::TS, bar, pol);
-      bulk_load(st + 2 * C::TD + 3 * C::TS, p.v_biases + row0 * NG, C::TS, bar, pol);
+      if constexpr (C::kSwizzled) {
+        tma_load_2d(cs, &tmK, 0, static_cast<int>(row0), bar, pol);
+        tma_load_2d(cs + C::TD, &tmV, 0, static_cast<int>(row0), bar, pol);
+      } else {
+        bulk_load(cs, p.kq + row0 * C::RB, C::TD, bar, pol);
+        bulk_load(cs + C::TD, p.vq + row0 * C::RB, C::TD, bar, pol);
+      }
+      bulk_load(ss, p.k_scales + row0 * NG, C::TS, bar, pol);
+      bulk_load(ss + C::TS, p.k_biases + row0 * NG, C::TS, bar, pol);
+      bulk_load(ss + 2 * C::TS, p.v_scales + row0 * NG, C::TS, bar, pol);
+      bulk_load(ss + 3 * C::TS, p.v_biases + row0 * NG, C::TS, bar, pol);
     }
   };
 
@@ -324,12 +365,12 @@ __global__ void __launch_bounds__(kWarps * 32, QCfg<D, BITS, NR>::kCtas)
 
     if (!wait_stage<S>(p, bar0, i, sch.issued, lane)) return;
 
-    const uint8_t *st = stages + s * C::kStageBytes;
-    const uint8_t *kd = st, *vd = st + C::TD;
-    const __half *ksc = reinterpret_cast<const __half *>(st + 2 * C::TD);
-    const __half *kbi = reinterpret_cast<const __half *>(st + 2 * C::TD + C::TS);
-    const __half *vsc = reinterpret_cast<const __half *>(st + 2 * C::TD + 2 * C::TS);
-    const __half *vbi = reinterpret_cast<const __half *>(st + 2 * C::TD + 3 * C::TS);
+    const uint8_t *kd = codes + s * C::kCodeStage, *vd = kd + C::TD;
+    const uint8_t *ss = scales + s * C::kScaleStage;
+    const __half *ksc = reinterpret_cast<const __half *>(ss);
+    const __half *kbi = reinterpret_cast<const __half *>(ss + C::TS);
+    const __half *vsc = reinterpret_cast<const __half *>(ss + 2 * C::TS);
+    const __half *vbi = reinterpret_cast<const __half *>(ss + 3 * C::TS);
     const int nvalid = min(kTileTok, cc.ctx - cc.t * kTileTok);
     const bool last_tile = (cc.t == cc.n - 1);
 
@@ -340,8 +381,8 @@ __global__ void __launch_bounds__(kWarps * 32, QCfg<D, BITS, NR>::kCtas)
 #pragma unroll
       for (int nr = 0; nr < NR; ++nr) acc[nr][G][0] = acc[nr][G][1] = acc[nr][G][2] = acc[nr][G][3] = 0.f;
       if constexpr (BITS == 8) {
-        const uint4 k0 = *reinterpret_cast<const uint4 *>(kd + g * C::RB + 64 * G + 16 * cq);
-        const uint4 k1 = *reinterpret_cast<const uint4 *>(kd + (g + 8) * C::RB + 64 * G + 16 * cq);
+        const uint4 k0 = *reinterpret_cast<const uint4 *>(kd + code_off<C>(tok_of<C>(g), 64 * G + 16 * cq));
+        const uint4 k1 = *reinterpret_cast<const uint4 *>(kd + code_off<C>(tok_of<C>(g + 8), 64 * G + 16 * cq));
         const uint32_t w0[4] = {k0.x, k0.y, k0.z, k0.w}, w1[4] = {k1.x, k1.y, k1.z, k1.w};
 #pragma unroll
         for (int w = 0; w < 4; ++w) {
@@ -354,8 +395,8 @@ __global__ void __launch_bounds__(kWarps * 32, QCfg<D, BITS, NR>::kCtas)
           for (int nr = 0; nr < NR; ++nr) mma_16816<false>(acc[nr][G], a, qb[nr][G][w][0], qb[nr][G][w][1]);
         }
       } else {
-        const uint2 k0 = *reinterpret_cast<const uint2 *>(kd + g * C::RB + 32 * G + 8 * cq);
-        const uint2 k1 = *reinterpret_cast<const uint2 *>(kd + (g + 8) * C::RB + 32 * G + 8 * cq);
+        const uint2 k0 = *reinterpret_cast<const uint2 *>(kd + code_off<C>(g, 32 * G + 8 * cq));
+        const uint2 k1 = *reinterpret_cast<const uint2 *>(kd + code_off<C>(g + 8, 32 * G + 8 * cq));
 #pragma unroll
         for (int w = 0; w < 4; ++w) {
           const uint32_t x0 = (w >> 1) ? k0.y : k0.x, x1 = (w >> 1) ? k1.y : k1.x;
@@ -370,17 +411,27 @@ __global__ void __launch_bounds__(kWarps * 32, QCfg<D, BITS, NR>::kCtas)
         }
       }
     }
-    // scores: reg 2*ts + rs <-> (token g + 8*ts, row 2c + rs)
+    // scores: reg 2*ts + rs <-> (token tok_of(g + 8*ts), row 2c + rs)
     float sc[NR][2][2];
     {
       float skv[2][NG], bkv[2][NG];
 #pragma unroll
-      for (int ts = 0; ts < 2; ++ts)
+      for (int ts = 0; ts < 2; ++ts) {
+        if constexpr (NG == 2) {
+          const float2 sk = __half22float2(*reinterpret_cast<const __half2 *>(ksc + tok_of<C>(g + 8 * ts) * 2));
+          const float2 bk = __half22float2(*reinterpret_cast<const __half2 *>(kbi + tok_of<C>(g + 8 * ts) * 2));
+          skv[ts][0] = sk.x;
+          skv[ts][1] = sk.y;
+          bkv[ts][0] = bk.x;
+          bkv[ts][1] = bk.y;
+        } else {
 #pragma unroll
-        for (int G = 0; G < NG; ++G) {
-          skv[ts][G] = __half2float(ksc[(g + 8 * ts) * NG + G]);
-          bkv[ts][G] = __half2float(kbi[(g + 8 * ts) * NG + G]);
+          for (int G = 0; G < NG; ++G) {
+            skv[ts][G] = __half2float(ksc[tok_of<C>(g + 8 * ts) * NG + G]);
+            bkv[ts][G] = __half2float(kbi[tok_of<C>(g + 8 * ts) * NG + G]);
+          }
         }
+      }
 #pragma unroll
       for (int nr = 0; nr < NR; ++nr)
 #pragma unroll
@@ -392,7 +443,7 @@ __global__ void __launch_bounds__(kWarps * 32, QCfg<D, BITS, NR>::kCtas)
             for (int G = 0; G < NG; ++G)
               x += skv[ts][G] * acc[nr][G][2 * ts + rs] + bkv[ts][G] * qs[nr][rs][G];
             x *= p.scale_log2;
-            if (g + 8 * ts >= nvalid) x = -INFINITY;
+            if (tok_of<C>(g + 8 * ts) >= nvalid) x = -INFINITY;
             sc[nr][ts][rs] = x;
           }
     }
@@ -442,7 +493,7 @@ __global__ void __launch_bounds__(kWarps * 32, QCfg<D, BITS, NR>::kCtas)
       float sv[2], bv[2];
 #pragma unroll
       for (int ts = 0; ts < 2; ++ts) {
-        const int tok = g + 8 * ts;
+        const int tok = tok_of<C>(g + 8 * ts);
         const bool ok = tok < nvalid;
         sv[ts] = ok ? __half2float(vsc[tok * NG + G]) * C::kPScale : 0.f;
         bv[ts] = ok ? __half2float(vbi[tok * NG + G]) : 0.f;
@@ -460,12 +511,12 @@ __global__ void __launch_bounds__(kWarps * 32, QCfg<D, BITS, NR>::kCtas)
         pb[nr][0] = movmatrix_trans(*reinterpret_cast<const uint32_t *>(&h0));
         pb[nr][1] = movmatrix_trans(*reinterpret_cast<const uint32_t *>(&h1));
       }
-      // V codes of tokens 2c, 2c+1, 2c+8, 2c+9 for head dims 64G + 8g + [0, 8)
+      // V codes of k indices 2c, 2c+1, 2c+8, 2c+9 (tokens tok_of(.)) for head dims 64G + 8g + [0, 8)
       if constexpr (BITS == 8) {
-        const uint2 v0 = *reinterpret_cast<const uint2 *>(vd + (2 * cq) * C::RB + 64 * G + 8 * g);
-        const uint2 v1 = *reinterpret_cast<const uint2 *>(vd + (2 * cq + 1) * C::RB + 64 * G + 8 * g);
-        const uint2 v2 = *reinterpret_cast<const uint2 *>(vd + (2 * cq + 8) * C::RB + 64 * G + 8 * g);
-        const uint2 v3 = *reinterpret_cast<const uint2 *>(vd + (2 * cq + 9) * C::RB + 64 * G + 8 * g);
+        const uint2 v0 = *reinterpret_cast<const uint2 *>(vd + code_off<C>(tok_of<C>(2 * cq), 64 * G + 8 * g));
+        const uint2 v1 = *reinterpret_cast<const uint2 *>(vd + code_off<C>(tok_of<C>(2 * cq + 1), 64 * G + 8 * g));
+        const uint2 v2 = *reinterpret_cast<const uint2 *>(vd + code_off<C>(tok_of<C>(2 * cq + 8), 64 * G + 8 * g));
+        const uint2 v3 = *reinterpret_cast<const uint2 *>(vd + code_off<C>(tok_of<C>(2 * cq + 9), 64 * G + 8 * g));
         // byte interleaves: [ra.bk, rb.bk, ra.bk+1, rb.bk+1]
         const uint32_t lo01a = __byte_perm(v0.x, v1.x, 0x5140), lo23a = __byte_perm(v0.x, v1.x, 0x7362);
         const uint32_t hi01a = __byte_perm(v0.y, v1.y, 0x5140), hi23a = __byte_perm(v0.y, v1.y, 0x7362);
@@ -483,10 +534,10 @@ __global__ void __launch_bounds__(kWarps * 32, QCfg<D, BITS, NR>::kCtas)
           for (int nr = 0; nr < NR; ++nr) mma_16816<false>(oacc[nr][4 * G + v], a, pb[nr][0], pb[nr][1]);
         }
       } else {
-        const uint32_t v0 = *reinterpret_cast<const uint32_t *>(vd + (2 * cq) * C::RB + 32 * G + 4 * g);
-        const uint32_t v1 = *reinterpret_cast<const uint32_t *>(vd + (2 * cq + 1) * C::RB + 32 * G + 4 * g);
-        const uint32_t v2 = *reinterpret_cast<const uint32_t *>(vd + (2 * cq + 8) * C::RB + 32 * G + 4 * g);
-        const uint32_t v3 = *reinterpret_cast<const uint32_t *>(vd + (2 * cq + 9) * C::RB + 32 * G + 4 * g);
+        const uint32_t v0 = *reinterpret_cast<const uint32_t *>(vd + code_off<C>((2 * cq), 32 * G + 4 * g));
+        const uint32_t v1 = *reinterpret_cast<const uint32_t *>(vd + code_off<C>((2 * cq + 1), 32 * G + 4 * g));
+        const uint32_t v2 = *reinterpret_cast<const uint32_t *>(vd + code_off<C>((2 * cq + 8), 32 * G + 4 * g));
+        const uint32_t v3 = *reinterpret_cast<const uint32_t *>(vd + code_off<C>((2 * cq + 9), 32 * G + 4 * g));
 #pragma unroll
         for (int v = 0; v < 4; ++v) {
           // nibble v -> byte v/2 (low or high half); nibble 4 + v -> byte 2 + v/2
@@ -804,12 +855,23 @@ extern "C" int mz_paged_decode_q(void *out, int32_t out_dtype, int64_t out_seq_s
   set_schedule(p, ws);
   p.err = dev_err;
 
+  // 2-D maps over the code pools (rows of D * bits / 8 bytes), used by the
+  // swizzled instantiations (128-byte rows); others take 1-D bulk copies.
+  CUtensorMap tk{}, tv{};
+  const int64_t rows_total = n_blocks * n_kv_heads * block_size;
+  const int rb = head_dim * bits / 8;
+  if (rb == 128) {
+    if (rows_total >= (int64_t(1) << 31))
+      return fail(MZ_ERR_UNSUPPORTED, "%s: pool has >= 2^31 rows", fn);
+    if (int rc = make_row_map(&tk, k_codes, rows_total, rb, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, 128)) return rc;
+    if (int rc = make_row_map(&tv, v_codes, rows_total, rb, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, 128)) return rc;
+  }
   int per_sm = 0;  // also sets the kernels' shared-memory attributes (once)
   if (int rc = q_ctas_per_sm(head_dim, bits, &per_sm)) return rc;
   const unsigned grid = static_cast<unsigned>(warps / kWarps);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
 #define MZ_LQ(D_, B_, NR_)                                                                    \
-  paged_decode_q_kernel<D_, B_, NR_><<<grid, kWarps * 32, QCfg<D_, B_, NR_>::kSmemBytes, s>>>(p)
+  paged_decode_q_kernel<D_, B_, NR_><<<grid, kWarps * 32, QCfg<D_, B_, NR_>::kSmemBytes, s>>>(tk, tv, p)
   if (rows <= 8) {
     if (head_dim == 128) {
       if (bits == 8) MZ_LQ(128, 8, 1); else MZ_LQ(128, 4, 1);
