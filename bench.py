@@ -35,6 +35,10 @@ METRIC = ("paged-decode KV-read GB/s (% of HBM peak) and decode tok/s, 8B shape,
 L, HQ, HKV, D, BS, B_PER_GPU = 32, 32, 8, 128, 16, 64
 CTX_LO, CTX_HI = 512, 8192
 FALLBACK_HBM_GBS = 6650.0
+C5_METRIC = ("head-sharded paged-decode KV-read GB/s (all GPUs) and decode tok/s, "
+             "70B shape, batch 256")
+C5_L, C5_HQ, C5_B = 80, 64, 256
+C5_MEDIAN, C5_SIGMA, C5_LO, C5_HI = 4096, 1.0, 256, 32768
 
 
 def parse_args():
@@ -43,7 +47,10 @@ def parse_args():
     ap.add_argument("--steps", type=int, default=300)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="mlxz_b200", choices=["mlxz_b200", "reference"])
-    ap.add_argument("--layers", type=int, default=L)
+    ap.add_argument("--layers", type=int, default=None,
+                    help="layers (decode: default 32); sharded70b: resident layers cap")
+    ap.add_argument("--resident-gb", type=float, default=120.0,
+                    help="sharded70b: HBM budget for the resident layers' pools")
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0,
@@ -53,11 +60,17 @@ def parse_args():
     ap.add_argument("--separate-append", action="store_true",
                     help="append with mz_kv_append_paged, then mz_paged_decode (two launches)")
     ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--config", default="decode", choices=["decode", "prefix", "quant"],
+    ap.add_argument("--config", default="decode",
+                    choices=["decode", "prefix", "quant", "sharded70b"],
                     help="decode: the paged decode step (headline); prefix: prefix-cache "
                          "restore / copy-on-write / host-tier eviction and reload; quant: "
-                         "4/8-bit quantised KV decode step")
+                         "4/8-bit quantised KV decode step; sharded70b: 70B-shape decode "
+                         "step head-sharded over the ranks (strong scaling)")
     ap.add_argument("--bits", type=int, default=8, choices=[4, 8])
+    ap.add_argument("--gather", default="p2p", choices=["p2p", "nccl"],
+                    help="N > 1: p2p = output rows stored into every rank's buffer by the "
+                         "decode launch itself (peer memory over NVLink) + bounded signal "
+                         "wait; nccl = ordinary launch, then NCCL all-gather + layout copy")
     return ap.parse_args()
 
 
@@ -223,29 +236,57 @@ def run_reference(args, rank: int, world: int) -> None:
 # GPU benchmark
 # ---------------------------------------------------------------------------
 
+def c5_ctx(seed: int, n: int):
+    """70B sharded workload: lognormal context lengths, median 4096, sigma 1,
+    clipped to [256, 32768] (seeded)."""
+    import numpy as np
+
+    z = np.random.default_rng(seed).standard_normal(n)
+    c = np.exp(np.log(C5_MEDIAN) + C5_SIGMA * z)
+    return np.clip(np.rint(c), C5_LO, C5_HI).astype(np.int64)
+
+
 def run_gpu(args, rank: int, world: int, local_rank: int) -> None:
+    """The paged decode step on this rank's KV-head shard.
+
+    decode (default): 8B shape, 64 sequences per GPU (weak scaling).
+    sharded70b: 70B shape, 256 sequences in total split by KV head across
+    the ranks (strong scaling); the layers that fit in HBM are resident and
+    timed, and the 80-layer step time is the per-layer time x 80."""
     import numpy as np
     import torch
     import torch.distributed as dist
 
     from mlxz_b200 import ops
     from mlxz_b200.engine import PagedDecodeStep, PagedKVStore
+    from mlxz_b200.engine.sharding import HeadAllGather, HeadShard, PeerAllGather
 
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
+    c5 = args.config == "sharded70b"
+    hq_all = C5_HQ if c5 else HQ
+    shard = HeadShard(rank, world, HKV, hq_all)  # raises unless world divides 8 KV heads
     if world > 1:
-        if HKV % world:
-            raise SystemExit(f"--gpus {world} must divide {HKV} KV heads")
         import datetime
 
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=dev)
-    hkv, hq = HKV // world, HQ // world
-    nl = args.layers
-    B = B_PER_GPU * world
-    ctx = workload_ctx(args.seed, B)
+    hkv, hq = shard.kv_local, shard.q_local
+    if c5:
+        B = C5_B
+        ctx = c5_ctx(args.seed, B)
+        model_layers = C5_L
+    else:
+        B = B_PER_GPU * world
+        ctx = workload_ctx(args.seed, B)
+        model_layers = args.layers or L
     need = (ctx + 1 + BS - 1) // BS
     n_blocks = int(math.ceil(need.sum() * 1.1))
+    layer_pool_bytes = n_blocks * hkv * BS * D * 2 * 2
+    nl = model_layers
+    if c5:
+        fit = int(args.resident_gb * 1e9 // layer_pool_bytes)
+        nl = max(1, min(args.layers or C5_L, C5_L, fit))
     perm = np.random.default_rng(args.seed + 1).permutation(n_blocks)
 
     torch.manual_seed(args.seed * 1000 + rank)
@@ -264,7 +305,13 @@ def run_gpu(args, rank: int, world: int, local_rank: int) -> None:
     kn = torch.randn(nl, B, hkv, D, device=dev).to(torch.bfloat16)
     vn = torch.randn(nl, B, hkv, D, device=dev).to(torch.bfloat16)
     out = torch.empty_like(q)
-    gathered = torch.empty((nl, world, B, hq, D), dtype=torch.bfloat16, device=dev) if world > 1 else None
+    p2p = world > 1 and args.gather == "p2p"
+    gat = HeadAllGather(shard, B, D, torch.bfloat16, dev)
+    peer = PeerAllGather(shard, B, D, torch.bfloat16, dev, n_slots=nl) if p2p else None
+    if p2p:
+        full = peer.full
+    else:
+        full = torch.empty((nl, B, hq_all, D), dtype=torch.bfloat16, device=dev) if world > 1 else out
 
     kv_bytes_rank = float((ctx + 1).sum()) * hkv * D * 2 * 2  # per layer, this rank
     qo_bytes = 2.0 * B * hq * D * 2
@@ -283,12 +330,16 @@ def run_gpu(args, rank: int, world: int, local_rank: int) -> None:
                 ops.paged_decode(q[l], st.k_pool(l), st.v_pool(l), step.tables, step.lengths,
                                  scale=step.scale, out=out[l], workspace=step.workspace,
                                  num_warps=args.num_warps)
+            elif p2p:
+                peer.launch(step, l, q[l], kn[l], vn[l], slot=l, num_warps=args.num_warps)
             else:
                 step.layer(l, q[l], kn[l], vn[l], out[l], num_warps=args.num_warps)
             if ev is not None:
                 ev[l][1].record()
-            if world > 1:
-                dist.all_gather_into_tensor(gathered[l], out[l])
+            if p2p:
+                peer.wait()
+            elif world > 1:
+                gat.full(out[l], out=full[l])
 
     def barrier():
         if world > 1:
@@ -324,11 +375,12 @@ def run_gpu(args, rank: int, world: int, local_rank: int) -> None:
 
     e2e_ms, h2d, d2h = float('nan'), 0, 0
     if not args.no_e2e:
-        # End to end through the public step API: pinned host inputs/outputs.
+        # End to end through the public step API: this rank's inputs from
+        # pinned host memory, the gathered [B, Hq, D] outputs back to the host.
         qh = q.cpu().pin_memory()
         kh = kn.cpu().pin_memory()
         vh = vn.cpu().pin_memory()
-        oh = torch.empty(q.shape if world == 1 else (nl, world, B, hq, D), dtype=torch.bfloat16).pin_memory()
+        oh = torch.empty(full.shape, dtype=torch.bfloat16).pin_memory()
         h2d = qh.numel() * 2 + kh.numel() * 2 + vh.numel() * 2
         d2h = oh.numel() * 2
 
@@ -341,10 +393,15 @@ def run_gpu(args, rank: int, world: int, local_rank: int) -> None:
             q_e.copy_(qh, non_blocking=True)
             k_e.copy_(kh, non_blocking=True)
             v_e.copy_(vh, non_blocking=True)
-            step.step(q_e, k_e, v_e, out=out)
-            for l in range(nl):
-                dist.all_gather_into_tensor(gathered[l], out[l])
-            oh.copy_(gathered, non_blocking=True)
+            if p2p:
+                step.prepare_writes()
+                for l in range(nl):
+                    peer.layer(step, l, q_e[l], k_e[l], v_e[l], slot=l)
+            else:
+                step.step(q_e, k_e, v_e, out=out)
+                for l in range(nl):
+                    gat.full(out[l], out=full[l])
+            oh.copy_(full, non_blocking=True)
 
         for _ in range(2):
             e2e_step()
@@ -359,58 +416,85 @@ def run_gpu(args, rank: int, world: int, local_rank: int) -> None:
         barrier()
         e2e_ms = e0.elapsed_time(e1) / args.steps
 
-
     if world > 1:
         t = torch.tensor([ms, e2e_ms, dec_mean], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms, e2e_ms, dec_mean = (float(x) for x in t.tolist())
 
-    kv_step_total = float((ctx + 1).sum()) * HKV * D * 2 * 2 * nl  # all heads, all ranks
-    value = kv_step_total / (ms / 1e3) / 1e9
+    # a step of the model: every layer (resident layers timed, x model/resident)
+    per_layer_ms = ms / nl
+    step_ms = per_layer_ms * model_layers
+    e2e_step_ms = e2e_ms / nl * model_layers
+    kv_step_total = float((ctx + 1).sum()) * HKV * D * 2 * 2 * model_layers  # all heads, all ranks
+    value = kv_step_total / (step_ms / 1e3) / 1e9
     peak, peak_kind = peaks()
     achieved = decode_alg_bytes / (dec_mean / 1e3) / 1e9
-    result = None
     if rank == 0:
         cpu = None
-        if world == 1 and not args.no_cpu_baseline:
+        if world == 1 and not args.no_cpu_baseline and not c5:
             threads = os.cpu_count() or 1
             r = cpu_sample(args.seed, args.cpu_seconds, threads)
             cpu = {"value": round(r["gbs"], 3), "unit": "GB/s", "cores": threads, "kind": "port",
                    "sample": (f"1 layer x {r['n_seqs']} sequences of the same ctx distribution, "
                               f"{r['reps']} reps (median), torch-CPU port of get_kv + GQA attention")}
-        traffic = profile_traffic("paged_decode_c2.md")
+        traffic = profile_traffic("paged_decode_c2.md") if not c5 else None
+        if world == 1:
+            par = "1 GPU"
+        elif p2p:
+            par = (f"kv-head sharding x{world}; all-gather fused into the decode launch "
+                   f"(peer-memory stores over NVLink + signal wait) per layer")
+        else:
+            par = f"kv-head sharding x{world} + NCCL all-gather per layer"
+        if c5:
+            metric = C5_METRIC
+            workload = (f"head-sharded paged decode step, Llama-3.1-70B KV shape: 80 layers "
+                        f"({nl} resident and timed, step = per-layer time x 80), 64 q heads, "
+                        f"8 kv heads ({hkv} per GPU), head_dim 128, block 16; {B} seqs, ctx "
+                        f"lognormal(median {C5_MEDIAN}, sigma {C5_SIGMA}) clipped to "
+                        f"[{C5_LO},{C5_HI}]; append 1 token + attention + all-gather per layer")
+            seq_len = f"lognormal median {C5_MEDIAN} sigma {C5_SIGMA} in [{C5_LO},{C5_HI}]"
+        else:
+            metric = METRIC
+            workload = (f"paged decode step, Llama-3.1-8B KV shape: {nl} layers, 32 q heads, "
+                        f"8 kv heads, head_dim 128, block 16; {B_PER_GPU} seqs per GPU, "
+                        f"ctx U[{CTX_LO},{CTX_HI}]; append 1 token + attention per layer")
+            seq_len = f"U[{CTX_LO},{CTX_HI}]"
         result = {
-            "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
-            "steps": args.steps, "warmup": max(3, args.warmup), "ms_per_step": round(ms, 4),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "metric": metric, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
+            "steps": args.steps, "warmup": max(3, args.warmup), "ms_per_step": round(step_ms, 4),
+            "higher_is_better": True, "scaling": "strong" if c5 else "weak", "vs_baseline": None,
+            "dtype": "bf16",
             "data": "synthetic (seeded N(0,1) bf16 K/V/Q, random block tables)",
             "config": {
-                "workload": (f"paged decode step, Llama-3.1-8B KV shape: {nl} layers, 32 q heads, "
-                             f"8 kv heads, head_dim 128, block 16; {B_PER_GPU} seqs per GPU, "
-                             f"ctx U[{CTX_LO},{CTX_HI}]; append 1 token + attention per layer"),
-                "layers": nl, "global_batch": B, "seq_len": f"U[{CTX_LO},{CTX_HI}]",
+                "workload": workload, "layers": model_layers, "layers_resident": nl,
+                "global_batch": B, "seq_len": seq_len,
                 "mean_ctx": round(float(ctx.mean()), 1),
-                "parallelism": "1 GPU" if world == 1 else f"kv-head sharding x{world} + NCCL all-gather",
-                "l2": f"KV read per step {kv_step_total / world / 1e9:.1f} GB per GPU >> 126 MB L2",
+                "parallelism": par,
+                "l2": f"KV read per layer {kv_step_total / model_layers / world / 1e9:.2f} GB per "
+                      f"GPU >> 126 MB L2",
                 "pool_blocks": n_blocks,
             },
-            "decode_tok_s": round(B / (ms / 1e3), 1),
+            "decode_tok_s": round(B / (step_ms / 1e3), 1),
             "hbm_frac": round(value / world / peak, 4),
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
                          "unit": "GB/s", "frac": round(achieved / peak, 4),
-                         "traffic": traffic, "kernel": "paged_decode_kernel<128,bf16> (fused append + decode)",
+                         "traffic": traffic,
+                         "kernel": "paged_decode_kernel<128,bf16> (fused append + decode"
+                                   + (" + peer all-gather)" if p2p else ")"),
                          "peak_kind": peak_kind,
                          "decode_ms_mean": round(dec_mean, 4),
                          "alg_bytes_per_launch": decode_alg_bytes},
             "cpu_baseline": cpu,
             "e2e": None if args.no_e2e else {
-                "value": round(kv_step_total / (e2e_ms / 1e3) / 1e9, 2), "unit": "GB/s",
-                "ms_per_step": round(e2e_ms, 4), "h2d_bytes_per_step": int(h2d),
+                "value": round(kv_step_total / (e2e_step_ms / 1e3) / 1e9, 2), "unit": "GB/s",
+                "ms_per_step": round(e2e_step_ms, 4), "h2d_bytes_per_step": int(h2d),
                 "d2h_bytes_per_step": int(d2h)},
-            "gpu_launches": args.steps * nl * (2 if args.separate_append else 1),
+            "gpu_launches": args.steps * nl * (2 if (args.separate_append or p2p) else 1),
             "clocks": clk,
         }
         print(json.dumps(result), flush=True)
+    if peer is not None:
+        peer.close()
     if world > 1:
         dist.destroy_process_group()
 
@@ -695,6 +779,8 @@ def main():
     if world == 1 and args.gpus != 1 and rank == 0:
         print(f"note: --gpus {args.gpus} without torchrun runs 1 rank", file=sys.stderr)
     sys.path.insert(0, str(ROOT))
+    if args.layers is None and args.config != "sharded70b":
+        args.layers = L
     if args.impl == "reference":
         run_reference(args, rank, world)
     elif args.config == "prefix":

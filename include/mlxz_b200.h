@@ -41,6 +41,11 @@ extern "C" {
 /* A cudaStream_t (CUstream).  NULL selects the legacy default stream. */
 typedef void *mz_stream_t;
 
+/* Largest group of ranks an all-gather over peer memory spans (GPUs of one
+ * NVLink domain), and the size of an exported memory handle. */
+#define MZ_MAX_RANKS 8
+#define MZ_IPC_HANDLE_BYTES 64
+
 enum mz_status {
   MZ_OK = 0,
   MZ_ERR_INVALID_ARG = -1, /* a size, stride or pointer argument is invalid  */
@@ -173,6 +178,68 @@ MZ_API int mz_paged_append_decode(void *out, int32_t out_dtype, int64_t out_seq_
                                   int32_t head_dim, int32_t block_size, int64_t n_blocks,
                                   float scale, int32_t dtype, int32_t num_warps, void *workspace,
                                   size_t workspace_bytes, int32_t *dev_err, mz_stream_t stream);
+
+/* Destinations of one rank's decode output in a head-sharded group of
+ * n_ranks GPUs (one process each, KV heads split evenly; rank r holds query
+ * heads [r*n_heads, (r+1)*n_heads) of the n_ranks*n_heads in the gathered
+ * [n_seqs][n_ranks*n_heads][head_dim] buffer every rank keeps).
+ *   out[r]:    in rank r's gathered buffer, the first element of THIS rank's
+ *              head block (base + rank*n_heads*head_dim), as an address this
+ *              GPU can store to (out[rank] local; the others mapped with
+ *              mz_ipc_open);
+ *   signal[r]: rank r's n_ranks signal words (zero before the first launch),
+ *              mapped likewise (signal[rank] is not used);
+ *   arrivals:  one int32 in this GPU's memory, zero before the first launch
+ *              (each launch leaves it zero);
+ *   epoch:     nonzero, one more per launch, the same on every rank. */
+typedef struct mz_peer_outputs {
+  int32_t n_ranks;
+  int32_t rank;
+  void *out[MZ_MAX_RANKS];
+  int32_t *signal[MZ_MAX_RANKS];
+  int32_t *arrivals;
+  uint32_t epoch;
+} mz_peer_outputs;
+
+/* mz_paged_append_decode whose output rows are stored into every rank's
+ * gathered buffer (this GPU's own and, over NVLink, each peer's) as they are
+ * finished, instead of a separate all-gather after the launch; the launch's
+ * last block then publishes `epoch` into signal word `rank` of every peer.
+ * Each rank follows the launch with mz_peer_wait before it reads the gathered
+ * buffer.  out_seq_stride / out_head_stride are those of the gathered buffer
+ * (n_ranks*n_heads*head_dim and head_dim for a dense one).
+ * No counterpart in the reference (one device only); it replaces the
+ * all-gather of head-sharded attention outputs that a multi-GPU step runs
+ * after mz_paged_append_decode.  A rank's readers of a gathered buffer must
+ * be queued before its next launch that writes that buffer (peers write into
+ * it as soon as their own next launch runs).  n_seqs must be positive.  Other
+ * arguments and rules as mz_paged_append_decode. */
+MZ_API int mz_paged_append_decode_allgather(
+    const mz_peer_outputs *peers, int32_t out_dtype, int64_t out_seq_stride,
+    int64_t out_head_stride, const void *q, int64_t q_seq_stride, int64_t q_head_stride,
+    void *k_pool, void *v_pool, const void *k_new, const void *v_new, int64_t new_seq_stride,
+    int64_t new_head_stride, const int32_t *block_tables, int32_t max_blocks_per_seq,
+    const int32_t *ctx_lens, int32_t n_seqs, int32_t n_heads, int32_t n_kv_heads,
+    int32_t head_dim, int32_t block_size, int64_t n_blocks, float scale, int32_t dtype,
+    int32_t num_warps, void *workspace, size_t workspace_bytes, int32_t *dev_err,
+    mz_stream_t stream);
+
+/* Enqueue on `stream` a wait until signal[s] (this rank's words, s != rank)
+ * has reached `epoch` for every peer s, with acquire semantics at system
+ * scope, so work queued after it sees the peers' stored rows.  Gives up after
+ * timeout_ns (at most 60 s) and sets MZ_DEVERR_TIMEOUT in *dev_err.  No
+ * counterpart in the reference (one device only). */
+MZ_API int mz_peer_wait(const int32_t *signal, int32_t n_ranks, int32_t rank, uint32_t epoch,
+                        uint64_t timeout_ns, int32_t *dev_err, mz_stream_t stream);
+
+/* CUDA IPC for the gathered buffers and signal words: export writes an
+ * MZ_IPC_HANDLE_BYTES handle of the allocation that holds `ptr` and ptr's
+ * byte offset in it; open (in another process of the node, with its device
+ * current) maps it and returns the mapping's base (for close) and base +
+ * offset.  No counterpart in the reference (one device only). */
+MZ_API int mz_ipc_export(const void *ptr, void *handle, uint64_t *offset);
+MZ_API int mz_ipc_open(const void *handle, uint64_t offset, void **base, void **ptr);
+MZ_API int mz_ipc_close(void *base);
 
 /* mz_paged_decode without a workspace argument: it allocates nothing.
  * No counterpart in the reference (which has no device memory management);

@@ -67,6 +67,19 @@ class DeviceError(RuntimeError):
 _i32, _i64, _f32, _vp, _sz = (ctypes.c_int32, ctypes.c_int64, ctypes.c_float,
                               ctypes.c_void_p, ctypes.c_size_t)
 
+MZ_MAX_RANKS = 8
+MZ_IPC_HANDLE_BYTES = 64
+
+
+class PeerOutputs(ctypes.Structure):
+    """mz_peer_outputs: one rank's output destinations in a head-sharded group."""
+
+    _fields_ = [("n_ranks", ctypes.c_int32), ("rank", ctypes.c_int32),
+                ("out", ctypes.c_void_p * MZ_MAX_RANKS),
+                ("signal", ctypes.c_void_p * MZ_MAX_RANKS),
+                ("arrivals", ctypes.c_void_p), ("epoch", ctypes.c_uint32)]
+
+
 # name -> argtypes (every function returns int32 status)
 _SIGNATURES: dict[str, list] = {
     "mz_abi_version": [],
@@ -85,6 +98,14 @@ _SIGNATURES: dict[str, list] = {
     "mz_paged_append_decode": [_vp, _i32, _i64, _i64, _vp, _i64, _i64, _vp, _vp, _vp, _vp, _i64,
                                _i64, _vp, _i32, _vp, _i32, _i32, _i32, _i32, _i32, _i64, _f32,
                                _i32, _i32, _vp, _sz, _vp, _vp],
+    "mz_paged_append_decode_allgather": [ctypes.POINTER(PeerOutputs), _i32, _i64, _i64, _vp,
+                                         _i64, _i64, _vp, _vp, _vp, _vp, _i64, _i64, _vp, _i32,
+                                         _vp, _i32, _i32, _i32, _i32, _i32, _i64, _f32, _i32,
+                                         _i32, _vp, _sz, _vp, _vp],
+    "mz_peer_wait": [_vp, _i32, _i32, ctypes.c_uint32, ctypes.c_uint64, _vp, _vp],
+    "mz_ipc_export": [_vp, _vp, ctypes.POINTER(ctypes.c_uint64)],
+    "mz_ipc_open": [_vp, ctypes.c_uint64, ctypes.POINTER(_vp), ctypes.POINTER(_vp)],
+    "mz_ipc_close": [_vp],
     "mz_paged_decode_noalloc": [_vp, _i32, _i64, _i64, _i64, _vp, _i64, _i64, _i64, _i32, _vp,
                                 _vp, _vp, _i32, _vp, _i32, _i32, _i32, _i32, _i32, _i64, _f32,
                                 _i32, _i32, _vp, _vp],

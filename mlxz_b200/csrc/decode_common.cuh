@@ -65,6 +65,15 @@ struct Params {
   int static_pct;  // share of tiles handed out statically (1..100)
   int min_chunk;   // smallest dynamic chunk (tiles)
   int32_t *err;
+  // all-gather over peer memory (n_peer > 0): every output store also goes to
+  // peer_out[r] (the same rows in rank r's gathered buffer, mapped into this
+  // GPU's address space); once all warps have stored, the last one publishes
+  // `epoch` into each peer_sig[r] (rank r's signal word for this rank).
+  int n_peer = 0;
+  void *peer_out[MZ_MAX_RANKS - 1] = {};
+  uint32_t *peer_sig[MZ_MAX_RANKS - 1] = {};
+  uint32_t epoch = 0;
+  int32_t *arrivals = nullptr;  // grid arrival counter, zero between launches
 };
 
 struct Cursor {
@@ -159,6 +168,46 @@ __device__ __forceinline__ void store_pair(const Params &p, int64_t off, float x
   }
 }
 
+// All-gather instantiation: once a warp has stored pair (b, h)'s rows in this
+// GPU's buffer, it copies them -- rows * D contiguous elements, since the
+// gathered buffer has dense rows and one query token -- to the same place in
+// every peer's buffer, 16 bytes per lane, 512 contiguous bytes per warp store.
+template <int D>
+__device__ __forceinline__ void forward_rows(const Params &p, int b, int h, int lane) {
+  __syncwarp();
+  const int eb = p.out_f32 ? 4 : 2;
+  const int64_t off = row_offset(p.o_sb, p.o_st, p.o_sh, b, h, 0, p.G) * eb;
+  const int bytes = p.rows * D * eb;
+  const uint8_t *src = static_cast<const uint8_t *>(p.out) + off;
+  for (int x = 16 * lane; x < bytes; x += 512) {
+    const uint4 v = __ldcg(reinterpret_cast<const uint4 *>(src + x));
+    for (int r = 0; r < p.n_peer; ++r)
+      *reinterpret_cast<uint4 *>(static_cast<uint8_t *>(p.peer_out[r]) + off + x) = v;
+  }
+}
+
+__device__ __forceinline__ void st_release_sys(uint32_t *addr, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(addr), "r"(v) : "memory");
+}
+
+// Called by every thread of the grid after its last output store (every exit
+// path leads here, so the block barrier is reached by all).  The block's
+// stores are gathered by the barrier; one thread per block fences them at
+// system scope and counts the block in; the block that completes the count
+// re-zeroes the counter and publishes the launch's epoch to every peer.
+// Barrier -> fence -> counter -> fence -> release store orders every block's
+// peer stores before the signal a peer acquires.
+__device__ __forceinline__ void gather_arrive(const Params &p) {
+  if (p.n_peer == 0) return;
+  __syncthreads();
+  if (threadIdx.x != 0) return;
+  __threadfence_system();
+  if (atomicAdd(p.arrivals, 1) != static_cast<int>(gridDim.x) - 1) return;
+  *p.arrivals = 0;  // every block has arrived; the next launch starts from zero
+  __threadfence_system();
+  for (int r = 0; r < p.n_peer; ++r) st_release_sys(p.peer_sig[r], p.epoch);
+}
+
 // 128-byte swizzle of a [16 rows][128 bytes] box (what a bulk tensor copy with
 // CU_TENSOR_MAP_SWIZZLE_128B writes): 16-byte unit u of row r lives at unit
 // u ^ (r & 7).  Rows wider than 128 bytes are split into 2-KiB boxes.
@@ -168,15 +217,17 @@ __device__ __forceinline__ uint32_t swz128(int row, int byte) {
 }
 
 // Sequences with no context produce zeros (every warp takes b = wid mod W).
-template <int D>
+template <int D, bool GATHER = false>
 __device__ __forceinline__ void zero_empty_outputs(const Params &p, int wid, int W, int lane) {
   for (int b = wid; b < p.B; b += W) {
     if (clamped_ctx(p, b) != 0) continue;
-    for (int h = 0; h < p.Hkv; ++h)
+    for (int h = 0; h < p.Hkv; ++h) {
       for (int r = 0; r < p.rows; ++r) {
         const int64_t o = row_offset(p.o_sb, p.o_st, p.o_sh, b, h, r, p.G);
         for (int d = 2 * lane; d < D; d += 64) store_pair(p, o + d, 0.f, 0.f);
       }
+      if constexpr (GATHER) forward_rows<D>(p, b, h, lane);
+    }
   }
 }
 
@@ -315,7 +366,7 @@ struct UnitReader {
 // arrival; the warp that brings the count to nparts merges every piece's
 // (m, l, O) (slots uf + bh .. uf + nparts - 1 + bh) into the output and resets
 // the counter.
-template <int D>
+template <int D, bool GATHER = false>
 __device__ __forceinline__ void arrive_and_merge(const Params &p, const Cursor &cc, int bh, int uf,
                                                  int nparts, int lane) {
   __threadfence();
@@ -348,6 +399,7 @@ __device__ __forceinline__ void arrive_and_merge(const Params &p, const Cursor &
     store_pair(p, o, acc.x * inv, acc.y * inv);
     store_pair(p, o + 2, acc.z * inv, acc.w * inv);
   }
+  if constexpr (GATHER) forward_rows<D>(p, cc.b, cc.h, lane);
   if (lane == 0) p.counters[bh] = 0;
 }
 
@@ -356,7 +408,9 @@ __device__ __forceinline__ void arrive_and_merge(const Params &p, const Cursor &
 template <int S>
 __device__ __forceinline__ bool wait_stage(const Params &p, uint32_t bar0, int i, int issued,
                                            int lane) {
-  if (mbar_wait_bounded(bar0 + 8 * (i % S), (i / S) & 1, kTimeoutNs)) return true;
+  // warp-uniform outcome: a lane that saw the phase complete waits for the rest
+  if (__all_sync(0xffffffffu, mbar_wait_bounded(bar0 + 8 * (i % S), (i / S) & 1, kTimeoutNs)))
+    return true;
   if (lane == 0) dev_error(p.err, MZ_DEVERR_TIMEOUT);
   for (int k = i; k < issued; ++k) (void)mbar_wait_bounded(bar0 + 8 * (k % S), (k / S) & 1, kTimeoutNs);
   return false;

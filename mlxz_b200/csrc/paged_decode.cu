@@ -41,10 +41,9 @@ struct Cfg {
   static constexpr int kSmemBytes = kSmemTiles + kSmemBars + kSmemUnits + 1024;  // + align
 };
 
-template <int D, bool BF16>
-__global__ void __launch_bounds__(kWarps * 32, 2)
-    paged_decode_kernel(const __grid_constant__ CUtensorMap tmK,
-                        const __grid_constant__ CUtensorMap tmV, const Params p) {
+template <int D, bool BF16, bool GATHER>
+__device__ __forceinline__ void decode_tiles(const CUtensorMap &tmK, const CUtensorMap &tmV,
+                                             const Params &p) {
   using C = Cfg<D>;
   constexpr int S = C::kStages;
   constexpr int KS = D / 16;  // k-steps of Q.K^T, also n-tile pairs of P.V
@@ -70,7 +69,7 @@ __global__ void __launch_bounds__(kWarps * 32, 2)
   }
   __syncwarp();
 
-  zero_empty_outputs<D>(p, wid, W, lane);
+  zero_empty_outputs<D, GATHER>(p, wid, W, lane);
   Sched sch;
   if (!sch.init(p, lane, wid, W, uq)) return;  // T == 0: no counter is touched
 
@@ -298,6 +297,7 @@ __global__ void __launch_bounds__(kWarps * 32, 2)
           for (int n = 0; n < NT; ++n)
             store_pair(p, o + n * 8 + 2 * cq, oacc[n][2] * i1, oacc[n][3] * i1);
         }
+        if constexpr (GATHER) forward_rows<D>(p, cc.b, cc.h, lane);
       } else {
         const int64_t slot = (int64_t)ur.unit + bh;
         float *pr = p.part + slot * p.rows * D;
@@ -316,7 +316,7 @@ __global__ void __launch_bounds__(kWarps * 32, 2)
                 make_float2(oacc[n][2], oacc[n][3]);
           if (cq == 0) *reinterpret_cast<float2 *>(mlr + 2 * (g + 8)) = make_float2(m1, L1);
         }
-        arrive_and_merge<D>(p, cc, bh, uf, ul - uf + 1, lane);
+        arrive_and_merge<D, GATHER>(p, cc, bh, uf, ul - uf + 1, lane);
       }
       seg_first = true;  // the next tile starts a new piece
     }
@@ -327,6 +327,24 @@ __global__ void __launch_bounds__(kWarps * 32, 2)
     sch.refill<S>(p, i + 1, issue);
   }
 }
+
+template <int D, bool BF16>
+__global__ void __launch_bounds__(kWarps * 32, 2)
+    paged_decode_kernel(const __grid_constant__ CUtensorMap tmK,
+                        const __grid_constant__ CUtensorMap tmV, const Params p) {
+  decode_tiles<D, BF16, false>(tmK, tmV, p);
+}
+
+// The all-gather instantiation: every output store also goes to the peers'
+// buffers, and the grid's last block signals them.
+template <int D, bool BF16>
+__global__ void __launch_bounds__(kWarps * 32, 2)
+    paged_decode_gather_kernel(const __grid_constant__ CUtensorMap tmK,
+                               const __grid_constant__ CUtensorMap tmV, const Params p) {
+  decode_tiles<D, BF16, true>(tmK, tmV, p);
+  gather_arrive(p);
+}
+
 
 // ---------------------------------------------------------------------------
 // Host side.
@@ -346,6 +364,19 @@ int kernel_ctas_per_sm(int *out) {
   static cudaError_t err = cudaSuccess;
   return kernel_occupancy(paged_decode_kernel<D, BF16>, Cfg<D>::kSmemBytes, &cached, &once, &err,
                           out);
+}
+
+// Dynamic shared-memory opt-in for the all-gather instantiation (once).
+template <int D, bool BF16>
+int gather_smem_attr() {
+  static std::once_flag once;
+  static cudaError_t err = cudaSuccess;
+  std::call_once(once, []() {
+    err = cudaFuncSetAttribute(paged_decode_gather_kernel<D, BF16>,
+                               cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<D>::kSmemBytes);
+  });
+  if (err != cudaSuccess) return cuda_fail(err, "setting the all-gather kernel's shared memory");
+  return MZ_OK;
 }
 
 int ctas_per_sm(int D, bool bf16, int *out) {
@@ -392,6 +423,7 @@ struct DecodeArgs {
   int64_t kn_sb, kn_sh;
   int32_t *err;
   cudaStream_t stream;
+  const mz_peer_outputs *peers = nullptr;  // all-gather over peer memory, or none
 };
 
 // Host-side checks shared by the entry points; fills the resolved warp count
@@ -429,6 +461,25 @@ int validate(const DecodeArgs &a, const char *fn, int64_t *warps, WsLayout *ws) 
       return fail(MZ_ERR_ALIGNMENT,
                   "%s: k_new/v_new need 16-byte alignment and strides that are multiples of 8", fn);
     if (a.n_q != 1) return fail(MZ_ERR_UNSUPPORTED, "%s: fused append needs n_q_tokens == 1", fn);
+  }
+  if (a.peers) {
+    const mz_peer_outputs &pe = *a.peers;
+    if (pe.n_ranks < 1 || pe.n_ranks > MZ_MAX_RANKS || pe.rank < 0 || pe.rank >= pe.n_ranks)
+      return fail(MZ_ERR_INVALID_ARG, "%s: n_ranks %d / rank %d out of range (1..%d ranks)", fn,
+                  pe.n_ranks, pe.rank, MZ_MAX_RANKS);
+    if (pe.epoch == 0) return fail(MZ_ERR_INVALID_ARG, "%s: epoch must be nonzero", fn);
+    if (a.o_sh != a.D || (a.o_sb * (ob / 2)) % 16 != 0)
+      return fail(MZ_ERR_INVALID_ARG,
+                  "%s: the gathered buffer needs dense rows (out_head_stride == head_dim) and "
+                  "16-byte aligned sequence rows", fn);
+    if (!pe.arrivals || !aligned(pe.arrivals, 4))
+      return fail(MZ_ERR_INVALID_ARG, "%s: arrivals must be a 4-byte aligned device word", fn);
+    for (int r = 0; r < pe.n_ranks; ++r) {
+      if (!pe.out[r] || !aligned(pe.out[r], 16))
+        return fail(MZ_ERR_ALIGNMENT, "%s: out[%d] is null or not 16-byte aligned", fn, r);
+      if (r != pe.rank && (!pe.signal[r] || !aligned(pe.signal[r], 4)))
+        return fail(MZ_ERR_INVALID_ARG, "%s: signal[%d] is null or misaligned", fn, r);
+    }
   }
   const int64_t rows_total = a.n_blocks * a.Hkv * a.bs;
   if (rows_total >= (int64_t(1) << 31))
@@ -489,6 +540,20 @@ int launch(const DecodeArgs &a, int64_t warps, const WsLayout &ws, void *scratch
   p.kq = p.vq = nullptr;
   p.k_scales = p.k_biases = p.v_scales = p.v_biases = nullptr;
   p.err = a.err;
+  if (a.peers) {
+    const mz_peer_outputs &pe = *a.peers;
+    p.out = pe.out[pe.rank];
+    int j = 0;
+    for (int r = 0; r < pe.n_ranks; ++r) {
+      if (r == pe.rank) continue;
+      p.peer_out[j] = pe.out[r];
+      p.peer_sig[j] = reinterpret_cast<uint32_t *>(pe.signal[r]) + pe.rank;
+      ++j;
+    }
+    p.n_peer = j;
+    p.epoch = pe.epoch;
+    p.arrivals = pe.arrivals;
+  }
 
   int per_sm = 0;  // also sets the kernel's shared-memory attribute (once)
   if (int rc = ctas_per_sm(a.D, bf16, &per_sm)) return rc;
@@ -497,8 +562,17 @@ int launch(const DecodeArgs &a, int64_t warps, const WsLayout &ws, void *scratch
     if (e != cudaSuccess) return cuda_fail(e, "clearing decode counters");
   }
   const unsigned grid = static_cast<unsigned>(warps / kWarps);
-#define MZ_LAUNCH(D_, BF_)                                                                   \
-  paged_decode_kernel<D_, BF_><<<grid, kWarps * 32, Cfg<D_>::kSmemBytes, a.stream>>>(tk, tv, p)
+#define MZ_LAUNCH(D_, BF_)                                                                     \
+  do {                                                                                         \
+    if (a.peers) {                                                                             \
+      if (int rc = gather_smem_attr<D_, BF_>()) return rc;                                     \
+      paged_decode_gather_kernel<D_, BF_><<<grid, kWarps * 32, Cfg<D_>::kSmemBytes, a.stream>>>( \
+          tk, tv, p);                                                                          \
+    } else {                                                                                   \
+      paged_decode_kernel<D_, BF_><<<grid, kWarps * 32, Cfg<D_>::kSmemBytes, a.stream>>>(tk, tv, \
+                                                                                     p);       \
+    }                                                                                          \
+  } while (0)
   if (a.D == 128) {
     if (bf16) MZ_LAUNCH(128, true); else MZ_LAUNCH(128, false);
   } else {
@@ -623,6 +697,42 @@ extern "C" int mz_paged_append_decode(
     return fail(MZ_ERR_WORKSPACE, "mz_paged_append_decode: workspace %zu bytes < required %zu",
                 workspace_bytes, ws.total);
   return launch(a, warps, ws, workspace, false, "mz_paged_append_decode");
+}
+
+extern "C" int mz_paged_append_decode_allgather(
+    const mz_peer_outputs *peers, int32_t out_dtype, int64_t out_seq_stride,
+    int64_t out_head_stride, const void *q, int64_t q_seq_stride, int64_t q_head_stride,
+    void *k_pool, void *v_pool, const void *k_new, const void *v_new, int64_t new_seq_stride,
+    int64_t new_head_stride, const int32_t *block_tables, int32_t max_blocks_per_seq,
+    const int32_t *ctx_lens, int32_t n_seqs, int32_t n_heads, int32_t n_kv_heads,
+    int32_t head_dim, int32_t block_size, int64_t n_blocks, float scale, int32_t dtype,
+    int32_t num_warps, void *workspace, size_t workspace_bytes, int32_t *dev_err,
+    mz_stream_t stream) {
+  const char *fn = "mz_paged_append_decode_allgather";
+  if (!peers) return fail(MZ_ERR_INVALID_ARG, "%s: peers is null", fn);
+  if (peers->rank < 0 || peers->rank >= MZ_MAX_RANKS)
+    return fail(MZ_ERR_INVALID_ARG, "%s: rank %d out of range", fn, peers->rank);
+  DecodeArgs a = make_args(peers->out[peers->rank], out_dtype, out_seq_stride, 0, out_head_stride,
+                           q, q_seq_stride, 0, q_head_stride, 1, k_pool, v_pool, block_tables,
+                           max_blocks_per_seq, ctx_lens, n_seqs, n_heads, n_kv_heads, head_dim,
+                           block_size, n_blocks, scale, dtype, num_warps, dev_err, stream);
+  a.kn = k_new;
+  a.vn = v_new;
+  a.kn_sb = new_seq_stride;
+  a.kn_sh = new_head_stride;
+  a.peers = peers;
+  if (!k_new || !v_new) return fail(MZ_ERR_INVALID_ARG, "%s: null k_new / v_new", fn);
+  if (n_seqs <= 0)
+    return fail(MZ_ERR_INVALID_ARG, "%s: n_seqs must be positive (the peers wait for a signal)",
+                fn);
+  int64_t warps = 0;
+  WsLayout ws;
+  if (int rc = validate(a, fn, &warps, &ws)) return rc;
+  if (!workspace) return fail(MZ_ERR_WORKSPACE, "%s: workspace is null", fn);
+  if (workspace_bytes < ws.total)
+    return fail(MZ_ERR_WORKSPACE, "%s: workspace %zu bytes < required %zu", fn, workspace_bytes,
+                ws.total);
+  return launch(a, warps, ws, workspace, false, fn);
 }
 
 // ---------------------------------------------------------------------------

@@ -311,6 +311,80 @@ def paged_append_decode(q: torch.Tensor, k_pool: torch.Tensor, v_pool: torch.Ten
     return out
 
 
+def paged_append_decode_allgather(peers: "nat.PeerOutputs", q: torch.Tensor,
+                                  k_pool: torch.Tensor, v_pool: torch.Tensor,
+                                  k_new: torch.Tensor, v_new: torch.Tensor,
+                                  block_tables: torch.Tensor, ctx_lens: torch.Tensor,
+                                  out_seq_stride: int, out_head_stride: int,
+                                  out_dtype: torch.dtype, scale: float | None = None,
+                                  num_warps: int = 0,
+                                  workspace: torch.Tensor | None = None) -> None:
+    """paged_append_decode whose output rows go to every rank's gathered
+    buffer (``peers.out[r]``: this rank's head block there) and whose last
+    warp signals the peers (mz_paged_append_decode_allgather); follow it with
+    ``peer_wait`` before reading the gathered buffer."""
+    n_blocks, Hkv, bs, D = _check_pools(k_pool, v_pool)
+    if q.dim() != 3 or q.shape[2] != D or q.stride(-1) != 1 or q.dtype != k_pool.dtype:
+        raise ValueError(f"q must be [B, Hq, {D}] of the pool dtype with unit last stride")
+    B, Hq, _ = q.shape
+    if B == 0:
+        raise ValueError("an all-gather launch needs at least one sequence")
+    if k_new.shape != (B, Hkv, D) or v_new.shape != (B, Hkv, D):
+        raise ValueError(f"k_new/v_new must be [{B}, {Hkv}, {D}]")
+    if k_new.dtype != k_pool.dtype or v_new.dtype != k_pool.dtype:
+        raise ValueError("k_new/v_new dtype must match the pools")
+    if k_new.stride() != v_new.stride() or k_new.stride(2) != 1:
+        k_new, v_new = k_new.contiguous(), v_new.contiguous()
+    _as_i32(block_tables, k_pool.device, "block_tables")
+    _as_i32(ctx_lens, k_pool.device, "ctx_lens")
+    if scale is None:
+        scale = D ** -0.5
+    dev = _dev_index(q)
+    if workspace is None:
+        workspace = decode_workspace(B, Hkv, Hq // Hkv, D, dev, num_warps)
+    nat.call("mz_paged_append_decode_allgather", ctypes.byref(peers), dtype_code(out_dtype),
+             out_seq_stride, out_head_stride, q.data_ptr(), q.stride(0), q.stride(1),
+             k_pool.data_ptr(), v_pool.data_ptr(), k_new.data_ptr(), v_new.data_ptr(),
+             k_new.stride(0), k_new.stride(1), block_tables.data_ptr(), block_tables.shape[1],
+             ctx_lens.data_ptr(), B, Hq, Hkv, D, bs, n_blocks, float(scale),
+             dtype_code(q.dtype), num_warps, workspace.data_ptr(), workspace.numel(),
+             error_word(dev).data_ptr(), _stream(dev))
+    _after(dev)
+
+
+def peer_wait(signal: torch.Tensor, n_ranks: int, rank: int, epoch: int,
+              timeout_s: float = 2.0) -> None:
+    """Enqueue the bounded wait for every peer's signal word to reach
+    ``epoch`` (mz_peer_wait); a timeout shows up as a device error."""
+    if signal.dtype != torch.int32 or signal.numel() < n_ranks or not signal.is_cuda:
+        raise ValueError(f"signal must be a CUDA int32 tensor of at least {n_ranks} words")
+    dev = _dev_index(signal)
+    nat.call("mz_peer_wait", signal.data_ptr(), n_ranks, rank, epoch & 0xFFFFFFFF,
+             int(timeout_s * 1e9), error_word(dev).data_ptr(), _stream(dev))
+    _after(dev)
+
+
+def ipc_export(t: torch.Tensor) -> tuple[bytes, int]:
+    """(handle, byte offset) of the device allocation holding ``t``'s data."""
+    h = ctypes.create_string_buffer(nat.MZ_IPC_HANDLE_BYTES)
+    off = ctypes.c_uint64()
+    nat.call("mz_ipc_export", t.data_ptr(), h, ctypes.byref(off))
+    return h.raw, int(off.value)
+
+
+def ipc_open(handle: bytes, offset: int) -> tuple[int, int]:
+    """Map a peer's exported allocation on the current device: (base, ptr)."""
+    if len(handle) != nat.MZ_IPC_HANDLE_BYTES:
+        raise ValueError("bad IPC handle length")
+    base, ptr = ctypes.c_void_p(), ctypes.c_void_p()
+    nat.call("mz_ipc_open", handle, offset, ctypes.byref(base), ctypes.byref(ptr))
+    return int(base.value), int(ptr.value)
+
+
+def ipc_close(base: int) -> None:
+    nat.call("mz_ipc_close", base)
+
+
 # ---------------------------------------------------------------------------
 # Quantised KV
 # ---------------------------------------------------------------------------
