@@ -362,20 +362,56 @@ struct UnitReader {
   }
 };
 
-// After this warp's piece of pair bh has been written to its slot: count the
-// arrival; the warp that brings the count to nparts merges every piece's
-// (m, l, O) (slots uf + bh .. uf + nparts - 1 + bh) into the output and resets
-// the counter.
-template <int D, bool GATHER = false>
-__device__ __forceinline__ void arrive_and_merge(const Params &p, const Cursor &cc, int bh, int uf,
-                                                 int nparts, int lane) {
+// ---------------------------------------------------------------------------
+// Merge of split pairs.  After a warp has written its piece of pair bh to its
+// slot it counts its arrival; the warp that brings the count to nparts owns
+// the merge of every piece's (m, l, O) (slots uf + bh .. uf + nparts - 1 + bh,
+// consecutive) into the output, and resets the counter.
+//
+// Most pieces end where their warp's unit ends, so merges cluster at the end
+// of the kernel and their latency would be its tail.  The owner therefore
+// records the merge in a per-warp list in shared memory and carries on
+// streaming; when its tile loop is over (its stage ring idle) it runs the list,
+// staging each pair's partials into the ring with cp.async -- one round trip
+// for all of them -- and combining them from shared memory.  A list that is
+// full falls back to merging at once from global memory.
+// ---------------------------------------------------------------------------
+constexpr int kMaxDeferred = 8;  // deferred merges per warp
+
+struct Deferred {
+  int b, h, uf, nparts;
+};
+
+// Counts this warp's arrival for pair bh; true for the warp that owns the merge.
+__device__ __forceinline__ bool arrive(const Params &p, int bh, int nparts, int lane) {
   __threadfence();
   __syncwarp();
   int old = 0;
   if (lane == 0) old = atomicAdd(p.counters + bh, 1);
   old = __shfl_sync(0xffffffffu, old, 0);
-  if (old != nparts - 1) return;
+  if (old != nparts - 1) return false;
   __threadfence();
+  return true;
+}
+
+// Combine of one piece (m, l, O-slice) into the running (M, Ls, acc): the
+// online-softmax merge, pieces taken in slot order.
+__device__ __forceinline__ void merge_piece(float &M, float &Ls, float4 &acc, float2 ml, float4 o) {
+  const float Mn = fmaxf(M, ml.x);
+  const float sa = fast_exp2(M - Mn), sb = fast_exp2(ml.x - Mn);
+  Ls = Ls * sa + ml.y * sb;
+  acc.x = acc.x * sa + o.x * sb;
+  acc.y = acc.y * sa + o.y * sb;
+  acc.z = acc.z * sa + o.z * sb;
+  acc.w = acc.w * sa + o.w * sb;
+  M = Mn;
+}
+
+// Merge straight from global memory (the fallback).
+template <int D, bool GATHER>
+__device__ __forceinline__ void merge_global(const Params &p, int b, int h, int uf, int nparts,
+                                             int lane) {
+  const int bh = b * p.Hkv + h;
   const int E = p.rows * D;
   for (int e = 4 * lane; e < E; e += 128) {
     const int r = e / D, d = e - (e / D) * D;
@@ -385,22 +421,119 @@ __device__ __forceinline__ void arrive_and_merge(const Params &p, const Cursor &
       const int64_t sl = (int64_t)uf + k + bh;
       const float2 mlk = __ldcg(reinterpret_cast<const float2 *>(p.ml + (sl * p.rows + r) * 2));
       const float4 ok = __ldcg(reinterpret_cast<const float4 *>(p.part + (sl * p.rows + r) * D + d));
-      const float Mn = fmaxf(M, mlk.x);
-      const float sa = fast_exp2(M - Mn), sb = fast_exp2(mlk.x - Mn);
-      Ls = Ls * sa + mlk.y * sb;
-      acc.x = acc.x * sa + ok.x * sb;
-      acc.y = acc.y * sa + ok.y * sb;
-      acc.z = acc.z * sa + ok.z * sb;
-      acc.w = acc.w * sa + ok.w * sb;
-      M = Mn;
+      merge_piece(M, Ls, acc, mlk, ok);
     }
     const float inv = 1.f / Ls;
-    const int64_t o = row_offset(p.o_sb, p.o_st, p.o_sh, cc.b, cc.h, r, p.G) + d;
+    const int64_t o = row_offset(p.o_sb, p.o_st, p.o_sh, b, h, r, p.G) + d;
     store_pair(p, o, acc.x * inv, acc.y * inv);
     store_pair(p, o + 2, acc.z * inv, acc.w * inv);
   }
-  if constexpr (GATHER) forward_rows<D>(p, cc.b, cc.h, lane);
+  if constexpr (GATHER) forward_rows<D>(p, b, h, lane);
   if (lane == 0) p.counters[bh] = 0;
+}
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void *src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async8(uint32_t dst, const void *src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+}
+
+// Merge with the pieces staged in shared memory `buf` (buf_bytes, 16-byte
+// aligned, idle), as many pieces per round trip as fit.
+template <int D, bool GATHER>
+__device__ __forceinline__ void merge_staged(const Params &p, int b, int h, int uf, int nparts,
+                                             uint8_t *buf, int buf_bytes, int lane) {
+  const int bh = b * p.Hkv + h;
+  const int part_bytes = p.rows * D * 4;
+  const int per = buf_bytes / (part_bytes + p.rows * 8);
+  if (per < 1) {
+    merge_global<D, GATHER>(p, b, h, uf, nparts, lane);
+    return;
+  }
+  constexpr int kIt = 16 * D / 128;  // 4-element steps per lane for up to 16 rows
+  const int E = p.rows * D;
+  float M[kIt], Ls[kIt];
+  float4 acc[kIt];
+#pragma unroll
+  for (int it = 0; it < kIt; ++it) {
+    M[it] = -INFINITY;
+    Ls[it] = 0.f;
+    acc[it] = make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  const uint32_t buf_s = smem_u32(buf);
+  const float *part_s = reinterpret_cast<const float *>(buf);
+  for (int k0 = 0; k0 < nparts; k0 += per) {
+    const int cnt = min(per, nparts - k0);
+    const int64_t slot = (int64_t)uf + k0 + bh;
+    const uint8_t *src = reinterpret_cast<const uint8_t *>(p.part + slot * p.rows * D);
+    const int pb = cnt * part_bytes;
+    __syncwarp();  // the previous round's reads of buf are done
+    for (int x = 16 * lane; x < pb; x += 512) cp_async16(buf_s + x, src + x);
+    const float *mls = p.ml + slot * p.rows * 2;
+    for (int x = lane; x < cnt * p.rows; x += 32) cp_async8(buf_s + pb + 8 * x, mls + 2 * x);
+    cp_async_wait_all();
+    __syncwarp();
+    const float2 *ml_s = reinterpret_cast<const float2 *>(buf + pb);
+    for (int k = 0; k < cnt; ++k) {
+#pragma unroll
+      for (int it = 0; it < kIt; ++it) {
+        const int e = 4 * lane + 128 * it;
+        if (e < E) {
+          const float2 ml = ml_s[k * p.rows + e / D];
+          const float4 o = *reinterpret_cast<const float4 *>(part_s + k * (p.rows * D) + e);
+          merge_piece(M[it], Ls[it], acc[it], ml, o);
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int it = 0; it < kIt; ++it) {
+    const int e = 4 * lane + 128 * it;
+    if (e < E) {
+      const int r = e / D, d = e - r * D;
+      const float inv = 1.f / Ls[it];
+      const int64_t o = row_offset(p.o_sb, p.o_st, p.o_sh, b, h, r, p.G) + d;
+      store_pair(p, o, acc[it].x * inv, acc[it].y * inv);
+      store_pair(p, o + 2, acc[it].z * inv, acc[it].w * inv);
+    }
+  }
+  if constexpr (GATHER) forward_rows<D>(p, b, h, lane);
+  if (lane == 0) p.counters[bh] = 0;
+}
+
+// In the tile loop, after this warp's piece of the pair has been written.
+template <int D, bool GATHER = false>
+__device__ __forceinline__ void arrive_or_defer(const Params &p, const Cursor &cc, int bh, int uf,
+                                                int nparts, int lane, Deferred *dq, int &nd) {
+  if (!arrive(p, bh, nparts, lane)) return;
+  if (nd < kMaxDeferred) {
+    if (lane == 0) dq[nd] = Deferred{cc.b, cc.h, uf, nparts};
+    ++nd;
+  } else {
+    merge_global<D, GATHER>(p, cc.b, cc.h, uf, nparts, lane);
+  }
+}
+
+// After the tile loop: run the deferred merges with the idle stage ring `buf`.
+// `ring_idle` false (a wait gave up with copies maybe still landing): leave
+// the outputs and only reset the pairs' counters.
+template <int D, bool GATHER = false>
+__device__ __forceinline__ void run_deferred(const Params &p, const Deferred *dq, int nd,
+                                             uint8_t *buf, int buf_bytes, bool ring_idle,
+                                             int lane) {
+  __syncwarp();
+  for (int j = 0; j < nd; ++j) {
+    const Deferred d = dq[j];
+    if (ring_idle) {
+      merge_staged<D, GATHER>(p, d.b, d.h, d.uf, d.nparts, buf, buf_bytes, lane);
+    } else if (lane == 0) {
+      p.counters[d.b * p.Hkv + d.h] = 0;
+    }
+  }
 }
 
 // Bounded wait on a stage; on timeout, record it and let this warp's copies

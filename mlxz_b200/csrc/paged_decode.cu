@@ -38,7 +38,8 @@ struct Cfg {
   static constexpr int kSmemTiles = kWarps * kStages * kStageBytes;
   static constexpr int kSmemBars = kWarps * kStages * 8;
   static constexpr int kSmemUnits = kWarps * kUnitQ * 32;
-  static constexpr int kSmemBytes = kSmemTiles + kSmemBars + kSmemUnits + 1024;  // + align
+  static constexpr int kSmemDefer = kWarps * kMaxDeferred * static_cast<int>(sizeof(Deferred));
+  static constexpr int kSmemBytes = kSmemTiles + kSmemBars + kSmemUnits + kSmemDefer + 1024;
 };
 
 template <int D, bool BF16, bool GATHER>
@@ -60,6 +61,9 @@ __device__ __forceinline__ void decode_tiles(const CUtensorMap &tmK, const CUten
   uint8_t *stages = smem + warp * S * C::kStageBytes;
   uint64_t *bars = reinterpret_cast<uint64_t *>(smem + C::kSmemTiles) + warp * S;
   Unit *uq = reinterpret_cast<Unit *>(smem + C::kSmemTiles + C::kSmemBars) + warp * kUnitQ;
+  Deferred *dq = reinterpret_cast<Deferred *>(smem + C::kSmemTiles + C::kSmemBars + C::kSmemUnits) +
+                 warp * kMaxDeferred;
+  int nd = 0;  // merges this warp owns, run after its tile loop
   const uint32_t bar0 = smem_u32(bars);
   const uint32_t stage0 = smem_u32(stages);
 
@@ -108,6 +112,7 @@ __device__ __forceinline__ void decode_tiles(const CUtensorMap &tmK, const CUten
   bool seg_first = true;
 
   sch.refill<S>(p, 0, issue);
+  bool ring_idle = true;
   for (int i = 0; i < sch.issued; ++i) {
     const int s = i % S;
     if (ur.need_pop()) {
@@ -137,7 +142,10 @@ __device__ __forceinline__ void decode_tiles(const CUtensorMap &tmK, const CUten
       }
     }
 
-    if (!wait_stage<S>(p, bar0, i, sch.issued, lane)) return;
+    if (!wait_stage<S>(p, bar0, i, sch.issued, lane)) {
+      ring_idle = false;
+      break;
+    }
 
     uint8_t *kt = stages + s * C::kStageBytes;
     uint8_t *vt = kt + C::kTileBytes;
@@ -316,7 +324,7 @@ __device__ __forceinline__ void decode_tiles(const CUtensorMap &tmK, const CUten
                 make_float2(oacc[n][2], oacc[n][3]);
           if (cq == 0) *reinterpret_cast<float2 *>(mlr + 2 * (g + 8)) = make_float2(m1, L1);
         }
-        arrive_and_merge<D, GATHER>(p, cc, bh, uf, ul - uf + 1, lane);
+        arrive_or_defer<D, GATHER>(p, cc, bh, uf, ul - uf + 1, lane, dq, nd);
       }
       seg_first = true;  // the next tile starts a new piece
     }
@@ -326,6 +334,7 @@ __device__ __forceinline__ void decode_tiles(const CUtensorMap &tmK, const CUten
     advance(ur.cc, p);
     sch.refill<S>(p, i + 1, issue);
   }
+  run_deferred<D, GATHER>(p, dq, nd, stages, S * C::kStageBytes, ring_idle, lane);
 }
 
 template <int D, bool BF16>

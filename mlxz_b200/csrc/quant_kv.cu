@@ -177,7 +177,9 @@ struct QCfg {
   static constexpr int kSmemScales = kWarps * kStages * kScaleStage;
   static constexpr int kSmemBars = kWarps * kStages * 8;
   static constexpr int kSmemUnits = kWarps * kUnitQ * 32;
-  static constexpr int kSmemBytes = kSmemCodes + kSmemScales + kSmemBars + kSmemUnits + 1024;
+  static constexpr int kSmemDefer = kWarps * kMaxDeferred * static_cast<int>(sizeof(Deferred));
+  static constexpr int kSmemBytes =
+      kSmemCodes + kSmemScales + kSmemBars + kSmemUnits + kSmemDefer + 1024;
   // P' = p * s_v is stored in fp16 scaled by this power of two (keeps small
   // weights out of fp16 subnormals; removed exactly at the end).
   static constexpr float kPScale = BITS == 8 ? 256.f : 16.f;
@@ -253,6 +255,10 @@ __global__ void __launch_bounds__(kWarps * 32, QCfg<D, BITS, NR>::kCtas)
   uint64_t *bars = reinterpret_cast<uint64_t *>(smem + C::kSmemCodes + C::kSmemScales) + warp * S;
   Unit *uq = reinterpret_cast<Unit *>(smem + C::kSmemCodes + C::kSmemScales + C::kSmemBars) +
              warp * kUnitQ;
+  Deferred *dq = reinterpret_cast<Deferred *>(smem + C::kSmemCodes + C::kSmemScales +
+                                              C::kSmemBars + C::kSmemUnits) +
+                 warp * kMaxDeferred;
+  int nd = 0;  // merges this warp owns, run after its tile loop
   const uint32_t bar0 = smem_u32(bars);
   const uint32_t code0 = smem_u32(codes);
   const uint32_t scale0 = smem_u32(scales);
@@ -307,6 +313,7 @@ __global__ void __launch_bounds__(kWarps * 32, QCfg<D, BITS, NR>::kCtas)
   bool seg_first = true;
 
   sch.refill<S>(p, 0, issue);
+  bool ring_idle = true;
   for (int i = 0; i < sch.issued; ++i) {
     const int s = i % S;
     if (ur.need_pop()) {
@@ -363,7 +370,10 @@ __global__ void __launch_bounds__(kWarps * 32, QCfg<D, BITS, NR>::kCtas)
       }
     }
 
-    if (!wait_stage<S>(p, bar0, i, sch.issued, lane)) return;
+    if (!wait_stage<S>(p, bar0, i, sch.issued, lane)) {
+      ring_idle = false;
+      break;
+    }
 
     const uint8_t *kd = codes + s * C::kCodeStage, *vd = kd + C::TD;
     const uint8_t *ss = scales + s * C::kScaleStage;
@@ -609,7 +619,7 @@ __global__ void __launch_bounds__(kWarps * 32, QCfg<D, BITS, NR>::kCtas)
             *reinterpret_cast<float2 *>(p.ml + (slot * p.rows + row) * 2) =
                 make_float2(mrow[nr][rs], L);
         }
-      if (!full) arrive_and_merge<D>(p, cc, bh, uf, ul - uf + 1, lane);
+      if (!full) arrive_or_defer<D>(p, cc, bh, uf, ul - uf + 1, lane, dq, nd);
       seg_first = true;
     }
 
@@ -618,6 +628,7 @@ __global__ void __launch_bounds__(kWarps * 32, QCfg<D, BITS, NR>::kCtas)
     advance(ur.cc, p);
     sch.refill<S>(p, i + 1, issue);
   }
+  run_deferred<D>(p, dq, nd, codes, S * C::kCodeStage, ring_idle, lane);
 }
 
 template <int D, int BITS, int NR>
