@@ -144,8 +144,12 @@ MZ_API int mz_paged_decode_workspace_size(int32_t n_seqs, int32_t n_kv_heads, in
  * alignment, q and out 4-byte (8-byte for F32 out) alignment and even strides.
  * A sequence with ctx_lens[b] == 0 gets zeros.
  * workspace: >= mz_paged_decode_workspace_size bytes, zero-filled before its
- * first use; every successful call leaves its counter region zeroed again.
- * After a call that set a dev_err bit, zero the workspace before reuse.
+ * first use; every successful call leaves its counter region -- the first
+ * 4 * (n_seqs * n_kv_heads + 2) bytes -- zeroed again.  Where that region
+ * ends depends on the sizes, so a workspace reused by a call with other
+ * n_seqs, n_kv_heads, rows or head_dim must be zero-filled again first (its
+ * partials may lie where the new counters go).  After a call that set a
+ * dev_err bit, zero the workspace before reuse.
  * num_warps: persistent warps to launch (0 = one full wave of the device). */
 MZ_API int mz_paged_decode(void *out, int32_t out_dtype, int64_t out_seq_stride, int64_t out_tok_stride,
                     int64_t out_head_stride, const void *q, int64_t q_seq_stride,

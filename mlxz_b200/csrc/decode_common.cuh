@@ -10,7 +10,9 @@
 //     of T, all of it by default), one contiguous share of per_s = ceil(T_s / W)
 //     tiles per warp (W persistent warps);
 //   * dynamic units: the rest, if any, in chunks of C tiles that warps claim
-//     with an atomic ticket once their static share is done.
+//     with an atomic ticket once their static share is done.  C is at least
+//     1/64 of the longest pair; when that is more than a quarter of a warp's
+//     fair share (few, long pairs) the split is all static.
 // A pair that lies inside one unit is finished by the warp that runs the unit.
 // A pair cut by unit boundaries leaves one partial (running max m, running sum
 // l, unnormalised O) per piece in the workspace at slot (unit + pair); the
@@ -34,6 +36,7 @@ constexpr int kWarps = 4;           // warps per CTA, each an independent tile s
 constexpr int kTileTok = 16;        // tokens per tile
 constexpr int kUnitQ = 8;           // per-warp ring of unit descriptors
 constexpr uint64_t kTimeoutNs = 2000000000ull;  // 2 s bound on any single wait
+constexpr int kMaxDynPieces = 64;  // dynamic chunks cut a pair into at most this many pieces
 
 struct Params {
   void *out;
@@ -67,7 +70,7 @@ struct Params {
   int32_t *err;
   // all-gather over peer memory (n_peer > 0): every output store also goes to
   // peer_out[r] (the same rows in rank r's gathered buffer, mapped into this
-  // GPU's address space); once all warps have stored, the last one publishes
+  // GPU's address space); once all blocks have stored, the last one publishes
   // `epoch` into each peer_sig[r] (rank r's signal word for this rank).
   int n_peer = 0;
   void *peer_out[MZ_MAX_RANKS - 1] = {};
@@ -117,26 +120,45 @@ __device__ __forceinline__ void advance(Cursor &c, const Params &p) {
   }
 }
 
-// Cursor at flat tile x (0 <= x < T), found with a warp scan over sequences.
+// Cursor at flat tile x (0 <= x < T).  Two rounds of independent loads: lane
+// l sums the tiles of sequences [l*K, l*K + K) (K = ceil(B/32)), a warp scan
+// finds the lane whose range holds x, then the range is scanned 32 sequences
+// at a time (once when B <= 1024).
 __device__ __forceinline__ Cursor locate(const Params &p, int x, int lane) {
-  int base = 0, bf = 0;
-  for (int b0 = 0; b0 < p.B; b0 += 32) {
+  const int K = (p.B + 31) >> 5;
+  const int lo = min(lane * K, p.B), hi = min(lo + K, p.B);
+  int s = 0;
+#pragma unroll 4
+  for (int b = lo; b < hi; ++b) s += ntiles_of(clamped_ctx(p, b));
+  s *= p.Hkv;
+  int incl = s;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += y;
+  }
+  const unsigned owner = __ballot_sync(0xffffffffu, incl > x);
+  const int L = owner ? __ffs(owner) - 1 : 31;
+  int base = __shfl_sync(0xffffffffu, incl - s, L);
+  const int rlo = __shfl_sync(0xffffffffu, lo, L), rhi = __shfl_sync(0xffffffffu, hi, L);
+  int bf = rlo;
+  for (int b0 = rlo; b0 < rhi; b0 += 32) {
     const int b = b0 + lane;
-    const int c = (b < p.B) ? ntiles_of(clamped_ctx(p, b)) * p.Hkv : 0;
-    int incl = c;
+    const int c = (b < rhi) ? ntiles_of(clamped_ctx(p, b)) * p.Hkv : 0;
+    int in2 = c;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
-      const int y = __shfl_up_sync(0xffffffffu, incl, o);
-      if (lane >= o) incl += y;
+      const int y = __shfl_up_sync(0xffffffffu, in2, o);
+      if (lane >= o) in2 += y;
     }
-    const unsigned m = __ballot_sync(0xffffffffu, base + incl > x);
+    const unsigned m = __ballot_sync(0xffffffffu, base + in2 > x);
     if (m) {
-      const int L = __ffs(m) - 1;
-      base += __shfl_sync(0xffffffffu, incl - c, L);
-      bf = b0 + L;
+      const int L2 = __ffs(m) - 1;
+      base += __shfl_sync(0xffffffffu, in2 - c, L2);
+      bf = b0 + L2;
       break;
     }
-    base += __shfl_sync(0xffffffffu, incl, 31);
+    base += __shfl_sync(0xffffffffu, in2, 31);
   }
   Cursor cur;
   cur.b = bf;
@@ -250,10 +272,17 @@ struct Sched {
     wid = wid_;
     W = W_;
     uq = uq_;
-    int t = 0;
-    for (int b = lane; b < p.B; b += 32) t += ntiles_of(clamped_ctx(p, b));
+    int t = 0, longest = 0;
+    for (int b = lane; b < p.B; b += 32) {
+      const int n = ntiles_of(clamped_ctx(p, b));
+      t += n;
+      longest = max(longest, n);
+    }
 #pragma unroll
-    for (int o = 16; o; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+    for (int o = 16; o; o >>= 1) {
+      t += __shfl_xor_sync(0xffffffffu, t, o);
+      longest = max(longest, __shfl_xor_sync(0xffffffffu, longest, o));
+    }
     tot = t * p.Hkv;
     if (tot == 0) return false;
     // static share: ceil(T * pct / 100 / W) tiles per warp (the last shares
@@ -261,9 +290,21 @@ struct Sched {
     const int64_t target = (int64_t)tot * p.static_pct / 100;
     per_s = static_cast<int>((target + W - 1) / W);
     t_s = static_cast<int>(min((int64_t)per_s * W, (int64_t)tot));
-    const int dyn = tot - t_s;
+    int dyn = tot - t_s;
     chunk = (dyn + p.max_chunks - 1) / p.max_chunks;
     if (chunk < p.min_chunk) chunk = p.min_chunk;
+    // The dynamic chunks cut a pair into at most kMaxDynPieces pieces (a merge
+    // of many pieces is the owner's tail).  When that needs chunks longer than
+    // a quarter of a warp's fair share they would no longer even out the
+    // finish times, so the split is all static.
+    const int need = (longest + kMaxDynPieces - 1) / kMaxDynPieces;
+    if (chunk < need) chunk = need;
+    const int fair = static_cast<int>((tot + W - 1) / W);
+    if (dyn > 0 && 4 * chunk > fair) {
+      per_s = fair;
+      t_s = tot;
+      dyn = 0;
+    }
     n_chunks = (dyn + chunk - 1) / chunk;
     ticket = p.counters + (int64_t)p.B * p.Hkv;
     p_left = pushed = issued = 0;

@@ -17,10 +17,11 @@
 // Roofline: each tile moves 2 * 16 * D * 2 bytes (K and V) and needs
 // 4 * rows * 16 * D flops; with rows = 4 (GQA group 4) that is 2 flop/byte,
 // so the kernel is HBM-bound and the bulk-copy pipeline depth is what matters.
-// Measured on B200 at the 8B shape, the per-warp tile rate is uniform to a
-// few percent, and a dynamic chunk is too coarse (one warp streams a 16-tile
-// chunk in ~23 us) to shorten the tail, so the default hands out everything
-// statically; the dynamic path stays for tuning and is tested.
+// Measured on B200, per-warp streaming rates differ by 5-10 %, which leaves a
+// tail, but dynamic chunks cost more than they save (8B shape, batch 64: 196
+// us static, 237 us with 15 % in 9-tile chunks: every chunk adds a piece to
+// merge), so the default hands out everything statically; merges of split
+// pairs are deferred to the end of each warp's loop.
 #include "decode_common.cuh"
 
 #ifndef MZ_DECODE_STAGES_D128

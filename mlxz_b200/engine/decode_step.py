@@ -174,8 +174,11 @@ class PagedDecodeStep:
         self.lengths = torch.zeros(self.B, dtype=torch.int32, device=dev)
         self.sync_metadata()
         G = n_heads // store.n_kv_heads
+        # a workspace of its own: a step's launches never share one with
+        # launches of other sizes
         self.workspace = ops.decode_workspace(self.B, store.n_kv_heads, G, store.head_dim,
-                                              dev.index if dev.index is not None else 0)
+                                              dev.index if dev.index is not None else 0,
+                                              shared=False)
         self._dev_in = None
         self._graph = None
 
@@ -337,7 +340,8 @@ class QuantizedPagedDecodeStep(PagedDecodeStep):
         G = n_heads // store.n_kv_heads
         self.workspace = ops.decode_q_workspace(self.B, store.n_kv_heads, G, store.head_dim,
                                                 store.bits,
-                                                dev.index if dev.index is not None else 0)
+                                                dev.index if dev.index is not None else 0,
+                                                shared=False)
         self._dev_in = None
 
     def layer(self, l: int, q: torch.Tensor, k_new: torch.Tensor, v_new: torch.Tensor,

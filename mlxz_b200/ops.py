@@ -11,6 +11,7 @@ from __future__ import annotations
 import ctypes
 import math
 import os
+from collections import OrderedDict
 
 import torch
 
@@ -21,7 +22,29 @@ _DTYPES = {torch.float16: nat.MZ_DTYPE_F16, torch.bfloat16: nat.MZ_DTYPE_BF16,
 _DEBUG = os.environ.get("MLXZ_B200_DEBUG", "0") not in ("", "0")
 
 _err_words: dict[int, torch.Tensor] = {}
-_workspaces: dict[tuple[int, int], torch.Tensor] = {}
+# Decode workspaces handed out when the caller passes none, one per exact
+# problem layout.  The kernels need the arrival counters and scheduler words at
+# the front of a workspace to be zero at launch (each launch leaves them zero),
+# and where those words sit depends on the problem sizes: a workspace last used
+# with other sizes may hold partials there.  So a workspace is never shared
+# between layouts.  A few layouts are kept, least recently used dropped first.
+_WS_KEEP = 16
+_workspaces: "OrderedDict[tuple, torch.Tensor]" = OrderedDict()
+_qworkspaces: "OrderedDict[tuple, torch.Tensor]" = OrderedDict()
+
+
+def _layout_workspace(cache, key: tuple, need: int, device: int, shared: bool) -> torch.Tensor:
+    if not shared:
+        return torch.zeros(max(need, 256), dtype=torch.uint8, device=f"cuda:{device}")
+    ws = cache.get(key)
+    if ws is None:
+        ws = torch.zeros(max(need, 256), dtype=torch.uint8, device=f"cuda:{device}")
+        cache[key] = ws
+        while len(cache) > _WS_KEEP:
+            cache.popitem(last=False)
+    else:
+        cache.move_to_end(key)
+    return ws
 
 
 def dtype_code(dt: torch.dtype) -> int:
@@ -193,18 +216,14 @@ def kv_gather(k_pool: torch.Tensor, v_pool: torch.Tensor, block_tables: torch.Te
 # ---------------------------------------------------------------------------
 
 def decode_workspace(n_seqs: int, n_kv_heads: int, rows: int, head_dim: int, device: int,
-                     num_warps: int = 0) -> torch.Tensor:
-    """A zero-initialised workspace big enough for these sizes (cached, grows)."""
+                     num_warps: int = 0, shared: bool = True) -> torch.Tensor:
+    """A zero-initialised decode workspace for exactly these sizes: the one
+    kept for this layout (``shared``), or a new one the caller owns."""
     size = ctypes.c_size_t(0)
     nat.call("mz_paged_decode_workspace_size", n_seqs, n_kv_heads, rows, head_dim, num_warps,
              device, ctypes.byref(size))
-    need = int(size.value)
-    key = (device, 0)
-    ws = _workspaces.get(key)
-    if ws is None or ws.numel() < need:
-        ws = torch.zeros(max(need, 1 << 20), dtype=torch.uint8, device=f"cuda:{device}")
-        _workspaces[key] = ws
-    return ws
+    key = (device, n_seqs, n_kv_heads, rows, head_dim, num_warps)
+    return _layout_workspace(_workspaces, key, int(size.value), device, shared)
 
 
 def reset_workspaces() -> None:
@@ -462,20 +481,14 @@ def kv_quant_append_paged(pools, keys: torch.Tensor, values: torch.Tensor,
     _after(dev)
 
 
-_qworkspaces: dict[int, torch.Tensor] = {}
-
-
 def decode_q_workspace(n_seqs: int, n_kv_heads: int, rows: int, head_dim: int, bits: int,
-                       device: int, num_warps: int = 0) -> torch.Tensor:
+                       device: int, num_warps: int = 0, shared: bool = True) -> torch.Tensor:
+    """As ``decode_workspace``, for the quantised decode."""
     size = ctypes.c_size_t(0)
     nat.call("mz_paged_decode_q_workspace_size", n_seqs, n_kv_heads, rows, head_dim, bits,
              num_warps, device, ctypes.byref(size))
-    need = int(size.value)
-    ws = _qworkspaces.get(device)
-    if ws is None or ws.numel() < need:
-        ws = torch.zeros(max(need, 1 << 20), dtype=torch.uint8, device=f"cuda:{device}")
-        _qworkspaces[device] = ws
-    return ws
+    key = (device, n_seqs, n_kv_heads, rows, head_dim, bits, num_warps)
+    return _layout_workspace(_qworkspaces, key, int(size.value), device, shared)
 
 
 def paged_decode_q(q: torch.Tensor, pools, block_tables: torch.Tensor, ctx_lens: torch.Tensor,

@@ -379,6 +379,52 @@ def test_decode_many_ragged_sequences_dynamic_schedule(cuda, monkeypatch, nw, st
         assert attn_err(out, ref) <= ATOL_REL
 
 
+@pytest.mark.parametrize("G,static_pct", [(8, 100), (8, 85), (16, 85), (4, 85)])
+def test_decode_few_long_pairs_many_piece_merges(cuda, monkeypatch, G, static_pct):
+    """Three sequences of up to 30k tokens on the full default grid: every
+    pair is cut into hundreds of pieces, so a merge stages its pieces into the
+    stage ring over many rounds (up to 16 rows per piece); the dynamic split
+    falls back to static here (pairs far longer than a warp's share)."""
+    monkeypatch.setenv("MLXZ_B200_DECODE_STATIC_PCT", str(static_pct))
+    dtype, D, Hkv, bs = "bf16", 128, 1, 16
+    ctx = [30000, 20011, 5]
+    case = random_paged_case(71, len(ctx), Hkv, D, bs, ctx, dtype, G=G)
+    kp, vp = to_dev(case["kp"], dtype, cuda), to_dev(case["vp"], dtype, cuda)
+    q = to_dev(case["q"][:, 0], dtype, cuda)
+    tables = torch.from_numpy(case["tables"]).to(cuda)
+    ctx_t = torch.from_numpy(case["ctx"]).to(cuda)
+    ref = opaged.paged_decode(case["q"][:, 0], case["kp"], case["vp"], case["tables"], case["ctx"],
+                              dtype)
+    for _ in range(2):
+        out = ops.paged_decode(q, kp, vp, tables, ctx_t, out_dtype=torch.float32)
+        torch.cuda.synchronize()
+        ops.check_device_errors(0)
+        assert attn_err(out, ref) <= ATOL_REL
+
+
+def test_workspaces_of_different_sizes_do_not_mix(cuda):
+    """Calls with different pair counts and group sizes, interleaved, each
+    against the oracle: the workspaces handed out are per layout, so one
+    call's partials never sit where another expects zeroed counters."""
+    shapes = [(3, 1, 8, [30000, 77, 4100]), (40, 4, 4, None), (9, 8, 2, None)]
+    cases = []
+    for i, (B, Hkv, G, ctx) in enumerate(shapes):
+        ctx = ctx or [int(x) for x in rng.randint(90 + i, B, 1, 3000)]
+        case = random_paged_case(91 + i, B, Hkv, 128, 16, ctx, "bf16", G=G)
+        ref = opaged.paged_decode(case["q"][:, 0], case["kp"], case["vp"], case["tables"],
+                                  case["ctx"], "bf16")
+        dev = [to_dev(case[k], "bf16", cuda) for k in ("kp", "vp")]
+        cases.append((to_dev(case["q"][:, 0], "bf16", cuda), *dev,
+                      torch.from_numpy(case["tables"]).to(cuda),
+                      torch.from_numpy(case["ctx"]).to(cuda), ref))
+    for rnd in range(2):
+        for q, kp, vp, tables, ctx_t, ref in (cases if rnd == 0 else cases[::-1]):
+            out = ops.paged_decode(q, kp, vp, tables, ctx_t, out_dtype=torch.float32)
+            torch.cuda.synchronize()
+            ops.check_device_errors(0)
+            assert attn_err(out, ref) <= ATOL_REL
+
+
 def test_decode_step_multi_layer_with_table_growth(cuda):
     """PagedDecodeStep over 2 layers for 20 steps with advance(): appends cross
     block boundaries (tables grow through the BlockManager) and every step's
