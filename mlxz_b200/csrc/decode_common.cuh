@@ -120,45 +120,26 @@ __device__ __forceinline__ void advance(Cursor &c, const Params &p) {
   }
 }
 
-// Cursor at flat tile x (0 <= x < T).  Two rounds of independent loads: lane
-// l sums the tiles of sequences [l*K, l*K + K) (K = ceil(B/32)), a warp scan
-// finds the lane whose range holds x, then the range is scanned 32 sequences
-// at a time (once when B <= 1024).
+// Cursor at flat tile x (0 <= x < T), found with a warp scan over sequences.
 __device__ __forceinline__ Cursor locate(const Params &p, int x, int lane) {
-  const int K = (p.B + 31) >> 5;
-  const int lo = min(lane * K, p.B), hi = min(lo + K, p.B);
-  int s = 0;
-#pragma unroll 4
-  for (int b = lo; b < hi; ++b) s += ntiles_of(clamped_ctx(p, b));
-  s *= p.Hkv;
-  int incl = s;
-#pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    const int y = __shfl_up_sync(0xffffffffu, incl, o);
-    if (lane >= o) incl += y;
-  }
-  const unsigned owner = __ballot_sync(0xffffffffu, incl > x);
-  const int L = owner ? __ffs(owner) - 1 : 31;
-  int base = __shfl_sync(0xffffffffu, incl - s, L);
-  const int rlo = __shfl_sync(0xffffffffu, lo, L), rhi = __shfl_sync(0xffffffffu, hi, L);
-  int bf = rlo;
-  for (int b0 = rlo; b0 < rhi; b0 += 32) {
+  int base = 0, bf = 0;
+  for (int b0 = 0; b0 < p.B; b0 += 32) {
     const int b = b0 + lane;
-    const int c = (b < rhi) ? ntiles_of(clamped_ctx(p, b)) * p.Hkv : 0;
-    int in2 = c;
+    const int c = (b < p.B) ? ntiles_of(clamped_ctx(p, b)) * p.Hkv : 0;
+    int incl = c;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
-      const int y = __shfl_up_sync(0xffffffffu, in2, o);
-      if (lane >= o) in2 += y;
+      const int y = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += y;
     }
-    const unsigned m = __ballot_sync(0xffffffffu, base + in2 > x);
+    const unsigned m = __ballot_sync(0xffffffffu, base + incl > x);
     if (m) {
-      const int L2 = __ffs(m) - 1;
-      base += __shfl_sync(0xffffffffu, in2 - c, L2);
-      bf = b0 + L2;
+      const int L = __ffs(m) - 1;
+      base += __shfl_sync(0xffffffffu, incl - c, L);
+      bf = b0 + L;
       break;
     }
-    base += __shfl_sync(0xffffffffu, in2, 31);
+    base += __shfl_sync(0xffffffffu, incl, 31);
   }
   Cursor cur;
   cur.b = bf;
@@ -448,7 +429,8 @@ __device__ __forceinline__ void merge_piece(float &M, float &Ls, float4 &acc, fl
   M = Mn;
 }
 
-// Merge straight from global memory (the fallback).
+// Merge straight from global memory: the pieces are read four at a time, all
+// four loads in flight before the combine that needs them.
 template <int D, bool GATHER>
 __device__ __forceinline__ void merge_global(const Params &p, int b, int h, int uf, int nparts,
                                              int lane) {
@@ -458,11 +440,22 @@ __device__ __forceinline__ void merge_global(const Params &p, int b, int h, int 
     const int r = e / D, d = e - (e / D) * D;
     float M = -INFINITY, Ls = 0.f;
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int k = 0; k < nparts; ++k) {
-      const int64_t sl = (int64_t)uf + k + bh;
-      const float2 mlk = __ldcg(reinterpret_cast<const float2 *>(p.ml + (sl * p.rows + r) * 2));
-      const float4 ok = __ldcg(reinterpret_cast<const float4 *>(p.part + (sl * p.rows + r) * D + d));
-      merge_piece(M, Ls, acc, mlk, ok);
+    for (int k0 = 0; k0 < nparts; k0 += 4) {
+      float2 mlk[4];
+      float4 ok[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        mlk[j] = make_float2(-INFINITY, 0.f);
+        ok[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (k0 + j < nparts) {
+          const int64_t sl = (int64_t)uf + k0 + j + bh;
+          mlk[j] = __ldcg(reinterpret_cast<const float2 *>(p.ml + (sl * p.rows + r) * 2));
+          ok[j] = __ldcg(reinterpret_cast<const float4 *>(p.part + (sl * p.rows + r) * D + d));
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        if (k0 + j < nparts) merge_piece(M, Ls, acc, mlk[j], ok[j]);
     }
     const float inv = 1.f / Ls;
     const int64_t o = row_offset(p.o_sb, p.o_st, p.o_sh, b, h, r, p.G) + d;
@@ -547,11 +540,15 @@ __device__ __forceinline__ void merge_staged(const Params &p, int b, int h, int 
 }
 
 // In the tile loop, after this warp's piece of the pair has been written.
+// Small merges (rows * pieces <= kMergeNow) run at once; larger ones are
+// deferred while the list has room.
+constexpr int kMergeNow = 16;
+
 template <int D, bool GATHER = false>
 __device__ __forceinline__ void arrive_or_defer(const Params &p, const Cursor &cc, int bh, int uf,
                                                 int nparts, int lane, Deferred *dq, int &nd) {
   if (!arrive(p, bh, nparts, lane)) return;
-  if (nd < kMaxDeferred) {
+  if (p.rows * nparts > kMergeNow && nd < kMaxDeferred) {
     if (lane == 0) dq[nd] = Deferred{cc.b, cc.h, uf, nparts};
     ++nd;
   } else {
