@@ -212,11 +212,6 @@ __device__ __forceinline__ int tok_of(int m) {
 
 constexpr uint32_t kMagic = 0x64646464u;  // fp16 0x64xx = 1024 + xx
 
-__device__ __forceinline__ uint32_t h2_sub1024(uint32_t x) {
-  __half2 h = *reinterpret_cast<__half2 *>(&x);
-  h = __hsub2(h, __floats2half2_rn(1024.f, 1024.f));
-  return *reinterpret_cast<uint32_t *>(&h);
-}
 // two nibbles at bit 0 and bit 16 of x -> half2 of (1024 + nibble)
 __device__ __forceinline__ uint32_t nib2_biased(uint32_t x) {
   return (x & 0x000F000Fu) | 0x64006400u;
@@ -229,7 +224,8 @@ __device__ __forceinline__ float load_q16(const uint16_t *q, int64_t off, bool b
 
 // Transposed formulation: tokens (QK) and head dims (PV) are the M = 16 side
 // of mma.m16n8k16, the query rows of a KV head the N = 8 side (NR tiles of 8).
-//   QK:  S^T[tok][row] = sum_k A[tok][k] * B[k][row], A = K codes over a
+//   QK:  S^T[tok][row] = sum_k A[tok][k] * B[k][row], A = K codes + 1024 (the
+//        fp16 magic bias, removed through the bias term with sum_k Q) over a
 //        permutation pi of the head dim, B = Q with the same permutation;
 //   PV:  O^T[d][row] = sum_t A[d][t] * B[t][row], A = V codes (+1024, the
 //        fp16 magic bias, removed through sum_t P'), B = P'^T by movmatrix.
@@ -397,10 +393,10 @@ __global__ void __launch_bounds__(kWarps * 32, QCfg<D, BITS, NR>::kCtas)
 #pragma unroll
         for (int w = 0; w < 4; ++w) {
           uint32_t a[4];
-          a[0] = h2_sub1024(__byte_perm(w0[w], kMagic, 0x4140));
-          a[1] = h2_sub1024(__byte_perm(w1[w], kMagic, 0x4140));
-          a[2] = h2_sub1024(__byte_perm(w0[w], kMagic, 0x4342));
-          a[3] = h2_sub1024(__byte_perm(w1[w], kMagic, 0x4342));
+          a[0] = __byte_perm(w0[w], kMagic, 0x4140);  // 1024 + code
+          a[1] = __byte_perm(w1[w], kMagic, 0x4140);
+          a[2] = __byte_perm(w0[w], kMagic, 0x4342);
+          a[3] = __byte_perm(w1[w], kMagic, 0x4342);
 #pragma unroll
           for (int nr = 0; nr < NR; ++nr) mma_16816<false>(acc[nr][G], a, qb[nr][G][w][0], qb[nr][G][w][1]);
         }
@@ -412,10 +408,10 @@ __global__ void __launch_bounds__(kWarps * 32, QCfg<D, BITS, NR>::kCtas)
           const uint32_t x0 = (w >> 1) ? k0.y : k0.x, x1 = (w >> 1) ? k1.y : k1.x;
           const int j0 = 2 * (w & 1);
           uint32_t a[4];
-          a[0] = h2_sub1024(nib2_biased(x0 >> (4 * j0)));
-          a[1] = h2_sub1024(nib2_biased(x1 >> (4 * j0)));
-          a[2] = h2_sub1024(nib2_biased(x0 >> (4 * (j0 + 1))));
-          a[3] = h2_sub1024(nib2_biased(x1 >> (4 * (j0 + 1))));
+          a[0] = nib2_biased(x0 >> (4 * j0));  // 1024 + code
+          a[1] = nib2_biased(x1 >> (4 * j0));
+          a[2] = nib2_biased(x0 >> (4 * (j0 + 1)));
+          a[3] = nib2_biased(x1 >> (4 * (j0 + 1)));
 #pragma unroll
           for (int nr = 0; nr < NR; ++nr) mma_16816<false>(acc[nr][G], a, qb[nr][G][w][0], qb[nr][G][w][1]);
         }
@@ -441,6 +437,10 @@ __global__ void __launch_bounds__(kWarps * 32, QCfg<D, BITS, NR>::kCtas)
             bkv[ts][G] = __half2float(kbi[tok_of<C>(g + 8 * ts) * NG + G]);
           }
         }
+        // the K codes entered the mma as 1024 + code: fold 1024 * s * sum(Q)
+        // into the bias term
+#pragma unroll
+        for (int G = 0; G < NG; ++G) bkv[ts][G] = fmaf(-1024.f, skv[ts][G], bkv[ts][G]);
       }
 #pragma unroll
       for (int nr = 0; nr < NR; ++nr)
@@ -499,15 +499,31 @@ __global__ void __launch_bounds__(kWarps * 32, QCfg<D, BITS, NR>::kCtas)
 
     // ---- O^T += (V codes + 1024) . (p * s_v)^T ; rb += p * b_v ; cp += P' ----
 #pragma unroll
-    for (int G = 0; G < NG; ++G) {
-      float sv[2], bv[2];
+    // V scales (pre-multiplied by the P' scale) and biases of this lane's
+    // tokens g, g+8 for every group; 0 past the context
+    float svg[2][NG], bvg[2][NG];
 #pragma unroll
-      for (int ts = 0; ts < 2; ++ts) {
-        const int tok = tok_of<C>(g + 8 * ts);
-        const bool ok = tok < nvalid;
-        sv[ts] = ok ? __half2float(vsc[tok * NG + G]) * C::kPScale : 0.f;
-        bv[ts] = ok ? __half2float(vbi[tok * NG + G]) : 0.f;
+    for (int ts = 0; ts < 2; ++ts) {
+      const int tok = tok_of<C>(g + 8 * ts);
+      const bool ok = tok < nvalid;
+      if constexpr (NG == 2) {
+        const float2 sv2 = __half22float2(*reinterpret_cast<const __half2 *>(vsc + tok * 2));
+        const float2 bv2 = __half22float2(*reinterpret_cast<const __half2 *>(vbi + tok * 2));
+        svg[ts][0] = ok ? sv2.x * C::kPScale : 0.f;
+        svg[ts][1] = ok ? sv2.y * C::kPScale : 0.f;
+        bvg[ts][0] = ok ? bv2.x : 0.f;
+        bvg[ts][1] = ok ? bv2.y : 0.f;
+      } else {
+#pragma unroll
+        for (int G = 0; G < NG; ++G) {
+          svg[ts][G] = ok ? __half2float(vsc[tok * NG + G]) * C::kPScale : 0.f;
+          bvg[ts][G] = ok ? __half2float(vbi[tok * NG + G]) : 0.f;
+        }
       }
+    }
+#pragma unroll
+    for (int G = 0; G < NG; ++G) {
+      const float sv[2] = {svg[0][G], svg[1][G]}, bv[2] = {bvg[0][G], bvg[1][G]};
       uint32_t pb[NR][2];
 #pragma unroll
       for (int nr = 0; nr < NR; ++nr) {
