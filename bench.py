@@ -763,6 +763,7 @@ def run_quant(args, local_rank: int) -> None:
         "roofline": {"bound": "hbm", "achieved": round(alg / (dec_ms / 1e3) / 1e9, 1),
                      "peak": peak, "unit": "GB/s",
                      "frac": round(alg / (dec_ms / 1e3) / 1e9 / peak, 4),
+                     "traffic": profile_traffic("paged_decode_q8_c4.md") if bits == 8 else None,
                      "kernel": f"paged_decode_q_kernel<128,{bits}>", "peak_kind": peak_kind,
                      "decode_ms_mean": round(dec_ms, 4), "alg_bytes_per_launch": alg},
         "gpu_launches": steps * nl * 2,

@@ -163,9 +163,14 @@ struct QCfg {
   static constexpr int NG = D / 64;         // groups per row
   static constexpr int TD = kTileTok * RB;  // code bytes per tile (K or V)
   static constexpr int TS = kTileTok * NG * 2;  // scale (or bias) bytes per tile
-  // 128-byte code rows arrive by 2-D bulk tensor copies with the 128-byte
-  // swizzle (conflict-free fragment reads); narrower rows by 1-D bulk copies.
-  static constexpr bool kSwizzled = (RB == 128);
+  // 128-byte code rows (8-bit, D = 128) arrive by 2-D bulk tensor copies with
+  // the 128-byte swizzle (conflict-free fragment reads with tok_of below);
+  // other rows by 1-D bulk copies.  (For the 64-byte rows of 4-bit codes the
+  // 64-byte swizzle with tok_of(m) = m ^ (((m >> 1) & 1) * 5) removes the bank
+  // conflicts too, but measured slower: that kernel is bound by its ALU work,
+  // and the swizzled addresses add to it.)
+  static constexpr int kSwz = (RB == 128) ? 128 : 0;
+  static constexpr bool kSwizzled = kSwz != 0;
   static constexpr int kTx = 2 * TD + 4 * TS;
   static constexpr int kCodeStage = 2 * TD;          // K + V codes (1024-aligned)
   static constexpr int kScaleStage = 4 * TS;         // K/V scales and biases
@@ -185,25 +190,27 @@ struct QCfg {
   static constexpr float kPScale = BITS == 8 ? 256.f : 16.f;
 };
 
-// Byte offset of (row, byte) in a code tile: swizzled 128-byte rows, or plain.
+// Byte offset of (row, byte) in a code tile: the 128-byte swizzle (16-byte
+// unit u of row r at u ^ (r & 7)), or plain rows.
 template <class C>
 __device__ __forceinline__ uint32_t code_off(int row, int byte) {
-  if constexpr (C::kSwizzled) {
+  if constexpr (C::kSwz == 128) {
     return swz128(row, byte);
   } else {
     return row * C::RB + byte;
   }
 }
 
-// Token of the tile held in mma row (or k index) m.  With swizzled rows the
-// odd rows are exchanged with their partner four rows away (m ^ 4), so that
-// the K reads (rows m, m+1 in one quarter-warp phase) and the V reads (rows
-// 2c or 2c+1 for c = 0..3 in one half-warp phase) fall in distinct bank
-// groups under the 128-byte swizzle.  Scores, masks, scales and V rows all go
-// through this map, so the order of the tokens inside a tile is immaterial.
+// Token of the tile held in mma row (or k index) m, chosen so that the K reads
+// (rows m, m+1 in one quarter-warp phase) and the V reads (rows 2c or 2c+1,
+// c = 0..3, in one half-warp phase) fall in distinct bank groups under the
+// 128-byte swizzle (checked against a model of the shared-memory banks: the
+// minimum number of wavefronts for every read): odd rows are exchanged with
+// the row four away (m ^ 4).  Scores, masks, scales and V rows all go through
+// this map, so the order of the tokens inside a tile is immaterial.
 template <class C>
 __device__ __forceinline__ int tok_of(int m) {
-  if constexpr (C::kSwizzled) {
+  if constexpr (C::kSwz == 128) {
     return m ^ ((m & 1) << 2);
   } else {
     return m;
@@ -401,8 +408,8 @@ __global__ void __launch_bounds__(kWarps * 32, QCfg<D, BITS, NR>::kCtas)
           for (int nr = 0; nr < NR; ++nr) mma_16816<false>(acc[nr][G], a, qb[nr][G][w][0], qb[nr][G][w][1]);
         }
       } else {
-        const uint2 k0 = *reinterpret_cast<const uint2 *>(kd + code_off<C>(g, 32 * G + 8 * cq));
-        const uint2 k1 = *reinterpret_cast<const uint2 *>(kd + code_off<C>(g + 8, 32 * G + 8 * cq));
+        const uint2 k0 = *reinterpret_cast<const uint2 *>(kd + code_off<C>(tok_of<C>(g), 32 * G + 8 * cq));
+        const uint2 k1 = *reinterpret_cast<const uint2 *>(kd + code_off<C>(tok_of<C>(g + 8), 32 * G + 8 * cq));
 #pragma unroll
         for (int w = 0; w < 4; ++w) {
           const uint32_t x0 = (w >> 1) ? k0.y : k0.x, x1 = (w >> 1) ? k1.y : k1.x;
@@ -560,10 +567,10 @@ __global__ void __launch_bounds__(kWarps * 32, QCfg<D, BITS, NR>::kCtas)
           for (int nr = 0; nr < NR; ++nr) mma_16816<false>(oacc[nr][4 * G + v], a, pb[nr][0], pb[nr][1]);
         }
       } else {
-        const uint32_t v0 = *reinterpret_cast<const uint32_t *>(vd + code_off<C>((2 * cq), 32 * G + 4 * g));
-        const uint32_t v1 = *reinterpret_cast<const uint32_t *>(vd + code_off<C>((2 * cq + 1), 32 * G + 4 * g));
-        const uint32_t v2 = *reinterpret_cast<const uint32_t *>(vd + code_off<C>((2 * cq + 8), 32 * G + 4 * g));
-        const uint32_t v3 = *reinterpret_cast<const uint32_t *>(vd + code_off<C>((2 * cq + 9), 32 * G + 4 * g));
+        const uint32_t v0 = *reinterpret_cast<const uint32_t *>(vd + code_off<C>(tok_of<C>(2 * cq), 32 * G + 4 * g));
+        const uint32_t v1 = *reinterpret_cast<const uint32_t *>(vd + code_off<C>(tok_of<C>(2 * cq + 1), 32 * G + 4 * g));
+        const uint32_t v2 = *reinterpret_cast<const uint32_t *>(vd + code_off<C>(tok_of<C>(2 * cq + 8), 32 * G + 4 * g));
+        const uint32_t v3 = *reinterpret_cast<const uint32_t *>(vd + code_off<C>(tok_of<C>(2 * cq + 9), 32 * G + 4 * g));
 #pragma unroll
         for (int v = 0; v < 4; ++v) {
           // nibble v -> byte v/2 (low or high half); nibble 4 + v -> byte 2 + v/2
