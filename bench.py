@@ -307,9 +307,11 @@ def run_gpu(args, rank: int, world: int, local_rank: int) -> None:
     out = torch.empty_like(q)
     p2p = world > 1 and args.gather == "p2p"
     gat = HeadAllGather(shard, B, D, torch.bfloat16, dev)
-    peer = PeerAllGather(shard, B, D, torch.bfloat16, dev, n_slots=nl) if p2p else None
+    # two sets of slots, alternated per step in the end-to-end loop (whose
+    # outputs are read back while the next step runs)
+    peer = PeerAllGather(shard, B, D, torch.bfloat16, dev, n_slots=2 * nl) if p2p else None
     if p2p:
-        full = peer.full
+        full = peer.full[:nl]
     else:
         full = torch.empty((nl, B, hq_all, D), dtype=torch.bfloat16, device=dev) if world > 1 else out
 
@@ -384,24 +386,17 @@ def run_gpu(args, rank: int, world: int, local_rank: int) -> None:
         h2d = qh.numel() * 2 + kh.numel() * 2 + vh.numel() * 2
         d2h = oh.numel() * 2
 
-        q_e, k_e, v_e = torch.empty_like(q), torch.empty_like(kn), torch.empty_like(vn)
+        rounds = [0]
+
+        def gather_layer(l, ql, kl, vl, ol):
+            if p2p:
+                return peer.layer(step, l, ql, kl, vl, slot=l + nl * (rounds[0] % 2))
+            step.layer(l, ql, kl, vl, ol)
+            return gat.full(ol, out=full[l])
 
         def e2e_step():
-            if world == 1:
-                step.step_host(qh, kh, vh, oh)
-                return
-            q_e.copy_(qh, non_blocking=True)
-            k_e.copy_(kh, non_blocking=True)
-            v_e.copy_(vh, non_blocking=True)
-            if p2p:
-                step.prepare_writes()
-                for l in range(nl):
-                    peer.layer(step, l, q_e[l], k_e[l], v_e[l], slot=l)
-            else:
-                step.step(q_e, k_e, v_e, out=out)
-                for l in range(nl):
-                    gat.full(out[l], out=full[l])
-            oh.copy_(full, non_blocking=True)
+            step.step_host(qh, kh, vh, oh, layer_fn=None if world == 1 else gather_layer)
+            rounds[0] += 1
 
         for _ in range(2):
             e2e_step()

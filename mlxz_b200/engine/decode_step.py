@@ -243,21 +243,55 @@ class PagedDecodeStep:
             self.lengths.add_(1)
 
     def step_host(self, q_host: torch.Tensor, k_host: torch.Tensor, v_host: torch.Tensor,
-                  out_host: torch.Tensor, advance: bool = False) -> torch.Tensor:
-        """End-to-end step from host buffers (pinned for async copies): H2D of
-        the inputs, every layer's append + attention, D2H of the outputs."""
+                  out_host: torch.Tensor, advance: bool = False, layer_fn=None) -> torch.Tensor:
+        """End-to-end step from host buffers (pinned for async copies).
+
+        The copies are pipelined with the layers: every layer's inputs go up on
+        one copy stream (each layer's launch waits only for its own), and each
+        layer's output comes back on a second copy stream as soon as it is
+        done, while later layers run.  The current stream waits for the last
+        copy, so synchronising it covers the whole step.  ``layer_fn(l, q, k,
+        v, out)``, if given, runs layer l instead of ``layer`` and returns the
+        tensor to copy back (a head-sharded step returns its gathered output)."""
         dev = self.store.device
+        L = self.store.n_layers
         if self._dev_in is None or self._dev_in[0].shape != q_host.shape:
             self._dev_in = (torch.empty(q_host.shape, dtype=q_host.dtype, device=dev),
                             torch.empty(k_host.shape, dtype=k_host.dtype, device=dev),
                             torch.empty(v_host.shape, dtype=v_host.dtype, device=dev),
                             torch.empty(q_host.shape, dtype=q_host.dtype, device=dev))
+            self._copy_streams = (torch.cuda.Stream(dev), torch.cuda.Stream(dev))
+            self._in_ready = [torch.cuda.Event() for _ in range(L)]
+            self._out_ready = [torch.cuda.Event() for _ in range(L)]
         q, k, v, o = self._dev_in
-        q.copy_(q_host, non_blocking=True)
-        k.copy_(k_host, non_blocking=True)
-        v.copy_(v_host, non_blocking=True)
-        self.step(q, k, v, out=o, advance=advance)
-        out_host.copy_(o, non_blocking=True)
+        up, down = self._copy_streams
+        compute = torch.cuda.current_stream(dev)
+        # the previous step's kernels and copies are done with these buffers
+        up.wait_stream(compute)
+        down.wait_stream(compute)
+        with torch.cuda.stream(up):
+            for l in range(L):
+                q[l].copy_(q_host[l], non_blocking=True)
+                k[l].copy_(k_host[l], non_blocking=True)
+                v[l].copy_(v_host[l], non_blocking=True)
+                self._in_ready[l].record(up)
+        self.prepare_writes()
+        results = []
+        for l in range(L):
+            compute.wait_event(self._in_ready[l])
+            if layer_fn is None:
+                self.layer(l, q[l], k[l], v[l], o[l])
+                results.append(o[l])
+            else:
+                results.append(layer_fn(l, q[l], k[l], v[l], o[l]))
+            self._out_ready[l].record(compute)
+        with torch.cuda.stream(down):
+            for l in range(L):
+                down.wait_event(self._out_ready[l])
+                out_host[l].copy_(results[l], non_blocking=True)
+        compute.wait_stream(down)
+        if advance:
+            self.advance()
         return out_host
 
 

@@ -146,9 +146,12 @@ class PeerAllGather:
     peers' over NVLink -- then mz_peer_wait for the peers' signals, so work
     queued after it sees the whole ``[B, Hq, D]``.  No separate collective
     and no layout copy.  All ranks must call ``layer`` the same number of
-    times (the epochs must agree); a rank's readers of a slot must be queued
-    before its next ``layer`` call on that slot.  ``close`` (collective) ends
-    the mappings.
+    times (the epochs must agree).  Peers write a slot for the next time as
+    soon as this rank's launch before that one has completed, so this rank's
+    readers of a slot must be ordered (on its stream) before that preceding
+    launch; cycling through two sets of slots per round of layers (slot
+    ``l + n_layers * (round % 2)``) makes any reader ordered before the next
+    round's first launch safe.  ``close`` (collective) ends the mappings.
     """
 
     def __init__(self, shard: HeadShard, batch: int, head_dim: int, dtype: torch.dtype,

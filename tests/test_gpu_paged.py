@@ -465,3 +465,36 @@ def test_decode_step_multi_layer_with_table_growth(cuda):
             assert attn_err(out[l], ref) <= ATOL_REL, (it, l)
         step.advance()
     assert np.array_equal(to_bits(store.pools), mirror)
+
+
+def test_step_host_pipelined_matches_device_step(cuda):
+    """step_host (inputs up and outputs down on copy streams, per layer,
+    overlapped with the layers) gives bit-for-bit the outputs and pools of the
+    device-side step, over steps that advance and grow the tables."""
+    from mlxz_b200.engine import PagedDecodeStep, PagedKVStore
+
+    L, Hkv, G, D, bs = 3, 2, 4, 128, 16
+    Hq = Hkv * G
+    offsets = [0, 15, 31, 200]
+    stores, steps = [], []
+    for _ in range(2):
+        st = PagedKVStore(L, 64, Hkv, D, bs, torch.bfloat16, cuda, init="zeros")
+        st.pools.copy_(to_dev(rng.normal(71, tuple(st.pools.shape), "bf16"), "bf16", cuda))
+        for i, o in enumerate(offsets):
+            st.add_sequence(f"r{i}", o)
+        stores.append(st)
+        steps.append(PagedDecodeStep(st, [f"r{i}" for i in range(len(offsets))], Hq,
+                                     max_blocks=16))
+    B = len(offsets)
+    out_h = torch.empty((L, B, Hq, D), dtype=torch.bfloat16).pin_memory()
+    for it in range(4):
+        qb = rng.normal(72, (L, B, Hq, D), "bf16", stream=it)
+        kb = rng.normal(73, (L, B, Hkv, D), "bf16", stream=it)
+        vb = rng.normal(74, (L, B, Hkv, D), "bf16", stream=it)
+        host = [to_dev(x, "bf16", "cpu").pin_memory() for x in (qb, kb, vb)]
+        ref = steps[0].step(*(h.to(cuda) for h in host), advance=True)
+        steps[1].step_host(*host, out_h, advance=True)
+        torch.cuda.synchronize()
+        ops.check_device_errors(0)
+        assert torch.equal(out_h, ref.cpu()), it
+    assert torch.equal(stores[0].pools, stores[1].pools)
