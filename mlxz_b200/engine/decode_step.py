@@ -242,6 +242,48 @@ class PagedDecodeStep:
             self.positions.add_(1)
             self.lengths.add_(1)
 
+    def capture(self, q_dtype: torch.dtype | None = None) -> None:
+        """Capture every layer's launch of one step into a CUDA graph over
+        static buffers ``q_in [L, B, Hq, D]``, ``k_in``/``v_in [L, B, Hkv, D]``
+        and ``out [L, B, Hq, D]``.  The block tables, positions and lengths are
+        device tensors that ``advance`` / ``sync_metadata`` update in place, so
+        each replay runs the step the host state describes.  Copy-on-write
+        (``prepare_writes``) and table growth stay on the host, outside the
+        graph; a table outgrowing ``max_blocks`` needs a new step."""
+        st = self.store
+        dev = st.device
+        dt = q_dtype or st.dtype  # q and the new K/V rows (the source dtype of a quantised store)
+        L, B = st.n_layers, self.B
+        self.q_in = torch.zeros((L, B, self.n_heads, st.head_dim), dtype=dt, device=dev)
+        self.k_in = torch.zeros((L, B, st.n_kv_heads, st.head_dim), dtype=dt, device=dev)
+        self.v_in = torch.zeros_like(self.k_in)
+        self.out = torch.empty_like(self.q_in)
+        ops.error_word(dev.index if dev.index is not None else torch.cuda.current_device())
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        self._graph = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(side):
+            with torch.cuda.graph(self._graph, stream=side):
+                for l in range(L):
+                    self.layer(l, self.q_in[l], self.k_in[l], self.v_in[l], self.out[l])
+        torch.cuda.current_stream(dev).wait_stream(side)
+
+    def replay(self, q: torch.Tensor | None = None, k_new: torch.Tensor | None = None,
+               v_new: torch.Tensor | None = None, advance: bool = False) -> torch.Tensor:
+        """One captured step: copy the given inputs into the static buffers
+        (or leave what the caller wrote there), copy-on-write shared blocks,
+        replay, and return ``out``."""
+        if self._graph is None:
+            raise RuntimeError("capture() first")
+        for src, dst in ((q, self.q_in), (k_new, self.k_in), (v_new, self.v_in)):
+            if src is not None:
+                dst.copy_(src, non_blocking=True)
+        self.prepare_writes()
+        self._graph.replay()
+        if advance:
+            self.advance()
+        return self.out
+
     def step_host(self, q_host: torch.Tensor, k_host: torch.Tensor, v_host: torch.Tensor,
                   out_host: torch.Tensor, advance: bool = False, layer_fn=None) -> torch.Tensor:
         """End-to-end step from host buffers (pinned for async copies).
@@ -377,6 +419,7 @@ class QuantizedPagedDecodeStep(PagedDecodeStep):
                                                 dev.index if dev.index is not None else 0,
                                                 shared=False)
         self._dev_in = None
+        self._graph = None
 
     def layer(self, l: int, q: torch.Tensor, k_new: torch.Tensor, v_new: torch.Tensor,
               out: torch.Tensor, num_warps: int = 0) -> None:

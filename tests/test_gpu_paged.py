@@ -498,3 +498,47 @@ def test_step_host_pipelined_matches_device_step(cuda):
         ops.check_device_errors(0)
         assert torch.equal(out_h, ref.cpu()), it
     assert torch.equal(stores[0].pools, stores[1].pools)
+
+
+@pytest.mark.parametrize("quantized", [False, True])
+def test_captured_step_matches_eager_step(cuda, quantized):
+    """A step captured once into a CUDA graph and replayed (tables and lengths
+    advanced in place, blocks appended as tables grow) gives bit-for-bit the
+    outputs and pools of eager steps on the same inputs."""
+    from mlxz_b200.engine import (PagedDecodeStep, PagedKVStore, QuantizedPagedDecodeStep,
+                                  QuantizedPagedKVStore)
+
+    L, Hkv, G, D, bs = 2, 2, 4, 128, 16
+    Hq = Hkv * G
+    offsets = [3, 15, 30, 200]
+    stores, steps = [], []
+    for _ in range(2):
+        if quantized:
+            st = QuantizedPagedKVStore(L, 64, Hkv, D, bs, bits=8, device=cuda)
+        else:
+            st = PagedKVStore(L, 64, Hkv, D, bs, torch.bfloat16, cuda, init="zeros")
+            st.pools.copy_(to_dev(rng.normal(81, tuple(st.pools.shape), "bf16"), "bf16", cuda))
+        for i, o in enumerate(offsets):
+            st.add_sequence(f"r{i}", 0)
+        ids = [f"r{i}" for i in range(len(offsets))]
+        # fill the prefixes through the store's own append path
+        for i, o in enumerate(offsets):
+            if o:
+                kk = to_dev(rng.normal(82 + i, (L, Hkv, o, D), "bf16"), "bf16", cuda)
+                st.append_tokens(f"r{i}", kk, kk)
+        cls = QuantizedPagedDecodeStep if quantized else PagedDecodeStep
+        stores.append(st)
+        steps.append(cls(st, ids, Hq, max_blocks=16))
+    steps[1].capture(torch.bfloat16)
+    B = len(offsets)
+    for it in range(5):
+        q = to_dev(rng.normal(83, (L, B, Hq, D), "bf16", stream=it), "bf16", cuda)
+        k = to_dev(rng.normal(84, (L, B, Hkv, D), "bf16", stream=it), "bf16", cuda)
+        v = to_dev(rng.normal(85, (L, B, Hkv, D), "bf16", stream=it), "bf16", cuda)
+        ref = steps[0].step(q, k, v, advance=True)
+        got = steps[1].replay(q, k, v, advance=True)
+        torch.cuda.synchronize()
+        ops.check_device_errors(0)
+        assert torch.equal(got, ref), it
+    for a, b in zip(stores[0].pool_stacks(), stores[1].pool_stacks()):
+        assert torch.equal(a, b)
