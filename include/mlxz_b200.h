@@ -183,6 +183,31 @@ MZ_API int mz_paged_append_decode(void *out, int32_t out_dtype, int64_t out_seq_
                                   float scale, int32_t dtype, int32_t num_warps, void *workspace,
                                   size_t workspace_bytes, int32_t *dev_err, mz_stream_t stream);
 
+/* Launch flags of the _ex / allgather entry points.
+ * MZ_LAUNCH_OVERLAP_PREVIOUS: the launch may begin while the kernel ahead of it
+ * on the stream is still running (programmatic dependent launch): its blocks
+ * take SMs as that kernel's blocks finish, schedule their work and start the
+ * copies of their first K/V tiles, then wait for that kernel to complete before
+ * they read q / k_new / v_new or write anything.  Valid only when the kernel
+ * ahead writes none of this launch's pools, block tables or ctx_lens (e.g. it
+ * is the previous layer's decode). */
+#define MZ_LAUNCH_OVERLAP_PREVIOUS 1u
+
+/* mz_paged_append_decode with launch flags (MZ_LAUNCH_*).  Same reference
+ * counterpart and rules as mz_paged_append_decode. */
+MZ_API int mz_paged_append_decode_ex(void *out, int32_t out_dtype, int64_t out_seq_stride,
+                                     int64_t out_head_stride, const void *q,
+                                     int64_t q_seq_stride, int64_t q_head_stride, void *k_pool,
+                                     void *v_pool, const void *k_new, const void *v_new,
+                                     int64_t new_seq_stride, int64_t new_head_stride,
+                                     const int32_t *block_tables, int32_t max_blocks_per_seq,
+                                     const int32_t *ctx_lens, int32_t n_seqs, int32_t n_heads,
+                                     int32_t n_kv_heads, int32_t head_dim, int32_t block_size,
+                                     int64_t n_blocks, float scale, int32_t dtype,
+                                     int32_t num_warps, uint32_t flags, void *workspace,
+                                     size_t workspace_bytes, int32_t *dev_err,
+                                     mz_stream_t stream);
+
 /* Destinations of one rank's decode output in a head-sharded group of
  * n_ranks GPUs (one process each, KV heads split evenly; rank r holds query
  * heads [r*n_heads, (r+1)*n_heads) of the n_ranks*n_heads in the gathered
@@ -214,9 +239,10 @@ typedef struct mz_peer_outputs {
  * (n_ranks*n_heads*head_dim and head_dim for a dense one).
  * No counterpart in the reference (one device only); it replaces the
  * all-gather of head-sharded attention outputs that a multi-GPU step runs
- * after mz_paged_append_decode.  A rank's readers of a gathered buffer must
- * be queued before its next launch that writes that buffer (peers write into
- * it as soon as their own next launch runs).  n_seqs must be positive.  Other
+ * after mz_paged_append_decode.  Peers write a gathered buffer for the next
+ * time as soon as this rank's launch before that one has completed, so this
+ * rank's readers of a buffer must be ordered before that preceding launch.
+ * n_seqs must be positive.  flags: MZ_LAUNCH_*.  Other
  * arguments and rules as mz_paged_append_decode. */
 MZ_API int mz_paged_append_decode_allgather(
     const mz_peer_outputs *peers, int32_t out_dtype, int64_t out_seq_stride,
@@ -225,8 +251,8 @@ MZ_API int mz_paged_append_decode_allgather(
     int64_t new_head_stride, const int32_t *block_tables, int32_t max_blocks_per_seq,
     const int32_t *ctx_lens, int32_t n_seqs, int32_t n_heads, int32_t n_kv_heads,
     int32_t head_dim, int32_t block_size, int64_t n_blocks, float scale, int32_t dtype,
-    int32_t num_warps, void *workspace, size_t workspace_bytes, int32_t *dev_err,
-    mz_stream_t stream);
+    int32_t num_warps, uint32_t flags, void *workspace, size_t workspace_bytes,
+    int32_t *dev_err, mz_stream_t stream);
 
 /* Enqueue on `stream` a wait until signal[s] (this rank's words, s != rank)
  * has reached `epoch` for every peer s, with acquire semantics at system

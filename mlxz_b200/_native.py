@@ -69,6 +69,7 @@ _i32, _i64, _f32, _vp, _sz = (ctypes.c_int32, ctypes.c_int64, ctypes.c_float,
 
 MZ_MAX_RANKS = 8
 MZ_IPC_HANDLE_BYTES = 64
+MZ_LAUNCH_OVERLAP_PREVIOUS = 1
 
 
 class PeerOutputs(ctypes.Structure):
@@ -98,10 +99,13 @@ _SIGNATURES: dict[str, list] = {
     "mz_paged_append_decode": [_vp, _i32, _i64, _i64, _vp, _i64, _i64, _vp, _vp, _vp, _vp, _i64,
                                _i64, _vp, _i32, _vp, _i32, _i32, _i32, _i32, _i32, _i64, _f32,
                                _i32, _i32, _vp, _sz, _vp, _vp],
+    "mz_paged_append_decode_ex": [_vp, _i32, _i64, _i64, _vp, _i64, _i64, _vp, _vp, _vp, _vp,
+                                  _i64, _i64, _vp, _i32, _vp, _i32, _i32, _i32, _i32, _i32,
+                                  _i64, _f32, _i32, _i32, ctypes.c_uint32, _vp, _sz, _vp, _vp],
     "mz_paged_append_decode_allgather": [ctypes.POINTER(PeerOutputs), _i32, _i64, _i64, _vp,
                                          _i64, _i64, _vp, _vp, _vp, _vp, _i64, _i64, _vp, _i32,
                                          _vp, _i32, _i32, _i32, _i32, _i32, _i64, _f32, _i32,
-                                         _i32, _vp, _sz, _vp, _vp],
+                                         _i32, ctypes.c_uint32, _vp, _sz, _vp, _vp],
     "mz_peer_wait": [_vp, _i32, _i32, ctypes.c_uint32, ctypes.c_uint64, _vp, _vp],
     "mz_ipc_export": [_vp, _vp, ctypes.POINTER(ctypes.c_uint64)],
     "mz_ipc_open": [_vp, ctypes.c_uint64, ctypes.POINTER(_vp), ctypes.POINTER(_vp)],

@@ -72,6 +72,7 @@ struct Params {
   // peer_out[r] (the same rows in rank r's gathered buffer, mapped into this
   // GPU's address space); once all blocks have stored, the last one publishes
   // `epoch` into each peer_sig[r] (rank r's signal word for this rank).
+  int overlap_prev = 0;  // launched as a programmatic dependent of the kernel ahead
   int n_peer = 0;
   void *peer_out[MZ_MAX_RANKS - 1] = {};
   uint32_t *peer_sig[MZ_MAX_RANKS - 1] = {};
@@ -187,6 +188,16 @@ __device__ __forceinline__ void forward_rows(const Params &p, int b, int h, int 
     for (int r = 0; r < p.n_peer; ++r)
       *reinterpret_cast<uint4 *>(static_cast<uint8_t *>(p.peer_out[r]) + off + x) = v;
   }
+}
+
+// Programmatic dependent launch: let the next launch on the stream begin its
+// prologue, and wait for the launch ahead to complete (both no-ops when the
+// launches were not made with programmatic stream serialization).
+__device__ __forceinline__ void launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void wait_for_previous_grid() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
 }
 
 __device__ __forceinline__ void st_release_sys(uint32_t *addr, uint32_t v) {
@@ -328,6 +339,12 @@ struct Sched {
       end = min(start + chunk, tot);
       u = W + tk;
     }
+    push_unit(p, start, end, u);
+    return true;
+  }
+
+  // Cursor at the unit's first tile; the unit descriptor goes to the ring.
+  __device__ __forceinline__ void push_unit(const Params &p, int start, int end, int u) {
     pc = locate(p, start, lane);
     if (lane == 0) {
       Unit un;
@@ -343,7 +360,25 @@ struct Sched {
     }
     ++pushed;
     p_left = end - start;
-    return true;
+  }
+
+  // Before the launch waits for the kernel ahead of it (programmatic dependent
+  // launch): start the copies of the first (up to S) tiles of this warp's
+  // static share.  Reads only ctx, the block tables and the pools (through
+  // locate and issue); no ticket, no workspace word.
+  template <int S, class IssueFn>
+  __device__ __forceinline__ void prefetch_static(const Params &p, IssueFn &&issue) {
+    if (static_taken) return;
+    static_taken = true;
+    if (!(per_s > 0 && (int64_t)wid * per_s < t_s)) return;
+    const int start = wid * per_s;
+    push_unit(p, start, min(start + per_s, t_s), wid);
+    while (p_left > 0 && issued < S) {
+      issue(issued % S, pc);
+      advance(pc, p);
+      --p_left;
+      ++issued;
+    }
   }
 
   // Keep S tiles in flight; issue(stage, cursor) starts one tile's copies.

@@ -74,9 +74,8 @@ __device__ __forceinline__ void decode_tiles(const CUtensorMap &tmK, const CUten
   }
   __syncwarp();
 
-  zero_empty_outputs<D, GATHER>(p, wid, W, lane);
   Sched sch;
-  if (!sch.init(p, lane, wid, W, uq)) return;  // T == 0: no counter is touched
+  const bool any_work = sch.init(p, lane, wid, W, uq);  // T == 0: no counter is touched
 
   const uint64_t pol = l2_policy_evict_first();
   auto issue = [&](int s, const Cursor &c) {
@@ -111,6 +110,14 @@ __device__ __forceinline__ void decode_tiles(const CUtensorMap &tmK, const CUten
 
   UnitReader ur;
   bool seg_first = true;
+
+  // Until the launch ahead has completed (programmatic dependent launch) only
+  // ctx, the tables and the pools are read: the first tiles of the static
+  // share are already on their way when the wait returns.
+  if (any_work) sch.prefetch_static<S>(p, issue);
+  wait_for_previous_grid();
+  zero_empty_outputs<D, GATHER>(p, wid, W, lane);
+  if (!any_work) return;
 
   sch.refill<S>(p, 0, issue);
   bool ring_idle = true;
@@ -342,6 +349,7 @@ template <int D, bool BF16>
 __global__ void __launch_bounds__(kWarps * 32, 2)
     paged_decode_kernel(const __grid_constant__ CUtensorMap tmK,
                         const __grid_constant__ CUtensorMap tmV, const Params p) {
+  launch_dependents();
   decode_tiles<D, BF16, false>(tmK, tmV, p);
 }
 
@@ -351,6 +359,7 @@ template <int D, bool BF16>
 __global__ void __launch_bounds__(kWarps * 32, 2)
     paged_decode_gather_kernel(const __grid_constant__ CUtensorMap tmK,
                                const __grid_constant__ CUtensorMap tmV, const Params p) {
+  launch_dependents();
   decode_tiles<D, BF16, true>(tmK, tmV, p);
   gather_arrive(p);
 }
@@ -434,6 +443,7 @@ struct DecodeArgs {
   int32_t *err;
   cudaStream_t stream;
   const mz_peer_outputs *peers = nullptr;  // all-gather over peer memory, or none
+  uint32_t flags = 0;                      // MZ_LAUNCH_*
 };
 
 // Host-side checks shared by the entry points; fills the resolved warp count
@@ -572,16 +582,25 @@ int launch(const DecodeArgs &a, int64_t warps, const WsLayout &ws, void *scratch
     if (e != cudaSuccess) return cuda_fail(e, "clearing decode counters");
   }
   const unsigned grid = static_cast<unsigned>(warps / kWarps);
-#define MZ_LAUNCH(D_, BF_)                                                                     \
-  do {                                                                                         \
-    if (a.peers) {                                                                             \
-      if (int rc = gather_smem_attr<D_, BF_>()) return rc;                                     \
-      paged_decode_gather_kernel<D_, BF_><<<grid, kWarps * 32, Cfg<D_>::kSmemBytes, a.stream>>>( \
-          tk, tv, p);                                                                          \
-    } else {                                                                                   \
-      paged_decode_kernel<D_, BF_><<<grid, kWarps * 32, Cfg<D_>::kSmemBytes, a.stream>>>(tk, tv, \
-                                                                                     p);       \
-    }                                                                                          \
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kWarps * 32);
+  cfg.stream = a.stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = (a.flags & MZ_LAUNCH_OVERLAP_PREVIOUS) ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t le = cudaSuccess;
+#define MZ_LAUNCH(D_, BF_)                                                          \
+  do {                                                                              \
+    cfg.dynamicSmemBytes = Cfg<D_>::kSmemBytes;                                     \
+    if (a.peers) {                                                                  \
+      if (int rc = gather_smem_attr<D_, BF_>()) return rc;                          \
+      le = cudaLaunchKernelEx(&cfg, paged_decode_gather_kernel<D_, BF_>, tk, tv, p); \
+    } else {                                                                        \
+      le = cudaLaunchKernelEx(&cfg, paged_decode_kernel<D_, BF_>, tk, tv, p);       \
+    }                                                                               \
   } while (0)
   if (a.D == 128) {
     if (bf16) MZ_LAUNCH(128, true); else MZ_LAUNCH(128, false);
@@ -589,6 +608,7 @@ int launch(const DecodeArgs &a, int64_t warps, const WsLayout &ws, void *scratch
     if (bf16) MZ_LAUNCH(64, true); else MZ_LAUNCH(64, false);
   }
 #undef MZ_LAUNCH
+  if (le != cudaSuccess) return cuda_fail(le, fn);
   MZ_CHECK_LAUNCH(fn);
   return MZ_OK;
 }
@@ -680,14 +700,16 @@ extern "C" int mz_paged_decode(void *out, int32_t out_dtype, int64_t out_seq_str
   return launch(a, warps, ws, workspace, false, "mz_paged_decode");
 }
 
-extern "C" int mz_paged_append_decode(
-    void *out, int32_t out_dtype, int64_t out_seq_stride, int64_t out_head_stride, const void *q,
-    int64_t q_seq_stride, int64_t q_head_stride, void *k_pool, void *v_pool, const void *k_new,
-    const void *v_new, int64_t new_seq_stride, int64_t new_head_stride,
-    const int32_t *block_tables, int32_t max_blocks_per_seq, const int32_t *ctx_lens,
-    int32_t n_seqs, int32_t n_heads, int32_t n_kv_heads, int32_t head_dim, int32_t block_size,
-    int64_t n_blocks, float scale, int32_t dtype, int32_t num_warps, void *workspace,
-    size_t workspace_bytes, int32_t *dev_err, mz_stream_t stream) {
+static int append_decode(void *out, int32_t out_dtype, int64_t out_seq_stride,
+                         int64_t out_head_stride, const void *q, int64_t q_seq_stride,
+                         int64_t q_head_stride, void *k_pool, void *v_pool, const void *k_new,
+                         const void *v_new, int64_t new_seq_stride, int64_t new_head_stride,
+                         const int32_t *block_tables, int32_t max_blocks_per_seq,
+                         const int32_t *ctx_lens, int32_t n_seqs, int32_t n_heads,
+                         int32_t n_kv_heads, int32_t head_dim, int32_t block_size,
+                         int64_t n_blocks, float scale, int32_t dtype, int32_t num_warps,
+                         uint32_t flags, void *workspace, size_t workspace_bytes,
+                         int32_t *dev_err, mz_stream_t stream, const char *fn) {
   DecodeArgs a = make_args(out, out_dtype, out_seq_stride, 0, out_head_stride, q, q_seq_stride, 0,
                            q_head_stride, 1, k_pool, v_pool, block_tables, max_blocks_per_seq,
                            ctx_lens, n_seqs, n_heads, n_kv_heads, head_dim, block_size, n_blocks,
@@ -696,17 +718,50 @@ extern "C" int mz_paged_append_decode(
   a.vn = v_new;
   a.kn_sb = new_seq_stride;
   a.kn_sh = new_head_stride;
-  if (!k_new || !v_new)
-    return fail(MZ_ERR_INVALID_ARG, "mz_paged_append_decode: null k_new / v_new");
+  if (flags & ~MZ_LAUNCH_OVERLAP_PREVIOUS) return fail(MZ_ERR_INVALID_ARG, "%s: unknown flags", fn);
+  a.flags = flags;
+  if (!k_new || !v_new) return fail(MZ_ERR_INVALID_ARG, "%s: null k_new / v_new", fn);
   int64_t warps = 0;
   WsLayout ws;
-  if (int rc = validate(a, "mz_paged_append_decode", &warps, &ws)) return rc;
+  if (int rc = validate(a, fn, &warps, &ws)) return rc;
   if (n_seqs == 0) return MZ_OK;
-  if (!workspace) return fail(MZ_ERR_WORKSPACE, "mz_paged_append_decode: workspace is null");
+  if (!workspace) return fail(MZ_ERR_WORKSPACE, "%s: workspace is null", fn);
   if (workspace_bytes < ws.total)
-    return fail(MZ_ERR_WORKSPACE, "mz_paged_append_decode: workspace %zu bytes < required %zu",
-                workspace_bytes, ws.total);
-  return launch(a, warps, ws, workspace, false, "mz_paged_append_decode");
+    return fail(MZ_ERR_WORKSPACE, "%s: workspace %zu bytes < required %zu", fn, workspace_bytes,
+                ws.total);
+  return launch(a, warps, ws, workspace, false, fn);
+}
+
+extern "C" int mz_paged_append_decode(
+    void *out, int32_t out_dtype, int64_t out_seq_stride, int64_t out_head_stride, const void *q,
+    int64_t q_seq_stride, int64_t q_head_stride, void *k_pool, void *v_pool, const void *k_new,
+    const void *v_new, int64_t new_seq_stride, int64_t new_head_stride,
+    const int32_t *block_tables, int32_t max_blocks_per_seq, const int32_t *ctx_lens,
+    int32_t n_seqs, int32_t n_heads, int32_t n_kv_heads, int32_t head_dim, int32_t block_size,
+    int64_t n_blocks, float scale, int32_t dtype, int32_t num_warps, void *workspace,
+    size_t workspace_bytes, int32_t *dev_err, mz_stream_t stream) {
+  return append_decode(out, out_dtype, out_seq_stride, out_head_stride, q, q_seq_stride,
+                       q_head_stride, k_pool, v_pool, k_new, v_new, new_seq_stride,
+                       new_head_stride, block_tables, max_blocks_per_seq, ctx_lens, n_seqs,
+                       n_heads, n_kv_heads, head_dim, block_size, n_blocks, scale, dtype,
+                       num_warps, 0u, workspace, workspace_bytes, dev_err, stream,
+                       "mz_paged_append_decode");
+}
+
+extern "C" int mz_paged_append_decode_ex(
+    void *out, int32_t out_dtype, int64_t out_seq_stride, int64_t out_head_stride, const void *q,
+    int64_t q_seq_stride, int64_t q_head_stride, void *k_pool, void *v_pool, const void *k_new,
+    const void *v_new, int64_t new_seq_stride, int64_t new_head_stride,
+    const int32_t *block_tables, int32_t max_blocks_per_seq, const int32_t *ctx_lens,
+    int32_t n_seqs, int32_t n_heads, int32_t n_kv_heads, int32_t head_dim, int32_t block_size,
+    int64_t n_blocks, float scale, int32_t dtype, int32_t num_warps, uint32_t flags,
+    void *workspace, size_t workspace_bytes, int32_t *dev_err, mz_stream_t stream) {
+  return append_decode(out, out_dtype, out_seq_stride, out_head_stride, q, q_seq_stride,
+                       q_head_stride, k_pool, v_pool, k_new, v_new, new_seq_stride,
+                       new_head_stride, block_tables, max_blocks_per_seq, ctx_lens, n_seqs,
+                       n_heads, n_kv_heads, head_dim, block_size, n_blocks, scale, dtype,
+                       num_warps, flags, workspace, workspace_bytes, dev_err, stream,
+                       "mz_paged_append_decode_ex");
 }
 
 extern "C" int mz_paged_append_decode_allgather(
@@ -716,9 +771,10 @@ extern "C" int mz_paged_append_decode_allgather(
     int64_t new_head_stride, const int32_t *block_tables, int32_t max_blocks_per_seq,
     const int32_t *ctx_lens, int32_t n_seqs, int32_t n_heads, int32_t n_kv_heads,
     int32_t head_dim, int32_t block_size, int64_t n_blocks, float scale, int32_t dtype,
-    int32_t num_warps, void *workspace, size_t workspace_bytes, int32_t *dev_err,
-    mz_stream_t stream) {
+    int32_t num_warps, uint32_t flags, void *workspace, size_t workspace_bytes,
+    int32_t *dev_err, mz_stream_t stream) {
   const char *fn = "mz_paged_append_decode_allgather";
+  if (flags & ~MZ_LAUNCH_OVERLAP_PREVIOUS) return fail(MZ_ERR_INVALID_ARG, "%s: unknown flags", fn);
   if (!peers) return fail(MZ_ERR_INVALID_ARG, "%s: peers is null", fn);
   if (peers->rank < 0 || peers->rank >= MZ_MAX_RANKS)
     return fail(MZ_ERR_INVALID_ARG, "%s: rank %d out of range", fn, peers->rank);
@@ -731,6 +787,7 @@ extern "C" int mz_paged_append_decode_allgather(
   a.kn_sb = new_seq_stride;
   a.kn_sh = new_head_stride;
   a.peers = peers;
+  a.flags = flags;
   if (!k_new || !v_new) return fail(MZ_ERR_INVALID_ARG, "%s: null k_new / v_new", fn);
   if (n_seqs <= 0)
     return fail(MZ_ERR_INVALID_ARG, "%s: n_seqs must be positive (the peers wait for a signal)",

@@ -505,7 +505,6 @@ __global__ void __launch_bounds__(kWarps * 32, QCfg<D, BITS, NR>::kCtas)
     }
 
     // ---- O^T += (V codes + 1024) . (p * s_v)^T ; rb += p * b_v ; cp += P' ----
-#pragma unroll
     // V scales (pre-multiplied by the P' scale) and biases of this lane's
     // tokens g, g+8 for every group; 0 past the context
     float svg[2][NG], bvg[2][NG];

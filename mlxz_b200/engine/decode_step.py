@@ -147,6 +147,16 @@ class PagedKVStore:
         return grew
 
 
+def _copy_groups(n_layers: int) -> list[tuple[int, int]]:
+    """[a, b) layer ranges with boundaries at 0, 1, 2, 4, ... from each end."""
+    cuts, b = {0, n_layers}, 1
+    while b < n_layers:
+        cuts.update((b, n_layers - b))
+        b *= 2
+    edges = sorted(c for c in cuts if 0 <= c <= n_layers)
+    return list(zip(edges[:-1], edges[1:]))
+
+
 class PagedDecodeStep:
     """One decode step for a fixed set of sequences.
 
@@ -198,11 +208,15 @@ class PagedDecodeStep:
 
     def layer(self, l: int, q: torch.Tensor, k_new: torch.Tensor, v_new: torch.Tensor,
               out: torch.Tensor, num_warps: int = 0) -> None:
-        """Append this step's token of layer l and attend, one launch (device tensors)."""
+        """Append this step's token of layer l and attend, one launch (device
+        tensors).  Layers after the first may start while the previous layer's
+        launch finishes (it writes none of this layer's pools, and the tables
+        and lengths change only between steps)."""
         st = self.store
         ops.paged_append_decode(q, st.k_pool(l), st.v_pool(l), k_new, v_new, self.tables,
                                 self.lengths, scale=self.scale, out=out,
-                                workspace=self.workspace, num_warps=num_warps)
+                                workspace=self.workspace, num_warps=num_warps,
+                                overlap_previous=l > 0)
 
     def prepare_writes(self) -> int:
         """Copy-on-write every block this step will write that is shared (a
@@ -288,23 +302,27 @@ class PagedDecodeStep:
                   out_host: torch.Tensor, advance: bool = False, layer_fn=None) -> torch.Tensor:
         """End-to-end step from host buffers (pinned for async copies).
 
-        The copies are pipelined with the layers: every layer's inputs go up on
-        one copy stream (each layer's launch waits only for its own), and each
-        layer's output comes back on a second copy stream as soon as it is
-        done, while later layers run.  The current stream waits for the last
-        copy, so synchronising it covers the whole step.  ``layer_fn(l, q, k,
-        v, out)``, if given, runs layer l instead of ``layer`` and returns the
-        tensor to copy back (a head-sharded step returns its gathered output)."""
+        The copies are pipelined with the layers in groups that double in
+        size from each end (1, 1, 2, 4, ... 4, 2, 1, 1 layers): a group's
+        inputs go up on one copy stream (its launches wait only for their
+        group), and its outputs come back on a second copy stream while later
+        groups run, so only one layer's copies are exposed at either end.
+        (Groups, not single layers: an event between two launches stops the
+        later one from starting while the earlier drains.)  The current stream waits for the last copy, so
+        synchronising it covers the whole step.  ``layer_fn(l, q, k, v, out)``,
+        if given, runs layer l instead of ``layer`` and returns the tensor to
+        copy back (a head-sharded step returns its gathered output)."""
         dev = self.store.device
         L = self.store.n_layers
+        groups = _copy_groups(L)
         if self._dev_in is None or self._dev_in[0].shape != q_host.shape:
             self._dev_in = (torch.empty(q_host.shape, dtype=q_host.dtype, device=dev),
                             torch.empty(k_host.shape, dtype=k_host.dtype, device=dev),
                             torch.empty(v_host.shape, dtype=v_host.dtype, device=dev),
                             torch.empty(q_host.shape, dtype=q_host.dtype, device=dev))
             self._copy_streams = (torch.cuda.Stream(dev), torch.cuda.Stream(dev))
-            self._in_ready = [torch.cuda.Event() for _ in range(L)]
-            self._out_ready = [torch.cuda.Event() for _ in range(L)]
+            self._in_ready = [torch.cuda.Event() for _ in groups]
+            self._out_ready = [torch.cuda.Event() for _ in groups]
         q, k, v, o = self._dev_in
         up, down = self._copy_streams
         compute = torch.cuda.current_stream(dev)
@@ -312,25 +330,27 @@ class PagedDecodeStep:
         up.wait_stream(compute)
         down.wait_stream(compute)
         with torch.cuda.stream(up):
-            for l in range(L):
-                q[l].copy_(q_host[l], non_blocking=True)
-                k[l].copy_(k_host[l], non_blocking=True)
-                v[l].copy_(v_host[l], non_blocking=True)
-                self._in_ready[l].record(up)
+            for gi, (a, b) in enumerate(groups):
+                q[a:b].copy_(q_host[a:b], non_blocking=True)
+                k[a:b].copy_(k_host[a:b], non_blocking=True)
+                v[a:b].copy_(v_host[a:b], non_blocking=True)
+                self._in_ready[gi].record(up)
         self.prepare_writes()
         results = []
-        for l in range(L):
-            compute.wait_event(self._in_ready[l])
-            if layer_fn is None:
-                self.layer(l, q[l], k[l], v[l], o[l])
-                results.append(o[l])
-            else:
-                results.append(layer_fn(l, q[l], k[l], v[l], o[l]))
-            self._out_ready[l].record(compute)
+        for gi, (a, b) in enumerate(groups):
+            compute.wait_event(self._in_ready[gi])
+            for l in range(a, b):
+                if layer_fn is None:
+                    self.layer(l, q[l], k[l], v[l], o[l])
+                    results.append(o[l])
+                else:
+                    results.append(layer_fn(l, q[l], k[l], v[l], o[l]))
+            self._out_ready[gi].record(compute)
         with torch.cuda.stream(down):
-            for l in range(L):
-                down.wait_event(self._out_ready[l])
-                out_host[l].copy_(results[l], non_blocking=True)
+            for gi, (a, b) in enumerate(groups):
+                down.wait_event(self._out_ready[gi])
+                for l in range(a, b):
+                    out_host[l].copy_(results[l], non_blocking=True)
         compute.wait_stream(down)
         if advance:
             self.advance()

@@ -217,10 +217,12 @@ class PeerAllGather:
         pe = self._peers[slot]
         pe.epoch = self.epoch
         st = step.store
+        # layers after the first may start while the previous layer's wait runs
         ops.paged_append_decode_allgather(pe, q, st.k_pool(l), st.v_pool(l), k_new, v_new,
                                           step.tables, step.lengths, self.out_seq_stride,
                                           self.out_head_stride, self.dtype, scale=step.scale,
-                                          num_warps=num_warps, workspace=step.workspace)
+                                          num_warps=num_warps, workspace=step.workspace,
+                                          overlap_previous=l > 0)
 
     def wait(self) -> None:
         """Queue the bounded wait for every peer's rows of the last launch."""

@@ -291,10 +291,14 @@ def paged_append_decode(q: torch.Tensor, k_pool: torch.Tensor, v_pool: torch.Ten
                         k_new: torch.Tensor, v_new: torch.Tensor, block_tables: torch.Tensor,
                         ctx_lens: torch.Tensor, scale: float | None = None,
                         out: torch.Tensor | None = None, out_dtype: torch.dtype | None = None,
-                        num_warps: int = 0, workspace: torch.Tensor | None = None) -> torch.Tensor:
+                        num_warps: int = 0, workspace: torch.Tensor | None = None,
+                        overlap_previous: bool = False) -> torch.Tensor:
     """Fused decode step for one layer: write ``k_new/v_new [B, Hkv, D]`` at
     position ``ctx_lens[b] - 1`` of each sequence, then attend ``q [B, Hq, D]``
-    over the first ``ctx_lens[b]`` tokens (one launch)."""
+    over the first ``ctx_lens[b]`` tokens (one launch).  ``overlap_previous``:
+    the launch may start while the kernel ahead of it on the stream runs
+    (MZ_LAUNCH_OVERLAP_PREVIOUS) -- only when that kernel writes none of the
+    pools, ``block_tables`` or ``ctx_lens``."""
     n_blocks, Hkv, bs, D = _check_pools(k_pool, v_pool)
     if q.dim() != 3 or q.shape[2] != D or q.stride(-1) != 1 or q.dtype != k_pool.dtype:
         raise ValueError(f"q must be [B, Hq, {D}] of the pool dtype with unit last stride")
@@ -319,13 +323,14 @@ def paged_append_decode(q: torch.Tensor, k_pool: torch.Tensor, v_pool: torch.Ten
     dev = _dev_index(q)
     if workspace is None:
         workspace = decode_workspace(B, Hkv, Hq // Hkv, D, dev, num_warps)
-    nat.call("mz_paged_append_decode", out.data_ptr(), dtype_code(out_dtype), out.stride(0),
+    nat.call("mz_paged_append_decode_ex", out.data_ptr(), dtype_code(out_dtype), out.stride(0),
              out.stride(1), q.data_ptr(), q.stride(0), q.stride(1), k_pool.data_ptr(),
              v_pool.data_ptr(), k_new.data_ptr(), v_new.data_ptr(), k_new.stride(0),
              k_new.stride(1), block_tables.data_ptr(), block_tables.shape[1],
              ctx_lens.data_ptr(), B, Hq, Hkv, D, bs, n_blocks, float(scale),
-             dtype_code(q.dtype), num_warps, workspace.data_ptr(), workspace.numel(),
-             error_word(dev).data_ptr(), _stream(dev))
+             dtype_code(q.dtype), num_warps,
+             nat.MZ_LAUNCH_OVERLAP_PREVIOUS if overlap_previous else 0,
+             workspace.data_ptr(), workspace.numel(), error_word(dev).data_ptr(), _stream(dev))
     _after(dev)
     return out
 
@@ -337,7 +342,8 @@ def paged_append_decode_allgather(peers: "nat.PeerOutputs", q: torch.Tensor,
                                   out_seq_stride: int, out_head_stride: int,
                                   out_dtype: torch.dtype, scale: float | None = None,
                                   num_warps: int = 0,
-                                  workspace: torch.Tensor | None = None) -> None:
+                                  workspace: torch.Tensor | None = None,
+                                  overlap_previous: bool = False) -> None:
     """paged_append_decode whose output rows go to every rank's gathered
     buffer (``peers.out[r]``: this rank's head block there) and whose last
     warp signals the peers (mz_paged_append_decode_allgather); follow it with
@@ -366,8 +372,9 @@ def paged_append_decode_allgather(peers: "nat.PeerOutputs", q: torch.Tensor,
              k_pool.data_ptr(), v_pool.data_ptr(), k_new.data_ptr(), v_new.data_ptr(),
              k_new.stride(0), k_new.stride(1), block_tables.data_ptr(), block_tables.shape[1],
              ctx_lens.data_ptr(), B, Hq, Hkv, D, bs, n_blocks, float(scale),
-             dtype_code(q.dtype), num_warps, workspace.data_ptr(), workspace.numel(),
-             error_word(dev).data_ptr(), _stream(dev))
+             dtype_code(q.dtype), num_warps,
+             nat.MZ_LAUNCH_OVERLAP_PREVIOUS if overlap_previous else 0,
+             workspace.data_ptr(), workspace.numel(), error_word(dev).data_ptr(), _stream(dev))
     _after(dev)
 
 

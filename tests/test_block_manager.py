@@ -135,3 +135,14 @@ class BlockManagerMachine(RuleBasedStateMachine):
 TestBlockManagerMachine = BlockManagerMachine.TestCase
 TestBlockManagerMachine.settings = settings(max_examples=150, stateful_step_count=30,
                                             deadline=None)
+
+
+def test_step_copy_groups_cover_the_layers_in_order():
+    from mlxz_b200.engine.decode_step import _copy_groups
+
+    for L in range(1, 130):
+        g = _copy_groups(L)
+        assert g[0][0] == 0 and g[-1][1] == L
+        assert all(a < b for a, b in g) and all(g[i][1] == g[i + 1][0] for i in range(len(g) - 1))
+        if L >= 2:
+            assert g[0] == (0, 1) and g[-1] == (L - 1, L)

@@ -542,3 +542,35 @@ def test_captured_step_matches_eager_step(cuda, quantized):
         assert torch.equal(got, ref), it
     for a, b in zip(stores[0].pool_stacks(), stores[1].pool_stacks()):
         assert torch.equal(a, b)
+
+
+def test_overlapped_launch_waits_for_the_kernel_ahead(cuda):
+    """MZ_LAUNCH_OVERLAP_PREVIOUS: q and k_new/v_new written by a long kernel
+    right ahead of the launch (the last elements of a 512 MiB elementwise op)
+    are what the launch reads: its result equals a plain launch's bit for bit."""
+    B, Hkv, G, D, bs = 16, 4, 4, 128, 16
+    lengths = [int(x) for x in rng.randint(12, B, 1, 3000)]
+    case = random_paged_case(13, B, Hkv, D, bs, lengths, "bf16", G=G)
+    tables = torch.from_numpy(case["tables"]).to(cuda)
+    lens = torch.tensor(lengths, dtype=torch.int32, device=cuda)
+    q = to_dev(case["q"][:, 0], "bf16", cuda)
+    kn = to_dev(rng.normal(14, (B, Hkv, D), "bf16"), "bf16", cuda)
+    vn = to_dev(rng.normal(15, (B, Hkv, D), "bf16"), "bf16", cuda)
+    pools = [to_dev(case[k], "bf16", cuda) for k in ("kp", "vp")]
+    ref = ops.paged_append_decode(q, pools[0].clone(), pools[1].clone(), kn, vn, tables, lens)
+    pad = 256 << 20  # elements ahead of the inputs in the buffer the kernel ahead writes
+    src = torch.cat([torch.ones(pad, dtype=torch.bfloat16, device=cuda), q.flatten(),
+                     kn.flatten(), vn.flatten()])
+    big = torch.zeros_like(src)
+    nq, nk = q.numel(), kn.numel()
+    q_in = big[pad:pad + nq].view(q.shape)
+    k_in = big[pad + nq:pad + nq + nk].view(kn.shape)
+    v_in = big[pad + nq + nk:].view(vn.shape)
+    kp, vp = pools[0].clone(), pools[1].clone()
+    torch.cuda.synchronize()
+    torch.mul(src, 1.0, out=big)  # the kernel ahead: writes q / k_new / v_new last
+    out = ops.paged_append_decode(q_in, kp, vp, k_in, v_in, tables, lens,
+                                  overlap_previous=True)
+    torch.cuda.synchronize()
+    ops.check_device_errors(0)
+    assert torch.equal(out, ref)
