@@ -389,21 +389,26 @@ def run_gpu(args, rank: int, world: int, local_rank: int) -> None:
     e2e_ms, h2d, d2h = float('nan'), 0, 0
     if not args.no_e2e:
         # End to end through the public step API: this rank's inputs from
-        # pinned host memory, the gathered [B, Hq, D] outputs back to the host.
+        # pinned host memory; back to the host, this rank's heads of the
+        # gathered [B, Hq, D] output (the ranks' parts together are the whole
+        # output once).  Bytes are whole-job totals.
         qh = q.cpu().pin_memory()
         kh = kn.cpu().pin_memory()
         vh = vn.cpu().pin_memory()
-        oh = torch.empty(full.shape, dtype=torch.bfloat16).pin_memory()
-        h2d = qh.numel() * 2 + kh.numel() * 2 + vh.numel() * 2
-        d2h = oh.numel() * 2
+        qlo, qhi = shard.q_range
+        oh = torch.empty((nl, B, hq, D), dtype=torch.bfloat16).pin_memory()
+        h2d = (qh.numel() * 2 + kh.numel() * 2 + vh.numel() * 2) * world
+        d2h = oh.numel() * 2 * world
 
         rounds = [0]
 
         def gather_layer(l, ql, kl, vl, ol):
             if p2p:
-                return peer.layer(step, l, ql, kl, vl, slot=l + nl * (rounds[0] % 2))
-            step.layer(l, ql, kl, vl, ol)
-            return gat.full(ol, out=full[l])
+                g = peer.layer(step, l, ql, kl, vl, slot=l + nl * (rounds[0] % 2))
+            else:
+                step.layer(l, ql, kl, vl, ol)
+                g = gat.full(ol, out=full[l])
+            return g[:, qlo:qhi]
 
         def e2e_step():
             step.step_host(qh, kh, vh, oh, layer_fn=None if world == 1 else gather_layer)
