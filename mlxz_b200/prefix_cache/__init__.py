@@ -5,6 +5,7 @@
 copy-on-write, eviction to a pinned host tier).
 """
 from .base import CachedPrefix, PrefixMatch, compute_size_bytes
+from .disk import PrefixCacheCorruption, PrefixCacheDisk
 from .hasher import RollingPrefixHasher
 from .host_tier import PinnedHostTier
 from .memory import PrefixCacheMemory
@@ -14,6 +15,8 @@ __all__ = [
     "CachedPrefix",
     "PagedPrefixCache",
     "PagedPrefixState",
+    "PrefixCacheCorruption",
+    "PrefixCacheDisk",
     "PinnedHostTier",
     "PrefixCacheMemory",
     "PrefixMatch",

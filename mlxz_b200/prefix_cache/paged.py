@@ -20,13 +20,18 @@ next write.  Here, with every layer's K/V in one PagedKVStore:
   * host tier: ``evict_to_host`` moves the least recently used entries' blocks
              that only the cache still holds to pinned host memory
              (PinnedHostTier: pack kernel + side-stream D2H) and frees them on
-             the device; ``restore`` of such an entry reloads them first.
+             the device; ``restore`` of such an entry reloads them first;
+  * disk tier: ``spill_to_disk`` / ``load_from_disk`` write an entry to and
+             read it from a PrefixCacheDisk in the reference's safetensors
+             format (src/mlxz/prefix_cache/disk.py).
 """
 from __future__ import annotations
 
 import itertools
 from dataclasses import dataclass
 from typing import Any
+
+import torch
 
 from ..types import PrefixCacheStats
 from .base import CachedPrefix
@@ -219,3 +224,93 @@ class PagedPrefixCache:
 
     def entry_location(self, state: PagedPrefixState) -> list[str]:
         return [self._loc[lb][0] for lb in state.blocks]
+
+    # -- disk tier -------------------------------------------------------------
+
+    def _layer_states(self, blocks: list[int], n_tokens: int) -> list[Any]:
+        """Per-layer states [1, H, n, W] of the given device blocks: (K, V) for
+        a plain store, ((codes, scales, biases) of K, same of V) for a
+        quantised one."""
+        stacks = self.store.pool_stacks()
+        idx = torch.tensor(blocks, dtype=torch.long, device=stacks[0].device)
+
+        def rows(stack, p):
+            t = stack[p].index_select(0, idx)             # [nb, H, bs, W]
+            nb, H, bs, W = t.shape
+            return t.permute(1, 0, 2, 3).reshape(1, H, nb * bs, W)[:, :, :n_tokens]
+
+        states = []
+        for l in range(self.store.n_layers):
+            if len(stacks) == 1:
+                states.append((rows(stacks[0], 2 * l), rows(stacks[0], 2 * l + 1)))
+            else:
+                states.append((tuple(rows(s, 2 * l) for s in stacks),
+                               tuple(rows(s, 2 * l + 1) for s in stacks)))
+        return states
+
+    def spill_to_disk(self, token_hashes: tuple[bytes, ...], disk) -> bool:
+        """Write the entry stored under ``token_hashes`` to a PrefixCacheDisk in
+        its format (host-resident blocks are reloaded first).  False when there
+        is no such entry."""
+        entry = self._entries.get(token_hashes)
+        if entry is None:
+            return False
+        state = entry.kv_states
+        self.reload(state)
+        blocks = [self._loc[lb][1] for lb in state.blocks]
+        ctype = "QuantizedKVCache" if len(self.store.pool_stacks()) > 1 else "KVCache"
+        disk.store_states(token_hashes, self._layer_states(blocks, state.n_tokens),
+                          state.n_tokens, ctype)
+        return True
+
+    def load_from_disk(self, token_hashes: tuple[bytes, ...], disk, block_size: int = 8
+                       ) -> int:
+        """Longest prefix of ``token_hashes`` on disk, written into fresh device
+        blocks (raw, no requantisation) and cached as an entry; returns its
+        token count (0 on a miss or a format this store does not hold)."""
+        quantized = len(self.store.pool_stacks()) > 1
+        n, states, _ = disk.lookup_sync(token_hashes,
+                                        "QuantizedKVCache" if quantized else "KVCache")
+        if not n or states is None or len(states) != self.store.n_layers:
+            return 0
+        bs = self.store.block_size
+        nb = -(-n // bs)
+        new = self.store.bm.allocate(nb)
+        stacks = self.store.pool_stacks()
+        idx = torch.tensor(new, dtype=torch.long, device=stacks[0].device)
+
+        def put(stack, p, t):
+            H, W = t.shape[1], t.shape[3]
+            buf = torch.zeros((H, nb * bs, W), dtype=stack.dtype, device=stack.device)
+            buf[:, :n] = t[0].to(stack.device, stack.dtype)
+            stack[p].index_copy_(0, idx, buf.view(H, nb, bs, W).permute(1, 0, 2, 3))
+
+        for l, st in enumerate(states):
+            if quantized:
+                # a quantised layer reads back as its tensors in name order:
+                # K's (codes, scales, biases) then V's
+                if len(st) != 2 * len(stacks):
+                    self.store.bm.free(new)
+                    return 0
+                k, v = st[:len(stacks)], st[len(stacks):]
+                for s, kt, vt in zip(stacks, k, v):
+                    put(s, 2 * l, kt)
+                    put(s, 2 * l + 1, vt)
+            else:
+                put(stacks[0], 2 * l, st[0])
+                put(stacks[0], 2 * l + 1, st[1])
+        key = token_hashes[: -(-n // block_size)]
+        size = n * self.bytes_per_token
+        if size > self._budget:
+            self.store.bm.free(new)
+            return 0
+        if key not in self._entries:
+            self._evict_until_room(size)
+            lbs = tuple(self._hold(b) for b in new)
+            self._entries[key] = CachedPrefix(token_hashes=key,
+                                              kv_states=PagedPrefixState(lbs, n),
+                                              n_tokens=n, size_bytes=size,
+                                              cache_type=CACHE_TYPE, last_access=next(_clock))
+            self._used += size
+        self.store.bm.free(new)  # the entry holds its own reference
+        return n

@@ -131,3 +131,47 @@ def test_host_tier_roundtrip_many_chunks(cuda):
     for a, b in zip(ids, fresh):
         assert np.array_equal(after[:, b], before[:, a])
     ops.check_device_errors(0)
+
+
+@pytest.mark.parametrize("quantized", [False, True])
+def test_paged_entry_disk_round_trip(cuda, tmp_path, quantized):
+    """A cached paged prefix spilled to the disk tier and loaded into a fresh
+    store: the same K/V (codes, scales, biases) bit for bit, a restorable entry,
+    and the file readable as the per-layer states of the reference's format."""
+    from mlxz_b200.engine import PagedKVStore, QuantizedPagedKVStore
+    from mlxz_b200.prefix_cache import PagedPrefixCache, PrefixCacheDisk
+
+    L, H, D, bs, n = 2, 2, 128, 16, 37
+
+    def make():
+        if quantized:
+            return QuantizedPagedKVStore(L, 16, H, D, bs, bits=8, device=cuda)
+        return PagedKVStore(L, 16, H, D, bs, torch.bfloat16, cuda)
+
+    a = make()
+    a.add_sequence("s")
+    kv = torch.randn(L, H, n, D, device=cuda).to(torch.bfloat16)
+    a.append_tokens("s", kv, kv * 2)
+    cache_a = PagedPrefixCache(a, 1 << 30)
+    hashes = tuple(bytes([i]) * 32 for i in range(5))
+    cache_a.store_sync(hashes, "s", n_tokens=n, block_size=8)
+    disk = PrefixCacheDisk(tmp_path, 1 << 30, "model")
+    assert cache_a.spill_to_disk(hashes, disk)
+
+    b = make()
+    cache_b = PagedPrefixCache(b, 1 << 30)
+    assert cache_b.load_from_disk(hashes, disk, block_size=8) == n
+    got, state, _ = cache_b.lookup_sync(hashes)
+    assert got == n
+    table_b = cache_b.restore("r", state)
+    ta = torch.tensor(a.tables["s"][: -(-n // bs)], device=cuda)
+    tb = torch.tensor(table_b, device=cuda)
+    for sa, sb in zip(a.pool_stacks(), b.pool_stacks()):
+        xa = sa.index_select(1, ta).permute(0, 2, 1, 3, 4).flatten(2, 3)[:, :, :n]
+        xb = sb.index_select(1, tb).permute(0, 2, 1, 3, 4).flatten(2, 3)[:, :, :n]
+        assert torch.equal(xa, xb)
+    _, states, ctype = disk.lookup_sync(hashes)
+    assert ctype == ("QuantizedKVCache" if quantized else "KVCache") and len(states) == L
+    if not quantized:
+        assert torch.equal(states[1][0].to(cuda)[0], kv[1])
+        assert torch.equal(states[1][1].to(cuda)[0], kv[1] * 2)
