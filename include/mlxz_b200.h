@@ -183,6 +183,30 @@ MZ_API int mz_paged_append_decode(void *out, int32_t out_dtype, int64_t out_seq_
                                   float scale, int32_t dtype, int32_t num_warps, void *workspace,
                                   size_t workspace_bytes, int32_t *dev_err, mz_stream_t stream);
 
+/* Chunked prefill attention over paged KV.  Sequence b's n_b = q_len[b]
+ * query tokens are rows q_start[b] .. q_start[b] + n_b - 1 of q and out
+ * (element (row t, head hq, dim d) at base + t*tok_stride + hq*head_stride + d,
+ * of dtype; out of out_dtype = dtype or F32) at positions
+ * [ctx_lens[b] - n_b, ctx_lens[b]) of the sequence, their K/V already in the
+ * pools (mz_kv_append).  Token i attends to the sequence's first
+ * ctx_lens[b] - n_b + i + 1 tokens (causal), query head hq reading KV head
+ * hq / (n_heads / n_kv_heads); softmax(q.K^T*scale).V with fp32 accumulation.
+ * max_q_len >= every q_len[b] sizes the grid.
+ * Replaces the prompt pass over a request cache that follows
+ * ChunkedPrefillScheduler.get_next_chunk (src/mlxz/scheduler/chunker.py:53-76):
+ * mlx_lm's causal scaled_dot_product_attention of a prompt chunk at a cache
+ * offset, here over paged KV.  Supported: F16 / BF16, head_dim 64 or 128,
+ * block_size a multiple of 16, n_heads / n_kv_heads dividing 16. */
+MZ_API int mz_paged_prefill(void *out, int32_t out_dtype, int64_t out_tok_stride,
+                            int64_t out_head_stride, const void *q, int64_t q_tok_stride,
+                            int64_t q_head_stride, const int32_t *q_start, const int32_t *q_len,
+                            int32_t max_q_len, const void *k_pool, const void *v_pool,
+                            const int32_t *block_tables, int32_t max_blocks_per_seq,
+                            const int32_t *ctx_lens, int32_t n_seqs, int32_t n_heads,
+                            int32_t n_kv_heads, int32_t head_dim, int32_t block_size,
+                            int64_t n_blocks, float scale, int32_t dtype, int32_t *dev_err,
+                            mz_stream_t stream);
+
 /* Launch flags of the _ex / allgather entry points.
  * MZ_LAUNCH_OVERLAP_PREVIOUS: the launch may begin while the kernel ahead of it
  * on the stream is still running (programmatic dependent launch): its blocks

@@ -335,6 +335,45 @@ def paged_append_decode(q: torch.Tensor, k_pool: torch.Tensor, v_pool: torch.Ten
     return out
 
 
+def paged_prefill(q: torch.Tensor, k_pool: torch.Tensor, v_pool: torch.Tensor,
+                  block_tables: torch.Tensor, q_start: torch.Tensor, q_len: torch.Tensor,
+                  ctx_lens: torch.Tensor, max_q_len: int, scale: float | None = None,
+                  out: torch.Tensor | None = None,
+                  out_dtype: torch.dtype | None = None) -> torch.Tensor:
+    """Chunked prefill attention (mz_paged_prefill): ``q [T, Hq, D]`` holds
+    sequence b's ``q_len[b]`` query tokens at rows ``q_start[b]...``; they sit
+    at the last ``q_len[b]`` of the sequence's ``ctx_lens[b]`` positions (their
+    K/V already appended) and attend causally."""
+    n_blocks, Hkv, bs, D = _check_pools(k_pool, v_pool)
+    if q.dim() != 3 or q.shape[2] != D or q.stride(-1) != 1 or q.dtype != k_pool.dtype:
+        raise ValueError(f"q must be [T, Hq, {D}] of the pool dtype with unit last stride")
+    T, Hq, _ = q.shape
+    B = block_tables.shape[0]
+    for t, name in ((q_start, "q_start"), (q_len, "q_len"), (ctx_lens, "ctx_lens")):
+        _as_i32(t, k_pool.device, name)
+        if t.numel() != B:
+            raise ValueError(f"{name} must hold one entry per sequence ({B})")
+    _as_i32(block_tables, k_pool.device, "block_tables")
+    out_dtype = out_dtype or q.dtype
+    if out is None:
+        out = torch.empty(q.shape, dtype=out_dtype, device=q.device)
+    if out.shape != q.shape or out.dtype != out_dtype or out.stride(-1) != 1:
+        raise ValueError("out must match q's shape with unit last stride")
+    if scale is None:
+        scale = D ** -0.5
+    if B == 0 or T == 0 or max_q_len == 0:
+        return out
+    dev = _dev_index(q)
+    nat.call("mz_paged_prefill", out.data_ptr(), dtype_code(out_dtype), out.stride(0),
+             out.stride(1), q.data_ptr(), q.stride(0), q.stride(1), q_start.data_ptr(),
+             q_len.data_ptr(), int(max_q_len), k_pool.data_ptr(), v_pool.data_ptr(),
+             block_tables.data_ptr(), block_tables.shape[1], ctx_lens.data_ptr(), B, Hq, Hkv,
+             D, bs, n_blocks, float(scale), dtype_code(q.dtype), error_word(dev).data_ptr(),
+             _stream(dev))
+    _after(dev)
+    return out
+
+
 def paged_append_decode_allgather(peers: "nat.PeerOutputs", q: torch.Tensor,
                                   k_pool: torch.Tensor, v_pool: torch.Tensor,
                                   k_new: torch.Tensor, v_new: torch.Tensor,

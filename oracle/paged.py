@@ -135,3 +135,54 @@ def block_unpack(pools: np.ndarray, ids: list[int], staging: np.ndarray) -> None
     raw = pools.reshape(P, pools.shape[1], -1).view(np.uint8)
     for i, b in enumerate(ids):
         raw[:, b] = staging[i]
+
+
+def prefill_attention(q: np.ndarray, k: np.ndarray, v: np.ndarray, start: int,
+                      scale: float | None = None) -> np.ndarray:
+    """Causal attention of a prompt chunk at cache offset ``start``.
+
+    The reference runs a prompt (or a ChunkedPrefillScheduler chunk,
+    src/mlxz/scheduler/chunker.py:53-76) through mlx_lm's model forward
+    (mlx-lm >=0.21,<0.23, pyproject.toml:11; not vendored), whose attention is
+    scaled_dot_product_attention with the causal mask of a chunk of n queries
+    over a cache of ``start`` tokens: query i sees key j iff j <= start + i.
+
+    q: (Hq, n, D) float; k, v: (Hkv, start + n, D) float.  Query token i sees
+    keys [0, start + i]; query head h reads KV head h // (Hq // Hkv).  Float64.
+    """
+    Hq, n, D = q.shape
+    Hkv = k.shape[0]
+    G = Hq // Hkv
+    scale = D ** -0.5 if scale is None else scale
+    kk = np.repeat(k.astype(np.float64), G, axis=0)
+    vv = np.repeat(v.astype(np.float64), G, axis=0)
+    s = np.einsum("hqd,htd->hqt", q.astype(np.float64), kk) * scale
+    T = k.shape[1]
+    mask = np.arange(T)[None, :] > (start + np.arange(n))[:, None]
+    s = np.where(mask[None], -np.inf, s)
+    s = s - s.max(axis=-1, keepdims=True)
+    p = np.exp(s)
+    p /= p.sum(axis=-1, keepdims=True)
+    return np.einsum("hqt,htd->hqd", p, vv)
+
+
+def paged_prefill(q: np.ndarray, k_pool: np.ndarray, v_pool: np.ndarray, tables: np.ndarray,
+                  q_start: np.ndarray, q_len: np.ndarray, ctx_lens: np.ndarray, dtype: str,
+                  scale: float | None = None) -> np.ndarray:
+    """Batched form: sequence b's q_len[b] query rows of q (T, Hq, D) uint16
+    bits, from row q_start[b], sit at the last q_len[b] of its ctx_lens[b]
+    tokens; gather its KV then prefill_attention.  Returns float64 (T, Hq, D);
+    rows of no sequence stay zero."""
+    from .rng import to_f32
+
+    bs = k_pool.shape[2]
+    out = np.zeros(q.shape, dtype=np.float64)
+    for b in range(len(q_len)):
+        n, c, r0 = int(q_len[b]), int(ctx_lens[b]), int(q_start[b])
+        if n == 0:
+            continue
+        kb, vb = gather(k_pool, v_pool, list(tables[b]), c, bs)
+        qb = to_f32(q[r0:r0 + n], dtype).transpose(1, 0, 2)  # (Hq, n, D)
+        o = prefill_attention(qb, to_f32(kb, dtype), to_f32(vb, dtype), c - n, scale)
+        out[r0:r0 + n] = o.transpose(1, 0, 2)
+    return out
