@@ -196,7 +196,8 @@ MZ_API int mz_paged_append_decode(void *out, int32_t out_dtype, int64_t out_seq_
  * ChunkedPrefillScheduler.get_next_chunk (src/mlxz/scheduler/chunker.py:53-76):
  * mlx_lm's causal scaled_dot_product_attention of a prompt chunk at a cache
  * offset, here over paged KV.  Supported: F16 / BF16, head_dim 64 or 128,
- * block_size a multiple of 16, n_heads / n_kv_heads dividing 16. */
+ * block_size a multiple of 16, n_heads / n_kv_heads dividing 128, scale > 0;
+ * q and out 16-byte aligned with strides of whole 16-byte vectors. */
 MZ_API int mz_paged_prefill(void *out, int32_t out_dtype, int64_t out_tok_stride,
                             int64_t out_head_stride, const void *q, int64_t q_tok_stride,
                             int64_t q_head_stride, const int32_t *q_start, const int32_t *q_len,

@@ -640,15 +640,16 @@ inline PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
-// 2-D tensor map over `rows` rows of `row_elems` elements, box = box_elems x 16
-// rows, 128-byte swizzle.
+// 2-D tensor map over `rows` rows of `row_elems` elements, box = box_elems x
+// box_rows rows, 128-byte swizzle.
 inline int make_row_map(CUtensorMap *m, const void *base, int64_t rows, int row_elems,
-                        CUtensorMapDataType type, int elem_bytes, int box_elems) {
+                        CUtensorMapDataType type, int elem_bytes, int box_elems,
+                        int box_rows = kTileTok) {
   auto fn = encode_fn();
   if (!fn) return fail(MZ_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
   cuuint64_t dims[2] = {static_cast<cuuint64_t>(row_elems), static_cast<cuuint64_t>(rows)};
   cuuint64_t strides[1] = {static_cast<cuuint64_t>(row_elems) * elem_bytes};
-  cuuint32_t box[2] = {static_cast<cuuint32_t>(box_elems), static_cast<cuuint32_t>(kTileTok)};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(box_elems), static_cast<cuuint32_t>(box_rows)};
   cuuint32_t es[2] = {1, 1};
   CUresult r = fn(m, type, 2, const_cast<void *>(base), dims, strides, box, es,
                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,

@@ -5,17 +5,11 @@
 // token i attends causally to the sequence's first ctx_b - n_b + i + 1 tokens,
 // as the causal SDPA of a prompt chunk over a cache of that offset does.
 //
-// One CTA per (query block, KV head, sequence): 4 warps, each with 16 query
-// rows (16/G tokens x the G query heads of the KV head), so a CTA covers
-// 64/G tokens and reads every K/V tile of its causal range once for all 64
-// rows.  Thread 0 streams the tiles with 2-D bulk tensor copies (128-byte
-// swizzle, no multicast) into a 4-stage ring shared by the warps: a stage's
-// "full" mbarrier completes on the copy's bytes, its "empty" mbarrier on the
-// four warps' release, after which thread 0 refills it.  Per warp and tile:
-// S = Q.K^T with mma.sync.m16n8k16, the causal mask per row, an fp32 online
-// softmax in the exp2 domain, O += P.V (bf16: P as hi + lo parts).  Every wait
-// is bounded; a wait that gives up sets MZ_DEVERR_TIMEOUT and the CTA stops.
+// Tensor-core form (tcgen05 + TMEM), see the kernel's own comment below.
+// Shapes: head_dim 64 or 128, n_heads / n_kv_heads dividing 128, block_size a
+// multiple of 16, scale > 0 (the row max is taken on the raw scores).
 #include "decode_common.cuh"
+#include "tcgen05.cuh"
 
 namespace mz {
 namespace prefill {
@@ -23,9 +17,6 @@ namespace prefill {
 using decode::kTileTok;
 using decode::kTimeoutNs;
 using decode::make_row_map;
-
-constexpr int kWarps = 4;
-constexpr int kStages = 4;
 
 struct PParams {
   void *out;
@@ -39,280 +30,456 @@ struct PParams {
   const int32_t *ctx;      // [B] tokens in the pools, the chunk included
   const int32_t *tables;
   int max_blocks;
-  int B, Hkv, G, bs, tpb;
+  int B, Hkv, G, bs;
   int64_t n_blocks;
   float scale_log2;
-  int tok_per_warp;  // 16 / G
+  int sub_log2;      // rows per bulk copy box: gcd(block_size, 128) = 1 << sub_log2
   int32_t *err;
-};
-
-template <int D>
-struct PCfg {
-  static constexpr int kTileBytes = kTileTok * D * 2;  // one of K or V
-  static constexpr int kStageBytes = 2 * kTileBytes;
-  static constexpr int kSmemBytes = kStages * kStageBytes + 2 * kStages * 8 + 1024;
 };
 
 __device__ __forceinline__ void mbar_arrive(uint32_t bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
 }
 
+// ---------------------------------------------------------------------------
+// One CTA per (128 query rows, KV head, sequence): row m is
+// token q0 + m / G, query head h*G + m % G.  Six warps:
+//   warps 0-3  softmax + epilogue; thread t owns row t (TMEM lane t)
+//   warp 4     streams 128-key K and V tiles (2-D bulk tensor copies of
+//              gcd(block_size, 128)-row boxes, 128-byte swizzle, no
+//              multicast) into a 3-stage K ring (a slot frees when its S MMA
+//              completes) and a 2-stage V ring (when its PV MMA completes), K
+//              running one tile ahead of V
+//   warp 5     allocates TMEM and issues the MMAs (one elected lane)
+// TMEM columns: O [0, D) fp32; three 128-column S buffers at 128, 256, 384.
+// Per key tile i:  S_i = Q.K_i^T (SS MMA, M=128 N=128 K=16 steps) into buffer
+// i % 3; softmax reads S_i, writes P_i over it (16-bit, two per column; bf16 as
+// hi + lo halves in columns [0,64) and [64,128)); O += P_i.V_i (TS MMA, A = P
+// from TMEM, B = V MN-major, N = D).  S_{i+1} is issued before PV_i so the
+// tensor core works on it during softmax_i.  The running max is only moved
+// when a row's tile max exceeds it by more than 8 (log2 units): P then stays
+// below 2^8 and O is rescaled in TMEM only on those tiles.
+// Every wait is bounded; a wait that gives up sets MZ_DEVERR_TIMEOUT and the
+// abort flag, every role leaves its loop, the issuing threads wait (bounded)
+// for their copies / MMAs in flight, and warp 5 frees the TMEM.
+namespace tcp {
+constexpr int kM = 128;
+constexpr int kN = 128;
+constexpr int kKRing = 3;
+constexpr int kVRing = 2;
+constexpr int kSBufs = 3;
+constexpr int kThreads = 192;
+constexpr uint32_t kTmemCols = 512;
+constexpr float kRescaleLog2 = 8.f;
+
+template <int D>
+struct TCfg {
+  static constexpr int kChunk = kN * 128;               // 128 keys x 64 dims
+  static constexpr int kTile = (D / 64) * kChunk;       // one K or V tile
+  static constexpr int kQ = (D / 64) * kM * 128;        // 128 rows x D
+  static constexpr int kK0 = kQ;                        // K slot s at kK0 + s kTile
+  static constexpr int kV0 = kQ + kKRing * kTile;       // V slot s at kV0 + s kTile
+  static constexpr int kBar = kV0 + kVRing * kTile;     // barriers after the tiles
+  static constexpr int kSmemBytes = kBar + 256 + 1024;
+};
+
+// barrier slots (8 bytes each) after the tiles
+constexpr int kBarKFull = 0, kBarVFull = 3, kBarSFull = 5, kBarPFull = 8, kBarPvDone = 11,
+              kBarDrain = 14, kNumBars = 15;
+static_assert(kKRing == kSBufs, "K slots are released through the S barriers");
+}  // namespace tcp
+
 template <int D, bool BF16>
-__global__ void __launch_bounds__(kWarps * 32, 1)
-    paged_prefill_kernel(const __grid_constant__ CUtensorMap tmK,
-                         const __grid_constant__ CUtensorMap tmV, const PParams p) {
-  using C = PCfg<D>;
-  constexpr int S = kStages;
-  constexpr int KS = D / 16;
-  constexpr int NT = D / 8;
+__global__ void __launch_bounds__(tcp::kThreads, 1)
+    paged_prefill_tc_kernel(const __grid_constant__ CUtensorMap tmK,
+                            const __grid_constant__ CUtensorMap tmV, const PParams p) {
+  using namespace tcp;
+  using C = TCfg<D>;
   const int b = blockIdx.z, h = blockIdx.y;
-  const int tpc = kWarps * p.tok_per_warp;  // query tokens per CTA
+  const int tpc = kM / p.G;
   const int n = p.q_len[b];
   const int q0 = blockIdx.x * tpc;
   if (n <= 0 || q0 >= n) return;
-  int ctx = p.ctx[b];
-  const int cap = p.max_blocks * p.bs;
-  if (ctx < n || ctx > cap) {
+  const int ctx = p.ctx[b];
+  if (ctx < n || ctx > p.max_blocks * p.bs) {
     if (threadIdx.x == 0) dev_error(p.err, MZ_DEVERR_CONTEXT);
     return;
   }
-  const int start = ctx - n;              // position of query token 0
-  const int q_hi = min(q0 + tpc, n);      // query tokens [q0, q_hi) in this CTA
-  const int kv_len = start + q_hi;        // keys [0, kv_len) are needed
-  const int ntiles = (kv_len + kTileTok - 1) / kTileTok;
+  const int start = ctx - n;
+  const int q_hi = min(q0 + tpc, n);
+  const int kv_len = start + q_hi;
+  const int ntiles = (kv_len + kN - 1) / kN;
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                               ~static_cast<uintptr_t>(1023));
-  const uint32_t stage0 = smem_u32(smem);
-  const uint32_t full0 = stage0 + S * C::kStageBytes;
-  const uint32_t empty0 = full0 + 8 * S;
+  const uint32_t sbase = smem_u32(smem);
+  const uint32_t qs = sbase;
+  auto kst = [&](int s) { return sbase + C::kK0 + s * C::kTile; };
+  auto vst = [&](int s) { return sbase + C::kV0 + s * C::kTile; };
+  const uint32_t bars = sbase + C::kBar;
+  auto bar = [&](int i) { return bars + 8 * i; };
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + C::kBar + 8 * kNumBars);
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + C::kBar + 8 * kNumBars + 4);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < S; ++s) {
-      mbar_init(full0 + 8 * s, 1);
-      mbar_init(empty0 + 8 * s, kWarps);
+    for (int s = 0; s < kKRing; ++s) mbar_init(bar(kBarKFull + s), 1);
+    for (int s = 0; s < kVRing; ++s) mbar_init(bar(kBarVFull + s), 1);
+    for (int s = 0; s < kSBufs; ++s) {
+      mbar_init(bar(kBarSFull + s), 1);
+      mbar_init(bar(kBarPFull + s), 4);
+      mbar_init(bar(kBarPvDone + s), 1);
     }
+    mbar_init(bar(kBarDrain), 1);
+    *abort_flag = 0;
     fence_mbar_init();
   }
+  if (warp == 5) tc::tmem_alloc(smem_u32(tmem_slot), kTmemCols);
+
+  // this thread's row (softmax warps)
+  const int row = threadIdx.x;
+  const int tok = q0 + row / p.G;
+  const int hq = h * p.G + row % p.G;
+  const bool live = warp < 4 && tok < q_hi;
+  const int lim = start + min(tok, q_hi - 1);  // last visible key of the row
+  if (warp < 4) {
+    // Q row -> shared memory in the 128-byte-swizzled K-major layout
+    const uint4 *src = reinterpret_cast<const uint4 *>(
+        static_cast<const uint16_t *>(p.q) + (int64_t)(p.q_start[b] + tok) * p.q_st +
+        (int64_t)hq * p.q_sh);
+#pragma unroll
+    for (int u = 0; u < D / 8; ++u) {
+      const uint4 v = live ? src[u] : make_uint4(0, 0, 0, 0);
+      const int c = u >> 3, uu = u & 7;
+      *reinterpret_cast<uint4 *>(smem + c * (kM * 128) + row * 128 + ((uu ^ (row & 7)) << 4)) = v;
+    }
+    fence_proxy_async_smem();
+  }
+  tc::fence_before_sync();
   __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tmem = *tmem_slot;
 
-  const uint64_t pol = l2_policy_evict_first();
-  auto issue = [&](int t) {  // thread 0: tile t into stage t % S
-    const int s = t % S;
-    int32_t blk = p.tables[(int64_t)b * p.max_blocks + t / p.tpb];
-    if (blk < 0 || blk >= p.n_blocks) {
-      dev_error(p.err, MZ_DEVERR_BLOCK_ID);
-      blk = 0;
-    }
-    const int y = static_cast<int>(((int64_t)blk * p.Hkv + h) * p.bs + (t % p.tpb) * kTileTok);
-    const uint32_t bar = full0 + 8 * s;
-    const uint32_t dk = stage0 + s * C::kStageBytes;
-    mbar_arrive_expect_tx(bar, C::kStageBytes);
-#pragma unroll
-    for (int c2 = 0; c2 < D / 64; ++c2) {
-      tma_load_2d(dk + c2 * 2048, &tmK, c2 * 64, y, bar, pol);
-      tma_load_2d(dk + C::kTileBytes + c2 * 2048, &tmV, c2 * 64, y, bar, pol);
-    }
+  auto give_up = [&]() {
+    dev_error(p.err, MZ_DEVERR_TIMEOUT);
+    *abort_flag = 1;
   };
-  int issued = 0;  // tiles issued so far (thread 0's count)
-  if (threadIdx.x == 0)
-    for (; issued < S && issued < ntiles; ++issued) issue(issued);
 
-  // This warp's rows: r = 0..15 <-> token q0 + warp*tpw + r / G, head h*G + r % G.
-  const int g = lane >> 2, cq = lane & 3;
-  const int mi = lane >> 3, r8 = lane & 7;
-  const int tokK = r8 + 8 * (mi >> 1), subK = mi & 1;
-  const int tokV = r8 + 8 * (mi & 1), subV = mi >> 1;
-  const int tw0 = q0 + warp * p.tok_per_warp;  // first query token of the warp
-  const int t_row0 = tw0 + g / p.G, t_row1 = tw0 + (g + 8) / p.G;
-  const bool live0 = t_row0 < q_hi, live1 = t_row1 < q_hi;
-  // causal limit (last visible key position); rows past the chunk reuse the
-  // last live token's so that their (unstored) softmax stays finite
-  const int lim0 = start + min(t_row0, q_hi - 1), lim1 = start + min(t_row1, q_hi - 1);
-
-  uint32_t qa[KS][4];
-  {
-    const auto *q16 = static_cast<const uint16_t *>(p.q);
-    const int64_t base0 = (int64_t)(p.q_start[b] + t_row0) * p.q_st + (int64_t)(h * p.G + g % p.G) * p.q_sh;
-    const int64_t base1 =
-        (int64_t)(p.q_start[b] + t_row1) * p.q_st + (int64_t)(h * p.G + (g + 8) % p.G) * p.q_sh;
-#pragma unroll
-    for (int j = 0; j < KS; ++j) {
-      const int d = 16 * j + 2 * cq;
-      qa[j][0] = live0 ? *reinterpret_cast<const uint32_t *>(q16 + base0 + d) : 0u;
-      qa[j][1] = live1 ? *reinterpret_cast<const uint32_t *>(q16 + base1 + d) : 0u;
-      qa[j][2] = live0 ? *reinterpret_cast<const uint32_t *>(q16 + base0 + d + 8) : 0u;
-      qa[j][3] = live1 ? *reinterpret_cast<const uint32_t *>(q16 + base1 + d + 8) : 0u;
-    }
-  }
-  float oacc[NT][4];
-#pragma unroll
-  for (int k = 0; k < NT; ++k) oacc[k][0] = oacc[k][1] = oacc[k][2] = oacc[k][3] = 0.f;
-  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
-
-  for (int i = 0; i < ntiles; ++i) {
-    const int s = i % S;
-    const uint32_t ph = (i / S) & 1;
-    if (!__all_sync(0xffffffffu, mbar_wait_bounded(full0 + 8 * s, ph, kTimeoutNs))) {
-      if (lane == 0) dev_error(p.err, MZ_DEVERR_TIMEOUT);
-      // the issuing thread waits (bounded) for its copies still in flight
-      if (threadIdx.x == 0)
-        for (int k = i + 1; k < issued; ++k)
-          (void)mbar_wait_bounded(full0 + 8 * (k % S), (k / S) & 1, kTimeoutNs);
-      return;
-    }
-    uint8_t *vt = smem + s * C::kStageBytes + C::kTileBytes;
-    const uint32_t kb = stage0 + s * C::kStageBytes;
-    const uint32_t vb = kb + C::kTileBytes;
-    const int t0 = i * kTileTok;
-    const int nvalid = min(kTileTok, kv_len - t0);
-    if (nvalid < kTileTok) {
-      // keys past kv_len may be stale: exact zeros so that 0 * V stays 0
-      // (every warp writes the same zeros before it reads)
-      for (int e = lane; e < (kTileTok - nvalid) * (D / 8); e += 32) {
-        const int tok = nvalid + e / (D / 8), d = (e % (D / 8)) * 8;
-        *reinterpret_cast<uint4 *>(vt + decode::swz128(tok, 2 * d)) = make_uint4(0, 0, 0, 0);
+  if (warp == 4) {
+    // ---------------- producer (whole warp) ----------------
+    // A tile is nst = 128 / sub boxes of sub = gcd(block_size, 128) keys.
+    // Block rows come in groups of four tiles: lane l < 4 nst covers box
+    // l % nst of tile 4g + l / nst.  A group's block ids are loaded four steps
+    // before use and only then checked and turned into pool rows, so the
+    // loads' latency stays off the issue path; a shuffle hands each issuing
+    // lane (lane < nst: box lane) the row it copies.
+    const uint64_t pol = l2_policy_evict_last();
+    const int sub = 1 << p.sub_log2, nst_log2 = 7 - p.sub_log2, nst = 1 << nst_log2;
+    auto group_key = [&](int g) {
+      return lane < 4 * nst ? (4 * g + (lane >> nst_log2)) * kN + (lane & (nst - 1)) * sub
+                            : kv_len;
+    };
+    auto group_ids = [&](int g) -> int32_t {
+      const int t = group_key(g);
+      return t < kv_len ? p.tables[(int64_t)b * p.max_blocks + t / p.bs] : 0;
+    };
+    auto group_rows = [&](int g, int32_t blk) -> int {
+      const int t = group_key(g);
+      if (t >= kv_len) return 0;
+      if (blk < 0 || blk >= p.n_blocks) {
+        dev_error(p.err, MZ_DEVERR_BLOCK_ID);
+        blk = 0;
       }
+      return static_cast<int>(((int64_t)blk * p.Hkv + h) * p.bs + t % p.bs);
+    };
+    auto load = [&](const CUtensorMap *tm, uint32_t dst, uint32_t fbar, int j, int y) {
+      const int nsub = min(nst, (kv_len - j * kN + sub - 1) >> p.sub_log2);
+      if (lane == 0)
+        mbar_arrive_expect_tx(fbar, static_cast<uint32_t>(nsub * (D / 64) * sub * 128));
       __syncwarp();
-    }
-
-    float sacc[2][4];
+      if (lane < nsub) {
 #pragma unroll
-    for (int k = 0; k < 2; ++k) sacc[k][0] = sacc[k][1] = sacc[k][2] = sacc[k][3] = 0.f;
-#pragma unroll
-    for (int j = 0; j < KS; ++j) {
-      uint32_t b0, b1, b2, b3;
-      ldsm_x4(kb + decode::swz128(tokK, 2 * (16 * j + 8 * subK)), b0, b1, b2, b3);
-      mma_16816<BF16>(sacc[0], qa[j], b0, b1);
-      mma_16816<BF16>(sacc[1], qa[j], b2, b3);
-    }
-
-    float mx0 = -INFINITY, mx1 = -INFINITY;
-#pragma unroll
-    for (int k = 0; k < 2; ++k)
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int key = t0 + k * 8 + 2 * cq + (e & 1);
-        float x = sacc[k][e] * p.scale_log2;
-        if (key >= kv_len || key > (e < 2 ? lim0 : lim1)) x = -INFINITY;
-        sacc[k][e] = x;
-        if (e < 2) mx0 = fmaxf(mx0, x); else mx1 = fmaxf(mx1, x);
+        for (int c = 0; c < D / 64; ++c)
+          tma_load_2d(dst + c * C::kChunk + lane * (sub * 128), tm, c * 64, y, fbar, pol);
       }
-    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
-    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
-    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
-    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
-    // a row whose keys in this tile are all masked keeps its running max
-    const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
-    const float a0 = (mn0 == -INFINITY) ? 1.f : fast_exp2(m0 - mn0);
-    const float a1 = (mn1 == -INFINITY) ? 1.f : fast_exp2(m1 - mn1);
-    m0 = mn0;
-    m1 = mn1;
-    float rs0 = 0.f, rs1 = 0.f;
-#pragma unroll
-    for (int k = 0; k < 2; ++k) {
-      sacc[k][0] = (m0 == -INFINITY) ? 0.f : fast_exp2(sacc[k][0] - m0);
-      sacc[k][1] = (m0 == -INFINITY) ? 0.f : fast_exp2(sacc[k][1] - m0);
-      sacc[k][2] = (m1 == -INFINITY) ? 0.f : fast_exp2(sacc[k][2] - m1);
-      sacc[k][3] = (m1 == -INFINITY) ? 0.f : fast_exp2(sacc[k][3] - m1);
-      rs0 += sacc[k][0] + sacc[k][1];
-      rs1 += sacc[k][2] + sacc[k][3];
-    }
-    l0 = l0 * a0 + rs0;
-    l1 = l1 * a1 + rs1;
-    if (__any_sync(0xffffffffu, a0 != 1.f || a1 != 1.f)) {
-#pragma unroll
-      for (int k = 0; k < NT; ++k) {
-        oacc[k][0] *= a0;
-        oacc[k][1] *= a0;
-        oacc[k][2] *= a1;
-        oacc[k][3] *= a1;
+    };
+    int k_issued = 0, v_issued = 0;
+    int y_prv = 0, y_cur = group_rows(0, group_ids(0));
+    int32_t id_nxt = group_ids(1);
+    // step t: K_t, then V_{t-1}
+    for (int t = 0; t <= ntiles; ++t) {
+      if (__any_sync(0xffffffffu, *abort_flag != 0)) break;
+      if (t > 0 && (t & 3) == 0) {
+        y_prv = y_cur;
+        y_cur = group_rows(t >> 2, id_nxt);
+        id_nxt = group_ids((t >> 2) + 1);
+      }
+      if (t < ntiles) {
+        const int s = t % kKRing;
+        const int y = __shfl_sync(0xffffffffu, y_cur, ((t & 3) << nst_log2) + (lane & (nst - 1)));
+        // K slot s frees when S_{t-3} completed (kKRing == kSBufs)
+        if (t >= kKRing &&
+            !__all_sync(0xffffffffu, mbar_wait_bounded(bar(kBarSFull + (t - kKRing) % kSBufs),
+                                                        ((t - kKRing) / kSBufs) & 1, kTimeoutNs))) {
+          if (lane == 0) give_up();
+          break;
+        }
+        load(&tmK, kst(s), bar(kBarKFull + s), t, y);
+        k_issued = t + 1;
+      }
+      if (t >= 1) {
+        const int j = t - 1, s = j % kVRing;
+        const int y = __shfl_sync(0xffffffffu, (j >> 2) == (t >> 2) ? y_cur : y_prv,
+                                  ((j & 3) << nst_log2) + (lane & (nst - 1)));
+        // V slot s frees when PV_{j-2} completed
+        if (j >= kVRing &&
+            !__all_sync(0xffffffffu, mbar_wait_bounded(bar(kBarPvDone + (j - kVRing) % kSBufs),
+                                                        ((j - kVRing) / kSBufs) & 1, kTimeoutNs))) {
+          if (lane == 0) give_up();
+          break;
+        }
+        load(&tmV, vst(s), bar(kBarVFull + s), j, y);
+        v_issued = j + 1;
       }
     }
-
-    uint32_t ph_[4], pl_[4];
-    {
-      float hi[2][4];
-#pragma unroll
-      for (int k = 0; k < 2; ++k)
-#pragma unroll
-        for (int e = 0; e < 4; ++e) hi[k][e] = round16<BF16>(sacc[k][e]);
-      ph_[0] = pack2<BF16>(hi[0][0], hi[0][1]);
-      ph_[1] = pack2<BF16>(hi[0][2], hi[0][3]);
-      ph_[2] = pack2<BF16>(hi[1][0], hi[1][1]);
-      ph_[3] = pack2<BF16>(hi[1][2], hi[1][3]);
-      if constexpr (BF16) {
-        pl_[0] = pack2<BF16>(sacc[0][0] - hi[0][0], sacc[0][1] - hi[0][1]);
-        pl_[1] = pack2<BF16>(sacc[0][2] - hi[0][2], sacc[0][3] - hi[0][3]);
-        pl_[2] = pack2<BF16>(sacc[1][0] - hi[1][0], sacc[1][1] - hi[1][1]);
-        pl_[3] = pack2<BF16>(sacc[1][2] - hi[1][2], sacc[1][3] - hi[1][3]);
-      }
+    // copies still in flight land before the CTA leaves
+    if (lane == 0) {
+      for (int j = max(0, k_issued - kKRing); j < k_issued; ++j)
+        (void)mbar_wait_bounded(bar(kBarKFull + j % kKRing), (j / kKRing) & 1, kTimeoutNs);
+      for (int j = max(0, v_issued - kVRing); j < v_issued; ++j)
+        (void)mbar_wait_bounded(bar(kBarVFull + j % kVRing), (j / kVRing) & 1, kTimeoutNs);
     }
-#pragma unroll
-    for (int j = 0; j < KS; ++j) {
-      uint32_t v0, v1, v2, v3;
-      ldsm_x4_trans(vb + decode::swz128(tokV, 2 * (16 * j + 8 * subV)), v0, v1, v2, v3);
-      mma_16816<BF16>(oacc[2 * j], ph_, v0, v1);
-      mma_16816<BF16>(oacc[2 * j + 1], ph_, v2, v3);
-      if constexpr (BF16) {
-        mma_16816<BF16>(oacc[2 * j], pl_, v0, v1);
-        mma_16816<BF16>(oacc[2 * j + 1], pl_, v2, v3);
-      }
-    }
-
-    // release the stage; thread 0 refills it once all four warps have
     __syncwarp();
-    if (lane == 0) mbar_arrive(empty0 + 8 * s);
-    if (threadIdx.x == 0 && i + S < ntiles) {
-      if (!mbar_wait_bounded(empty0 + 8 * s, ph, kTimeoutNs)) {
-        dev_error(p.err, MZ_DEVERR_TIMEOUT);
-      } else {
+  } else if (warp == 5) {
+    // ---------------- MMA issue (whole warp, one elected lane issues) ----------------
+    constexpr uint32_t idS = tc::idesc_f16(BF16, kM, kN, false);
+    constexpr uint32_t idPV = tc::idesc_f16(BF16, kM, D, true);
+    const uint32_t tm0 = __shfl_sync(0xffffffffu, tmem, 0);
+    auto issue_s = [&](int j) -> bool {
+      const int s = j % kKRing, buf = j % kSBufs;
+      if (!__all_sync(0xffffffffu,
+                      mbar_wait_bounded(bar(kBarKFull + s), (j / kKRing) & 1, kTimeoutNs)))
+        return false;
+      // buffer j % 3 is free once PV_{j-3} (which read P from it) completed
+      if (j >= kSBufs &&
+          !__all_sync(0xffffffffu, mbar_wait_bounded(bar(kBarPvDone + buf),
+                                                      ((j - kSBufs) / kSBufs) & 1, kTimeoutNs)))
+        return false;
+      tc::fence_after_sync();
+      const uint32_t d = tm0 + 128 * (1 + buf);
+#pragma unroll
+      for (int k = 0; k < D / 16; ++k) {
+        const uint32_t off = (k >> 2) * C::kChunk + (k & 3) * 32;
+        tc::mma_ss_elect(d, tc::smem_desc_sw128(qs + off, 16, 1024),
+                         tc::smem_desc_sw128(kst(s) + off, 16, 1024), idS, k > 0);
+      }
+      tc::commit_elect(bar(kBarSFull + buf));  // also frees K slot s
+      return true;
+    };
+    bool ok = issue_s(0);
+    for (int i = 0; ok && i < ntiles; ++i) {
+      if (__any_sync(0xffffffffu, *abort_flag != 0)) break;
+      if (i + 1 < ntiles && !issue_s(i + 1)) {
+        ok = false;
+        break;
+      }
+      const int s = i % kVRing, buf = i % kSBufs;
+      if (!__all_sync(0xffffffffu,
+                      mbar_wait_bounded(bar(kBarPFull + buf), (i / kSBufs) & 1, kTimeoutNs) &&
+                          mbar_wait_bounded(bar(kBarVFull + s), (i / kVRing) & 1, kTimeoutNs))) {
+        ok = false;
+        break;
+      }
+      tc::fence_after_sync();
+      const uint32_t pcol = tm0 + 128 * (1 + buf);
+#pragma unroll
+      for (int kk = 0; kk < kN / 16; ++kk) {
+        const uint64_t dv = tc::smem_desc_sw128(vst(s) + kk * 2048, C::kChunk, 1024);
+        tc::mma_ts_elect(tm0, pcol + 8 * kk, dv, idPV, (i > 0 || kk > 0) ? 1u : 0u);
+        if constexpr (BF16) tc::mma_ts_elect(tm0, pcol + 64 + 8 * kk, dv, idPV, 1u);
+      }
+      tc::commit_elect(bar(kBarPvDone + buf));  // also frees V slot s
+    }
+    if (!ok && lane == 0) give_up();
+    // every MMA issued has completed before the TMEM is freed
+    tc::commit_elect(bar(kBarDrain));
+    (void)mbar_wait_bounded(bar(kBarDrain), 0, kTimeoutNs);
+    __syncwarp();
+  } else {
+    // ---------------- softmax + epilogue (warps 0-3) ----------------
+    const uint32_t tl = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+    float m_used = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int i = 0; i < ntiles; ++i) {
+      if (__any_sync(0xffffffffu, *abort_flag != 0)) {
+        ok = false;
+        break;
+      }
+      const int buf = i % kSBufs;
+      if (!__all_sync(0xffffffffu,
+                      mbar_wait_bounded(bar(kBarSFull + buf), (i / kSBufs) & 1, kTimeoutNs))) {
+        if (lane == 0) give_up();
+        ok = false;
+        break;
+      }
+      tc::fence_after_sync();
+      float sv[kN];
+      {
+        uint32_t r[kN / 32][32];
+#pragma unroll
+        for (int c = 0; c < kN / 32; ++c) tc::ld32(tl + 128 * (1 + buf) + 32 * c, r[c]);
+        tc::wait_ld();
+#pragma unroll
+        for (int c = 0; c < kN / 32; ++c)
+#pragma unroll
+          for (int j = 0; j < 32; ++j) sv[32 * c + j] = __uint_as_float(r[c][j]);
+      }
+      const int key0 = i * kN;
+      if (key0 + kN - 1 > lim) {  // tile crosses this row's causal limit
+#pragma unroll
+        for (int j = 0; j < kN; ++j)
+          if (key0 + j > lim) sv[j] = -INFINITY;
+      }
+      // max over the raw scores (scale > 0), eight independent chains
+      float mx;
+      {
+        float m8[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) m8[j] = sv[j];
+#pragma unroll
+        for (int j = 8; j < kN; ++j) m8[j & 7] = fmaxf(m8[j & 7], sv[j]);
+        mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])),
+                   fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
+        mx *= p.scale_log2;
+      }
+      const bool need = mx > m_used + kRescaleLog2;
+      const float m_new = need ? mx : m_used;
+      const float alpha = need ? fast_exp2(m_used - m_new) : 1.f;
+      if (i > 0 && __any_sync(0xffffffffu, need)) {
+        const int pb = (i - 1) % kSBufs;
+        if (!__all_sync(0xffffffffu, mbar_wait_bounded(bar(kBarPvDone + pb),
+                                                        ((i - 1) / kSBufs) & 1, kTimeoutNs))) {
+          if (lane == 0) give_up();
+          ok = false;
+          break;
+        }
+        tc::fence_after_sync();
+#pragma unroll 1
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t r[32];
+          tc::ld32(tl + 32 * c, r);
+          tc::wait_ld();
+#pragma unroll
+          for (int j = 0; j < 32; ++j) r[j] = __float_as_uint(__uint_as_float(r[j]) * alpha);
+          tc::st32(tl + 32 * c, r);
+        }
+        tc::wait_st();
+      }
+      m_used = m_new;
+      const float neg_m = -m_used;
+      float l8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int c = 0; c < kN / 32; ++c) {
+        uint32_t hi[16], lo[16];
+#pragma unroll
+        for (int w = 0; w < 16; ++w) {
+          const float a = fast_exp2(fmaf(sv[32 * c + 2 * w], p.scale_log2, neg_m));
+          const float e = fast_exp2(fmaf(sv[32 * c + 2 * w + 1], p.scale_log2, neg_m));
+          l8[w & 7] += a + e;
+          hi[w] = pack2<BF16>(a, e);
+          if constexpr (BF16) {
+            const float ah = __uint_as_float(hi[w] << 16);
+            const float eh = __uint_as_float(hi[w] & 0xffff0000u);
+            lo[w] = pack2<BF16>(a - ah, e - eh);
+          }
+        }
+        tc::st16(tl + 128 * (1 + buf) + 16 * c, hi);
+        if constexpr (BF16) tc::st16(tl + 128 * (1 + buf) + 64 + 16 * c, lo);
+      }
+      l = l * alpha + (((l8[0] + l8[1]) + (l8[2] + l8[3])) + ((l8[4] + l8[5]) + (l8[6] + l8[7])));
+      const int nvalid = kv_len - key0;
+      if (nvalid < kN) {
+        // last tile: keys past kv_len hold stale smem / pool rows; their P is
+        // 0 but 0 * NaN is not, so the V rows become exact zeros first
+        const int s = i % kVRing;
+        if (!__all_sync(0xffffffffu,
+                        mbar_wait_bounded(bar(kBarVFull + s), (i / kVRing) & 1, kTimeoutNs))) {
+          if (lane == 0) give_up();
+          ok = false;
+          break;
+        }
+        const int units = (kN - nvalid) * (D / 8);
+        for (int e = threadIdx.x; e < units; e += 128) {
+          const int r = nvalid + e / (D / 8), u = e % (D / 8);
+          const int c = u >> 3, uu = u & 7;
+          *reinterpret_cast<uint4 *>(smem + C::kV0 + s * C::kTile + c * C::kChunk +
+                                     r * 128 + ((uu ^ (r & 7)) << 4)) = make_uint4(0, 0, 0, 0);
+        }
         fence_proxy_async_smem();
-        issue(i + S);
-        ++issued;
+      }
+      tc::wait_st();
+      tc::fence_before_sync();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(kBarPFull + buf));
+    }
+    if (ok) {
+      const int lb = (ntiles - 1) % kSBufs;
+      ok = __all_sync(0xffffffffu, mbar_wait_bounded(bar(kBarPvDone + lb),
+                                                     ((ntiles - 1) / kSBufs) & 1, kTimeoutNs));
+      if (!ok && lane == 0) give_up();
+    }
+    if (ok) {
+      tc::fence_after_sync();
+      const float inv = 1.f / l;
+      const int64_t ob = (int64_t)(p.q_start[b] + tok) * p.o_st + (int64_t)hq * p.o_sh;
+#pragma unroll
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t r[32];
+        tc::ld32(tl + 32 * c, r);
+        tc::wait_ld();
+        if (live) {
+          if (p.out_f32) {
+            float4 *dst = reinterpret_cast<float4 *>(static_cast<float *>(p.out) + ob + 32 * c);
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+              dst[j] = make_float4(__uint_as_float(r[4 * j]) * inv, __uint_as_float(r[4 * j + 1]) * inv,
+                                   __uint_as_float(r[4 * j + 2]) * inv,
+                                   __uint_as_float(r[4 * j + 3]) * inv);
+          } else {
+            uint4 *dst = reinterpret_cast<uint4 *>(static_cast<uint16_t *>(p.out) + ob + 32 * c);
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+              dst[j] = make_uint4(pack2<BF16>(__uint_as_float(r[8 * j]) * inv,
+                                              __uint_as_float(r[8 * j + 1]) * inv),
+                                  pack2<BF16>(__uint_as_float(r[8 * j + 2]) * inv,
+                                              __uint_as_float(r[8 * j + 3]) * inv),
+                                  pack2<BF16>(__uint_as_float(r[8 * j + 4]) * inv,
+                                              __uint_as_float(r[8 * j + 5]) * inv),
+                                  pack2<BF16>(__uint_as_float(r[8 * j + 6]) * inv,
+                                              __uint_as_float(r[8 * j + 7]) * inv));
+          }
+        }
       }
     }
   }
 
-  // normalise and store the live rows
-  float L0 = l0, L1 = l1;
-  L0 += __shfl_xor_sync(0xffffffffu, L0, 1);
-  L0 += __shfl_xor_sync(0xffffffffu, L0, 2);
-  L1 += __shfl_xor_sync(0xffffffffu, L1, 1);
-  L1 += __shfl_xor_sync(0xffffffffu, L1, 2);
-  const float i0 = 1.f / L0, i1 = 1.f / L1;
-  auto store = [&](int64_t off, float x, float y) {
-    if (p.out_f32) {
-      *reinterpret_cast<float2 *>(static_cast<float *>(p.out) + off) = make_float2(x, y);
-    } else if (p.q_bf16) {
-      *reinterpret_cast<__nv_bfloat162 *>(static_cast<__nv_bfloat16 *>(p.out) + off) =
-          __floats2bfloat162_rn(x, y);
-    } else {
-      *reinterpret_cast<__half2 *>(static_cast<__half *>(p.out) + off) = __floats2half2_rn(x, y);
-    }
-  };
-  if (live0) {
-    const int64_t o = (int64_t)(p.q_start[b] + t_row0) * p.o_st + (int64_t)(h * p.G + g % p.G) * p.o_sh;
-#pragma unroll
-    for (int k = 0; k < NT; ++k) store(o + k * 8 + 2 * cq, oacc[k][0] * i0, oacc[k][1] * i0);
-  }
-  if (live1) {
-    const int64_t o =
-        (int64_t)(p.q_start[b] + t_row1) * p.o_st + (int64_t)(h * p.G + (g + 8) % p.G) * p.o_sh;
-#pragma unroll
-    for (int k = 0; k < NT; ++k) store(o + k * 8 + 2 * cq, oacc[k][2] * i1, oacc[k][3] * i1);
+  tc::fence_before_sync();
+  __syncthreads();
+  if (warp == 5) {
+    tc::fence_after_sync();
+    tc::tmem_dealloc(tmem, kTmemCols);
   }
 }
 
 template <int D, bool BF16>
-int smem_attr() {
+int smem_attr_tc() {
   static std::once_flag once;
   static cudaError_t err = cudaSuccess;
   std::call_once(once, []() {
-    err = cudaFuncSetAttribute(paged_prefill_kernel<D, BF16>,
-                               cudaFuncAttributeMaxDynamicSharedMemorySize, PCfg<D>::kSmemBytes);
+    err = cudaFuncSetAttribute(paged_prefill_tc_kernel<D, BF16>,
+                               cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               tcp::TCfg<D>::kSmemBytes);
   });
   if (err != cudaSuccess) return cuda_fail(err, "mz_paged_prefill: shared memory attribute");
   return MZ_OK;
@@ -347,19 +514,21 @@ extern "C" int mz_paged_prefill(void *out, int32_t out_dtype, int64_t out_tok_st
       max_blocks_per_seq <= 0 || n_blocks <= 0)
     return fail(MZ_ERR_INVALID_ARG, "%s: bad sizes", fn);
   const int G = n_heads / n_kv_heads;
-  if (16 % G)
-    return fail(MZ_ERR_UNSUPPORTED, "%s: n_heads / n_kv_heads = %d does not divide 16", fn, G);
-  if (!std::isfinite(scale)) return fail(MZ_ERR_INVALID_ARG, "%s: scale not finite", fn);
+  if (tcp::kM % G)
+    return fail(MZ_ERR_UNSUPPORTED, "%s: n_heads / n_kv_heads = %d does not divide %d", fn, G,
+                tcp::kM);
+  if (!std::isfinite(scale) || !(scale > 0.f))
+    return fail(MZ_ERR_INVALID_ARG, "%s: scale must be finite and positive", fn);
   if (n_seqs == 0 || max_q_len == 0) return MZ_OK;
   if (!out || !q || !q_start || !q_len || !k_pool || !v_pool || !block_tables || !ctx_lens)
     return fail(MZ_ERR_INVALID_ARG, "%s: null pointer", fn);
-  if (!aligned(k_pool, 16) || !aligned(v_pool, 16) || !aligned(q, 4) || (q_tok_stride & 1) ||
-      (q_head_stride & 1))
+  // rows move as 16-byte vectors: q and out 16-byte aligned, strides whole vectors
+  const int oe = out_dtype == MZ_DTYPE_F32 ? 4 : 8;
+  if (!aligned(k_pool, 16) || !aligned(v_pool, 16) || !aligned(q, 16) || (q_tok_stride % 8) ||
+      (q_head_stride % 8) || !aligned(out, 16) || (out_tok_stride % oe) || (out_head_stride % oe))
     return fail(MZ_ERR_ALIGNMENT,
-                "%s: pools need 16-byte alignment, q 4-byte alignment and even strides", fn);
-  const int ob = out_dtype == MZ_DTYPE_F32 ? 8 : 4;
-  if (!aligned(out, ob) || (out_tok_stride & 1) || (out_head_stride & 1))
-    return fail(MZ_ERR_ALIGNMENT, "%s: out needs %d-byte alignment and even strides", fn, ob);
+                "%s: pools, q and out need 16-byte alignment and strides of whole 16-byte "
+                "vectors", fn);
   const int64_t rows_total = n_blocks * n_kv_heads * block_size;
   if (rows_total >= (int64_t(1) << 31))
     return fail(MZ_ERR_UNSUPPORTED, "%s: pool has >= 2^31 rows", fn);
@@ -367,8 +536,12 @@ extern "C" int mz_paged_prefill(void *out, int32_t out_dtype, int64_t out_tok_st
   const bool bf16 = dtype == MZ_DTYPE_BF16;
   CUtensorMap tk, tv;
   const auto type = bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
-  if (int rc = make_row_map(&tk, k_pool, rows_total, head_dim, type, 2, 64)) return rc;
-  if (int rc = make_row_map(&tv, v_pool, rows_total, head_dim, type, 2, 64)) return rc;
+  int sub_log2 = 4;  // rows per copy box: gcd(block_size, 128)
+  while (sub_log2 < 7 && block_size % (1 << (sub_log2 + 1)) == 0) ++sub_log2;
+  if (int rc = make_row_map(&tk, k_pool, rows_total, head_dim, type, 2, 64, 1 << sub_log2))
+    return rc;
+  if (int rc = make_row_map(&tv, v_pool, rows_total, head_dim, type, 2, 64, 1 << sub_log2))
+    return rc;
 
   PParams p;
   p.out = out;
@@ -388,28 +561,28 @@ extern "C" int mz_paged_prefill(void *out, int32_t out_dtype, int64_t out_tok_st
   p.Hkv = n_kv_heads;
   p.G = G;
   p.bs = block_size;
-  p.tpb = block_size / kTileTok;
   p.n_blocks = n_blocks;
   p.scale_log2 = static_cast<float>(static_cast<double>(scale) * 1.4426950408889634);
-  p.tok_per_warp = 16 / G;
+  p.sub_log2 = sub_log2;
   p.err = dev_err;
 
-  const int tpc = kWarps * p.tok_per_warp;
-  const dim3 grid((max_q_len + tpc - 1) / tpc, n_kv_heads, n_seqs);
-  if (grid.x > 2147483647u || n_seqs > 65535 || n_kv_heads > 65535)
-    return fail(MZ_ERR_UNSUPPORTED, "%s: grid too large", fn);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-#define MZ_PLAUNCH(D_, BF_)                                                                      \
+  if (n_seqs > 65535 || n_kv_heads > 65535)
+    return fail(MZ_ERR_UNSUPPORTED, "%s: grid too large", fn);
+  const int tpc = tcp::kM / G;
+  const dim3 grid((max_q_len + tpc - 1) / tpc, n_kv_heads, n_seqs);
+#define MZ_TCLAUNCH(D_, BF_)                                                                     \
   do {                                                                                           \
-    if (int rc = smem_attr<D_, BF_>()) return rc;                                                \
-    paged_prefill_kernel<D_, BF_><<<grid, kWarps * 32, PCfg<D_>::kSmemBytes, s>>>(tk, tv, p);     \
+    if (int rc = smem_attr_tc<D_, BF_>()) return rc;                                             \
+    paged_prefill_tc_kernel<D_, BF_>                                                             \
+        <<<grid, tcp::kThreads, tcp::TCfg<D_>::kSmemBytes, s>>>(tk, tv, p);                      \
   } while (0)
   if (head_dim == 128) {
-    if (bf16) MZ_PLAUNCH(128, true); else MZ_PLAUNCH(128, false);
+    if (bf16) MZ_TCLAUNCH(128, true); else MZ_TCLAUNCH(128, false);
   } else {
-    if (bf16) MZ_PLAUNCH(64, true); else MZ_PLAUNCH(64, false);
+    if (bf16) MZ_TCLAUNCH(64, true); else MZ_TCLAUNCH(64, false);
   }
-#undef MZ_PLAUNCH
+#undef MZ_TCLAUNCH
   MZ_CHECK_LAUNCH(fn);
   return MZ_OK;
 }

@@ -48,6 +48,8 @@ PREFILL_CASES = [
     ("f16", 128, 4, 64, [2000, 5], [200, 5]),
     ("bf16", 128, 2, 16, [16, 33, 1], [16, 33, 1]),
     ("bf16", 128, 1, 16, [4096], [128]),
+    ("f16", 128, 32, 128, [700, 260], [300, 260]),
+    ("bf16", 64, 4, 48, [1000, 333, 47], [513, 1, 47]),
 ]
 
 
@@ -116,6 +118,13 @@ def test_prefill_rejects_bad_inputs(cuda):
                           torch.zeros(1, dtype=torch.int32, device=cuda),
                           torch.full((1,), 10, dtype=torch.int32, device=cuda),
                           torch.full((1,), 20, dtype=torch.int32, device=cuda), 10)
+    # the row max is taken on raw scores: a non-positive scale is refused
+    q8 = torch.zeros(10, 8, D, dtype=torch.bfloat16, device=cuda)
+    with pytest.raises(NativeError):
+        ops.paged_prefill(q8, kp, kp, torch.from_numpy(case["tables"]).to(cuda),
+                          torch.zeros(1, dtype=torch.int32, device=cuda),
+                          torch.full((1,), 10, dtype=torch.int32, device=cuda),
+                          torch.full((1,), 20, dtype=torch.int32, device=cuda), 10, scale=-0.1)
     torch.cuda.synchronize()
 
 
