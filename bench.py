@@ -61,11 +61,12 @@ def parse_args():
                     help="append with mz_kv_append_paged, then mz_paged_decode (two launches)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--config", default="decode",
-                    choices=["decode", "prefix", "quant", "sharded70b"],
+                    choices=["decode", "prefix", "quant", "sharded70b", "prefill"],
                     help="decode: the paged decode step (headline); prefix: prefix-cache "
                          "restore / copy-on-write / host-tier eviction and reload; quant: "
                          "4/8-bit quantised KV decode step; sharded70b: 70B-shape decode "
-                         "step head-sharded over the ranks (strong scaling)")
+                         "step head-sharded over the ranks (strong scaling); prefill: one "
+                         "chunked-prefill iteration (append + causal attention per layer)")
     ap.add_argument("--bits", type=int, default=8, choices=[4, 8])
     ap.add_argument("--gather", default="p2p", choices=["p2p", "nccl"],
                     help="N > 1: p2p = output rows stored into every rank's buffer by the "
@@ -199,8 +200,246 @@ def cpu_sample(seed: int, budget_s: float, threads: int, n_seqs: int = 16):
             "layer_s": t, "n_seqs": n_seqs, "kv_bytes": kv_bytes}
 
 
+PF_B, PF_CHUNK, PF_CTX = 8, 512, 4096
+PF_METRIC = ("chunked-prefill attention TFLOP/s and prefill tok/s, 8B shape, "
+             "8 x 512-token chunks at offset 3584")
+
+
+def prefill_flops_layer(n_seqs: int = PF_B) -> float:
+    """Causal attention FLOPs of one layer: QK^T and PV, 2 per multiply-add,
+    over every (query, visible key) pair."""
+    start = PF_CTX - PF_CHUNK
+    pairs = PF_CHUNK * start + PF_CHUNK * (PF_CHUNK + 1) // 2
+    return 4.0 * D * HQ * pairs * n_seqs
+
+
+def cpu_prefill_sample(seed: int, threads: int):
+    """Times oracle.cpu_path.prefill_layer (torch-CPU restatement of a prompt
+    chunk's append + causal GQA attention) on one sequence of one layer."""
+    import torch
+
+    from oracle import cpu_path
+
+    torch.set_num_threads(threads)
+    g = torch.Generator().manual_seed(seed)
+    nb = PF_CTX // BS
+    kp = torch.randn((nb, HKV, BS, D), generator=g).to(torch.bfloat16)
+    vp = torch.randn((nb, HKV, BS, D), generator=g).to(torch.bfloat16)
+    tables = [torch.randperm(nb, generator=g)]
+    q = torch.randn((PF_CHUNK, HQ, D), generator=g).to(torch.bfloat16).float()
+    nk = torch.randn((PF_CHUNK, HKV, D), generator=g).to(torch.bfloat16)
+    nv = torch.randn((PF_CHUNK, HKV, D), generator=g).to(torch.bfloat16)
+    args = (q, kp, vp, tables, [PF_CTX], [PF_CHUNK], nk, nv, D ** -0.5)
+    cpu_path.prefill_layer(*args)
+    times = []
+    for _ in range(3):
+        t0 = time.perf_counter()
+        cpu_path.prefill_layer(*args)
+        times.append(time.perf_counter() - t0)
+    t = statistics.median(times)
+    return {"tflops": prefill_flops_layer(1) / t / 1e12, "layer_seq_s": t}
+
+
+def run_reference_prefill(args, world: int) -> None:
+    threads = os.cpu_count() or 1
+    vals = [cpu_prefill_sample(args.seed + i, threads)
+            for i in range(max(1, min(args.steps, 5)))]
+    v = statistics.median(x["tflops"] for x in vals)
+    ms = statistics.median(x["layer_seq_s"] for x in vals) * 1000.0 * PF_B * args.layers
+    sample = (f"1 of {PF_B} sequences x 1 of {args.layers} layers (a 512-token chunk at "
+              f"offset 3584), torch-CPU port of append + causal GQA attention, {threads} "
+              f"threads; ms_per_step extrapolated to {PF_B} sequences x {args.layers} layers")
+    line = {
+        "impl": "reference", "metric": PF_METRIC, "value": round(v, 5), "unit": "TFLOP/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded N(0,1) K/V/Q, random block tables)",
+        "config": {"workload": "8B-shape chunked-prefill iteration (CPU sample)",
+                   "layers": args.layers, "global_batch": PF_B, "seq_len": PF_CTX,
+                   "parallelism": "host threads"},
+        "prefill_tok_s": round(PF_B * PF_CHUNK / (ms / 1e3), 3),
+        "cpu_baseline": {"value": round(v, 5), "unit": "TFLOP/s", "cores": threads,
+                         "kind": "port", "sample": sample},
+        "e2e": {"value": round(v, 5), "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_prefill(args, local_rank: int) -> None:
+    """Chunked-prefill iteration, Llama-3.1-8B shape: 32 layers, 32 q heads, 8
+    KV heads, head_dim 128, block 16; 8 sequences each prefilling a 512-token
+    chunk on top of 3584 cached tokens.  One step = per layer, through
+    PagedPrefillStep.layer: mz_kv_append of the chunk's K/V, then
+    mz_paged_prefill (causal GQA attention over cache + chunk).  Every step
+    rewrites the same slots, so timed steps do identical work."""
+    import numpy as np
+    import torch
+
+    from mlxz_b200 import ops
+    from mlxz_b200.engine import PagedKVStore, PagedPrefillStep
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    nl = args.layers
+    nb_seq = PF_CTX // BS
+    n_blocks = int(math.ceil(PF_B * nb_seq * 1.1))
+    perm = np.random.default_rng(args.seed + 1).permutation(n_blocks)
+    store = PagedKVStore(nl, n_blocks, HKV, D, BS, torch.bfloat16, dev, init="empty")
+    torch.manual_seed(args.seed)
+    for l in range(nl):
+        store.pools[l].normal_()
+    ids = []
+    for b in range(PF_B):
+        store.add_sequence(f"s{b}", PF_CTX - PF_CHUNK,
+                           blocks=[int(x) for x in perm[b * nb_seq:(b + 1) * nb_seq]])
+        ids.append(f"s{b}")
+    step = PagedPrefillStep(store, [(s, PF_CHUNK) for s in ids], HQ)
+    T = PF_B * PF_CHUNK
+    q = torch.randn(nl, T, HQ, D, device=dev).to(torch.bfloat16)
+    kn = torch.randn(nl, T, HKV, D, device=dev).to(torch.bfloat16)
+    vn = torch.randn(nl, T, HKV, D, device=dev).to(torch.bfloat16)
+    out = torch.empty_like(q)
+    flops_layer = prefill_flops_layer()
+    warm = max(3, args.warmup)
+
+    def one_step():
+        for l in range(nl):
+            step.layer(l, q[l], kn[l], vn[l], out=out[l])
+
+    for _ in range(warm):
+        one_step()
+    torch.cuda.synchronize()
+    ops.check_device_errors(local_rank)
+    steps = args.steps
+    uuid = None
+    try:
+        uuid = "GPU-" + str(torch.cuda.get_device_properties(dev).uuid)
+    except Exception:
+        pass
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clocks = ClockSampler(uuid, enabled=not args.no_clocks)
+    t0.record()
+    for _ in range(steps):
+        one_step()
+    t1.record()
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    ops.check_device_errors(local_rank)
+    ms = t0.elapsed_time(t1) / steps
+
+    # the attention kernel alone: events around each launch (one extra pass)
+    kp0, vp0 = store.k_pool(0), store.v_pool(0)
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(nl)]
+    for l in range(nl):
+        kp, vp = store.k_pool(l), store.v_pool(l)
+        evs[l][0].record()
+        ops.paged_prefill(q[l], kp, vp, step.tables, step.q_start, step.q_len, step.ctx_lens,
+                          step.max_q_len, step.scale, out=out[l])
+        evs[l][1].record()
+    torch.cuda.synchronize()
+    pf_ms = statistics.mean(e[0].elapsed_time(e[1]) for e in evs)
+    del kp0, vp0
+
+    # end to end: per layer the chunk's q/k/v from pinned host memory and the
+    # attention output back, copies pipelined against the layers' launches
+    e2e = None
+    h2d = d2h = 0
+    if not args.no_e2e:
+        hq = q.cpu().pin_memory()
+        hk = kn.cpu().pin_memory()
+        hv = vn.cpu().pin_memory()
+        ho = torch.empty(out.shape, dtype=out.dtype, pin_memory=True)
+        cs = torch.cuda.Stream(dev)
+        stq = [torch.empty_like(q[0]) for _ in range(2)]
+        stk = [torch.empty_like(kn[0]) for _ in range(2)]
+        stv = [torch.empty_like(vn[0]) for _ in range(2)]
+        sto = [torch.empty_like(out[0]) for _ in range(2)]
+        main = torch.cuda.current_stream(dev)
+
+        def e2e_step():
+            done = [None, None]
+            for l in range(nl):
+                i = l & 1
+                with torch.cuda.stream(cs):
+                    if done[i] is not None:
+                        cs.wait_event(done[i])
+                    stq[i].copy_(hq[l], non_blocking=True)
+                    stk[i].copy_(hk[l], non_blocking=True)
+                    stv[i].copy_(hv[l], non_blocking=True)
+                    ready = torch.cuda.Event()
+                    ready.record(cs)
+                main.wait_event(ready)
+                step.layer(l, stq[i], stk[i], stv[i], out=sto[i])
+                fin = torch.cuda.Event()
+                fin.record(main)
+                with torch.cuda.stream(cs):
+                    cs.wait_event(fin)
+                    ho[l].copy_(sto[i], non_blocking=True)
+                    done[i] = torch.cuda.Event()
+                    done[i].record(cs)
+            main.wait_stream(cs)
+
+        for _ in range(2):
+            e2e_step()
+        torch.cuda.synchronize()
+        a, z = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e2e_steps = max(2, min(steps, 5))
+        a.record()
+        for _ in range(e2e_steps):
+            e2e_step()
+        z.record()
+        torch.cuda.synchronize()
+        ops.check_device_errors(local_rank)
+        e_ms = a.elapsed_time(z) / e2e_steps
+        h2d = nl * (q[0].numel() + 2 * kn[0].numel()) * 2
+        d2h = nl * out[0].numel() * 2
+        e2e = {"value": round(flops_layer * nl / (e_ms / 1e3) / 1e12, 2), "unit": "TFLOP/s",
+               "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": round(e_ms, 3)}
+
+    cpu = None
+    if not args.no_cpu_baseline:
+        threads = os.cpu_count() or 1
+        r = cpu_prefill_sample(args.seed, threads)
+        cpu = {"value": round(r["tflops"], 5), "unit": "TFLOP/s", "cores": threads, "kind": "port",
+               "sample": "1 of 8 sequences x 1 of 32 layers (512-token chunk at offset 3584), "
+                         f"torch-CPU port of append + causal GQA attention, {threads} threads"}
+    peaks_path = ROOT / "MEASURED_PEAKS.json"
+    if peaks_path.exists():
+        pk = json.loads(peaks_path.read_text())
+        peak, peak_kind = float(pk["bf16_tflops_sustained"]), "measured (sustained bf16 GEMM)"
+    else:
+        peak, peak_kind = 1400.0, "fallback (sustained)"
+    achieved = flops_layer / (pf_ms / 1e3) / 1e12
+    line = {
+        "metric": PF_METRIC, "value": round(flops_layer * nl / (ms / 1e3) / 1e12, 2),
+        "unit": "TFLOP/s", "n_gpus": 1, "steps": steps, "warmup": warm,
+        "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded N(0,1) bf16 K/V/Q, random block tables)",
+        "config": {"workload": ("chunked-prefill iteration: 32 layers, 32 q heads, 8 kv heads, "
+                                "head_dim 128, block 16; 8 seqs x 512-token chunk at offset "
+                                "3584 (ctx 4096); per layer kv_append + paged_prefill"),
+                   "layers": nl, "global_batch": PF_B, "seq_len": PF_CTX, "chunk": PF_CHUNK,
+                   "pool_blocks": n_blocks,
+                   "l2": "per layer 134 MB of K/V read > 126 MB L2; layers use distinct pools"},
+        "prefill_tok_s": round(T / (ms / 1e3), 1),
+        "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": peak,
+                     "unit": "TFLOP/s", "frac": round(achieved / peak, 4),
+                     "traffic": profile_traffic("paged_prefill_8b.md"),
+                     "kernel": "paged_prefill_tc_kernel<128,bf16>", "peak_kind": peak_kind,
+                     "prefill_ms_mean": round(pf_ms, 4), "alg_flops_per_launch": flops_layer},
+        "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": steps * nl * 2, "clocks": clk,
+    }
+    print(json.dumps(line), flush=True)
+
+
 def run_reference(args, rank: int, world: int) -> None:
     if rank != 0:
+        return
+    if args.config == "prefill":
+        run_reference_prefill(args, world)
         return
     threads = os.cpu_count() or 1
     budget = max(2.0, 120.0 / max(1, args.steps + args.warmup))
@@ -804,6 +1043,9 @@ def main():
     elif args.config == "quant":
         if rank == 0:
             run_quant(args, local_rank)
+    elif args.config == "prefill":
+        if rank == 0:
+            run_prefill(args, local_rank)
     else:
         run_gpu(args, rank, world, local_rank)
 

@@ -120,7 +120,7 @@ def test_prefill_rejects_bad_inputs(cuda):
                           torch.full((1,), 20, dtype=torch.int32, device=cuda), 10)
     # the row max is taken on raw scores: a non-positive scale is refused
     q8 = torch.zeros(10, 8, D, dtype=torch.bfloat16, device=cuda)
-    with pytest.raises(NativeError):
+    with pytest.raises(ValueError):
         ops.paged_prefill(q8, kp, kp, torch.from_numpy(case["tables"]).to(cuda),
                           torch.zeros(1, dtype=torch.int32, device=cuda),
                           torch.full((1,), 10, dtype=torch.int32, device=cuda),
