@@ -60,6 +60,8 @@ def parse_args():
     ap.add_argument("--separate-append", action="store_true",
                     help="append with mz_kv_append_paged, then mz_paged_decode (two launches)")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--batch-invariant", action="store_true",
+                    help="decode: MZ_DECODE_BATCH_INVARIANT (whole pairs, batch-independent bytes)")
     ap.add_argument("--config", default="decode",
                     choices=["decode", "prefix", "quant", "sharded70b", "prefill"],
                     help="decode: the paged decode step (headline); prefix: prefix-cache "
@@ -539,7 +541,7 @@ def run_gpu(args, rank: int, world: int, local_rank: int) -> None:
         store.add_sequence(sid, int(ctx[b]), blocks=[int(x) for x in perm[used:used + need[b]]])
         used += int(need[b])
         ids.append(sid)
-    step = PagedDecodeStep(store, ids, hq)
+    step = PagedDecodeStep(store, ids, hq, batch_invariant=args.batch_invariant)
     q = torch.randn(nl, B, hq, D, device=dev).to(torch.bfloat16)
     kn = torch.randn(nl, B, hkv, D, device=dev).to(torch.bfloat16)
     vn = torch.randn(nl, B, hkv, D, device=dev).to(torch.bfloat16)

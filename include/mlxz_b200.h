@@ -217,6 +217,14 @@ MZ_API int mz_paged_prefill(void *out, int32_t out_dtype, int64_t out_tok_stride
  * ahead writes none of this launch's pools, block tables or ctx_lens (e.g. it
  * is the previous layer's decode). */
 #define MZ_LAUNCH_OVERLAP_PREVIOUS 1u
+/* MZ_DECODE_BATCH_INVARIANT: every (sequence, KV head) pair is computed whole
+ * by one warp in a fixed tile order (pairs handed out by ticket; no split, no
+ * merge), so a sequence's output bytes do not depend on its position in the
+ * batch or on the other sequences.  The batch-position determinism gate of the
+ * reference's plan (MLXZ_IMPLEMENTATION_PLAN.md:1058-1059: prefix-cache drift
+ * < 1e-4, batch-position determinism bytewise).  Slower when the pairs are
+ * fewer than the launch's warps or very uneven. */
+#define MZ_DECODE_BATCH_INVARIANT 2u
 
 /* mz_paged_append_decode with launch flags (MZ_LAUNCH_*).  Same reference
  * counterpart and rules as mz_paged_append_decode. */

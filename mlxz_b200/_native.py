@@ -70,6 +70,7 @@ _i32, _i64, _f32, _vp, _sz = (ctypes.c_int32, ctypes.c_int64, ctypes.c_float,
 MZ_MAX_RANKS = 8
 MZ_IPC_HANDLE_BYTES = 64
 MZ_LAUNCH_OVERLAP_PREVIOUS = 1
+MZ_DECODE_BATCH_INVARIANT = 2
 
 
 class PeerOutputs(ctypes.Structure):

@@ -73,6 +73,7 @@ struct Params {
   // GPU's address space); once all blocks have stored, the last one publishes
   // `epoch` into each peer_sig[r] (rank r's signal word for this rank).
   int overlap_prev = 0;  // launched as a programmatic dependent of the kernel ahead
+  int batch_invariant = 0;  // whole pairs by ticket: a pair's bytes do not depend on the batch
   int n_peer = 0;
   void *peer_out[MZ_MAX_RANKS - 1] = {};
   uint32_t *peer_sig[MZ_MAX_RANKS - 1] = {};
@@ -277,6 +278,19 @@ struct Sched {
     }
     tot = t * p.Hkv;
     if (tot == 0) return false;
+    ticket = p.counters + (int64_t)p.B * p.Hkv;
+    p_left = pushed = issued = 0;
+    p_done = static_taken = false;
+    if (p.batch_invariant) {
+      // every (sequence, KV head) pair is one unit, taken whole by ticket in
+      // pair order: no pair is ever split, so no merge, and the arithmetic of
+      // a pair is the same whatever else is in the batch
+      per_s = 0;
+      t_s = 0;
+      chunk = 1 << 30;  // unit_of() is the same for every tile
+      n_chunks = p.B * p.Hkv;
+      return true;
+    }
     // static share: ceil(T * pct / 100 / W) tiles per warp (the last shares
     // may be short or empty), so with pct = 100 warps differ by <= one tile
     const int64_t target = (int64_t)tot * p.static_pct / 100;
@@ -298,9 +312,6 @@ struct Sched {
       dyn = 0;
     }
     n_chunks = (dyn + chunk - 1) / chunk;
-    ticket = p.counters + (int64_t)p.B * p.Hkv;
-    p_left = pushed = issued = 0;
-    p_done = static_taken = false;
     return true;
   }
 
@@ -320,7 +331,7 @@ struct Sched {
         ok = true;
       }
     }
-    if (!ok) {
+    while (!ok) {
       int tk = 0;
       if (lane == 0) tk = atomicAdd(ticket, 1);
       tk = __shfl_sync(0xffffffffu, tk, 0);
@@ -335,9 +346,24 @@ struct Sched {
         }
         return false;
       }
-      start = t_s + tk * chunk;
-      end = min(start + chunk, tot);
+      if (p.batch_invariant) {
+        // pair tk = (b, h): tiles [base_b + h n_b, base_b + (h + 1) n_b) of the
+        // flat list, base_b = Hkv * (tiles of the sequences before b)
+        const int b = tk / p.Hkv, h = tk - (tk / p.Hkv) * p.Hkv;
+        const int n = ntiles_of(clamped_ctx(p, b));
+        if (n == 0) continue;  // empty pair: its zeros are written elsewhere
+        int before = 0;
+        for (int bb = lane; bb < b; bb += 32) before += ntiles_of(clamped_ctx(p, bb));
+#pragma unroll
+        for (int o = 16; o; o >>= 1) before += __shfl_xor_sync(0xffffffffu, before, o);
+        start = before * p.Hkv + h * n;
+        end = start + n;
+      } else {
+        start = t_s + tk * chunk;
+        end = min(start + chunk, tot);
+      }
       u = W + tk;
+      ok = true;
     }
     push_unit(p, start, end, u);
     return true;

@@ -560,6 +560,7 @@ int launch(const DecodeArgs &a, int64_t warps, const WsLayout &ws, void *scratch
   p.kq = p.vq = nullptr;
   p.k_scales = p.k_biases = p.v_scales = p.v_biases = nullptr;
   p.err = a.err;
+  p.batch_invariant = (a.flags & MZ_DECODE_BATCH_INVARIANT) ? 1 : 0;
   if (a.peers) {
     const mz_peer_outputs &pe = *a.peers;
     p.out = pe.out[pe.rank];
@@ -718,7 +719,8 @@ static int append_decode(void *out, int32_t out_dtype, int64_t out_seq_stride,
   a.vn = v_new;
   a.kn_sb = new_seq_stride;
   a.kn_sh = new_head_stride;
-  if (flags & ~MZ_LAUNCH_OVERLAP_PREVIOUS) return fail(MZ_ERR_INVALID_ARG, "%s: unknown flags", fn);
+  if (flags & ~(MZ_LAUNCH_OVERLAP_PREVIOUS | MZ_DECODE_BATCH_INVARIANT))
+    return fail(MZ_ERR_INVALID_ARG, "%s: unknown flags", fn);
   a.flags = flags;
   if (!k_new || !v_new) return fail(MZ_ERR_INVALID_ARG, "%s: null k_new / v_new", fn);
   int64_t warps = 0;
@@ -774,7 +776,8 @@ extern "C" int mz_paged_append_decode_allgather(
     int32_t num_warps, uint32_t flags, void *workspace, size_t workspace_bytes,
     int32_t *dev_err, mz_stream_t stream) {
   const char *fn = "mz_paged_append_decode_allgather";
-  if (flags & ~MZ_LAUNCH_OVERLAP_PREVIOUS) return fail(MZ_ERR_INVALID_ARG, "%s: unknown flags", fn);
+  if (flags & ~(MZ_LAUNCH_OVERLAP_PREVIOUS | MZ_DECODE_BATCH_INVARIANT))
+    return fail(MZ_ERR_INVALID_ARG, "%s: unknown flags", fn);
   if (!peers) return fail(MZ_ERR_INVALID_ARG, "%s: peers is null", fn);
   if (peers->rank < 0 || peers->rank >= MZ_MAX_RANKS)
     return fail(MZ_ERR_INVALID_ARG, "%s: rank %d out of range", fn, peers->rank);

@@ -165,11 +165,15 @@ class PagedDecodeStep:
     takes the step's per-layer q ``[L, B, Hq, D]`` and new K/V ``[L, B, Hkv, D]``
     already on the device; ``step_host`` is the end-to-end form that copies
     them from (pinned) host memory and copies the output back.
+    ``batch_invariant``: every sequence's output bytes are independent of the
+    batch (each (sequence, KV head) pair is computed whole by one warp).
     """
 
     def __init__(self, store: PagedKVStore, seq_ids: list[str], n_heads: int,
-                 scale: float | None = None, max_blocks: int | None = None) -> None:
+                 scale: float | None = None, max_blocks: int | None = None,
+                 batch_invariant: bool = False) -> None:
         self.store = store
+        self.batch_invariant = batch_invariant
         self.seq_ids = list(seq_ids)
         self.n_heads = n_heads
         self.scale = scale if scale is not None else store.head_dim ** -0.5
@@ -216,7 +220,7 @@ class PagedDecodeStep:
         ops.paged_append_decode(q, st.k_pool(l), st.v_pool(l), k_new, v_new, self.tables,
                                 self.lengths, scale=self.scale, out=out,
                                 workspace=self.workspace, num_warps=num_warps,
-                                overlap_previous=l > 0)
+                                overlap_previous=l > 0, batch_invariant=self.batch_invariant)
 
     def prepare_writes(self) -> int:
         """Copy-on-write every block this step will write that is shared (a

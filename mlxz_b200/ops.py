@@ -292,13 +292,16 @@ def paged_append_decode(q: torch.Tensor, k_pool: torch.Tensor, v_pool: torch.Ten
                         ctx_lens: torch.Tensor, scale: float | None = None,
                         out: torch.Tensor | None = None, out_dtype: torch.dtype | None = None,
                         num_warps: int = 0, workspace: torch.Tensor | None = None,
-                        overlap_previous: bool = False) -> torch.Tensor:
+                        overlap_previous: bool = False,
+                        batch_invariant: bool = False) -> torch.Tensor:
     """Fused decode step for one layer: write ``k_new/v_new [B, Hkv, D]`` at
     position ``ctx_lens[b] - 1`` of each sequence, then attend ``q [B, Hq, D]``
     over the first ``ctx_lens[b]`` tokens (one launch).  ``overlap_previous``:
     the launch may start while the kernel ahead of it on the stream runs
     (MZ_LAUNCH_OVERLAP_PREVIOUS) -- only when that kernel writes none of the
-    pools, ``block_tables`` or ``ctx_lens``."""
+    pools, ``block_tables`` or ``ctx_lens``.  ``batch_invariant``: each
+    sequence's output bytes are independent of the rest of the batch
+    (MZ_DECODE_BATCH_INVARIANT)."""
     n_blocks, Hkv, bs, D = _check_pools(k_pool, v_pool)
     if q.dim() != 3 or q.shape[2] != D or q.stride(-1) != 1 or q.dtype != k_pool.dtype:
         raise ValueError(f"q must be [B, Hq, {D}] of the pool dtype with unit last stride")
@@ -329,7 +332,8 @@ def paged_append_decode(q: torch.Tensor, k_pool: torch.Tensor, v_pool: torch.Ten
              k_new.stride(1), block_tables.data_ptr(), block_tables.shape[1],
              ctx_lens.data_ptr(), B, Hq, Hkv, D, bs, n_blocks, float(scale),
              dtype_code(q.dtype), num_warps,
-             nat.MZ_LAUNCH_OVERLAP_PREVIOUS if overlap_previous else 0,
+             (nat.MZ_LAUNCH_OVERLAP_PREVIOUS if overlap_previous else 0)
+             | (nat.MZ_DECODE_BATCH_INVARIANT if batch_invariant else 0),
              workspace.data_ptr(), workspace.numel(), error_word(dev).data_ptr(), _stream(dev))
     _after(dev)
     return out
