@@ -16,7 +16,6 @@ namespace prefill {
 
 using decode::kTileTok;
 using decode::kTimeoutNs;
-using decode::make_row_map;
 
 struct PParams {
   void *out;
@@ -37,55 +36,99 @@ struct PParams {
   int32_t *err;
 };
 
+// 4-D bulk tensor copy (no multicast): box {64, 8, D / 64, rows / 8} of the
+// grouped map at row group `grp`.
+__device__ __forceinline__ void tma_load_4d(uint32_t dst, const void *tmap, int grp, uint32_t bar,
+                                            uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%2, %2, %2, %3}], [%4], %5;" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(0), "r"(grp), "r"(bar), "l"(policy)
+      : "memory");
+}
+
+// Pool [rows][D] viewed as 4-D: (64 columns, 8 rows, D / 64 chunks, rows / 8
+// groups) with strides (row D*2 B, chunk 128 B, group 8*D*2 B), box {64, 8,
+// D / 64, box_rows / 8}, 128-byte swizzle: one copy brings box_rows whole rows
+// in the grouped layout the MMA descriptors read.
+inline int make_group_map(CUtensorMap *m, const void *base, int64_t rows, int D,
+                          CUtensorMapDataType type, int box_rows) {
+  auto fn = decode::encode_fn();
+  if (!fn) return fail(MZ_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+  cuuint64_t dims[4] = {64, 8, static_cast<cuuint64_t>(D / 64), static_cast<cuuint64_t>(rows / 8)};
+  cuuint64_t strides[3] = {static_cast<cuuint64_t>(D) * 2, 128, static_cast<cuuint64_t>(D) * 16};
+  cuuint32_t box[4] = {64, 8, static_cast<cuuint32_t>(D / 64),
+                       static_cast<cuuint32_t>(box_rows / 8)};
+  cuuint32_t es[4] = {1, 1, 1, 1};
+  CUresult r = fn(m, type, 4, const_cast<void *>(base), dims, strides, box, es,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(MZ_ERR_CUDA, "cuTensorMapEncodeTiled (grouped) failed (%d)", (int)r);
+  return MZ_OK;
+}
+
 __device__ __forceinline__ void mbar_arrive(uint32_t bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
 }
 
 // ---------------------------------------------------------------------------
 // One CTA per (128 query rows, KV head, sequence): row m is
-// token q0 + m / G, query head h*G + m % G.  Six warps:
-//   warps 0-3  softmax + epilogue; thread t owns row t (TMEM lane t)
-//   warp 4     streams 128-key K and V tiles (2-D bulk tensor copies of
+// token q0 + m / G, query head h*G + m % G.  Ten warps:
+//   warps 0-7  softmax + epilogue; thread t owns row t % 128 (TMEM lane
+//              t % 128) and half t / 128 of its keys (64 of each 128-key tile)
+//              and of its O columns; the two halves of a row exchange their
+//              maxima through shared memory (bounded mbarrier waits)
+//   warp 8     streams 128-key K and V tiles (2-D bulk tensor copies of
 //              gcd(block_size, 128)-row boxes, 128-byte swizzle, no
 //              multicast) into a 3-stage K ring (a slot frees when its S MMA
 //              completes) and a 2-stage V ring (when its PV MMA completes), K
 //              running one tile ahead of V
-//   warp 5     allocates TMEM and issues the MMAs (one elected lane)
+//   warp 9     allocates TMEM and issues the MMAs (one elected lane)
 // TMEM columns: O [0, D) fp32; three 128-column S buffers at 128, 256, 384.
 // Per key tile i:  S_i = Q.K_i^T (SS MMA, M=128 N=128 K=16 steps) into buffer
-// i % 3; softmax reads S_i, writes P_i over it (16-bit, two per column; bf16 as
-// hi + lo halves in columns [0,64) and [64,128)); O += P_i.V_i (TS MMA, A = P
+// i % 3; softmax reads S_i, writes P_i over it (16-bit, two per column; each
+// half of the keys over its own 64 S columns: bf16 hi in the first 32, lo in
+// the last 32; fp16 in the first 32); O += P_i.V_i (TS MMA, A = P
 // from TMEM, B = V MN-major, N = D).  S_{i+1} is issued before PV_i so the
 // tensor core works on it during softmax_i.  The running max is only moved
 // when a row's tile max exceeds it by more than 8 (log2 units): P then stays
 // below 2^8 and O is rescaled in TMEM only on those tiles.
 // Every wait is bounded; a wait that gives up sets MZ_DEVERR_TIMEOUT and the
 // abort flag, every role leaves its loop, the issuing threads wait (bounded)
-// for their copies / MMAs in flight, and warp 5 frees the TMEM.
+// for their copies / MMAs in flight, and warp 9 frees the TMEM.
 namespace tcp {
 constexpr int kM = 128;
 constexpr int kN = 128;
 constexpr int kKRing = 3;
 constexpr int kVRing = 2;
 constexpr int kSBufs = 3;
-constexpr int kThreads = 192;
+constexpr int kSoftWarps = 8;
+constexpr int kProdWarp = 8, kMmaWarp = 9;
+constexpr int kThreads = 320;
 constexpr uint32_t kTmemCols = 512;
 constexpr float kRescaleLog2 = 8.f;
 
 template <int D>
 struct TCfg {
-  static constexpr int kChunk = kN * 128;               // 128 keys x 64 dims
-  static constexpr int kTile = (D / 64) * kChunk;       // one K or V tile
-  static constexpr int kQ = (D / 64) * kM * 128;        // 128 rows x D
+  // K / V tile layout in shared memory: 16 groups of 8 keys, each group the
+  // D / 64 column chunks of 8 rows x 128 bytes (one 128-byte-swizzle atom per
+  // chunk): key r, chunk c at (r / 8) * kGroup + c * 1024 + (r % 8) * 128.
+  static constexpr int kGroup = 8 * D * 2;              // 8 keys x D
+  static constexpr int kTile = (kN / 8) * kGroup;       // one K or V tile
+  static constexpr int kQ = (D / 64) * kM * 128;        // 128 rows x D, chunk-major
   static constexpr int kK0 = kQ;                        // K slot s at kK0 + s kTile
   static constexpr int kV0 = kQ + kKRing * kTile;       // V slot s at kV0 + s kTile
   static constexpr int kBar = kV0 + kVRing * kTile;     // barriers after the tiles
-  static constexpr int kSmemBytes = kBar + 256 + 1024;
+  static constexpr int kXm = kBar + 256;                // [2 parity][2 half][128] maxima
+  static constexpr int kXl = kXm + 2 * 2 * kM * 4;      // [2 half][128] row sums
+  static constexpr int kSmemBytes = kXl + 2 * kM * 4 + 1024;
 };
 
 // barrier slots (8 bytes each) after the tiles
 constexpr int kBarKFull = 0, kBarVFull = 3, kBarSFull = 5, kBarPFull = 8, kBarPvDone = 11,
-              kBarDrain = 14, kNumBars = 15;
+              kBarDrain = 14, kBarXchg = 15 /* [parity][pair] */, kBarLx = 23 /* [pair] */,
+              kNumBars = 27;
+static_assert(8 * kNumBars + 8 <= 256, "barrier area");
 static_assert(kKRing == kSBufs, "K slots are released through the S barriers");
 }  // namespace tcp
 
@@ -128,28 +171,30 @@ __global__ void __launch_bounds__(tcp::kThreads, 1)
     for (int s = 0; s < kVRing; ++s) mbar_init(bar(kBarVFull + s), 1);
     for (int s = 0; s < kSBufs; ++s) {
       mbar_init(bar(kBarSFull + s), 1);
-      mbar_init(bar(kBarPFull + s), 4);
+      mbar_init(bar(kBarPFull + s), kSoftWarps);
       mbar_init(bar(kBarPvDone + s), 1);
     }
     mbar_init(bar(kBarDrain), 1);
+    for (int x = 0; x < 8; ++x) mbar_init(bar(kBarXchg + x), 64);
+    for (int x = 0; x < 4; ++x) mbar_init(bar(kBarLx + x), 64);
     *abort_flag = 0;
     fence_mbar_init();
   }
-  if (warp == 5) tc::tmem_alloc(smem_u32(tmem_slot), kTmemCols);
+  if (warp == kMmaWarp) tc::tmem_alloc(smem_u32(tmem_slot), kTmemCols);
 
-  // this thread's row (softmax warps)
-  const int row = threadIdx.x;
+  // this thread's row and half (softmax warps)
+  const int row = threadIdx.x & (kM - 1), hf = threadIdx.x >> 7;
   const int tok = q0 + row / p.G;
   const int hq = h * p.G + row % p.G;
-  const bool live = warp < 4 && tok < q_hi;
+  const bool live = warp < kSoftWarps && tok < q_hi;
   const int lim = start + min(tok, q_hi - 1);  // last visible key of the row
-  if (warp < 4) {
-    // Q row -> shared memory in the 128-byte-swizzled K-major layout
+  if (warp < kSoftWarps) {
+    // half hf of the Q row -> shared memory (128-byte-swizzled K-major layout)
     const uint4 *src = reinterpret_cast<const uint4 *>(
         static_cast<const uint16_t *>(p.q) + (int64_t)(p.q_start[b] + tok) * p.q_st +
         (int64_t)hq * p.q_sh);
 #pragma unroll
-    for (int u = 0; u < D / 8; ++u) {
+    for (int u = hf * (D / 16); u < (hf + 1) * (D / 16); ++u) {
       const uint4 v = live ? src[u] : make_uint4(0, 0, 0, 0);
       const int c = u >> 3, uu = u & 7;
       *reinterpret_cast<uint4 *>(smem + c * (kM * 128) + row * 128 + ((uu ^ (row & 7)) << 4)) = v;
@@ -166,7 +211,7 @@ __global__ void __launch_bounds__(tcp::kThreads, 1)
     *abort_flag = 1;
   };
 
-  if (warp == 4) {
+  if (warp == kProdWarp) {
     // ---------------- producer (whole warp) ----------------
     // A tile is nst = 128 / sub boxes of sub = gcd(block_size, 128) keys.
     // Block rows come in groups of four tiles: lane l < 4 nst covers box
@@ -198,11 +243,7 @@ __global__ void __launch_bounds__(tcp::kThreads, 1)
       if (lane == 0)
         mbar_arrive_expect_tx(fbar, static_cast<uint32_t>(nsub * (D / 64) * sub * 128));
       __syncwarp();
-      if (lane < nsub) {
-#pragma unroll
-        for (int c = 0; c < D / 64; ++c)
-          tma_load_2d(dst + c * C::kChunk + lane * (sub * 128), tm, c * 64, y, fbar, pol);
-      }
+      if (lane < nsub) tma_load_4d(dst + lane * (sub / 8) * C::kGroup, tm, y >> 3, fbar, pol);
     };
     int k_issued = 0, v_issued = 0;
     int y_prv = 0, y_cur = group_rows(0, group_ids(0));
@@ -251,7 +292,7 @@ __global__ void __launch_bounds__(tcp::kThreads, 1)
         (void)mbar_wait_bounded(bar(kBarVFull + j % kVRing), (j / kVRing) & 1, kTimeoutNs);
     }
     __syncwarp();
-  } else if (warp == 5) {
+  } else if (warp == kMmaWarp) {
     // ---------------- MMA issue (whole warp, one elected lane issues) ----------------
     constexpr uint32_t idS = tc::idesc_f16(BF16, kM, kN, false);
     constexpr uint32_t idPV = tc::idesc_f16(BF16, kM, D, true);
@@ -270,9 +311,10 @@ __global__ void __launch_bounds__(tcp::kThreads, 1)
       const uint32_t d = tm0 + 128 * (1 + buf);
 #pragma unroll
       for (int k = 0; k < D / 16; ++k) {
-        const uint32_t off = (k >> 2) * C::kChunk + (k & 3) * 32;
-        tc::mma_ss_elect(d, tc::smem_desc_sw128(qs + off, 16, 1024),
-                         tc::smem_desc_sw128(kst(s) + off, 16, 1024), idS, k > 0);
+        const uint32_t ko = (k & 3) * 32;  // 16-column step inside the chunk's atom
+        tc::mma_ss_elect(d, tc::smem_desc_sw128(qs + (k >> 2) * (kM * 128) + ko, 16, 1024),
+                         tc::smem_desc_sw128(kst(s) + (k >> 2) * 1024 + ko, 16, C::kGroup),
+                         idS, k > 0);
       }
       tc::commit_elect(bar(kBarSFull + buf));  // also frees K slot s
       return true;
@@ -295,9 +337,11 @@ __global__ void __launch_bounds__(tcp::kThreads, 1)
       const uint32_t pcol = tm0 + 128 * (1 + buf);
 #pragma unroll
       for (int kk = 0; kk < kN / 16; ++kk) {
-        const uint64_t dv = tc::smem_desc_sw128(vst(s) + kk * 2048, C::kChunk, 1024);
-        tc::mma_ts_elect(tm0, pcol + 8 * kk, dv, idPV, (i > 0 || kk > 0) ? 1u : 0u);
-        if constexpr (BF16) tc::mma_ts_elect(tm0, pcol + 64 + 8 * kk, dv, idPV, 1u);
+        // keys 16 kk .. : half kk / 4, its hi columns from 64 half, lo 32 further
+        const uint32_t pa = pcol + 64 * (kk >> 2) + 8 * (kk & 3);
+        const uint64_t dv = tc::smem_desc_sw128(vst(s) + kk * 2 * C::kGroup, 1024, C::kGroup);
+        tc::mma_ts_elect(tm0, pa, dv, idPV, (i > 0 || kk > 0) ? 1u : 0u);
+        if constexpr (BF16) tc::mma_ts_elect(tm0, pa + 32, dv, idPV, 1u);
       }
       tc::commit_elect(bar(kBarPvDone + buf));  // also frees V slot s
     }
@@ -307,8 +351,12 @@ __global__ void __launch_bounds__(tcp::kThreads, 1)
     (void)mbar_wait_bounded(bar(kBarDrain), 0, kTimeoutNs);
     __syncwarp();
   } else {
-    // ---------------- softmax + epilogue (warps 0-3) ----------------
-    const uint32_t tl = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+    // ---------------- softmax + epilogue (warps 0-7) ----------------
+    constexpr int kH = kN / 2;  // keys of a tile per half
+    const uint32_t tl = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
+    const int pair = warp & 3;
+    float *xm = reinterpret_cast<float *>(smem + C::kXm);  // [parity][half][row]
+    float *xl = reinterpret_cast<float *>(smem + C::kXl);  // [half][row]
     float m_used = -INFINITY, l = 0.f;
     bool ok = true;
     for (int i = 0; i < ntiles; ++i) {
@@ -324,34 +372,45 @@ __global__ void __launch_bounds__(tcp::kThreads, 1)
         break;
       }
       tc::fence_after_sync();
-      float sv[kN];
+      const uint32_t scol = tl + 128 * (1 + buf) + kH * hf;  // this half's 64 S columns
+      float sv[kH];
       {
-        uint32_t r[kN / 32][32];
+        uint32_t r[kH / 32][32];
 #pragma unroll
-        for (int c = 0; c < kN / 32; ++c) tc::ld32(tl + 128 * (1 + buf) + 32 * c, r[c]);
+        for (int c = 0; c < kH / 32; ++c) tc::ld32(scol + 32 * c, r[c]);
         tc::wait_ld();
 #pragma unroll
-        for (int c = 0; c < kN / 32; ++c)
+        for (int c = 0; c < kH / 32; ++c)
 #pragma unroll
           for (int j = 0; j < 32; ++j) sv[32 * c + j] = __uint_as_float(r[c][j]);
       }
-      const int key0 = i * kN;
-      if (key0 + kN - 1 > lim) {  // tile crosses this row's causal limit
+      const int key0 = i * kN + kH * hf;
+      if (key0 + kH - 1 > lim) {  // this half crosses the row's causal limit
 #pragma unroll
-        for (int j = 0; j < kN; ++j)
+        for (int j = 0; j < kH; ++j)
           if (key0 + j > lim) sv[j] = -INFINITY;
       }
-      // max over the raw scores (scale > 0), eight independent chains
+      // max over the raw scores (scale > 0), eight independent chains, then
+      // the other half's through shared memory
       float mx;
       {
         float m8[8];
 #pragma unroll
         for (int j = 0; j < 8; ++j) m8[j] = sv[j];
 #pragma unroll
-        for (int j = 8; j < kN; ++j) m8[j & 7] = fmaxf(m8[j & 7], sv[j]);
+        for (int j = 8; j < kH; ++j) m8[j & 7] = fmaxf(m8[j & 7], sv[j]);
         mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])),
                    fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
-        mx *= p.scale_log2;
+        const int par = i & 1;
+        xm[(par * 2 + hf) * kM + row] = mx;
+        mbar_arrive(bar(kBarXchg + par * 4 + pair));
+        if (!__all_sync(0xffffffffu, mbar_wait_bounded(bar(kBarXchg + par * 4 + pair),
+                                                        (i >> 1) & 1, kTimeoutNs))) {
+          if (lane == 0) give_up();
+          ok = false;
+          break;
+        }
+        mx = fmaxf(xm[(par * 2) * kM + row], xm[(par * 2 + 1) * kM + row]) * p.scale_log2;
       }
       const bool need = mx > m_used + kRescaleLog2;
       const float m_new = need ? mx : m_used;
@@ -366,7 +425,7 @@ __global__ void __launch_bounds__(tcp::kThreads, 1)
         }
         tc::fence_after_sync();
 #pragma unroll 1
-        for (int c = 0; c < D / 32; ++c) {
+        for (int c = hf * (D / 64); c < (hf + 1) * (D / 64); ++c) {  // this half's O columns
           uint32_t r[32];
           tc::ld32(tl + 32 * c, r);
           tc::wait_ld();
@@ -380,7 +439,7 @@ __global__ void __launch_bounds__(tcp::kThreads, 1)
       const float neg_m = -m_used;
       float l8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-      for (int c = 0; c < kN / 32; ++c) {
+      for (int c = 0; c < kH / 32; ++c) {
         uint32_t hi[16], lo[16];
 #pragma unroll
         for (int w = 0; w < 16; ++w) {
@@ -394,11 +453,12 @@ __global__ void __launch_bounds__(tcp::kThreads, 1)
             lo[w] = pack2<BF16>(a - ah, e - eh);
           }
         }
-        tc::st16(tl + 128 * (1 + buf) + 16 * c, hi);
-        if constexpr (BF16) tc::st16(tl + 128 * (1 + buf) + 64 + 16 * c, lo);
+        // P over this half's own S columns: hi in the first 32, lo in the last
+        tc::st16(scol + 16 * c, hi);
+        if constexpr (BF16) tc::st16(scol + 32 + 16 * c, lo);
       }
       l = l * alpha + (((l8[0] + l8[1]) + (l8[2] + l8[3])) + ((l8[4] + l8[5]) + (l8[6] + l8[7])));
-      const int nvalid = kv_len - key0;
+      const int nvalid = kv_len - i * kN;
       if (nvalid < kN) {
         // last tile: keys past kv_len hold stale smem / pool rows; their P is
         // 0 but 0 * NaN is not, so the V rows become exact zeros first
@@ -410,11 +470,12 @@ __global__ void __launch_bounds__(tcp::kThreads, 1)
           break;
         }
         const int units = (kN - nvalid) * (D / 8);
-        for (int e = threadIdx.x; e < units; e += 128) {
+        for (int e = threadIdx.x; e < units; e += 32 * kSoftWarps) {
           const int r = nvalid + e / (D / 8), u = e % (D / 8);
           const int c = u >> 3, uu = u & 7;
-          *reinterpret_cast<uint4 *>(smem + C::kV0 + s * C::kTile + c * C::kChunk +
-                                     r * 128 + ((uu ^ (r & 7)) << 4)) = make_uint4(0, 0, 0, 0);
+          *reinterpret_cast<uint4 *>(smem + C::kV0 + s * C::kTile + (r >> 3) * C::kGroup +
+                                     c * 1024 + (r & 7) * 128 + ((uu ^ (r & 7)) << 4)) =
+              make_uint4(0, 0, 0, 0);
         }
         fence_proxy_async_smem();
       }
@@ -430,11 +491,18 @@ __global__ void __launch_bounds__(tcp::kThreads, 1)
       if (!ok && lane == 0) give_up();
     }
     if (ok) {
+      // row sum = the two halves' sums, added in a fixed order
+      xl[hf * kM + row] = l;
+      mbar_arrive(bar(kBarLx + pair));
+      ok = __all_sync(0xffffffffu, mbar_wait_bounded(bar(kBarLx + pair), 0, kTimeoutNs));
+      if (!ok && lane == 0) give_up();
+    }
+    if (ok) {
       tc::fence_after_sync();
-      const float inv = 1.f / l;
+      const float inv = 1.f / (xl[row] + xl[kM + row]);
       const int64_t ob = (int64_t)(p.q_start[b] + tok) * p.o_st + (int64_t)hq * p.o_sh;
 #pragma unroll
-      for (int c = 0; c < D / 32; ++c) {
+      for (int c = hf * (D / 64); c < (hf + 1) * (D / 64); ++c) {
         uint32_t r[32];
         tc::ld32(tl + 32 * c, r);
         tc::wait_ld();
@@ -466,7 +534,7 @@ __global__ void __launch_bounds__(tcp::kThreads, 1)
 
   tc::fence_before_sync();
   __syncthreads();
-  if (warp == 5) {
+  if (warp == kMmaWarp) {
     tc::fence_after_sync();
     tc::tmem_dealloc(tmem, kTmemCols);
   }
@@ -538,10 +606,8 @@ extern "C" int mz_paged_prefill(void *out, int32_t out_dtype, int64_t out_tok_st
   const auto type = bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   int sub_log2 = 4;  // rows per copy box: gcd(block_size, 128)
   while (sub_log2 < 7 && block_size % (1 << (sub_log2 + 1)) == 0) ++sub_log2;
-  if (int rc = make_row_map(&tk, k_pool, rows_total, head_dim, type, 2, 64, 1 << sub_log2))
-    return rc;
-  if (int rc = make_row_map(&tv, v_pool, rows_total, head_dim, type, 2, 64, 1 << sub_log2))
-    return rc;
+  if (int rc = make_group_map(&tk, k_pool, rows_total, head_dim, type, 1 << sub_log2)) return rc;
+  if (int rc = make_group_map(&tv, v_pool, rows_total, head_dim, type, 1 << sub_log2)) return rc;
 
   PParams p;
   p.out = out;
