@@ -62,7 +62,8 @@ enum mz_device_error {
   MZ_DEVERR_BLOCK_ID = 1, /* block-table entry outside [0, n_blocks)          */
   MZ_DEVERR_SLOT = 2,     /* slot outside [0, n_blocks * block_size)          */
   MZ_DEVERR_CONTEXT = 4,  /* context length < 0 or > table capacity           */
-  MZ_DEVERR_TIMEOUT = 8   /* a bounded wait on an mbarrier or flag gave up    */
+  MZ_DEVERR_TIMEOUT = 8,  /* a bounded wait on an mbarrier or flag gave up    */
+  MZ_DEVERR_ROWS = 16     /* a sequence's query rows outside [0, n_rows)      */
 };
 
 /* ABI version of this header (bumped on any signature change). */
@@ -184,7 +185,8 @@ MZ_API int mz_paged_append_decode(void *out, int32_t out_dtype, int64_t out_seq_
                                   size_t workspace_bytes, int32_t *dev_err, mz_stream_t stream);
 
 /* Chunked prefill attention over paged KV.  Sequence b's n_b = q_len[b]
- * query tokens are rows q_start[b] .. q_start[b] + n_b - 1 of q and out
+ * query tokens are rows q_start[b] .. q_start[b] + n_b - 1 of the n_rows rows
+ * of q and out (rows outside [0, n_rows): MZ_DEVERR_ROWS, sequence skipped)
  * (element (row t, head hq, dim d) at base + t*tok_stride + hq*head_stride + d,
  * of dtype; out of out_dtype = dtype or F32) at positions
  * [ctx_lens[b] - n_b, ctx_lens[b]) of the sequence, their K/V already in the
@@ -200,7 +202,8 @@ MZ_API int mz_paged_append_decode(void *out, int32_t out_dtype, int64_t out_seq_
  * q and out 16-byte aligned with strides of whole 16-byte vectors. */
 MZ_API int mz_paged_prefill(void *out, int32_t out_dtype, int64_t out_tok_stride,
                             int64_t out_head_stride, const void *q, int64_t q_tok_stride,
-                            int64_t q_head_stride, const int32_t *q_start, const int32_t *q_len,
+                            int64_t q_head_stride, int32_t n_rows, const int32_t *q_start,
+                            const int32_t *q_len,
                             int32_t max_q_len, const void *k_pool, const void *v_pool,
                             const int32_t *block_tables, int32_t max_blocks_per_seq,
                             const int32_t *ctx_lens, int32_t n_seqs, int32_t n_heads,

@@ -30,12 +30,14 @@ MZ_DEVERR_BLOCK_ID = 1
 MZ_DEVERR_SLOT = 2
 MZ_DEVERR_CONTEXT = 4
 MZ_DEVERR_TIMEOUT = 8
+MZ_DEVERR_ROWS = 16
 
 _DEVERR_NAMES = {
     MZ_DEVERR_BLOCK_ID: "block id out of range",
     MZ_DEVERR_SLOT: "slot out of range",
     MZ_DEVERR_CONTEXT: "context length out of range",
     MZ_DEVERR_TIMEOUT: "bounded wait timed out",
+    MZ_DEVERR_ROWS: "query rows out of range",
 }
 
 
@@ -108,7 +110,7 @@ _SIGNATURES: dict[str, list] = {
                                          _vp, _i32, _i32, _i32, _i32, _i32, _i64, _f32, _i32,
                                          _i32, ctypes.c_uint32, _vp, _sz, _vp, _vp],
     "mz_peer_wait": [_vp, _i32, _i32, ctypes.c_uint32, ctypes.c_uint64, _vp, _vp],
-    "mz_paged_prefill": [_vp, _i32, _i64, _i64, _vp, _i64, _i64, _vp, _vp, _i32, _vp, _vp, _vp,
+    "mz_paged_prefill": [_vp, _i32, _i64, _i64, _vp, _i64, _i64, _i32, _vp, _vp, _i32, _vp, _vp, _vp,
                          _i32, _vp, _i32, _i32, _i32, _i32, _i32, _i64, _f32, _i32, _vp, _vp],
     "mz_ipc_export": [_vp, _vp, ctypes.POINTER(ctypes.c_uint64)],
     "mz_ipc_open": [_vp, ctypes.c_uint64, ctypes.POINTER(_vp), ctypes.POINTER(_vp)],

@@ -24,6 +24,7 @@ struct PParams {
   const void *q;
   int64_t q_st, q_sh;
   int q_bf16;
+  int n_rows;              // rows of q / out
   const int32_t *q_start;  // [B] first row of sequence b in q / out
   const int32_t *q_len;    // [B] query tokens of sequence b
   const int32_t *ctx;      // [B] tokens in the pools, the chunk included
@@ -146,6 +147,10 @@ __global__ void __launch_bounds__(tcp::kThreads, 1)
   const int ctx = p.ctx[b];
   if (ctx < n || ctx > p.max_blocks * p.bs) {
     if (threadIdx.x == 0) dev_error(p.err, MZ_DEVERR_CONTEXT);
+    return;
+  }
+  if (p.q_start[b] < 0 || (int64_t)p.q_start[b] + n > p.n_rows) {
+    if (threadIdx.x == 0) dev_error(p.err, MZ_DEVERR_ROWS);
     return;
   }
   const int start = ctx - n;
@@ -561,7 +566,7 @@ using namespace mz::prefill;
 
 extern "C" int mz_paged_prefill(void *out, int32_t out_dtype, int64_t out_tok_stride,
                                 int64_t out_head_stride, const void *q, int64_t q_tok_stride,
-                                int64_t q_head_stride, const int32_t *q_start,
+                                int64_t q_head_stride, int32_t n_rows, const int32_t *q_start,
                                 const int32_t *q_len, int32_t max_q_len, const void *k_pool,
                                 const void *v_pool, const int32_t *block_tables,
                                 int32_t max_blocks_per_seq, const int32_t *ctx_lens,
@@ -579,7 +584,7 @@ extern "C" int mz_paged_prefill(void *out, int32_t out_dtype, int64_t out_tok_st
   if (block_size <= 0 || block_size % kTileTok)
     return fail(MZ_ERR_UNSUPPORTED, "%s: block_size %d is not a multiple of 16", fn, block_size);
   if (n_seqs < 0 || n_kv_heads <= 0 || n_heads <= 0 || n_heads % n_kv_heads || max_q_len < 0 ||
-      max_blocks_per_seq <= 0 || n_blocks <= 0)
+      max_blocks_per_seq <= 0 || n_blocks <= 0 || n_rows < 0)
     return fail(MZ_ERR_INVALID_ARG, "%s: bad sizes", fn);
   const int G = n_heads / n_kv_heads;
   if (tcp::kM % G)
@@ -618,6 +623,7 @@ extern "C" int mz_paged_prefill(void *out, int32_t out_dtype, int64_t out_tok_st
   p.q_st = q_tok_stride;
   p.q_sh = q_head_stride;
   p.q_bf16 = bf16;
+  p.n_rows = n_rows;
   p.q_start = q_start;
   p.q_len = q_len;
   p.ctx = ctx_lens;

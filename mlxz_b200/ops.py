@@ -369,7 +369,7 @@ def paged_prefill(q: torch.Tensor, k_pool: torch.Tensor, v_pool: torch.Tensor,
         return out
     dev = _dev_index(q)
     nat.call("mz_paged_prefill", out.data_ptr(), dtype_code(out_dtype), out.stride(0),
-             out.stride(1), q.data_ptr(), q.stride(0), q.stride(1), q_start.data_ptr(),
+             out.stride(1), q.data_ptr(), q.stride(0), q.stride(1), T, q_start.data_ptr(),
              q_len.data_ptr(), int(max_q_len), k_pool.data_ptr(), v_pool.data_ptr(),
              block_tables.data_ptr(), block_tables.shape[1], ctx_lens.data_ptr(), B, Hq, Hkv,
              D, bs, n_blocks, float(scale), dtype_code(q.dtype), error_word(dev).data_ptr(),

@@ -105,6 +105,10 @@ def test_prefill_rejects_bad_inputs(cuda):
     bad = dict(case, ctx=np.array([5], dtype=np.int32))
     with pytest.raises(DeviceError):
         _run(bad, dtype, cuda)
+    # query rows past the end of q (q_start + q_len > rows of q)
+    bad = dict(case, q_start=np.array([3], dtype=np.int32))
+    with pytest.raises(DeviceError, match="query rows"):
+        _run(bad, dtype, cuda)
     # a block id outside the pool
     bad = dict(case, tables=case["tables"].copy())
     bad["tables"][0, 0] = case["n_blocks"] + 3
