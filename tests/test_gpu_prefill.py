@@ -64,6 +64,18 @@ def test_paged_prefill_vs_oracle(cuda, dtype, D, G, bs, ctx, qlen, out32):
     assert attn_err(out, ref) <= ATOL_REL
 
 
+def test_prefill_long_context(cuda):
+    """32K-token caches: 256 key tiles per CTA, so every ring slot and S buffer
+    wraps its mbarrier phases many times; chunks end mid-block."""
+    dtype, D, G, bs, Hkv = "bf16", 128, 8, 16, 1
+    ctx, qlen = [32768, 20000], [72, 33]
+    case = _prefill_case(123, ctx, qlen, dtype, D, G, bs, Hkv)
+    out = _run(case, dtype, cuda, torch.float32)
+    ref = opaged.paged_prefill(case["qp"], case["kp"], case["vp"], case["tables"],
+                               case["q_start"], case["q_len"], case["ctx"], dtype)
+    assert attn_err(out, ref) <= ATOL_REL
+
+
 def test_prefill_strided_q_and_oversized_grid(cuda):
     """q as the query slice of a packed [T, Hq + 2 Hkv, D] projection, and a
     max_q_len above every chunk (the extra query blocks do nothing)."""
