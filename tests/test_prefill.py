@@ -88,3 +88,35 @@ def test_paged_prefill_oracle_matches_contiguous():
     ref = opaged.prefill_attention(rng.to_f32(q[:7], "f16").transpose(1, 0, 2),
                                    rng.to_f32(kb, "f16"), rng.to_f32(vb, "f16"), 33)
     np.testing.assert_allclose(out[:7], ref.transpose(1, 0, 2), rtol=1e-12, atol=1e-12)
+
+
+def test_prefill_step_host_metadata():
+    """PagedPrefillStep's host side on a CPU store (no kernel runs): tables grow
+    for the chunks, slots follow the tables from each sequence's offset, the
+    chunks stack in order, and finish() advances the offsets once."""
+    import torch
+
+    from mlxz_b200.engine import PagedKVStore, PagedPrefillStep
+
+    bs = 16
+    store = PagedKVStore(1, 32, 2, 64, bs, torch.float16, device="cpu")
+    store.add_sequence("a", 0)
+    store.add_sequence("b", 20)
+    store.add_sequence("c", 5)
+    step = PagedPrefillStep(store, [("a", 40), ("b", 12), ("c", 0)], n_heads=8)
+    assert step.T == 52 and step.max_q_len == 40
+    assert step.q_start.tolist() == [0, 40, 52]
+    assert step.q_len.tolist() == [40, 12, 0]
+    assert step.ctx_lens.tolist() == [40, 32, 5]
+    ta, tb = store.tables["a"], store.tables["b"]
+    assert len(ta) == 3 and len(tb) == 2
+    want = [ta[p // bs] * bs + p % bs for p in range(40)] + \
+           [tb[p // bs] * bs + p % bs for p in range(20, 32)]
+    assert step.slots.tolist() == want
+    assert step.tables.shape == (3, 3)
+    assert step.tables[1, :2].tolist() == tb and step.tables[1, 2].item() == -1
+    step.finish()
+    step.finish()
+    assert [store.offsets[s] for s in "abc"] == [40, 32, 5]
+    with pytest.raises(ValueError):
+        PagedPrefillStep(store, [("a", 1)], n_heads=7)
