@@ -142,7 +142,8 @@ __global__ void __launch_bounds__(tcp::kThreads, 1)
   const int b = blockIdx.z, h = blockIdx.y;
   const int tpc = kM / p.G;
   const int n = p.q_len[b];
-  const int q0 = blockIdx.x * tpc;
+  // last query block first: the blocks with the most key tiles start earliest
+  const int q0 = (gridDim.x - 1 - blockIdx.x) * tpc;
   if (n <= 0 || q0 >= n) return;
   const int ctx = p.ctx[b];
   if (ctx < n || ctx > p.max_blocks * p.bs) {
@@ -171,7 +172,10 @@ __global__ void __launch_bounds__(tcp::kThreads, 1)
   volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + C::kBar + 8 * kNumBars + 4);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
-  if (threadIdx.x == 0) {
+  // The copy warp sets up the barriers and starts its copies at once; the
+  // other warps load Q and allocate TMEM meanwhile and meet it at named
+  // barrier 1 (the copy warp only arrives there).
+  if (warp == kProdWarp && lane == 0) {
     for (int s = 0; s < kKRing; ++s) mbar_init(bar(kBarKFull + s), 1);
     for (int s = 0; s < kVRing; ++s) mbar_init(bar(kBarVFull + s), 1);
     for (int s = 0; s < kSBufs; ++s) {
@@ -184,6 +188,10 @@ __global__ void __launch_bounds__(tcp::kThreads, 1)
     for (int x = 0; x < 4; ++x) mbar_init(bar(kBarLx + x), 64);
     *abort_flag = 0;
     fence_mbar_init();
+  }
+  if (warp == kProdWarp) {
+    __syncwarp();
+    asm volatile("bar.arrive 1, %0;" ::"n"(kThreads) : "memory");
   }
   if (warp == kMmaWarp) tc::tmem_alloc(smem_u32(tmem_slot), kTmemCols);
 
@@ -206,10 +214,13 @@ __global__ void __launch_bounds__(tcp::kThreads, 1)
     }
     fence_proxy_async_smem();
   }
-  tc::fence_before_sync();
-  __syncthreads();
-  tc::fence_after_sync();
-  const uint32_t tmem = *tmem_slot;
+  uint32_t tmem = 0;
+  if (warp != kProdWarp) {
+    tc::fence_before_sync();
+    asm volatile("bar.sync 1, %0;" ::"n"(kThreads) : "memory");
+    tc::fence_after_sync();
+    tmem = *tmem_slot;
+  }
 
   auto give_up = [&]() {
     dev_error(p.err, MZ_DEVERR_TIMEOUT);
