@@ -23,14 +23,13 @@ struct PParams {
   int out_f32;
   const void *q;
   int64_t q_st, q_sh;
-  int q_bf16;
   int n_rows;              // rows of q / out
   const int32_t *q_start;  // [B] first row of sequence b in q / out
   const int32_t *q_len;    // [B] query tokens of sequence b
   const int32_t *ctx;      // [B] tokens in the pools, the chunk included
   const int32_t *tables;
   int max_blocks;
-  int B, Hkv, G, bs;
+  int Hkv, G, bs;
   int64_t n_blocks;
   float scale_log2;
   int sub_log2;      // rows per bulk copy box: gcd(block_size, 128) = 1 << sub_log2
@@ -633,14 +632,12 @@ extern "C" int mz_paged_prefill(void *out, int32_t out_dtype, int64_t out_tok_st
   p.q = q;
   p.q_st = q_tok_stride;
   p.q_sh = q_head_stride;
-  p.q_bf16 = bf16;
   p.n_rows = n_rows;
   p.q_start = q_start;
   p.q_len = q_len;
   p.ctx = ctx_lens;
   p.tables = block_tables;
   p.max_blocks = max_blocks_per_seq;
-  p.B = n_seqs;
   p.Hkv = n_kv_heads;
   p.G = G;
   p.bs = block_size;
