@@ -332,7 +332,6 @@ def run_prefill(args, local_rank: int) -> None:
     ms = t0.elapsed_time(t1) / steps
 
     # the attention kernel alone: events around each launch (one extra pass)
-    kp0, vp0 = store.k_pool(0), store.v_pool(0)
     evs = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(nl)]
     for l in range(nl):
         kp, vp = store.k_pool(l), store.v_pool(l)
@@ -342,7 +341,6 @@ def run_prefill(args, local_rank: int) -> None:
         evs[l][1].record()
     torch.cuda.synchronize()
     pf_ms = statistics.mean(e[0].elapsed_time(e[1]) for e in evs)
-    del kp0, vp0
 
     # end to end: per layer the chunk's q/k/v from pinned host memory and the
     # attention output back, copies pipelined against the layers' launches
