@@ -162,11 +162,11 @@ class ClockSampler:
 # CPU baseline: the reference's algorithm (oracle port) on the host cores
 # ---------------------------------------------------------------------------
 
-def cpu_sample(seed: int, budget_s: float, threads: int, n_seqs: int = 16):
-    """Times oracle.cpu_path.decode_layer (torch-CPU restatement of the
-    reference's get_kv + GQA attention) on one layer of `n_seqs` sequences
-    drawn from the workload's ctx distribution; repeats until ~budget_s."""
-    import numpy as np
+def cpu_case(seed: int, threads: int, n_seqs: int = 16):
+    """One layer of `n_seqs` sequences drawn from the workload's ctx
+    distribution, for oracle.cpu_path.decode_layer (torch-CPU restatement of
+    the reference's get_kv + GQA attention).  Returns (run, kv_bytes): run()
+    times one layer and returns its seconds."""
     import torch
 
     from oracle import cpu_path
@@ -188,13 +188,23 @@ def cpu_sample(seed: int, budget_s: float, threads: int, n_seqs: int = 16):
     nv = torch.randn((n_seqs, HKV, D), generator=g).to(torch.bfloat16)
     kv_bytes = float((ctx + 1).sum()) * HKV * D * 2 * 2
     ctx_l = [int(c) for c in ctx]
-    cpu_path.decode_layer(q, kp, vp, tables, ctx_l, nk, nv, D ** -0.5)
+
+    def run() -> float:
+        t0 = time.perf_counter()
+        cpu_path.decode_layer(q, kp, vp, tables, ctx_l, nk, nv, D ** -0.5)
+        return time.perf_counter() - t0
+
+    return run, kv_bytes
+
+
+def cpu_sample(seed: int, budget_s: float, threads: int, n_seqs: int = 16):
+    """Median time of one layer (cpu_case) over repeats until ~budget_s."""
+    run, kv_bytes = cpu_case(seed, threads, n_seqs)
+    run()
     times = []
     t_end = time.perf_counter() + budget_s
     while True:
-        t0 = time.perf_counter()
-        cpu_path.decode_layer(q, kp, vp, tables, ctx_l, nk, nv, D ** -0.5)
-        times.append(time.perf_counter() - t0)
+        times.append(run())
         if time.perf_counter() > t_end or len(times) >= 100:
             break
     t = statistics.median(times)
@@ -442,12 +452,15 @@ def run_reference(args, rank: int, world: int) -> None:
         run_reference_prefill(args, world)
         return
     threads = os.cpu_count() or 1
-    budget = max(2.0, 120.0 / max(1, args.steps + args.warmup))
+    # the sample is built once; every warm-up and timed step is one layer of it
+    n_seqs = 16
+    run, kv_bytes = cpu_case(args.seed, threads, n_seqs)
     vals = []
     for i in range(args.warmup + args.steps):
-        r = cpu_sample(args.seed, budget, threads)
+        t = run()
         if i >= args.warmup:
-            vals.append(r)
+            vals.append({"gbs": kv_bytes / t / 1e9, "tok_s": n_seqs / (t * 32), "layer_s": t,
+                         "n_seqs": n_seqs})
     v = statistics.median(x["gbs"] for x in vals)
     ms = statistics.median(x["layer_s"] for x in vals) * 1000.0 * args.layers
     sample = (f"1 of {args.layers} layers, {vals[0]['n_seqs']} of {B_PER_GPU} sequences "
