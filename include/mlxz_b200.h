@@ -411,6 +411,22 @@ MZ_API int mz_kv_quant_append_paged(void *k_codes, void *k_scales, void *k_biase
                                     int32_t group_size, int32_t dtype, int32_t *dev_err,
                                     mz_stream_t stream);
 
+/* Dequantise whole quantised blocks into a 16-bit staging pool: block
+ * block_ids[i] of the quantised K and V pools (layout of mz_kv_quant_append)
+ * becomes block i of k_out / v_out, [n_ids][n_kv_heads][block_size][head_dim]
+ * of out_dtype (F16 or BF16), value = f32(scale) * q + f32(bias) rounded to
+ * out_dtype.  Ids outside [0, n_blocks): MZ_DEVERR_BLOCK_ID, block skipped.
+ * Used for the prompt pass over a quantised cache: mlx_lm's QuantizedKVCache
+ * (src/mlxz/engine/cache_utils.py:54-92) attends a prompt chunk over the
+ * quantised keys and values; here the chunk's blocks are dequantised once per
+ * layer and mz_paged_prefill runs on them. */
+MZ_API int mz_kv_dequant_blocks(void *k_out, void *v_out, int32_t out_dtype, const void *k_codes,
+                                const void *k_scales, const void *k_biases, const void *v_codes,
+                                const void *v_scales, const void *v_biases,
+                                const int32_t *block_ids, int32_t n_ids, int32_t n_kv_heads,
+                                int32_t head_dim, int32_t block_size, int64_t n_blocks,
+                                int32_t bits, int32_t *dev_err, mz_stream_t stream);
+
 /* Workspace bytes for mz_paged_decode_q (same layout rules as
  * mz_paged_decode_workspace_size). */
 MZ_API int mz_paged_decode_q_workspace_size(int32_t n_seqs, int32_t n_kv_heads,

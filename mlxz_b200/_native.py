@@ -110,6 +110,8 @@ _SIGNATURES: dict[str, list] = {
                                          _vp, _i32, _i32, _i32, _i32, _i32, _i64, _f32, _i32,
                                          _i32, ctypes.c_uint32, _vp, _sz, _vp, _vp],
     "mz_peer_wait": [_vp, _i32, _i32, ctypes.c_uint32, ctypes.c_uint64, _vp, _vp],
+    "mz_kv_dequant_blocks": [_vp, _vp, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32,
+                             _i32, _i32, _i64, _i32, _vp, _vp],
     "mz_paged_prefill": [_vp, _i32, _i64, _i64, _vp, _i64, _i64, _i32, _vp, _vp, _i32, _vp, _vp, _vp,
                          _i32, _vp, _i32, _i32, _i32, _i32, _i32, _i64, _f32, _i32, _vp, _vp],
     "mz_ipc_export": [_vp, _vp, ctypes.POINTER(ctypes.c_uint64)],

@@ -15,6 +15,12 @@ of sequences' chunks at once (ragged chunk lengths, ragged cache offsets):
 Queries and new K/V arrive as the model's projections lay them out: q
 ``[T, Hq, D]`` and k / v ``[T, Hkv, D]``, the sequences' chunks stacked along
 T in the order given.
+
+Over a QuantizedPagedKVStore the chunk is quantised on append
+(mz_kv_quant_append) and the chunk attends over the quantised keys and values,
+as a quantised cache's attention does: per layer the step's blocks are
+dequantised once into a staging pool of q's dtype (mz_kv_dequant_blocks) and
+mz_paged_prefill runs on it through block tables renumbered to that pool.
 """
 from __future__ import annotations
 
@@ -23,7 +29,7 @@ from dataclasses import dataclass
 import torch
 
 from .. import ops
-from .decode_step import PagedKVStore
+from .decode_step import PagedKVStore, QuantizedPagedKVStore
 
 
 @dataclass(slots=True)
@@ -79,8 +85,9 @@ class PagedPrefillStep:
 
     def __init__(self, store: PagedKVStore, chunks: list[tuple[str, int]], n_heads: int,
                  scale: float | None = None) -> None:
-        if type(store) is not PagedKVStore:
-            raise NotImplementedError("chunked prefill runs over bf16/fp16 pools")
+        if not isinstance(store, PagedKVStore):
+            raise TypeError("chunked prefill needs a PagedKVStore")
+        self.quantized = isinstance(store, QuantizedPagedKVStore)
         if n_heads % store.n_kv_heads:
             raise ValueError("n_heads must be a multiple of n_kv_heads")
         self.store = store
@@ -100,11 +107,17 @@ class PagedPrefillStep:
         self.T = sum(n for _, n in self.chunks)
         width = max([1] + [len(store.tables[s]) for s, _ in self.chunks])
         tables = torch.full((B, width), -1, dtype=torch.int32)
+        # quantised store: the attention reads a staging pool holding the
+        # step's blocks in first-use order, through renumbered tables
+        uniq = list(dict.fromkeys(blk for s, _ in self.chunks for blk in store.tables[s]))
+        local = {blk: i for i, blk in enumerate(uniq)}
         q_start, q_len, ctx, slots = [], [], [], []
         row = 0
         for b, (s, n) in enumerate(self.chunks):
             t = store.tables[s]
-            tables[b, :len(t)] = torch.tensor(t, dtype=torch.int32)
+            tt = [local[blk] for blk in t] if self.quantized else t
+            if tt:
+                tables[b, :len(tt)] = torch.tensor(tt, dtype=torch.int32)
             off = store.offsets[s]
             q_start.append(row)
             q_len.append(n)
@@ -118,6 +131,8 @@ class PagedPrefillStep:
         self.q_len = torch.tensor(q_len, dtype=torch.int32).to(dev)
         self.ctx_lens = torch.tensor(ctx, dtype=torch.int32).to(dev)
         self.slots = torch.tensor(slots, dtype=torch.int64).to(dev)
+        self._ids = torch.tensor(uniq, dtype=torch.int32).to(dev) if self.quantized else None
+        self._stage = None
         self._done = False
 
     def layer(self, l: int, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
@@ -130,8 +145,18 @@ class PagedPrefillStep:
             raise ValueError(f"k/v must be [{self.T}, {st.n_kv_heads}, {st.head_dim}]")
         if q.shape != (self.T, self.n_heads, st.head_dim):
             raise ValueError(f"q must be [{self.T}, {self.n_heads}, {st.head_dim}]")
-        kp, vp = st.k_pool(l), st.v_pool(l)
-        ops.kv_append(kp, vp, k.transpose(0, 1), v.transpose(0, 1), self.slots)
+        if self.quantized:
+            pools = st.qpools(l)
+            ops.kv_quant_append(pools, k.transpose(0, 1), v.transpose(0, 1), self.slots)
+            shape = (self._ids.numel(), st.n_kv_heads, st.block_size, st.head_dim)
+            if self._stage is None or self._stage[0].dtype != q.dtype:
+                self._stage = tuple(torch.empty(shape, dtype=q.dtype, device=st.device)
+                                    for _ in range(2))
+            kp, vp = self._stage
+            ops.kv_dequant_blocks(pools, self._ids, kp, vp)
+        else:
+            kp, vp = st.k_pool(l), st.v_pool(l)
+            ops.kv_append(kp, vp, k.transpose(0, 1), v.transpose(0, 1), self.slots)
         return ops.paged_prefill(q, kp, vp, self.tables, self.q_start, self.q_len, self.ctx_lens,
                                  self.max_q_len, self.scale, out=out, out_dtype=out_dtype)
 

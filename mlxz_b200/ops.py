@@ -531,6 +531,29 @@ def kv_quant_append_paged(pools, keys: torch.Tensor, values: torch.Tensor,
     _after(dev)
 
 
+def kv_dequant_blocks(pools, block_ids: torch.Tensor, k_out: torch.Tensor,
+                      v_out: torch.Tensor) -> None:
+    """Dequantise quantised blocks ``block_ids`` (int32 on the pools' device)
+    of the 6-tuple ``pools`` into ``k_out`` / ``v_out`` ``[n, H, bs, D]``
+    (fp16 or bf16): block ``block_ids[i]`` becomes block ``i``."""
+    n_blocks, H, bs, D, bits = _check_qpools(pools)
+    _as_i32(block_ids, pools[0].device, "block_ids")
+    n = block_ids.numel()
+    for t in (k_out, v_out):
+        if (t.shape != (n, H, bs, D) or t.dtype not in (torch.float16, torch.bfloat16)
+                or not t.is_contiguous() or t.device != pools[0].device):
+            raise ValueError(f"outputs must be contiguous fp16/bf16 [{n}, {H}, {bs}, {D}]")
+    if k_out.dtype != v_out.dtype:
+        raise ValueError("k_out and v_out must have the same dtype")
+    if n == 0:
+        return
+    dev = _dev_index(pools[0])
+    nat.call("mz_kv_dequant_blocks", k_out.data_ptr(), v_out.data_ptr(), dtype_code(k_out.dtype),
+             *_qptrs(pools), block_ids.data_ptr(), n, H, D, bs, n_blocks, bits,
+             error_word(dev).data_ptr(), _stream(dev))
+    _after(dev)
+
+
 def decode_q_workspace(n_seqs: int, n_kv_heads: int, rows: int, head_dim: int, bits: int,
                        device: int, num_warps: int = 0, shared: bool = True) -> torch.Tensor:
     """As ``decode_workspace``, for the quantised decode."""
