@@ -60,6 +60,8 @@ def parse_args():
     ap.add_argument("--separate-append", action="store_true",
                     help="append with mz_kv_append_paged, then mz_paged_decode (two launches)")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-sub-records", action="store_true",
+                    help="decode: skip the sharded70b sub-record measured after the headline")
     ap.add_argument("--batch-invariant", action="store_true",
                     help="decode: MZ_DECODE_BATCH_INVARIANT (whole pairs, batch-independent bytes)")
     ap.add_argument("--config", default="decode",
@@ -445,47 +447,8 @@ def run_prefill(args, local_rank: int) -> None:
     print(json.dumps(line), flush=True)
 
 
-def run_reference(args, rank: int, world: int) -> None:
-    if rank != 0:
-        return
-    if args.config == "prefill":
-        run_reference_prefill(args, world)
-        return
-    threads = os.cpu_count() or 1
-    # the sample is built once; every warm-up and timed step is one layer of it
-    n_seqs = 16
-    run, kv_bytes = cpu_case(args.seed, threads, n_seqs)
-    vals = []
-    for i in range(args.warmup + args.steps):
-        t = run()
-        if i >= args.warmup:
-            vals.append({"gbs": kv_bytes / t / 1e9, "tok_s": n_seqs / (t * 32), "layer_s": t,
-                         "n_seqs": n_seqs})
-    v = statistics.median(x["gbs"] for x in vals)
-    ms = statistics.median(x["layer_s"] for x in vals) * 1000.0 * args.layers
-    sample = (f"1 of {args.layers} layers, {vals[0]['n_seqs']} of {B_PER_GPU} sequences "
-              f"(ctx ~ U[{CTX_LO},{CTX_HI}]), torch-CPU port of get_kv + GQA attention, "
-              f"{threads} threads; ms_per_step extrapolated to {args.layers} layers")
-    line = {
-        "impl": "reference", "metric": METRIC, "value": round(v, 3), "unit": "GB/s",
-        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": round(ms * B_PER_GPU / vals[0]["n_seqs"], 3), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
-        "data": "synthetic (seeded N(0,1) K/V/Q, random block tables)",
-        "config": {"workload": "8B KV shape decode step (CPU sample)", "layers": args.layers,
-                   "global_batch": B_PER_GPU, "seq_len": f"U[{CTX_LO},{CTX_HI}]",
-                   "parallelism": "host threads"},
-        "decode_tok_s": round(statistics.median(x["tok_s"] for x in vals) * (32 / args.layers), 3),
-        "cpu_baseline": {"value": round(v, 3), "unit": "GB/s", "cores": threads, "kind": "port",
-                         "sample": sample},
-        "e2e": {"value": round(v, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
-                "d2h_bytes_per_step": 0},
-    }
-    print(json.dumps(line), flush=True)
-
-
 # ---------------------------------------------------------------------------
-# GPU benchmark
+# Decode workloads (shared by both arms)
 # ---------------------------------------------------------------------------
 
 def c5_ctx(seed: int, n: int):
@@ -498,81 +461,222 @@ def c5_ctx(seed: int, n: int):
     return np.clip(np.rint(c), C5_LO, C5_HI).astype(np.int64)
 
 
-def run_gpu(args, rank: int, world: int, local_rank: int) -> None:
-    """The paged decode step on this rank's KV-head shard.
+class Workload:
+    """Shapes of a decode workload at world size `world` (host side only).
 
-    decode (default): 8B shape, 64 sequences per GPU (weak scaling).
-    sharded70b: 70B shape, 256 sequences in total split by KV head across
-    the ranks (strong scaling); the layers that fit in HBM are resident and
-    timed, and the 80-layer step time is the per-layer time x 80."""
+    decode (c5 False): 8B shape, 64 sequences per GPU (weak scaling), `layers`
+    model layers, all resident.  sharded70b (c5 True): 70B shape, 256
+    sequences in total split by KV head across the ranks (strong scaling);
+    the layers whose pools fit in `resident_gb` per GPU are resident and
+    timed (`layers` caps them), and the 80-layer step time is the per-layer
+    time x 80."""
+
+    def __init__(self, c5: bool, world: int, layers: int | None, resident_gb: float, seed: int,
+                 p2p: bool):
+        self.c5, self.world, self.p2p = c5, world, p2p
+        self.hq_all = C5_HQ if c5 else HQ
+        self.hkv = HKV // world
+        self.hq = self.hq_all // world
+        if c5:
+            self.B = C5_B
+            self.ctx = c5_ctx(seed, self.B)
+            self.model_layers = C5_L
+        else:
+            self.B = B_PER_GPU * world
+            self.ctx = workload_ctx(seed, self.B)
+            self.model_layers = layers or L
+        self.need = (self.ctx + 1 + BS - 1) // BS
+        self.n_blocks = int(math.ceil(self.need.sum() * 1.1))
+        layer_pool_bytes = self.n_blocks * self.hkv * BS * D * 2 * 2
+        self.nl = self.model_layers
+        if c5:
+            fit = int(resident_gb * 1e9 // layer_pool_bytes)
+            self.nl = max(1, min(layers or C5_L, C5_L, fit))
+        # KV bytes one step reads: all heads, all ranks, every model layer
+        self.kv_step_total = float((self.ctx + 1).sum()) * HKV * D * 2 * 2 * self.model_layers
+        self.kv_layer_rank = float((self.ctx + 1).sum()) * self.hkv * D * 2 * 2
+        self.decode_alg_bytes = (self.kv_layer_rank + 2.0 * self.B * self.hq * D * 2
+                                 + float(self.need.sum()) * 4)
+
+    @property
+    def metric(self) -> str:
+        return C5_METRIC if self.c5 else METRIC
+
+    def config(self) -> dict:
+        world, nl = self.world, self.nl
+        if world == 1:
+            par = "1 GPU"
+        elif self.p2p:
+            par = (f"kv-head sharding x{world}; all-gather fused into the decode launch "
+                   f"(peer-memory stores over NVLink; each layer's launch waits for the peers' "
+                   f"rows of the layer before it)")
+        else:
+            par = f"kv-head sharding x{world} + NCCL all-gather per layer"
+        if self.c5:
+            workload = (f"head-sharded paged decode step, Llama-3.1-70B KV shape: 80 layers "
+                        f"({nl} resident and timed, step = per-layer time x 80), 64 q heads, "
+                        f"8 kv heads ({self.hkv} per GPU), head_dim 128, block 16; {self.B} "
+                        f"seqs, ctx lognormal(median {C5_MEDIAN}, sigma {C5_SIGMA}) clipped to "
+                        f"[{C5_LO},{C5_HI}]; append 1 token + attention + all-gather per layer")
+            seq_len = f"lognormal median {C5_MEDIAN} sigma {C5_SIGMA} in [{C5_LO},{C5_HI}]"
+        else:
+            workload = (f"paged decode step, Llama-3.1-8B KV shape: {nl} layers, 32 q heads, "
+                        f"8 kv heads, head_dim 128, block 16; {B_PER_GPU} seqs per GPU, "
+                        f"ctx U[{CTX_LO},{CTX_HI}]; append 1 token + attention per layer")
+            seq_len = f"U[{CTX_LO},{CTX_HI}]"
+        return {
+            "workload": workload, "layers": self.model_layers, "layers_resident": nl,
+            "global_batch": self.B, "seq_len": seq_len,
+            "mean_ctx": round(float(self.ctx.mean()), 1), "parallelism": par,
+            "l2": (f"KV read per layer {self.kv_layer_rank / 1e9:.2f} GB per GPU >> 126 MB L2"),
+            "pool_blocks": self.n_blocks,
+        }
+
+
+def run_reference(args, rank: int, world: int) -> None:
+    """The reference's CPU algorithm (oracle port) on this box's host cores,
+    on the GPU arm's workload and config.  Each step is measured whole: every
+    layer of the step over every sequence of rank 0's KV-head shard (the whole
+    workload at N = 1; 1/N of it at N > 1, where the other ranks do nothing).
+    One layer's pools are built and every layer pass reads them again (1.2 GB
+    per pass from DRAM, far above the host caches), with its own q and new
+    tokens."""
+    if rank != 0:
+        return
+    if args.config == "prefill":
+        run_reference_prefill(args, world)
+        return
+    import torch
+
+    from oracle import cpu_path
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    w = Workload(False, world, args.layers, args.resident_gb, args.seed, args.gather == "p2p")
+    hkv, hq, B, nl = w.hkv, w.hq, w.B, w.nl
+    g = torch.Generator().manual_seed(args.seed)
+    perm = torch.randperm(w.n_blocks, generator=g)
+    tables, used = [], 0
+    for n in w.need:
+        tables.append(perm[used:used + int(n)])
+        used += int(n)
+    kp = torch.randn((w.n_blocks, hkv, BS, D), generator=g).to(torch.bfloat16)
+    vp = torch.randn((w.n_blocks, hkv, BS, D), generator=g).to(torch.bfloat16)
+    q = torch.randn((nl, B, hq, D), generator=g).to(torch.bfloat16).float()
+    nk = torch.randn((nl, B, hkv, D), generator=g).to(torch.bfloat16)
+    nv = torch.randn((nl, B, hkv, D), generator=g).to(torch.bfloat16)
+    ctx_l = [int(c) for c in w.ctx]
+    scale = D ** -0.5
+
+    def step() -> float:
+        t0 = time.perf_counter()
+        for l in range(nl):
+            cpu_path.decode_layer(q[l], kp, vp, tables, ctx_l, nk[l], nv[l], scale)
+        return time.perf_counter() - t0
+
+    times = [step() for _ in range(args.warmup + args.steps)][args.warmup:]
+    ms = statistics.median(times) * 1e3
+    step_bytes = w.kv_layer_rank * nl
+    v = step_bytes / (ms / 1e3) / 1e9
+    share = ("the whole workload" if world == 1 else
+             f"rank 0's KV-head shard ({hkv} of 8 kv heads of all {B} sequences, 1/{world} "
+             f"of the job; the other ranks idle)")
+    sample = (f"every step measured whole: {nl} layers x {B} sequences, {share}; "
+              f"torch-CPU port of get_kv + GQA attention, {threads} threads; one layer's pools "
+              f"re-read by every layer pass ({w.kv_layer_rank / 1e9:.2f} GB per pass)")
+    line = {
+        "impl": "reference", "metric": w.metric, "value": round(v, 3), "unit": "GB/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded N(0,1) bf16 K/V/Q, random block tables)",
+        "config": w.config(),
+        "decode_tok_s": round(B / (ms / 1e3), 3),
+        "cpu_baseline": {"value": round(v, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": round(v, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------
+# GPU benchmark
+# ---------------------------------------------------------------------------
+
+def torch_fp32_attention(store, l: int, table: list[int], length: int, q, scale: float):
+    """Plain-torch fp32 decode attention of one sequence over its first
+    `length` pool tokens (the parity check inside the bench)."""
+    import torch
+
+    kp, vp = store.k_pool(l), store.v_pool(l)
+    hkv, bs, Dh = kp.shape[1], kp.shape[2], kp.shape[3]
+    idx = torch.tensor(table[: -(-length // bs)], dtype=torch.int64, device=kp.device)
+    K = kp.index_select(0, idx).permute(1, 0, 2, 3).reshape(hkv, -1, Dh)[:, :length].float()
+    V = vp.index_select(0, idx).permute(1, 0, 2, 3).reshape(hkv, -1, Dh)[:, :length].float()
+    hq = q.shape[0]
+    s = torch.bmm(q.float().view(hkv, hq // hkv, Dh), K.transpose(1, 2)) * scale
+    return torch.bmm(torch.softmax(s, dim=-1), V).reshape(hq, Dh)
+
+
+def attn_rel_err(out, ref, unit_roundoff: float) -> float:
+    """max(|out - ref| - u |ref|, 0) / max |ref|: the error beyond the output
+    type's own rounding, relative to the largest reference value."""
+    d = ((out.float() - ref).abs() - unit_roundoff * ref.abs()).clamp_min(0)
+    return float(d.max() / ref.abs().max())
+
+
+def measure_decode(args, w: "Workload", rank: int, world: int, local_rank: int, steps: int,
+                   warmup: int, e2e: bool, parity: bool) -> dict:
+    """Build the workload's pools on this rank, time `steps` decode steps and
+    return the rank-max timings (and the parity checks when asked)."""
     import numpy as np
     import torch
     import torch.distributed as dist
 
     from mlxz_b200 import ops
     from mlxz_b200.engine import PagedDecodeStep, PagedKVStore
+    from mlxz_b200.engine.decode_step import _copy_groups
     from mlxz_b200.engine.sharding import HeadAllGather, HeadShard, PeerAllGather
 
-    torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
-    c5 = args.config == "sharded70b"
-    hq_all = C5_HQ if c5 else HQ
-    shard = HeadShard(rank, world, HKV, hq_all)  # raises unless world divides 8 KV heads
-    if world > 1:
-        import datetime
-
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
-                                device_id=dev)
-    hkv, hq = shard.kv_local, shard.q_local
-    if c5:
-        B = C5_B
-        ctx = c5_ctx(args.seed, B)
-        model_layers = C5_L
-    else:
-        B = B_PER_GPU * world
-        ctx = workload_ctx(args.seed, B)
-        model_layers = args.layers or L
-    need = (ctx + 1 + BS - 1) // BS
-    n_blocks = int(math.ceil(need.sum() * 1.1))
-    layer_pool_bytes = n_blocks * hkv * BS * D * 2 * 2
-    nl = model_layers
-    if c5:
-        fit = int(args.resident_gb * 1e9 // layer_pool_bytes)
-        nl = max(1, min(args.layers or C5_L, C5_L, fit))
-    perm = np.random.default_rng(args.seed + 1).permutation(n_blocks)
-
+    shard = HeadShard(rank, world, HKV, w.hq_all)
+    hkv, hq, B, nl, D_ = w.hkv, w.hq, w.B, w.nl, D
+    perm = np.random.default_rng(args.seed + 1).permutation(w.n_blocks)
     torch.manual_seed(args.seed * 1000 + rank)
-    store = PagedKVStore(nl, n_blocks, hkv, D, BS, torch.bfloat16, dev, init="empty")
+    store = PagedKVStore(nl, w.n_blocks, hkv, D_, BS, torch.bfloat16, dev, init="empty")
     for l in range(nl):
         store.pools[l].normal_()
-    used = 0
-    ids = []
+    used, ids = 0, []
     for b in range(B):
         sid = f"s{b}"
-        store.add_sequence(sid, int(ctx[b]), blocks=[int(x) for x in perm[used:used + need[b]]])
-        used += int(need[b])
+        store.add_sequence(sid, int(w.ctx[b]),
+                           blocks=[int(x) for x in perm[used:used + w.need[b]]])
+        used += int(w.need[b])
         ids.append(sid)
     step = PagedDecodeStep(store, ids, hq, batch_invariant=args.batch_invariant)
-    q = torch.randn(nl, B, hq, D, device=dev).to(torch.bfloat16)
-    kn = torch.randn(nl, B, hkv, D, device=dev).to(torch.bfloat16)
-    vn = torch.randn(nl, B, hkv, D, device=dev).to(torch.bfloat16)
+    q = torch.randn(nl, B, hq, D_, device=dev).to(torch.bfloat16)
+    kn = torch.randn(nl, B, hkv, D_, device=dev).to(torch.bfloat16)
+    vn = torch.randn(nl, B, hkv, D_, device=dev).to(torch.bfloat16)
     out = torch.empty_like(q)
-    p2p = world > 1 and args.gather == "p2p"
-    gat = HeadAllGather(shard, B, D, torch.bfloat16, dev)
+    p2p = world > 1 and w.p2p
+    gat = HeadAllGather(shard, B, D_, torch.bfloat16, dev)
     # two sets of slots, alternated per step in the end-to-end loop (whose
     # outputs are read back while the next step runs)
-    peer = PeerAllGather(shard, B, D, torch.bfloat16, dev, n_slots=2 * nl) if p2p else None
-    if p2p:
-        full = peer.full[:nl]
-    else:
-        full = torch.empty((nl, B, hq_all, D), dtype=torch.bfloat16, device=dev) if world > 1 else out
+    peer = PeerAllGather(shard, B, D_, torch.bfloat16, dev, n_slots=2 * nl) if p2p else None
+    full = None
+    if world > 1 and not p2p:
+        full = torch.empty((nl, B, w.hq_all, D_), dtype=torch.bfloat16, device=dev)
 
-    kv_bytes_rank = float((ctx + 1).sum()) * hkv * D * 2 * 2  # per layer, this rank
-    qo_bytes = 2.0 * B * hq * D * 2
-    table_bytes = float(need.sum()) * 4
-    decode_alg_bytes = kv_bytes_rank + qo_bytes + table_bytes
+    # p2p slots: two sets of nl, alternated per step (all step loops share the
+    # round counter), so no slot is reused while its readers may still run
+    rounds = [0]
 
     def one_step(ev=None):
+        # p2p: layer l's launch waits (in its prologue) for the peers' rows of
+        # layer l - 1; the last layer is followed by a wait launch
+        base = nl * (rounds[0] % 2)
+        rounds[0] += 1
         for l in range(nl):
             st = step.store
             if args.separate_append:
@@ -585,24 +689,69 @@ def run_gpu(args, rank: int, world: int, local_rank: int) -> None:
                                  scale=step.scale, out=out[l], workspace=step.workspace,
                                  num_warps=args.num_warps)
             elif p2p:
-                peer.launch(step, l, q[l], kn[l], vn[l], slot=l, num_warps=args.num_warps)
+                peer.launch(step, l, q[l], kn[l], vn[l], slot=base + l,
+                            num_warps=args.num_warps, wait_previous=l > 0)
             else:
                 step.layer(l, q[l], kn[l], vn[l], out[l], num_warps=args.num_warps)
             if ev is not None:
                 ev[l][1].record()
-            if p2p:
-                peer.wait()
-            elif world > 1:
+            if world > 1 and not p2p:
                 gat.full(out[l], out=full[l])
+        if p2p:
+            peer.wait()
 
     def barrier():
         if world > 1:
             dist.barrier(device_ids=[local_rank])
 
-    for _ in range(max(3, args.warmup)):
+    for _ in range(warmup):
         one_step()
     torch.cuda.synchronize()
     ops.check_device_errors(local_rank)
+
+    res = {}
+    if parity:
+        # (1) at N > 1: the fused gather's output of layer 0, bytewise, against
+        # the ordinary launch + NCCL all-gather on the same inputs (every step
+        # rewrites the same new tokens, so the pools are the same for both);
+        # (2) one sequence per rank against a plain-torch fp32 recomputation
+        res_p = {}
+        if world > 1:
+            if p2p:
+                slot0 = nl * (rounds[0] % 2)
+                rounds[0] += 1
+                peer.launch(step, 0, q[0], kn[0], vn[0], slot=slot0, num_warps=args.num_warps)
+                peer.wait()
+                full0 = peer.full[slot0]
+            else:
+                full0 = full[0]
+            want = torch.empty((B, w.hq_all, D_), dtype=torch.bfloat16, device=dev)
+            local = torch.empty((B, hq, D_), dtype=torch.bfloat16, device=dev)
+            step.layer(0, q[0], kn[0], vn[0], local, num_warps=args.num_warps)
+            gat.full(local, out=want)
+            torch.cuda.synchronize()
+            same = torch.equal(full0, want)
+            t = torch.tensor([0 if same else 1], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            res_p["fused_vs_nccl_bytewise"] = bool(t.item() == 0) if p2p else None
+            got_rows = full0
+        else:
+            got_rows = out[0]
+        ops.check_device_errors(local_rank)
+        b = (rank * 37) % B
+        table = store.tables[ids[b]]
+        ref = torch_fp32_attention(store, 0, table, int(w.ctx[b]) + 1, q[0, b], step.scale)
+        got = got_rows[b, rank * hq:(rank + 1) * hq]
+        err = attn_rel_err(got, ref, 2.0 ** -8)
+        t = torch.tensor([err], device=dev)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        res_p["torch_fp32_max_rel_err"] = float(t.item())
+        res_p["tolerance"] = 2e-3
+        res_p["sequences_checked"] = f"one per rank (seq (37 r) mod {B}), layer 0"
+        res_p["ok"] = (res_p["torch_fp32_max_rel_err"] <= 2e-3
+                       and res_p.get("fused_vs_nccl_bytewise", True) is not False)
+        res["parity"] = res_p
 
     uuid = None
     try:
@@ -619,13 +768,13 @@ def run_gpu(args, rank: int, world: int, local_rank: int) -> None:
     torch.cuda.synchronize()
     clocks = ClockSampler(uuid, enabled=not args.no_clocks)
     t0.record()
-    for k in range(args.steps):
+    for _ in range(steps):
         one_step()
     t1.record()
     torch.cuda.synchronize()
     barrier()
-    clk = clocks.stop()
-    ms = t0.elapsed_time(t1) / args.steps
+    res["clocks"] = clocks.stop()
+    ms = t0.elapsed_time(t1) / steps
     dec_mean = ms / nl
     # each decode launch timed on its own (events between launches), two steps
     evs = [[[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(nl)]
@@ -639,7 +788,7 @@ def run_gpu(args, rank: int, world: int, local_rank: int) -> None:
     ops.check_device_errors(local_rank)
 
     e2e_ms, h2d, d2h = float('nan'), 0, 0
-    if not args.no_e2e:
+    if e2e:
         # End to end through the public step API: this rank's inputs from
         # pinned host memory; back to the host, this rank's heads of the
         # gathered [B, Hq, D] output (the ranks' parts together are the whole
@@ -648,15 +797,23 @@ def run_gpu(args, rank: int, world: int, local_rank: int) -> None:
         kh = kn.cpu().pin_memory()
         vh = vn.cpu().pin_memory()
         qlo, qhi = shard.q_range
-        oh = torch.empty((nl, B, hq, D), dtype=torch.bfloat16).pin_memory()
+        oh = torch.empty((nl, B, hq, D_), dtype=torch.bfloat16).pin_memory()
         h2d = (qh.numel() * 2 + kh.numel() * 2 + vh.numel() * 2) * world
         d2h = oh.numel() * 2 * world
-
-        rounds = [0]
+        groups = _copy_groups(nl)
+        first = {a for a, _ in groups}
+        last = {b - 1 for _, b in groups}
 
         def gather_layer(l, ql, kl, vl, ol):
             if p2p:
-                g = peer.layer(step, l, ql, kl, vl, slot=l + nl * (rounds[0] % 2))
+                # chained inside a copy group; the group's last layer is waited
+                # for, so the group's outputs are complete when it is copied back
+                slot = l + nl * (rounds[0] % 2)
+                peer.launch(step, l, ql, kl, vl, slot=slot, num_warps=args.num_warps,
+                            wait_previous=l not in first)
+                if l in last:
+                    peer.wait()
+                g = peer.full[slot]
             else:
                 step.layer(l, ql, kl, vl, ol)
                 g = gat.full(ol, out=full[l])
@@ -672,95 +829,115 @@ def run_gpu(args, rank: int, world: int, local_rank: int) -> None:
         barrier()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
-        for _ in range(args.steps):
+        for _ in range(steps):
             e2e_step()
         e1.record()
         torch.cuda.synchronize()
         barrier()
-        e2e_ms = e0.elapsed_time(e1) / args.steps
+        ops.check_device_errors(local_rank)
+        e2e_ms = e0.elapsed_time(e1) / steps
 
     if world > 1:
         t = torch.tensor([ms, e2e_ms, dec_mean, dec_iso], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms, e2e_ms, dec_mean, dec_iso = (float(x) for x in t.tolist())
-
-    # a step of the model: every layer (resident layers timed, x model/resident)
+    if peer is not None:
+        peer.close()
     per_layer_ms = ms / nl
-    step_ms = per_layer_ms * model_layers
-    e2e_step_ms = e2e_ms / nl * model_layers
-    kv_step_total = float((ctx + 1).sum()) * HKV * D * 2 * 2 * model_layers  # all heads, all ranks
-    value = kv_step_total / (step_ms / 1e3) / 1e9
-    peak, peak_kind = peaks()
-    achieved = decode_alg_bytes / (dec_mean / 1e3) / 1e9
+    res.update(ms=ms, e2e_ms=e2e_ms, dec_mean=dec_mean, dec_iso=dec_iso, h2d=h2d, d2h=d2h,
+               step_ms=per_layer_ms * w.model_layers,
+               e2e_step_ms=e2e_ms / nl * w.model_layers,
+               launches=steps * nl * (2 if args.separate_append else 1) + (steps if p2p else 0))
+    return res
+
+
+def run_gpu(args, rank: int, world: int, local_rank: int) -> None:
+    """The paged decode step on this rank's KV-head shard.
+
+    decode (default): 8B shape, 64 sequences per GPU (weak scaling), followed
+    by a `sharded70b` sub-record measured in the same run (unless
+    --no-sub-records).  sharded70b: the 70B-shape line alone."""
+    import torch
+    import torch.distributed as dist
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    c5 = args.config == "sharded70b"
+    p2p = args.gather == "p2p"
+    w = Workload(c5, world, args.layers, args.resident_gb, args.seed, p2p)
+    if world > 1:
+        import datetime
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=dev)
+    warm = max(3, args.warmup)
+    r = measure_decode(args, w, rank, world, local_rank, args.steps, warm,
+                       e2e=not args.no_e2e, parity=True)
+    torch.cuda.empty_cache()
+    sub = None
+    if not c5 and not args.no_sub_records:
+        w5 = Workload(True, world, None, args.resident_gb, args.seed, p2p)
+        r5 = measure_decode(args, w5, rank, world, local_rank, args.steps, warm, e2e=False,
+                            parity=True)
+        sub = {
+            "metric": w5.metric, "value": round(w5.kv_step_total / (r5["step_ms"] / 1e3) / 1e9, 2),
+            "unit": "GB/s", "scaling": "strong", "ms_per_step": round(r5["step_ms"], 4),
+            "ms_per_layer": round(r5["ms"] / w5.nl, 5), "layers": w5.model_layers,
+            "layers_resident": w5.nl, "steps": args.steps, "warmup": warm,
+            "decode_tok_s": round(w5.B / (r5["step_ms"] / 1e3), 1),
+            "config": w5.config(), "parity": r5.get("parity"),
+            "roofline": {"bound": "hbm", "unit": "GB/s",
+                         "achieved": round(w5.decode_alg_bytes / (r5["dec_mean"] / 1e3) / 1e9, 1),
+                         "decode_ms_mean": round(r5["dec_mean"], 4),
+                         "alg_bytes_per_launch": w5.decode_alg_bytes},
+            "gpu_launches": r5["launches"], "clocks": r5["clocks"],
+        }
     if rank == 0:
+        peak, peak_kind = peaks()
         cpu = None
         if world == 1 and not args.no_cpu_baseline and not c5:
             threads = os.cpu_count() or 1
-            r = cpu_sample(args.seed, args.cpu_seconds, threads)
-            cpu = {"value": round(r["gbs"], 3), "unit": "GB/s", "cores": threads, "kind": "port",
-                   "sample": (f"1 layer x {r['n_seqs']} sequences of the same ctx distribution, "
-                              f"{r['reps']} reps (median), torch-CPU port of get_kv + GQA attention")}
-        traffic = profile_traffic("paged_decode_c2.md") if not c5 else None
-        if world == 1:
-            par = "1 GPU"
-        elif p2p:
-            par = (f"kv-head sharding x{world}; all-gather fused into the decode launch "
-                   f"(peer-memory stores over NVLink + signal wait) per layer")
-        else:
-            par = f"kv-head sharding x{world} + NCCL all-gather per layer"
-        if c5:
-            metric = C5_METRIC
-            workload = (f"head-sharded paged decode step, Llama-3.1-70B KV shape: 80 layers "
-                        f"({nl} resident and timed, step = per-layer time x 80), 64 q heads, "
-                        f"8 kv heads ({hkv} per GPU), head_dim 128, block 16; {B} seqs, ctx "
-                        f"lognormal(median {C5_MEDIAN}, sigma {C5_SIGMA}) clipped to "
-                        f"[{C5_LO},{C5_HI}]; append 1 token + attention + all-gather per layer")
-            seq_len = f"lognormal median {C5_MEDIAN} sigma {C5_SIGMA} in [{C5_LO},{C5_HI}]"
-        else:
-            metric = METRIC
-            workload = (f"paged decode step, Llama-3.1-8B KV shape: {nl} layers, 32 q heads, "
-                        f"8 kv heads, head_dim 128, block 16; {B_PER_GPU} seqs per GPU, "
-                        f"ctx U[{CTX_LO},{CTX_HI}]; append 1 token + attention per layer")
-            seq_len = f"U[{CTX_LO},{CTX_HI}]"
+            s = cpu_sample(args.seed, args.cpu_seconds, threads)
+            cpu = {"value": round(s["gbs"], 3), "unit": "GB/s", "cores": threads, "kind": "port",
+                   "sample": (f"1 layer x {s['n_seqs']} sequences of the same ctx distribution, "
+                              f"{s['reps']} reps (median), torch-CPU port of get_kv + GQA attention")}
+        value = w.kv_step_total / (r["step_ms"] / 1e3) / 1e9
+        achieved = w.decode_alg_bytes / (r["dec_mean"] / 1e3) / 1e9
+        if sub is not None:
+            sub["roofline"].update(peak=peak, peak_kind=peak_kind,
+                                   frac=round(sub["roofline"]["achieved"] / peak, 4))
         result = {
-            "metric": metric, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
-            "steps": args.steps, "warmup": max(3, args.warmup), "ms_per_step": round(step_ms, 4),
-            "higher_is_better": True, "scaling": "strong" if c5 else "weak", "vs_baseline": None,
-            "dtype": "bf16",
+            "metric": w.metric, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
+            "steps": args.steps, "warmup": warm, "ms_per_step": round(r["step_ms"], 4),
+            "higher_is_better": True, "scaling": "strong" if c5 else "weak",
+            "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (seeded N(0,1) bf16 K/V/Q, random block tables)",
-            "config": {
-                "workload": workload, "layers": model_layers, "layers_resident": nl,
-                "global_batch": B, "seq_len": seq_len,
-                "mean_ctx": round(float(ctx.mean()), 1),
-                "parallelism": par,
-                "l2": f"KV read per layer {kv_step_total / model_layers / world / 1e9:.2f} GB per "
-                      f"GPU >> 126 MB L2",
-                "pool_blocks": n_blocks,
-            },
-            "decode_tok_s": round(B / (step_ms / 1e3), 1),
+            "config": w.config(),
+            "decode_tok_s": round(w.B / (r["step_ms"] / 1e3), 1),
             "hbm_frac": round(value / world / peak, 4),
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
                          "unit": "GB/s", "frac": round(achieved / peak, 4),
-                         "traffic": traffic,
+                         "traffic": profile_traffic("paged_decode_c2.md") if not c5 else None,
                          "kernel": "paged_decode_kernel<128,bf16> (fused append + decode"
-                                   + (" + peer all-gather)" if p2p else ")"),
+                                   + (" + peer all-gather)" if world > 1 and p2p else ")"),
                          "peak_kind": peak_kind,
-                         "decode_ms_mean": round(dec_mean, 4),
+                         "decode_ms_mean": round(r["dec_mean"], 4),
                          "decode_ms_timing": ("timed region / launches" if world == 1 else
                                               "timed region / launches (includes the gather)"),
-                         "decode_ms_isolated": round(dec_iso, 4),
-                         "alg_bytes_per_launch": decode_alg_bytes},
+                         "decode_ms_isolated": round(r["dec_iso"], 4),
+                         "alg_bytes_per_launch": w.decode_alg_bytes},
             "cpu_baseline": cpu,
             "e2e": None if args.no_e2e else {
-                "value": round(kv_step_total / (e2e_step_ms / 1e3) / 1e9, 2), "unit": "GB/s",
-                "ms_per_step": round(e2e_step_ms, 4), "h2d_bytes_per_step": int(h2d),
-                "d2h_bytes_per_step": int(d2h)},
-            "gpu_launches": args.steps * nl * (2 if (args.separate_append or p2p) else 1),
-            "clocks": clk,
+                "value": round(w.kv_step_total / (r["e2e_step_ms"] / 1e3) / 1e9, 2),
+                "unit": "GB/s", "ms_per_step": round(r["e2e_step_ms"], 4),
+                "h2d_bytes_per_step": int(r["h2d"]), "d2h_bytes_per_step": int(r["d2h"])},
+            "gpu_launches": r["launches"],
+            "clocks": r["clocks"],
+            "parity": r.get("parity"),
         }
+        if sub is not None:
+            result["sharded70b"] = sub
         print(json.dumps(result), flush=True)
-    if peer is not None:
-        peer.close()
     if world > 1:
         dist.destroy_process_group()
 

@@ -228,6 +228,16 @@ MZ_API int mz_paged_prefill(void *out, int32_t out_dtype, int64_t out_tok_stride
  * < 1e-4, batch-position determinism bytewise).  Slower when the pairs are
  * fewer than the launch's warps or very uneven. */
 #define MZ_DECODE_BATCH_INVARIANT 2u
+/* MZ_LAUNCH_WAIT_PREVIOUS (mz_paged_append_decode_allgather only): the launch
+ * itself first waits, bounded like mz_peer_wait, until every peer's signal
+ * word in signal[rank] (this rank's own words) holds epoch - 1, i.e. until the
+ * peers' rows of this rank's previous launch are in its gathered buffer; only
+ * then does it read q / k_new / v_new or store anything.  It replaces the
+ * mz_peer_wait launch between two layers, so with MZ_LAUNCH_OVERLAP_PREVIOUS
+ * the next layer's first K/V copies still start while the previous layer
+ * drains.  Work queued after the launch then sees the previous launch's
+ * gathered buffer complete. */
+#define MZ_LAUNCH_WAIT_PREVIOUS 4u
 
 /* mz_paged_append_decode with launch flags (MZ_LAUNCH_*).  Same reference
  * counterpart and rules as mz_paged_append_decode. */
@@ -253,7 +263,8 @@ MZ_API int mz_paged_append_decode_ex(void *out, int32_t out_dtype, int64_t out_s
  *              GPU can store to (out[rank] local; the others mapped with
  *              mz_ipc_open);
  *   signal[r]: rank r's n_ranks signal words (zero before the first launch),
- *              mapped likewise (signal[rank] is not used);
+ *              mapped likewise (signal[rank], this rank's own words, is read
+ *              only by launches with MZ_LAUNCH_WAIT_PREVIOUS);
  *   arrivals:  one int32 in this GPU's memory, zero before the first launch
  *              (each launch leaves it zero);
  *   epoch:     nonzero, one more per launch, the same on every rank. */
@@ -270,8 +281,9 @@ typedef struct mz_peer_outputs {
  * gathered buffer (this GPU's own and, over NVLink, each peer's) as they are
  * finished, instead of a separate all-gather after the launch; the launch's
  * last block then publishes `epoch` into signal word `rank` of every peer.
- * Each rank follows the launch with mz_peer_wait before it reads the gathered
- * buffer.  out_seq_stride / out_head_stride are those of the gathered buffer
+ * Each rank follows the launch with mz_peer_wait, or with its next launch
+ * made with MZ_LAUNCH_WAIT_PREVIOUS, before it reads the gathered buffer.
+ * out_seq_stride / out_head_stride are those of the gathered buffer
  * (n_ranks*n_heads*head_dim and head_dim for a dense one).
  * No counterpart in the reference (one device only); it replaces the
  * all-gather of head-sharded attention outputs that a multi-GPU step runs

@@ -73,6 +73,7 @@ MZ_MAX_RANKS = 8
 MZ_IPC_HANDLE_BYTES = 64
 MZ_LAUNCH_OVERLAP_PREVIOUS = 1
 MZ_DECODE_BATCH_INVARIANT = 2
+MZ_LAUNCH_WAIT_PREVIOUS = 4
 
 
 class PeerOutputs(ctypes.Structure):

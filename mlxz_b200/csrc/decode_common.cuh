@@ -79,6 +79,12 @@ struct Params {
   uint32_t *peer_sig[MZ_MAX_RANKS - 1] = {};
   uint32_t epoch = 0;
   int32_t *arrivals = nullptr;  // grid arrival counter, zero between launches
+  // Wait folded into this launch (MZ_LAUNCH_WAIT_PREVIOUS): before anything is
+  // read from q or stored, every peer's word in own_sig (this GPU's signal
+  // words, one per rank; own_rank's is not used) must reach wait_epoch.
+  const uint32_t *own_sig = nullptr;
+  int own_rank = 0, n_ranks = 1;
+  uint32_t wait_epoch = 0;  // 0: no folded wait
 };
 
 struct Cursor {
@@ -203,6 +209,41 @@ __device__ __forceinline__ void wait_for_previous_grid() {
 
 __device__ __forceinline__ void st_release_sys(uint32_t *addr, uint32_t v) {
   asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(addr), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ uint32_t ld_acquire_sys_u32(const uint32_t *addr) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(addr) : "memory");
+  return v;
+}
+
+// The peer wait folded into a launch: thread s of each block polls signal word
+// s (s != own rank; the peers store it with a system-scope release once their
+// previous launch's rows are all in this GPU's buffer) until it reaches
+// wait_epoch (wrap-safe), bounded by kTimeoutNs; the block barrier then orders
+// every thread's later reads and stores after those acquires.  A word that
+// does not arrive in time sets MZ_DEVERR_TIMEOUT and the launch carries on.
+// Every thread of the block must call it.
+__device__ __forceinline__ void wait_peers_previous(const Params &p) {
+  if (p.wait_epoch == 0) return;
+  const int s = threadIdx.x;
+  if (s < p.n_ranks && s != p.own_rank) {
+    uint64_t t0 = 0;
+    for (uint32_t it = 0;; ++it) {
+      if (static_cast<int32_t>(ld_acquire_sys_u32(p.own_sig + s) - p.wait_epoch) >= 0) break;
+      if ((it & 63u) == 63u) {
+        const uint64_t now = global_timer_ns();
+        if (t0 == 0) {
+          t0 = now;
+        } else if (now - t0 > kTimeoutNs) {
+          dev_error(p.err, MZ_DEVERR_TIMEOUT);
+          break;
+        }
+        __nanosleep(128);
+      }
+    }
+  }
+  __syncthreads();
 }
 
 // Called by every thread of the grid after its last output store (every exit

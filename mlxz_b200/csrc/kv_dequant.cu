@@ -98,8 +98,11 @@ extern "C" int mz_kv_dequant_blocks(void *k_out, void *v_out, int32_t out_dtype,
       !aligned(v_biases, 2))
     return fail(MZ_ERR_ALIGNMENT, "%s: outputs need 16-byte, codes 4-byte alignment", fn);
   const int64_t units = 2LL * n_ids * n_kv_heads * block_size * (head_dim / 8);
+  // grid-stride kernel: at most 32 blocks of 256 threads per SM
+  const int sms = sm_count(current_device());
+  if (sms <= 0) return fail(MZ_ERR_CUDA, "%s: cannot query the device's SM count", fn);
   int64_t g = (units + 255) / 256;
-  if (g > 148LL * 32) g = 148LL * 32;
+  if (g > 32LL * sms) g = 32LL * sms;
   const unsigned grid = static_cast<unsigned>(g);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   auto *ko = static_cast<uint16_t *>(k_out);

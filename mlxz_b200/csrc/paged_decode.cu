@@ -116,6 +116,7 @@ __device__ __forceinline__ void decode_tiles(const CUtensorMap &tmK, const CUten
   // share are already on their way when the wait returns.
   if (any_work) sch.prefetch_static<S>(p, issue);
   wait_for_previous_grid();
+  if constexpr (GATHER) wait_peers_previous(p);
   zero_empty_outputs<D, GATHER>(p, wid, W, lane);
   if (!any_work) return;
 
@@ -574,6 +575,12 @@ int launch(const DecodeArgs &a, int64_t warps, const WsLayout &ws, void *scratch
     p.n_peer = j;
     p.epoch = pe.epoch;
     p.arrivals = pe.arrivals;
+    if (a.flags & MZ_LAUNCH_WAIT_PREVIOUS) {
+      p.own_sig = reinterpret_cast<const uint32_t *>(pe.signal[pe.rank]);
+      p.own_rank = pe.rank;
+      p.n_ranks = pe.n_ranks;
+      p.wait_epoch = pe.epoch == 1u ? 0xFFFFFFFFu : pe.epoch - 1u;  // epochs skip 0
+    }
   }
 
   int per_sm = 0;  // also sets the kernel's shared-memory attribute (once)
@@ -776,11 +783,15 @@ extern "C" int mz_paged_append_decode_allgather(
     int32_t num_warps, uint32_t flags, void *workspace, size_t workspace_bytes,
     int32_t *dev_err, mz_stream_t stream) {
   const char *fn = "mz_paged_append_decode_allgather";
-  if (flags & ~(MZ_LAUNCH_OVERLAP_PREVIOUS | MZ_DECODE_BATCH_INVARIANT))
+  if (flags & ~(MZ_LAUNCH_OVERLAP_PREVIOUS | MZ_DECODE_BATCH_INVARIANT | MZ_LAUNCH_WAIT_PREVIOUS))
     return fail(MZ_ERR_INVALID_ARG, "%s: unknown flags", fn);
   if (!peers) return fail(MZ_ERR_INVALID_ARG, "%s: peers is null", fn);
   if (peers->rank < 0 || peers->rank >= MZ_MAX_RANKS)
     return fail(MZ_ERR_INVALID_ARG, "%s: rank %d out of range", fn, peers->rank);
+  if ((flags & MZ_LAUNCH_WAIT_PREVIOUS) &&
+      (!peers->signal[peers->rank] || !aligned(peers->signal[peers->rank], 4)))
+    return fail(MZ_ERR_INVALID_ARG,
+                "%s: MZ_LAUNCH_WAIT_PREVIOUS needs signal[rank] (this rank's own words)", fn);
   DecodeArgs a = make_args(peers->out[peers->rank], out_dtype, out_seq_stride, 0, out_head_stride,
                            q, q_seq_stride, 0, q_head_stride, 1, k_pool, v_pool, block_tables,
                            max_blocks_per_seq, ctx_lens, n_seqs, n_heads, n_kv_heads, head_dim,
@@ -822,25 +833,31 @@ namespace decode {
 constexpr size_t kStaticScratchBytes = size_t(16) << 20;  // 16 MiB per device
 static __device__ __align__(256) uint8_t g_static_scratch[kStaticScratchBytes];
 
-struct StaticScratchSlot {
-  std::once_flag once;
-  void *ptr = nullptr;
-  cudaError_t err = cudaSuccess;
-};
 constexpr int kMaxStaticDevices = 64;
-StaticScratchSlot g_static_slots[kMaxStaticDevices];
+std::mutex g_static_mu;
+void *g_static_ptr[kMaxStaticDevices] = {};
 
 // Device address of g_static_scratch on `device`, which must be the current
 // device.  Host code cannot use the symbol's name as a device pointer, so the
-// address is looked up once per device with cudaGetSymbolAddress.
+// address is looked up with cudaGetSymbolAddress and kept once it succeeded.
+// A failed lookup (for example one made while the stream is being captured)
+// is not remembered: its error is cleared from the runtime's sticky slot and
+// the next call looks the address up again.
 int static_scratch_ptr(int device, void **ptr) {
   if (device < 0 || device >= kMaxStaticDevices)
     return fail(MZ_ERR_CUDA, "no usable current device (%d)", device);
-  StaticScratchSlot &s = g_static_slots[device];
-  std::call_once(s.once, [&s]() { s.err = cudaGetSymbolAddress(&s.ptr, g_static_scratch); });
-  if (s.err != cudaSuccess) return cuda_fail(s.err, "cudaGetSymbolAddress(decode scratch)");
-  if (!s.ptr) return fail(MZ_ERR_CUDA, "decode scratch has no device address");
-  *ptr = s.ptr;
+  std::lock_guard<std::mutex> lock(g_static_mu);
+  if (!g_static_ptr[device]) {
+    void *p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_static_scratch);
+    if (e != cudaSuccess) {
+      (void)cudaGetLastError();  // later launch checks must not see this error
+      return cuda_fail(e, "cudaGetSymbolAddress(decode scratch)");
+    }
+    if (!p) return fail(MZ_ERR_CUDA, "decode scratch has no device address");
+    g_static_ptr[device] = p;
+  }
+  *ptr = g_static_ptr[device];
   return MZ_OK;
 }
 

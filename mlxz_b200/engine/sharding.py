@@ -141,26 +141,39 @@ class PeerAllGather:
 
     Every rank keeps ``n_slots`` gathered buffers ``[B, Hq, D]`` and ``N``
     signal words in one device allocation, exchanged once with CUDA IPC.
-    ``layer`` runs mz_paged_append_decode_allgather -- each output row is
+    ``launch`` runs mz_paged_append_decode_allgather: each output row is
     stored into the slot of every rank's buffer as soon as it is final, the
-    peers' over NVLink -- then mz_peer_wait for the peers' signals, so work
-    queued after it sees the whole ``[B, Hq, D]``.  No separate collective
-    and no layout copy.  All ranks must call ``layer`` the same number of
-    times (the epochs must agree).  Peers write a slot for the next time as
-    soon as this rank's launch before that one has completed, so this rank's
-    readers of a slot must be ordered (on its stream) before that preceding
-    launch; cycling through two sets of slots per round of layers (slot
-    ``l + n_layers * (round % 2)``) makes any reader ordered before the next
-    round's first launch safe.  ``close`` (collective) ends the mappings.
+    peers' over NVLink, and the launch's last block then signals the peers.
+    No separate collective and no layout copy.  A launch's gathered buffer is
+    complete for work queued after either
+
+    * ``wait()`` (a small bounded-wait launch), or
+    * the next ``launch(..., wait_previous=True)``, which waits for the peers'
+      rows of the launch before it inside its own prologue (after its first
+      K/V copies have started), so consecutive layers need no launch between
+      them and keep their overlap.
+
+    ``layer`` is ``launch`` + ``wait``.  Every launch must be followed by one
+    of the two before the next plain launch (enforced), and all ranks must make
+    the same sequence of launches (the epochs must agree).
+
+    Slot reuse: peers store into a slot again as soon as this rank's launch
+    before that one has completed, so the readers of a slot must be queued
+    before that launch.  With readers queued right where the slot becomes
+    complete, that means a slot is never reused by the next launch, nor, when
+    the next launch is a ``wait_previous`` one (whose slot is then complete
+    only after the launch after it), by the launch after that; both are
+    checked.  Hence at least 2 slots for ``layer`` and 3 for chained launches.
+    ``close`` (collective) ends the mappings.
     """
 
     def __init__(self, shard: HeadShard, batch: int, head_dim: int, dtype: torch.dtype,
-                 device, n_slots: int = 1, group=None, timeout_s: float = 2.0) -> None:
+                 device, n_slots: int = 3, group=None, timeout_s: float = 2.0) -> None:
         from .. import _native as nat
         from .. import ops
 
-        if batch < 1 or n_slots < 1:
-            raise ValueError("batch and n_slots must be positive")
+        if batch < 1 or n_slots < 2:
+            raise ValueError("batch must be positive and n_slots at least 2")
         if shard.world > nat.MZ_MAX_RANKS:
             raise ValueError(f"at most {nat.MZ_MAX_RANKS} ranks")
         self.shard = shard
@@ -182,6 +195,10 @@ class PeerAllGather:
         self.out_seq_stride = Hq * head_dim
         self.out_head_stride = head_dim
         self._handles: list[bytes] = []
+        # (slot, chained) of the last two launches, and whether the last one
+        # still needs wait() or a chained launch
+        self._recent: list[tuple[int, bool]] = []
+        self._pending = False
         bases = [self.arena.data_ptr()] * N
         if N > 1:
             import torch.distributed as dist
@@ -203,32 +220,54 @@ class PeerAllGather:
             pe.n_ranks, pe.rank = N, r
             for s in range(N):
                 pe.out[s] = bases[s] + k * self.slot_elems * elem + head_off
-                pe.signal[s] = bases[s] + sig_off
+                pe.signal[s] = bases[s] + sig_off  # signal[r]: this rank's own words
             pe.arrivals = self.arrivals.data_ptr()
             self._peers.append(pe)
 
+    def _check_slot(self, slot: int, wait_previous: bool) -> None:
+        if not 0 <= slot < len(self._peers):
+            raise ValueError(f"slot {slot} out of range (n_slots {len(self._peers)})")
+        if self._pending and not wait_previous:
+            raise RuntimeError("the previous launch was neither waited for nor followed by a "
+                               "wait_previous launch")
+        if self._recent and self._recent[-1][0] == slot:
+            raise ValueError(f"slot {slot} is the previous launch's: peers could overwrite it "
+                             "before this rank has read it")
+        if len(self._recent) == 2 and self._recent[1][1] and self._recent[0][0] == slot:
+            raise ValueError(f"slot {slot} was used two launches ago and the launch after it "
+                             "waited for it (wait_previous): peers could overwrite it before "
+                             "this rank has read it")
+
     def launch(self, step, l: int, q: torch.Tensor, k_new: torch.Tensor, v_new: torch.Tensor,
-               slot: int = 0, num_warps: int = 0) -> None:
+               slot: int = 0, num_warps: int = 0, wait_previous: bool = False) -> None:
         """Queue layer ``l`` of a PagedDecodeStep on this rank's heads (append +
-        attention), its rows stored into ``full[slot]`` of every rank."""
+        attention), its rows stored into ``full[slot]`` of every rank.  With
+        ``wait_previous`` the launch first waits (on the device, bounded) for
+        every peer's rows of this rank's previous launch, which then completes
+        that launch's slot for work queued after this one."""
         from .. import ops
 
+        self._check_slot(slot, wait_previous)
         self.epoch = self.epoch % 0xFFFFFFFF + 1  # 1, 2, ..., 2^32 - 1, 1, ...
         pe = self._peers[slot]
         pe.epoch = self.epoch
         st = step.store
-        # layers after the first may start while the previous layer's wait runs
+        # layers after the first may start while the previous layer drains
         ops.paged_append_decode_allgather(pe, q, st.k_pool(l), st.v_pool(l), k_new, v_new,
                                           step.tables, step.lengths, self.out_seq_stride,
                                           self.out_head_stride, self.dtype, scale=step.scale,
                                           num_warps=num_warps, workspace=step.workspace,
-                                          overlap_previous=l > 0)
+                                          overlap_previous=l > 0,
+                                          wait_previous=wait_previous and self.epoch > 1)
+        self._recent = (self._recent + [(slot, wait_previous)])[-2:]
+        self._pending = True
 
     def wait(self) -> None:
         """Queue the bounded wait for every peer's rows of the last launch."""
         from .. import ops
 
         ops.peer_wait(self.signal, self.shard.world, self.shard.rank, self.epoch, self.timeout_s)
+        self._pending = False
 
     def layer(self, step, l: int, q: torch.Tensor, k_new: torch.Tensor, v_new: torch.Tensor,
               slot: int = 0, num_warps: int = 0) -> torch.Tensor:

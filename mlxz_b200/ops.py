@@ -386,11 +386,15 @@ def paged_append_decode_allgather(peers: "nat.PeerOutputs", q: torch.Tensor,
                                   out_dtype: torch.dtype, scale: float | None = None,
                                   num_warps: int = 0,
                                   workspace: torch.Tensor | None = None,
-                                  overlap_previous: bool = False) -> None:
+                                  overlap_previous: bool = False,
+                                  wait_previous: bool = False) -> None:
     """paged_append_decode whose output rows go to every rank's gathered
     buffer (``peers.out[r]``: this rank's head block there) and whose last
     warp signals the peers (mz_paged_append_decode_allgather); follow it with
-    ``peer_wait`` before reading the gathered buffer."""
+    ``peer_wait``, or with a next launch made with ``wait_previous``, before
+    reading the gathered buffer.  ``wait_previous`` (MZ_LAUNCH_WAIT_PREVIOUS):
+    the launch first waits, on the device and bounded, for the peers' rows of
+    this rank's previous launch."""
     n_blocks, Hkv, bs, D = _check_pools(k_pool, v_pool)
     if q.dim() != 3 or q.shape[2] != D or q.stride(-1) != 1 or q.dtype != k_pool.dtype:
         raise ValueError(f"q must be [B, Hq, {D}] of the pool dtype with unit last stride")
@@ -416,7 +420,8 @@ def paged_append_decode_allgather(peers: "nat.PeerOutputs", q: torch.Tensor,
              k_new.stride(0), k_new.stride(1), block_tables.data_ptr(), block_tables.shape[1],
              ctx_lens.data_ptr(), B, Hq, Hkv, D, bs, n_blocks, float(scale),
              dtype_code(q.dtype), num_warps,
-             nat.MZ_LAUNCH_OVERLAP_PREVIOUS if overlap_previous else 0,
+             (nat.MZ_LAUNCH_OVERLAP_PREVIOUS if overlap_previous else 0)
+             | (nat.MZ_LAUNCH_WAIT_PREVIOUS if wait_previous else 0),
              workspace.data_ptr(), workspace.numel(), error_word(dev).data_ptr(), _stream(dev))
     _after(dev)
 

@@ -22,6 +22,22 @@ rules down exactly, and the CUDA kernel must match it bit for bit:
   7. dequantised value: f32(scale16) * q + f32(bias16).
 Scales and biases are stored as fp16 (the build's chosen format; MLX keeps
 them in the input dtype).  Inputs must be finite with |w| <= 65504.
+
+Standing of this rule (parity unpinned).  The rule above is this build's own
+restatement of the documented affine form.  Nothing pins it to MLX 0.22.1 /
+mlx-lm 0.22.1 (the reference's pins, pyproject.toml:10-11): MLX cannot run
+here, and no reference test or fixture holds quantised values
+(tests/unit/test_cache_utils.py:49-57 checks shapes and offsets only).  MLX's
+implementation may choose the pair differently: for example, taking as the
+bias whichever group edge (min or max) has the larger magnitude, with a
+scale whose sign follows that edge, rescaled so that the edge itself is
+exactly representable.  Where it does, the codes, scales and biases that
+quantise-on-append writes differ from what mlx_lm's QuantizedKVCache would
+hold for the same input, and "bit-exact quantised packing" holds against
+this rule only.  The dequantisation w = scale * q + bias, the group size,
+the packing and the layout do not depend on how the pair was chosen, so the
+dequant-fused attention reads either kind of code (tested with negative
+scales and edge biases).
 """
 from __future__ import annotations
 

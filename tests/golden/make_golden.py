@@ -1,9 +1,9 @@
 """Generate the golden fixtures in this directory from the reference's own code.
 
-Run from the repository root in a container that has the reference checkout
-at /root/reference (read-only):
+Run from the repository root, pointing at a checkout of the reference (read
+only; nothing is written there), either with --ref or MLXZ_REFERENCE:
 
-    python tests/golden/make_golden.py [--ref /root/reference]
+    python tests/golden/make_golden.py --ref <path to the metazen11/mlxz checkout>
 
 The reference (metazen11/mlxz) is pure Python over MLX, which is macOS/arm64
 only and not installed here.  Its KV-cache sources only use a handful of MLX
@@ -27,6 +27,7 @@ import argparse
 import hashlib
 import importlib.util
 import json
+import os
 import random
 import sys
 import types
@@ -442,8 +443,11 @@ def scenario_prefix_memory(ref) -> None:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", default=os.environ.get("MLXZ_REFERENCE"),
+                    help="path of the reference checkout (default: $MLXZ_REFERENCE)")
     a = ap.parse_args()
+    if not a.ref:
+        ap.error("give the reference checkout with --ref or MLXZ_REFERENCE")
     install_shims()
     ref = load_reference(Path(a.ref))
     scenario_c1(ref)

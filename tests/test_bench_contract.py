@@ -37,5 +37,25 @@ def test_reference_arm_prefill_line():
 
 
 def test_reference_arm_decode_line():
-    d = _line("--steps", "3", "--warmup", "1")
+    d = _line("--steps", "3", "--warmup", "1", "--layers", "2")
     assert d["unit"] == "GB/s" and d["steps"] == 3 and d["warmup"] == 1
+    # every step is measured whole, on the GPU arm's own config
+    assert d["config"]["layers"] == 2 and d["config"]["global_batch"] == 64
+    assert d["config"]["parallelism"] == "1 GPU"
+    assert "measured whole" in d["cpu_baseline"]["sample"]
+
+
+def test_reference_arm_config_matches_gpu_arm():
+    """The reference arm's config is the GPU arm's (Workload.config), so the
+    two lines describe the same workload."""
+    sys.path.insert(0, str(ROOT))
+    import bench
+
+    for world in (1, 2, 8):
+        w = bench.Workload(False, world, 32, 120.0, 0, True)
+        assert w.B == 64 * world and w.hkv == 8 // world and w.nl == 32
+        assert w.kv_layer_rank * world == w.kv_step_total / 32
+    w5 = bench.Workload(True, 8, None, 120.0, 0, True)
+    assert w5.B == 256 and w5.hkv == 1 and w5.hq == 8 and w5.nl == 80
+    w1 = bench.Workload(True, 1, None, 120.0, 0, True)
+    assert 1 <= w1.nl < 80  # 80 layers of the 70B shape do not fit one GPU

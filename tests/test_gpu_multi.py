@@ -1,7 +1,9 @@
 """Head-sharded decode on 2 GPUs (one process each, NCCL process group):
-the all-gather fused into the decode launch over peer memory (PeerAllGather)
-against the NCCL all-gather of the ordinary launch's output (HeadAllGather),
-bit for bit, over several layers and steps.  Skipped with fewer than 2 GPUs."""
+the all-gather fused into the decode launch over peer memory (PeerAllGather),
+waited for after every layer and chained (each launch waiting for the layer
+before it), against the NCCL all-gather of the ordinary launch's output
+(HeadAllGather), bit for bit, over several layers and steps.  Skipped with
+fewer than 2 GPUs."""
 import os
 import socket
 
@@ -78,11 +80,27 @@ def _rank(rank: int, world: int, port: int, results) -> None:
             for l in range(L):
                 got[t, l].copy_(peer.layer(step_b, l, qd[t, l], kd[t, l], vd[t, l], slot=l))
             step_b.advance()
+        # chained: each layer's launch waits in its prologue for the peers'
+        # rows of the layer before it; one wait launch after the last layer
+        step_c = make_step()
+        chain = PeerAllGather(sh, B, D, torch.bfloat16, dev, n_slots=2 * L)
+        got_c = torch.empty_like(want)
+        for t in range(2):
+            base = L * (t % 2)
+            for l in range(L):
+                chain.launch(step_c, l, qd[t, l], kd[t, l], vd[t, l], slot=base + l,
+                             wait_previous=l > 0)
+            chain.wait()
+            for l in range(L):
+                got_c[t, l].copy_(chain.full[base + l])
+            step_c.advance()
         torch.cuda.synchronize()
         ops.check_device_errors(rank)
-        same_pools = torch.equal(step_a.store.pools, step_b.store.pools)
+        same_pools = (torch.equal(step_a.store.pools, step_b.store.pools)
+                      and torch.equal(step_a.store.pools, step_c.store.pools))
         peer.close()
-        results[rank] = (bool(torch.equal(got, want)), same_pools,
+        chain.close()
+        results[rank] = (bool(torch.equal(got, want) and torch.equal(got_c, want)), same_pools,
                          float((got.float() - want.float()).abs().max()), peer.epoch)
     finally:
         dist.destroy_process_group()

@@ -95,6 +95,94 @@ def test_emulated_ranks_gather_bit_exact(cuda, N, nw):
     assert attn_err(bufs[0], ref) <= ATOL_REL
 
 
+@pytest.mark.parametrize("N", [2, 8])
+def test_emulated_ranks_chained_waits(cuda, N):
+    """Layers chained with MZ_LAUNCH_WAIT_PREVIOUS: each launch waits inside
+    its prologue for the peers' rows of the launch before it, and only the
+    last layer is followed by mz_peer_wait.  Launches go on one stream in
+    (layer, rank) order without overlap, so every word a launch waits for was
+    published by a kernel that completed before it began."""
+    B, Hkv, G, D, bs, L = 6, 8, 4, 128, 16, 3
+    Hq = Hkv * G
+    lengths = [1, 17, 300, 2049, 64, 777]
+    case = random_paged_case(93, B, Hkv, D, bs, lengths, "bf16", G=G)
+    kp, vp = to_dev(case["kp"], "bf16", cuda), to_dev(case["vp"], "bf16", cuda)
+    nk = to_dev(rng.normal(94, (B, Hkv, D), "bf16", stream=1), "bf16", cuda)
+    nv = to_dev(rng.normal(94, (B, Hkv, D), "bf16", stream=2), "bf16", cuda)
+    qs = [to_dev(rng.normal(95, (B, Hq, D), "bf16", stream=l), "bf16", cuda) for l in range(L)]
+    tables = torch.from_numpy(case["tables"]).to(cuda)
+    lens = torch.tensor(lengths, dtype=torch.int32, device=cuda)
+    hk, hq = Hkv // N, Hq // N
+    shards = []
+    for r in range(N):
+        sl = slice(r * hk, (r + 1) * hk)
+        shards.append((kp[:, sl].contiguous(), vp[:, sl].contiguous(), nk[:, sl].contiguous(),
+                       nv[:, sl].contiguous()))
+    want = []
+    for l in range(L):
+        parts = [ops.paged_append_decode(qs[l][:, r * hq:(r + 1) * hq].contiguous(),
+                                         kr.clone(), vr.clone(), nkr, nvr, tables, lens)
+                 for r, (kr, vr, nkr, nvr) in enumerate(shards)]
+        want.append(torch.cat(parts, dim=1))
+    bufs = [torch.full((L, B, Hq, D), float("nan"), dtype=torch.bfloat16, device=cuda)
+            for _ in range(N)]
+    sigs = [torch.zeros(N, dtype=torch.int32, device=cuda) for _ in range(N)]
+    arr = [torch.zeros(1, dtype=torch.int32, device=cuda) for _ in range(N)]
+    for l in range(L):
+        epoch = l + 1
+        for r, (kr, vr, nkr, nvr) in enumerate(shards):
+            pe = nat.PeerOutputs()
+            pe.n_ranks, pe.rank = N, r
+            for s in range(N):
+                pe.out[s] = bufs[s][l].data_ptr() + r * hq * D * 2
+                pe.signal[s] = sigs[s].data_ptr()
+            pe.arrivals = arr[r].data_ptr()
+            pe.epoch = epoch
+            ops.paged_append_decode_allgather(pe, qs[l][:, r * hq:(r + 1) * hq].contiguous(), kr,
+                                              vr, nkr, nvr, tables, lens, Hq * D, D,
+                                              torch.bfloat16, wait_previous=l > 0)
+    for r in range(N):
+        ops.peer_wait(sigs[r], N, r, L, timeout_s=2.0)
+    torch.cuda.synchronize()
+    ops.check_device_errors(0)
+    for r in range(N):
+        assert sigs[r].tolist() == [0 if s == r else L for s in range(N)]
+        for l in range(L):
+            assert torch.equal(bufs[r][l], want[l]), (r, l)
+
+
+def test_chained_wait_times_out_and_context_survives(cuda):
+    """A launch whose folded wait never sees its peer's word gives up after
+    the bound, reports MZ_DEVERR_TIMEOUT and still completes its own work."""
+    B, Hkv, G, D, bs = 2, 2, 2, 64, 16
+    case = random_paged_case(7, B, Hkv, D, bs, [5, 40], "bf16", G=G)
+    kp, vp = to_dev(case["kp"], "bf16", cuda), to_dev(case["vp"], "bf16", cuda)
+    q = to_dev(case["q"][:, 0], "bf16", cuda)
+    nk = torch.zeros(B, Hkv, D, dtype=torch.bfloat16, device=cuda)
+    tables = torch.from_numpy(case["tables"]).to(cuda)
+    lens = torch.tensor([5, 40], dtype=torch.int32, device=cuda)
+    buf = torch.zeros(B, Hkv * G, D, dtype=torch.bfloat16, device=cuda)
+    sig = torch.zeros(2, dtype=torch.int32, device=cuda)
+    arr = torch.zeros(1, dtype=torch.int32, device=cuda)
+    pe = nat.PeerOutputs()
+    pe.n_ranks, pe.rank, pe.epoch = 2, 0, 5  # waits for word 1 to reach 4: never set
+    pe.out[0] = buf.data_ptr()
+    pe.out[1] = buf.data_ptr()  # the "peer" is this buffer too: nothing else is touched
+    pe.signal[0] = sig.data_ptr()
+    pe.signal[1] = sig.data_ptr()
+    pe.arrivals = arr.data_ptr()
+    want = ops.paged_append_decode(q, kp.clone(), vp.clone(), nk, nk, tables, lens)
+    ops.paged_append_decode_allgather(pe, q, kp, vp, nk, nk, tables, lens, Hkv * G * D, D,
+                                      torch.bfloat16, wait_previous=True)
+    torch.cuda.synchronize()
+    with pytest.raises(nat.DeviceError) as e:
+        ops.check_device_errors(0)
+    assert e.value.bits & nat.MZ_DEVERR_TIMEOUT
+    assert torch.equal(buf, want)
+    assert sig.tolist() == [5, 0]  # its own launch still signalled the "peer"
+    assert arr.item() == 0
+
+
 def test_peer_wait_times_out_and_context_survives(cuda):
     sig = torch.zeros(2, dtype=torch.int32, device=cuda)
     ops.peer_wait(sig, 2, 0, 7, timeout_s=0.002)  # word 1 is never set

@@ -173,3 +173,38 @@ def test_paged_decode_q_multi_query_and_paged_append(cuda):
     torch.cuda.synchronize()
     ops.check_device_errors(0)
     assert attn_err(out, _oracle_decode(case, dtype)) <= 2e-3
+
+
+@pytest.mark.parametrize("bits", [8, 4])
+def test_paged_decode_q_reads_any_affine_codes(cuda, bits):
+    """The dequant-fused decode depends only on w = scale * q + bias, not on
+    how a quantiser chose the pair: groups with negative scales and a group
+    edge as the bias (the form another quantiser may write) decode like the
+    oracle's dequantisation of the same codes."""
+    ctx, Hkv, D, G, dtype = [700, 33, 2049, 1], 4, 128, 4, "bf16"
+    case = _quant_case(77 + bits, ctx, Hkv, D, bits, dtype, G=G)
+    g = np.random.default_rng(bits)
+    top = 2 ** bits - 1
+    host = list(case["host"])
+    for base in (0, 3):
+        shape = host[base + 1].shape
+        mag = (np.abs(g.standard_normal(shape)) * 3.0 + 0.5) / top
+        neg = g.random(shape) < 0.5
+        scale = np.where(neg, -mag, mag).astype(np.float16)
+        # bias: the group's max when the scale is negative (w = bias at q = 0
+        # and falls as q grows), its min otherwise
+        edge = np.where(neg, 1.0, -1.0) * np.abs(g.standard_normal(shape)) * 2.0
+        host[base + 1] = scale.view(np.uint16)
+        host[base + 2] = edge.astype(np.float16).view(np.uint16)
+        host[base] = g.integers(0, 2 ** 32, size=host[base].shape, dtype=np.uint64
+                                ).astype(np.uint32)
+    case["host"] = tuple(host)
+    case["kdeq"] = oq.dequantize(host[0], host[1], host[2], bits, D)
+    case["vdeq"] = oq.dequantize(host[3], host[4], host[5], bits, D)
+    pools = _dev_pools(case["host"], cuda)
+    q = to_dev(case["q"][:, 0], dtype, cuda)
+    out = ops.paged_decode_q(q, pools, torch.from_numpy(case["tables"]).to(cuda),
+                             torch.from_numpy(case["ctx"]).to(cuda), out_dtype=torch.float32)
+    torch.cuda.synchronize()
+    ops.check_device_errors(0)
+    assert attn_err(out, _oracle_decode(case, dtype)[:, 0]) <= 2e-3

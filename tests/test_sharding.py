@@ -96,3 +96,66 @@ def test_gloo_world2_head_sharded_gather():
     assert sorted(got) == [0, 1]
     for r, (e_full, e_out) in got.items():
         assert e_full <= 1e-12 and e_out <= 1e-12, (r, e_full, e_out)
+
+
+class _FakeStep:
+    """Just what PeerAllGather.launch reads from a PagedDecodeStep."""
+
+    class store:  # noqa: N801
+        @staticmethod
+        def k_pool(l):
+            return None
+
+        v_pool = k_pool
+
+    tables = lengths = workspace = None
+    scale = 1.0
+
+
+def _peer_world1(monkeypatch, n_slots):
+    """A world-size-1 PeerAllGather on the CPU with the kernel launches
+    recorded instead of run (the slot and ordering rules are host logic)."""
+    from mlxz_b200 import ops
+    from mlxz_b200.engine.sharding import PeerAllGather
+
+    calls = []
+    monkeypatch.setattr(ops, "paged_append_decode_allgather",
+                        lambda pe, *a, **k: calls.append((pe.epoch, k["wait_previous"])))
+    monkeypatch.setattr(ops, "peer_wait", lambda *a, **k: calls.append("wait"))
+    pg = PeerAllGather(HeadShard(0, 1, 8, 32), 2, 16, torch.bfloat16, "cpu", n_slots=n_slots)
+    return pg, calls
+
+
+def test_peer_gather_slot_rules(monkeypatch):
+    st = _FakeStep()
+    pg, calls = _peer_world1(monkeypatch, 3)
+    # launch + wait per layer: only the previous launch's slot is off limits
+    pg.layer(st, 0, None, None, None, slot=0)
+    with pytest.raises(ValueError):
+        pg.layer(st, 1, None, None, None, slot=0)
+    pg.layer(st, 1, None, None, None, slot=1)
+    pg.layer(st, 2, None, None, None, slot=0)
+    # chained launches: the launch after a wait_previous launch may not reuse
+    # the slot that launch completed
+    pg.launch(st, 0, None, None, None, slot=1)
+    pg.launch(st, 1, None, None, None, slot=2, wait_previous=True)
+    with pytest.raises(ValueError):
+        pg.launch(st, 2, None, None, None, slot=1, wait_previous=True)
+    pg.launch(st, 2, None, None, None, slot=0, wait_previous=True)
+    # a plain launch while the last one was neither waited for nor chained
+    with pytest.raises(RuntimeError):
+        pg.launch(st, 3, None, None, None, slot=1)
+    pg.wait()
+    pg.launch(st, 3, None, None, None, slot=1)
+    with pytest.raises(ValueError):
+        pg.launch(st, 4, None, None, None, slot=3, wait_previous=True)
+    epochs = [c[0] for c in calls if c != "wait"]
+    assert epochs == list(range(1, len(epochs) + 1))
+    assert [c[1] for c in calls if c != "wait"] == [False] * 3 + [False, True, True, False]
+
+
+def test_peer_gather_needs_two_slots():
+    from mlxz_b200.engine.sharding import PeerAllGather
+
+    with pytest.raises(ValueError):
+        PeerAllGather(HeadShard(0, 1, 8, 32), 2, 16, torch.bfloat16, "cpu", n_slots=1)
