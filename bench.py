@@ -61,16 +61,18 @@ def parse_args():
                     help="append with mz_kv_append_paged, then mz_paged_decode (two launches)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-sub-records", action="store_true",
-                    help="decode: skip the sharded70b sub-record measured after the headline")
+                    help="decode: skip the sub-records measured after the headline (sharded70b "
+                         "at every N; prefix, quant8 and quant4 at N = 1)")
     ap.add_argument("--batch-invariant", action="store_true",
                     help="decode: MZ_DECODE_BATCH_INVARIANT (whole pairs, batch-independent bytes)")
     ap.add_argument("--config", default="decode",
-                    choices=["decode", "prefix", "quant", "sharded70b", "prefill"],
+                    choices=["decode", "prefix", "quant", "sharded70b", "prefill", "kernels"],
                     help="decode: the paged decode step (headline); prefix: prefix-cache "
                          "restore / copy-on-write / host-tier eviction and reload; quant: "
                          "4/8-bit quantised KV decode step; sharded70b: 70B-shape decode "
                          "step head-sharded over the ranks (strong scaling); prefill: one "
-                         "chunked-prefill iteration (append + causal attention per layer)")
+                         "chunked-prefill iteration (append + causal attention per layer); "
+                         "kernels: each data-movement kernel timed alone")
     ap.add_argument("--bits", type=int, default=8, choices=[4, 8])
     ap.add_argument("--gather", default="p2p", choices=["p2p", "nccl"],
                     help="N > 1: p2p = output rows stored into every rank's buffer by the "
@@ -892,6 +894,15 @@ def run_gpu(args, rank: int, world: int, local_rank: int) -> None:
                          "alg_bytes_per_launch": w5.decode_alg_bytes},
             "gpu_launches": r5["launches"], "clocks": r5["clocks"],
         }
+    extra = {}
+    if world == 1 and not c5 and not args.no_sub_records:
+        # the single-GPU workloads of the other configs, measured in the same
+        # run: prefix-cache restore / copy-on-write / host-tier eviction (C3)
+        # and the quantised decode step at 8 and 4 bits (C4)
+        extra["prefix"] = run_prefix(args, local_rank)
+        torch.cuda.empty_cache()
+        extra["quant8"] = run_quant(args, local_rank, bits=8)
+        extra["quant4"] = run_quant(args, local_rank, bits=4)
     if rank == 0:
         peak, peak_kind = peaks()
         cpu = None
@@ -937,12 +948,13 @@ def run_gpu(args, rank: int, world: int, local_rank: int) -> None:
         }
         if sub is not None:
             result["sharded70b"] = sub
+        result.update(extra)
         print(json.dumps(result), flush=True)
     if world > 1:
         dist.destroy_process_group()
 
 
-def run_prefix(args, local_rank: int) -> None:
+def run_prefix(args, local_rank: int) -> dict:
     """Prefix-cache workload, 8B KV shape (32 layers, 8 KV heads, head_dim 128,
     bf16, block 16): a 2048-token shared prefix cached once; 32 requests
     restore it (zero-copy) and write a U[64, 512]-token suffix; each request's
@@ -1105,10 +1117,10 @@ def run_prefix(args, local_rank: int) -> None:
         "host_link": {"h2d_gbs": round(h2d_peak, 2), "d2h_gbs": round(d2h_peak, 2)},
         "stats": cache.stats().__repr__(),
     }
-    print(json.dumps(line), flush=True)
+    return line
 
 
-def run_quant(args, local_rank: int) -> None:
+def run_quant(args, local_rank: int, bits: int | None = None) -> dict:
     """Quantised KV decode step, Llama-3.1-8B shape: 32 layers, 32 q heads, 8 KV
     heads, head_dim 128, batch 32, ctx ~ U[4096, 16384], affine group-64
     codes at `--bits`, fp16 scales and biases.  Pools are filled by quantising
@@ -1123,7 +1135,8 @@ def run_quant(args, local_rank: int) -> None:
 
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
-    nl, B, bits = args.layers, 32, args.bits
+    nl, B = args.layers, 32
+    bits = args.bits if bits is None else bits
     ctx = np.random.default_rng(args.seed).integers(4096, 16385, size=B).astype(np.int64)
     need = (ctx + 1 + BS - 1) // BS
     n_blocks = int(math.ceil(need.sum() * 1.1))
@@ -1212,7 +1225,122 @@ def run_quant(args, local_rank: int) -> None:
         "gpu_launches": steps * nl * 2,
         "clocks": clk,
     }
-    print(json.dumps(line), flush=True)
+    del store, step, q, kn, vn, out
+    torch.cuda.empty_cache()
+    return line
+
+
+def run_kernels(args, local_rank: int) -> dict:
+    """Each data-movement kernel of the path timed alone (CUDA events around
+    `--steps` launches after `--warmup`), 8B KV shape (8 KV heads, head_dim
+    128, bf16, block 16), against its algorithmic bytes:
+      append_slots   mz_kv_append: 8192 prompt tokens to random slots
+      append_paged   mz_kv_append_paged: one token for each of 64 sequences
+      gather         mz_kv_gather: 16 sequences x 8192 tokens to contiguous KV
+      block_copy     mz_block_copy: 2048 blocks x 2 --layers pools (K and V)
+      block_pack     mz_block_pack: 2048 blocks into a staging buffer
+      block_unpack   mz_block_unpack: the staging buffer back into the pools
+      quant_append8/4  mz_kv_quant_append: 8192 tokens, 8 / 4 bits
+      dequant8/4     mz_kv_dequant_blocks: 4096 blocks to bf16
+    Inputs are far above L2 (126 MB) except the two appends, whose sizes are
+    what the decode and prefill steps write."""
+    import numpy as np
+    import torch
+
+    from mlxz_b200 import ops
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    torch.manual_seed(args.seed)
+    H, Dh, bs = HKV, D, BS
+    reps, warm = max(1, args.steps), max(1, args.warmup)
+    peak, peak_kind = peaks()
+    res = {}
+
+    def timed(name, fn, alg_bytes):
+        for _ in range(warm):
+            fn()
+        a, z = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(reps):
+            fn()
+        z.record()
+        torch.cuda.synchronize()
+        ops.check_device_errors(local_rank)
+        ms = a.elapsed_time(z) / reps
+        gbs = alg_bytes / (ms / 1e3) / 1e9
+        res[name] = {"ms": round(ms, 5), "alg_bytes": int(alg_bytes), "gbs": round(gbs, 1),
+                     "frac": round(gbs / peak, 4)}
+
+    row = H * Dh * 2  # bytes of one token's K (or V) in one layer
+    # appends
+    n_blocks = 4096
+    kp = torch.randn(n_blocks, H, bs, Dh, device=dev).to(torch.bfloat16)
+    vp = torch.randn_like(kp)
+    n = 8192
+    k = torch.randn(1, H, n, Dh, device=dev).to(torch.bfloat16)
+    v = torch.randn_like(k)
+    slots = torch.randperm(n_blocks * bs, device=dev)[:n].to(torch.int64)
+    timed("append_slots", lambda: ops.kv_append(kp, vp, k, v, slots), 2 * 2 * n * row)
+    B = 64
+    perm = torch.randperm(n_blocks, device=dev).to(torch.int32)
+    tables = perm[: B * 32].view(B, 32).contiguous()
+    pos = torch.randint(0, 32 * bs, (B,), device=dev, dtype=torch.int32)
+    kb = torch.randn(B, H, Dh, device=dev).to(torch.bfloat16)
+    vb = torch.randn_like(kb)
+    timed("append_paged", lambda: ops.kv_append_paged(kp, vp, kb, vb, tables, pos), 2 * 2 * B * row)
+    # gather: 16 sequences x 8192 tokens
+    nb_seq, G16 = 512, 16
+    gk = torch.randn(G16 * nb_seq + 8, H, bs, Dh, device=dev).to(torch.bfloat16)
+    gv = torch.randn_like(gk)
+    gt = torch.randperm(G16 * nb_seq, device=dev).to(torch.int32).view(G16, nb_seq).contiguous()
+    gl = [nb_seq * bs] * G16
+    gld = torch.tensor(gl, dtype=torch.int32, device=dev)
+    timed("gather", lambda: ops.kv_gather(gk, gv, gt, gld, gl), 2 * 2 * sum(gl) * row)
+    del kp, vp, k, v, gk, gv
+    torch.cuda.empty_cache()
+    # block moves over the pools of `--layers` layers (K and V of each)
+    P, NB = 2 * args.layers, 4608
+    pools = torch.empty((P, NB, H, bs, Dh), dtype=torch.bfloat16, device=dev)
+    pools.view(torch.int16).random_(-30000, 30000)
+    nmove = 2048
+    ids = torch.randperm(NB, device=dev).to(torch.int32)
+    src, dst = ids[:nmove].contiguous(), ids[nmove:2 * nmove].contiguous()
+    bb = H * bs * Dh * 2
+    timed("block_copy", lambda: ops.block_copy(pools, src, dst), 2 * nmove * P * bb)
+    staging = torch.empty((nmove, P, bb), dtype=torch.uint8, device=dev)
+    timed("block_pack", lambda: ops.block_pack(pools, src, staging), 2 * nmove * P * bb)
+    timed("block_unpack", lambda: ops.block_unpack(pools, dst, staging), 2 * nmove * P * bb)
+    del pools, staging
+    torch.cuda.empty_cache()
+    # quantised appends and dequantisation
+    for bits in (8, 4):
+        NQ = 8192
+        w = Dh * bits // 32
+        qp = (torch.zeros(NQ, H, bs, w, dtype=torch.int32, device=dev),
+              torch.zeros(NQ, H, bs, 2, dtype=torch.float16, device=dev),
+              torch.zeros(NQ, H, bs, 2, dtype=torch.float16, device=dev),
+              torch.zeros(NQ, H, bs, w, dtype=torch.int32, device=dev),
+              torch.zeros(NQ, H, bs, 2, dtype=torch.float16, device=dev),
+              torch.zeros(NQ, H, bs, 2, dtype=torch.float16, device=dev))
+        k = torch.randn(1, H, n, Dh, device=dev).to(torch.bfloat16)
+        v = torch.randn_like(k)
+        sl = torch.randperm(NQ * bs, device=dev)[:n].to(torch.int64)
+        qrow = H * (Dh * bits // 8 + 2 * 2 * 2)  # codes + scales + biases of one token's K
+        timed(f"quant_append{bits}", lambda: ops.kv_quant_append(qp, k, v, sl),
+              2 * n * row + 2 * n * qrow)
+        ndq = 4096
+        dids = torch.randperm(NQ, device=dev)[:ndq].to(torch.int32)
+        ko = torch.empty(ndq, H, bs, Dh, dtype=torch.bfloat16, device=dev)
+        vo = torch.empty_like(ko)
+        timed(f"dequant{bits}", lambda: ops.kv_dequant_blocks(qp, dids, ko, vo),
+              2 * ndq * bs * qrow + 2 * ndq * bs * row)
+        del qp, k, v, ko, vo
+        torch.cuda.empty_cache()
+    return {"metric": "per-kernel achieved GB/s of the path's data-movement kernels, 8B KV shape",
+            "unit": "GB/s", "steps": reps, "warmup": warm, "peak": peak, "peak_kind": peak_kind,
+            "data": "synthetic (seeded N(0,1) bf16)", "kernels": res}
+
 
 
 def main():
@@ -1229,13 +1357,16 @@ def main():
         run_reference(args, rank, world)
     elif args.config == "prefix":
         if rank == 0:
-            run_prefix(args, local_rank)
+            print(json.dumps(run_prefix(args, local_rank)), flush=True)
     elif args.config == "quant":
         if rank == 0:
-            run_quant(args, local_rank)
+            print(json.dumps(run_quant(args, local_rank)), flush=True)
     elif args.config == "prefill":
         if rank == 0:
             run_prefill(args, local_rank)
+    elif args.config == "kernels":
+        if rank == 0:
+            print(json.dumps(run_kernels(args, local_rank)), flush=True)
     else:
         run_gpu(args, rank, world, local_rank)
 

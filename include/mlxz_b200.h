@@ -220,13 +220,14 @@ MZ_API int mz_paged_prefill(void *out, int32_t out_dtype, int64_t out_tok_stride
  * ahead writes none of this launch's pools, block tables or ctx_lens (e.g. it
  * is the previous layer's decode). */
 #define MZ_LAUNCH_OVERLAP_PREVIOUS 1u
-/* MZ_DECODE_BATCH_INVARIANT: every (sequence, KV head) pair is computed whole
- * by one warp in a fixed tile order (pairs handed out by ticket; no split, no
- * merge), so a sequence's output bytes do not depend on its position in the
- * batch or on the other sequences.  The batch-position determinism gate of the
+/* MZ_DECODE_BATCH_INVARIANT: every (sequence, KV head) pair is cut into
+ * pieces at fixed pair-relative boundaries (512 tokens), the pieces are
+ * handed out by ticket, and a pair's pieces are merged in piece order, so a
+ * sequence's output bytes do not depend on its position in the batch or on
+ * the other sequences.  The batch-position determinism gate of the
  * reference's plan (MLXZ_IMPLEMENTATION_PLAN.md:1058-1059: prefix-cache drift
- * < 1e-4, batch-position determinism bytewise).  Slower when the pairs are
- * fewer than the launch's warps or very uneven. */
+ * < 1e-4, batch-position determinism bytewise).  Its workspace depends on the
+ * table width: size it with mz_paged_decode_workspace_size_ex. */
 #define MZ_DECODE_BATCH_INVARIANT 2u
 /* MZ_LAUNCH_WAIT_PREVIOUS (mz_paged_append_decode_allgather only): the launch
  * itself first waits, bounded like mz_peer_wait, until every peer's signal
@@ -238,6 +239,17 @@ MZ_API int mz_paged_prefill(void *out, int32_t out_dtype, int64_t out_tok_stride
  * drains.  Work queued after the launch then sees the previous launch's
  * gathered buffer complete. */
 #define MZ_LAUNCH_WAIT_PREVIOUS 4u
+
+/* Workspace bytes of a decode launch with these flags (MZ_LAUNCH_*,
+ * MZ_DECODE_BATCH_INVARIANT): mz_paged_decode_workspace_size, plus, for a
+ * batch-invariant launch, room for the partials of every piece the widest
+ * tables (max_blocks_per_seq blocks of block_size tokens) can cut.  No
+ * counterpart in the reference (MLX manages its own scratch). */
+MZ_API int mz_paged_decode_workspace_size_ex(int32_t n_seqs, int32_t n_kv_heads,
+                                             int32_t rows_per_kv_head, int32_t head_dim,
+                                             int32_t num_warps, int32_t max_blocks_per_seq,
+                                             int32_t block_size, uint32_t flags, int32_t device,
+                                             size_t *bytes);
 
 /* mz_paged_append_decode with launch flags (MZ_LAUNCH_*).  Same reference
  * counterpart and rules as mz_paged_append_decode. */

@@ -97,6 +97,8 @@ _SIGNATURES: dict[str, list] = {
                      _i64, _i32, _vp, _vp],
     "mz_paged_decode_workspace_size": [_i32, _i32, _i32, _i32, _i32, _i32,
                                        ctypes.POINTER(_sz)],
+    "mz_paged_decode_workspace_size_ex": [_i32, _i32, _i32, _i32, _i32, _i32, _i32,
+                                          ctypes.c_uint32, _i32, ctypes.POINTER(_sz)],
     "mz_paged_decode": [_vp, _i32, _i64, _i64, _i64, _vp, _i64, _i64, _i64, _i32, _vp, _vp,
                         _vp, _i32, _vp, _i32, _i32, _i32, _i32, _i32, _i64, _f32, _i32, _i32,
                         _vp, _sz, _vp, _vp],

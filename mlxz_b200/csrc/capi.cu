@@ -60,7 +60,7 @@ int sm_count(int device) {
 
 }  // namespace mz
 
-extern "C" int mz_abi_version(void) { return 5; }
+extern "C" int mz_abi_version(void) { return 6; }
 
 extern "C" int mz_last_error(char *buf, size_t len) {
   if (buf && len) {

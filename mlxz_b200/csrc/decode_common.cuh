@@ -37,6 +37,11 @@ constexpr int kTileTok = 16;        // tokens per tile
 constexpr int kUnitQ = 8;           // per-warp ring of unit descriptors
 constexpr uint64_t kTimeoutNs = 2000000000ull;  // 2 s bound on any single wait
 constexpr int kMaxDynPieces = 64;  // dynamic chunks cut a pair into at most this many pieces
+// Batch-invariant schedule: every pair is cut at the same pair-relative tile
+// boundaries, one piece per kBiPieceTiles tiles (512 tokens), whatever else is
+// in the batch; pieces go out by ticket and a pair's partials are merged in
+// piece order, so its bytes depend only on its own data.
+constexpr int kBiPieceTiles = 32;
 
 struct Params {
   void *out;
@@ -73,7 +78,7 @@ struct Params {
   // GPU's address space); once all blocks have stored, the last one publishes
   // `epoch` into each peer_sig[r] (rank r's signal word for this rank).
   int overlap_prev = 0;  // launched as a programmatic dependent of the kernel ahead
-  int batch_invariant = 0;  // whole pairs by ticket: a pair's bytes do not depend on the batch
+  int batch_invariant = 0;  // fixed pair-relative pieces: a pair's bytes do not depend on the batch
   int n_peer = 0;
   void *peer_out[MZ_MAX_RANKS - 1] = {};
   uint32_t *peer_sig[MZ_MAX_RANKS - 1] = {};
@@ -92,9 +97,10 @@ struct Cursor {
   int pos;
 };
 
-// A unit descriptor (32 bytes), passed from the producer to the consumer.
+// A unit descriptor, passed from the producer to the consumer.  fp / np: the
+// pair's first piece and piece count (batch-invariant schedule only).
 struct Unit {
-  int start, end, u, b, h, t, n, ctx;
+  int start, end, u, b, h, t, n, ctx, fp, np;
 };
 
 __device__ __forceinline__ int ntiles_of(int ctx) { return (ctx + kTileTok - 1) / kTileTok; }
@@ -323,13 +329,19 @@ struct Sched {
     p_left = pushed = issued = 0;
     p_done = static_taken = false;
     if (p.batch_invariant) {
-      // every (sequence, KV head) pair is one unit, taken whole by ticket in
-      // pair order: no pair is ever split, so no merge, and the arithmetic of
-      // a pair is the same whatever else is in the batch
+      // every (sequence, KV head) pair is cut into pieces of kBiPieceTiles
+      // tiles at fixed pair-relative boundaries, taken by ticket in pair and
+      // piece order; the arithmetic of a pair is the same whatever else is in
+      // the batch
+      int pc = 0;
+      for (int b = lane; b < p.B; b += 32)
+        pc += (ntiles_of(clamped_ctx(p, b)) + kBiPieceTiles - 1) / kBiPieceTiles;
+#pragma unroll
+      for (int o = 16; o; o >>= 1) pc += __shfl_xor_sync(0xffffffffu, pc, o);
       per_s = 0;
       t_s = 0;
-      chunk = 1 << 30;  // unit_of() is the same for every tile
-      n_chunks = p.B * p.Hkv;
+      chunk = 1 << 30;
+      n_chunks = pc * p.Hkv;
       return true;
     }
     // static share: ceil(T * pct / 100 / W) tiles per warp (the last shares
@@ -361,7 +373,7 @@ struct Sched {
   }
 
   __device__ bool next_unit(const Params &p) {
-    int start = 0, end = 0, u = 0;
+    int start = 0, end = 0, u = 0, fp = 0, np = 1;
     bool ok = false;
     if (!static_taken) {
       static_taken = true;
@@ -388,17 +400,44 @@ struct Sched {
         return false;
       }
       if (p.batch_invariant) {
-        // pair tk = (b, h): tiles [base_b + h n_b, base_b + (h + 1) n_b) of the
-        // flat list, base_b = Hkv * (tiles of the sequences before b)
-        const int b = tk / p.Hkv, h = tk - (tk / p.Hkv) * p.Hkv;
-        const int n = ntiles_of(clamped_ctx(p, b));
-        if (n == 0) continue;  // empty pair: its zeros are written elsewhere
-        int before = 0;
-        for (int bb = lane; bb < b; bb += 32) before += ntiles_of(clamped_ctx(p, bb));
+        // piece tk: sequence b found by a scan over the sequences' piece
+        // counts (Hkv * ceil(n_b / C) each; empty sequences have none), then
+        // head h and piece j of pair (b, h), whose tiles start at flat index
+        // Hkv * (tiles of the sequences before b) + h * n_b
+        int pbase = 0, tbase = 0, bf = 0;
+        for (int b0 = 0; b0 < p.B; b0 += 32) {
+          const int b = b0 + lane;
+          const int n = (b < p.B) ? ntiles_of(clamped_ctx(p, b)) : 0;
+          const int pc = p.Hkv * ((n + kBiPieceTiles - 1) / kBiPieceTiles);
+          int ip = pc, it = n;
 #pragma unroll
-        for (int o = 16; o; o >>= 1) before += __shfl_xor_sync(0xffffffffu, before, o);
-        start = before * p.Hkv + h * n;
-        end = start + n;
+          for (int o = 1; o < 32; o <<= 1) {
+            const int y = __shfl_up_sync(0xffffffffu, ip, o);
+            const int z = __shfl_up_sync(0xffffffffu, it, o);
+            if (lane >= o) {
+              ip += y;
+              it += z;
+            }
+          }
+          const unsigned m = __ballot_sync(0xffffffffu, pbase + ip > tk);
+          if (m) {
+            const int L = __ffs(m) - 1;
+            pbase += __shfl_sync(0xffffffffu, ip - pc, L);
+            tbase += __shfl_sync(0xffffffffu, it - n, L);
+            bf = b0 + L;
+            break;
+          }
+          pbase += __shfl_sync(0xffffffffu, ip, 31);
+          tbase += __shfl_sync(0xffffffffu, it, 31);
+        }
+        const int n = ntiles_of(clamped_ctx(p, bf));
+        np = (n + kBiPieceTiles - 1) / kBiPieceTiles;
+        const int r = tk - pbase;
+        const int h = r / np, j = r - (r / np) * np;
+        const int first = tbase * p.Hkv + h * n;
+        start = first + j * kBiPieceTiles;
+        end = min(start + kBiPieceTiles, first + n);
+        fp = pbase + h * np;
       } else {
         start = t_s + tk * chunk;
         end = min(start + chunk, tot);
@@ -406,12 +445,13 @@ struct Sched {
       u = W + tk;
       ok = true;
     }
-    push_unit(p, start, end, u);
+    push_unit(p, start, end, u, fp, np);
     return true;
   }
 
   // Cursor at the unit's first tile; the unit descriptor goes to the ring.
-  __device__ __forceinline__ void push_unit(const Params &p, int start, int end, int u) {
+  __device__ __forceinline__ void push_unit(const Params &p, int start, int end, int u,
+                                            int fp = 0, int np = 1) {
     pc = locate(p, start, lane);
     if (lane == 0) {
       Unit un;
@@ -423,6 +463,8 @@ struct Sched {
       un.t = pc.t;
       un.n = pc.n;
       un.ctx = pc.ctx;
+      un.fp = fp;
+      un.np = np;
       uq[pushed % kUnitQ] = un;
     }
     ++pushed;
@@ -468,7 +510,7 @@ struct Sched {
 // Consumer side of the unit ring.
 struct UnitReader {
   Cursor cc;
-  int left = 0, unit = 0, popped = 0;
+  int left = 0, unit = 0, popped = 0, fp = 0, np = 1;
 
   __device__ __forceinline__ bool need_pop() const { return left == 0; }
   __device__ __forceinline__ void pop(const Unit *uq) {
@@ -483,6 +525,8 @@ struct UnitReader {
     cc.pos = un.start;
     left = un.end - un.start;
     unit = un.u;
+    fp = un.fp;
+    np = un.np;
   }
 };
 
@@ -735,10 +779,12 @@ inline size_t align256(size_t x) { return (x + 255) & ~static_cast<size_t>(255);
 
 // Workspace for W warps: per-pair counters + 2 scheduler words, then (m, l)
 // and O partials for W static units + max_chunks dynamic units + one extra
-// slot per pair (slot = unit + pair).
-inline WsLayout ws_layout(int64_t n_pairs, int64_t warps, int rows, int D) {
+// slot per pair (slot = unit + pair).  max_pieces: the most pieces a
+// batch-invariant launch can cut (0 for the default schedule).
+inline WsLayout ws_layout(int64_t n_pairs, int64_t warps, int rows, int D,
+                          int64_t max_pieces = 0) {
   WsLayout w;
-  w.max_chunks = static_cast<int>(2 * warps);
+  w.max_chunks = static_cast<int>(2 * warps > max_pieces ? 2 * warps : max_pieces);
   const int64_t slots = warps + w.max_chunks + n_pairs;
   w.counter_words = n_pairs + 2;
   w.counters = 0;

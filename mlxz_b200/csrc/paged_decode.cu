@@ -38,7 +38,7 @@ struct Cfg {
   static constexpr int kStageBytes = 2 * kTileBytes;         // K + V
   static constexpr int kSmemTiles = kWarps * kStages * kStageBytes;
   static constexpr int kSmemBars = kWarps * kStages * 8;
-  static constexpr int kSmemUnits = kWarps * kUnitQ * 32;
+  static constexpr int kSmemUnits = kWarps * kUnitQ * static_cast<int>(sizeof(Unit));
   static constexpr int kSmemDefer = kWarps * kMaxDeferred * static_cast<int>(sizeof(Deferred));
   static constexpr int kSmemBytes = kSmemTiles + kSmemBars + kSmemUnits + kSmemDefer + 1024;
 };
@@ -299,7 +299,10 @@ __device__ __forceinline__ void decode_tiles(const CUtensorMap &tmK, const CUten
       L1 += __shfl_xor_sync(0xffffffffu, L1, 2);
       const int bh = cc.b * p.Hkv + cc.h;
       const int pbh = cc.pos - cc.t;  // flat index of tile 0 of this pair
-      const int uf = sch.unit_of(pbh), ul = sch.unit_of(pbh + cc.n - 1);
+      // units holding the pair's first and last piece (batch-invariant: the
+      // pair's pieces are the consecutive units W + fp ...)
+      const int uf = p.batch_invariant ? sch.W + ur.fp : sch.unit_of(pbh);
+      const int ul = p.batch_invariant ? uf + ur.np - 1 : sch.unit_of(pbh + cc.n - 1);
       if (uf == ul) {
         const float i0 = 1.f / L0, i1 = two_groups ? 1.f / L1 : 0.f;
         if (g < p.rows) {
@@ -447,6 +450,12 @@ struct DecodeArgs {
   uint32_t flags = 0;                      // MZ_LAUNCH_*
 };
 
+// The most pieces a batch-invariant launch cuts: every pair at full capacity.
+inline int64_t bi_max_pieces(int64_t B, int64_t Hkv, int64_t max_blocks, int bs) {
+  const int64_t tiles = max_blocks * (bs / kTileTok);
+  return B * Hkv * ((tiles + kBiPieceTiles - 1) / kBiPieceTiles);
+}
+
 // Host-side checks shared by the entry points; fills the resolved warp count
 // and workspace layout.
 int validate(const DecodeArgs &a, const char *fn, int64_t *warps, WsLayout *ws) {
@@ -509,7 +518,8 @@ int validate(const DecodeArgs &a, const char *fn, int64_t *warps, WsLayout *ws) 
     return fail(MZ_ERR_UNSUPPORTED, "%s: more than 2^30 tiles of context", fn);
   const int device = current_device();
   if (int rc = resolve_warps(a.D, a.dtype == MZ_DTYPE_BF16, a.num_warps, device, warps)) return rc;
-  *ws = ws_layout((int64_t)a.B * a.Hkv, *warps, rows, a.D);
+  *ws = ws_layout((int64_t)a.B * a.Hkv, *warps, rows, a.D,
+                  (a.flags & MZ_DECODE_BATCH_INVARIANT) ? bi_max_pieces(a.B, a.Hkv, a.max_blocks, a.bs) : 0);
   return MZ_OK;
 }
 
@@ -679,6 +689,29 @@ extern "C" int mz_paged_decode_workspace_size(int32_t n_seqs, int32_t n_kv_heads
   if (device < 0) device = current_device();
   if (int rc = resolve_warps(head_dim, true, num_warps, device, &warps)) return rc;
   *bytes = ws_layout((int64_t)n_seqs * n_kv_heads, warps, rows_per_kv_head, head_dim).total;
+  return MZ_OK;
+}
+
+extern "C" int mz_paged_decode_workspace_size_ex(int32_t n_seqs, int32_t n_kv_heads,
+                                                 int32_t rows_per_kv_head, int32_t head_dim,
+                                                 int32_t num_warps, int32_t max_blocks_per_seq,
+                                                 int32_t block_size, uint32_t flags,
+                                                 int32_t device, size_t *bytes) {
+  if (!bytes) return fail(MZ_ERR_INVALID_ARG, "bytes is null");
+  if (n_seqs < 0 || n_kv_heads <= 0 || rows_per_kv_head <= 0 || rows_per_kv_head > 16 ||
+      max_blocks_per_seq <= 0 || block_size <= 0 || block_size % kTileTok)
+    return fail(MZ_ERR_INVALID_ARG, "workspace_size_ex: bad sizes");
+  if (head_dim != 64 && head_dim != 128)
+    return fail(MZ_ERR_UNSUPPORTED, "head_dim %d (supported: 64, 128)", head_dim);
+  if (flags & ~(MZ_LAUNCH_OVERLAP_PREVIOUS | MZ_DECODE_BATCH_INVARIANT | MZ_LAUNCH_WAIT_PREVIOUS))
+    return fail(MZ_ERR_INVALID_ARG, "workspace_size_ex: unknown flags");
+  int64_t warps = 0;
+  if (device < 0) device = current_device();
+  if (int rc = resolve_warps(head_dim, true, num_warps, device, &warps)) return rc;
+  const int64_t pieces = (flags & MZ_DECODE_BATCH_INVARIANT)
+                             ? bi_max_pieces(n_seqs, n_kv_heads, max_blocks_per_seq, block_size)
+                             : 0;
+  *bytes = ws_layout((int64_t)n_seqs * n_kv_heads, warps, rows_per_kv_head, head_dim, pieces).total;
   return MZ_OK;
 }
 

@@ -25,6 +25,8 @@
 //
 // Roofline: a tile moves 2 * 16 * (D * bits / 8 + 4 * D / 64) bytes; with
 // D = 128 that is 4352 B (8-bit) or 2304 B (4-bit), against 8192 B at bf16.
+#include <algorithm>
+
 #include "decode_common.cuh"
 
 namespace mz {
@@ -181,7 +183,7 @@ struct QCfg {
   static constexpr int kSmemCodes = kWarps * kStages * kCodeStage;
   static constexpr int kSmemScales = kWarps * kStages * kScaleStage;
   static constexpr int kSmemBars = kWarps * kStages * 8;
-  static constexpr int kSmemUnits = kWarps * kUnitQ * 32;
+  static constexpr int kSmemUnits = kWarps * kUnitQ * static_cast<int>(sizeof(Unit));
   static constexpr int kSmemDefer = kWarps * kMaxDeferred * static_cast<int>(sizeof(Deferred));
   static constexpr int kSmemBytes =
       kSmemCodes + kSmemScales + kSmemBars + kSmemUnits + kSmemDefer + 1024;
@@ -704,6 +706,14 @@ int check_q_shape(int D, int bits, int group, const char *fn) {
 }  // namespace decode
 }  // namespace mz
 
+namespace mz {
+namespace decode {
+// tcgen05 (kind::i8) form, quant_decode_tc.cu
+bool qtc_supports(int head_dim, int rows);
+int launch_decode_q_tc(const Params &p, int bits, int64_t rows_total, int grid, cudaStream_t s);
+}  // namespace decode
+}  // namespace mz
+
 using namespace mz;
 using namespace mz::decode;
 
@@ -888,10 +898,21 @@ extern "C" int mz_paged_decode_q(void *out, int32_t out_dtype, int64_t out_seq_s
   set_schedule(p, ws);
   p.err = dev_err;
 
+  const int64_t rows_total = n_blocks * n_kv_heads * block_size;
+  // The tensor-core form (head_dim 128; 1, 2, 4, 8 or 16 query rows per KV
+  // head) when MLXZ_B200_QDECODE_TC=1, else the mma.sync kernel.  Its grid is
+  // one CTA per SM, or fewer when num_warps caps the launch (its partials then
+  // fit the workspace sized for num_warps).
+  if (qtc_supports(head_dim, rows) && env_int("MLXZ_B200_QDECODE_TC", 0, 0, 1) == 1) {
+    const int sms = sm_count(device);
+    if (sms <= 0) return fail(MZ_ERR_CUDA, "%s: cannot query SM count of device %d", fn, device);
+    int grid = sms;
+    if (num_warps > 0) grid = static_cast<int>(std::min<int64_t>(sms, std::max<int64_t>(1, warps / kWarps)));
+    return launch_decode_q_tc(p, bits, rows_total, grid, static_cast<cudaStream_t>(stream));
+  }
   // 2-D maps over the code pools (rows of D * bits / 8 bytes), used by the
   // swizzled instantiations (128-byte rows); others take 1-D bulk copies.
   CUtensorMap tk{}, tv{};
-  const int64_t rows_total = n_blocks * n_kv_heads * block_size;
   const int rb = head_dim * bits / 8;
   if (rb == 128) {
     if (rows_total >= (int64_t(1) << 31))

@@ -26,6 +26,21 @@ __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t start, uint32_t lbo
          (static_cast<uint64_t>((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46) | (2ull << 61);
 }
 
+// Operand without swizzle (layout type 0), MN-major: 16-byte units along
+// M/N `sbo` apart, 8-row K groups (8 rows of 16 bytes) `lbo` apart.
+__device__ __forceinline__ uint64_t smem_desc_none(uint32_t start, uint32_t lbo, uint32_t sbo) {
+  return (static_cast<uint64_t>((start >> 4) & 0x3FFFu)) |
+         (static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16) |
+         (static_cast<uint64_t>((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46);
+}
+
+// kind::i8 instruction descriptor: s32 accumulate, A and B unsigned 8-bit
+// (format 0 for both), majors as given.
+__host__ __device__ constexpr uint32_t idesc_u8(int M, int N, bool a_mn_major, bool b_mn_major) {
+  return (2u << 4) | ((a_mn_major ? 1u : 0u) << 15) | ((b_mn_major ? 1u : 0u) << 16) |
+         (static_cast<uint32_t>(N >> 3) << 17) | (static_cast<uint32_t>(M >> 4) << 24);
+}
+
 // kind::f16 instruction descriptor: f32 accumulate, A/B both bf16 or both f16.
 __host__ __device__ constexpr uint32_t idesc_f16(bool bf16, int M, int N, bool b_mn_major) {
   return (1u << 4) | ((bf16 ? 1u : 0u) << 7) | ((bf16 ? 1u : 0u) << 10) |
@@ -93,6 +108,17 @@ __device__ __forceinline__ void mma_ts_elect(uint32_t d, uint32_t a, uint64_t b,
       "r"(a), "l"(b), "r"(idesc), "r"(accumulate)
       : "memory");
 }
+// Whole warp: one elected lane issues D[tmem] (+)= A[smem] * B[smem], kind::i8.
+__device__ __forceinline__ void mma_i8_elect(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc,
+                                             uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p, e;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d),
+      "l"(a), "l"(b), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
 __device__ __forceinline__ void commit_elect(uint32_t bar) {
   asm volatile(
       "{\n\t.reg .pred e;\n\t"
@@ -124,6 +150,17 @@ __device__ __forceinline__ void ld32(uint32_t taddr, uint32_t (&r)[32]) {
         "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
         "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
         "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr)
+      : "memory");
+}
+// Whole warp: 16 consecutive 32-bit columns of this thread's lane.
+__device__ __forceinline__ void ld16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, "
+      "%12, %13, %14, %15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15])
       : "r"(taddr)
       : "memory");
 }

@@ -192,7 +192,9 @@ class PagedDecodeStep:
         # launches of other sizes
         self.workspace = ops.decode_workspace(self.B, store.n_kv_heads, G, store.head_dim,
                                               dev.index if dev.index is not None else 0,
-                                              shared=False)
+                                              shared=False, batch_invariant=batch_invariant,
+                                              max_blocks=self.max_blocks,
+                                              block_size=store.block_size)
         self._dev_in = None
         self._graph = None
 

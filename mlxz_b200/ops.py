@@ -216,13 +216,24 @@ def kv_gather(k_pool: torch.Tensor, v_pool: torch.Tensor, block_tables: torch.Te
 # ---------------------------------------------------------------------------
 
 def decode_workspace(n_seqs: int, n_kv_heads: int, rows: int, head_dim: int, device: int,
-                     num_warps: int = 0, shared: bool = True) -> torch.Tensor:
+                     num_warps: int = 0, shared: bool = True, batch_invariant: bool = False,
+                     max_blocks: int = 0, block_size: int = 16) -> torch.Tensor:
     """A zero-initialised decode workspace for exactly these sizes: the one
-    kept for this layout (``shared``), or a new one the caller owns."""
+    kept for this layout (``shared``), or a new one the caller owns.  A
+    batch-invariant launch needs room for the pieces of tables ``max_blocks``
+    wide (of ``block_size``-token blocks)."""
     size = ctypes.c_size_t(0)
-    nat.call("mz_paged_decode_workspace_size", n_seqs, n_kv_heads, rows, head_dim, num_warps,
-             device, ctypes.byref(size))
-    key = (device, n_seqs, n_kv_heads, rows, head_dim, num_warps)
+    if batch_invariant:
+        if max_blocks <= 0:
+            raise ValueError("a batch-invariant workspace needs max_blocks")
+        nat.call("mz_paged_decode_workspace_size_ex", n_seqs, n_kv_heads, rows, head_dim,
+                 num_warps, max_blocks, block_size, nat.MZ_DECODE_BATCH_INVARIANT, device,
+                 ctypes.byref(size))
+    else:
+        nat.call("mz_paged_decode_workspace_size", n_seqs, n_kv_heads, rows, head_dim,
+                 num_warps, device, ctypes.byref(size))
+    key = (device, n_seqs, n_kv_heads, rows, head_dim, num_warps,
+           (max_blocks, block_size) if batch_invariant else None)
     return _layout_workspace(_workspaces, key, int(size.value), device, shared)
 
 
@@ -325,7 +336,9 @@ def paged_append_decode(q: torch.Tensor, k_pool: torch.Tensor, v_pool: torch.Ten
         return out
     dev = _dev_index(q)
     if workspace is None:
-        workspace = decode_workspace(B, Hkv, Hq // Hkv, D, dev, num_warps)
+        workspace = decode_workspace(B, Hkv, Hq // Hkv, D, dev, num_warps,
+                                     batch_invariant=batch_invariant,
+                                     max_blocks=block_tables.shape[1], block_size=bs)
     nat.call("mz_paged_append_decode_ex", out.data_ptr(), dtype_code(out_dtype), out.stride(0),
              out.stride(1), q.data_ptr(), q.stride(0), q.stride(1), k_pool.data_ptr(),
              v_pool.data_ptr(), k_new.data_ptr(), v_new.data_ptr(), k_new.stride(0),

@@ -48,7 +48,7 @@ def _bf16(t):
     return to_bits(t)
 
 
-def _decode_vs_oracle(cuda, ctx, Hkv, G, seed):
+def _decode_vs_oracle(cuda, ctx, Hkv, G, seed, invariant=False):
     """Fused append + decode of one layer; returns (worst error, pools ok)."""
     B = len(ctx)
     tables, n_blocks = _tables(ctx + 1, seed)
@@ -61,7 +61,7 @@ def _decode_vs_oracle(cuda, ctx, Hkv, G, seed):
     lens = torch.from_numpy((ctx + 1).astype(np.int32)).to(cuda)
     kp_bits, vp_bits = _bf16(kp), _bf16(vp)  # before the append
     out = ops.paged_append_decode(q, kp, vp, kn, vn, torch.from_numpy(tables).to(cuda), lens,
-                                  out_dtype=torch.float32)
+                                  out_dtype=torch.float32, batch_invariant=invariant)
     torch.cuda.synchronize()
     ops.check_device_errors(cuda.index or 0)
     # the oracle's append: the new token at position ctx[b] (paged_kv.py:63-93)
@@ -85,6 +85,15 @@ def test_c2_full_layer_every_sequence(cuda):
     assert worst <= ATOL_REL, worst
 
 
+def test_c2_batch_invariant_every_sequence(cuda):
+    """The batch-invariant schedule (pairs cut every 512 tokens, pieces merged
+    in order) at the benchmark batch."""
+    ctx = np.random.default_rng(0).integers(512, 8193, size=64).astype(np.int64)
+    worst, pools_ok = _decode_vs_oracle(cuda, ctx, Hkv=8, G=4, seed=13, invariant=True)
+    assert pools_ok
+    assert worst <= ATOL_REL, worst
+
+
 def test_c5_rank_shard_every_sequence(cuda):
     z = np.random.default_rng(5).standard_normal(256)
     ctx = np.clip(np.rint(np.exp(np.log(4096) + z)), 256, 32768).astype(np.int64)
@@ -94,8 +103,12 @@ def test_c5_rank_shard_every_sequence(cuda):
     assert worst <= ATOL_REL, worst
 
 
+@pytest.mark.parametrize("tc", ["1", "0"])
 @pytest.mark.parametrize("bits", [8, 4])
-def test_c4_quantised_full_layer_every_sequence(cuda, bits):
+def test_c4_quantised_full_layer_every_sequence(cuda, bits, tc, monkeypatch):
+    """Both forms of the quantised decode (MLXZ_B200_QDECODE_TC: tcgen05 or
+    mma.sync)."""
+    monkeypatch.setenv("MLXZ_B200_QDECODE_TC", tc)
     B, Hkv, G = 32, 8, 4
     ctx = np.random.default_rng(bits).integers(4096, 16385, size=B).astype(np.int64)
     tables, n_blocks = _tables(ctx, 20 + bits)

@@ -208,3 +208,57 @@ def test_paged_decode_q_reads_any_affine_codes(cuda, bits):
     torch.cuda.synchronize()
     ops.check_device_errors(0)
     assert attn_err(out, _oracle_decode(case, dtype)[:, 0]) <= 2e-3
+
+
+# The tensor-core form (head_dim 128; 1, 2, 4, 8 or 16 query rows per KV head):
+# query rows from several tokens, every row count it is built for, capped
+# grids (many split pairs, merged by the last CTA), and the same inputs through
+# the mma.sync kernel.
+TC_CASES = [
+    # bits, G, n_q, ctx, num_warps
+    (8, 2, 1, [513, 1, 127, 128, 129, 300, 4095, 0], 0),
+    (4, 2, 1, [513, 1, 127, 128, 129, 300, 4095, 0], 0),
+    (8, 4, 2, [700, 33, 2049], 0),
+    (4, 8, 2, [700, 33, 2049], 0),
+    (8, 16, 1, [1000, 5], 0),
+    (4, 16, 1, [1000, 5], 0),
+    (8, 4, 1, [5000, 3000, 129, 1], 8),
+    (4, 4, 1, [5000, 3000, 129, 1], 20),
+]
+
+
+@pytest.mark.parametrize("bits,G,nq,ctx,nw", TC_CASES)
+def test_paged_decode_q_tensor_core_rows(cuda, bits, G, nq, ctx, nw, monkeypatch):
+    monkeypatch.setenv("MLXZ_B200_QDECODE_TC", "1")
+    Hkv = 2 if G * nq >= 16 else 4
+    case = _quant_case(90 + bits + G + nq, ctx, Hkv, 128, bits, "bf16", G=G, nq=nq)
+    pools = _dev_pools(case["host"], cuda)
+    q = to_dev(case["q"], "bf16", cuda)  # [B, n_q, Hq, D]
+    tables = torch.from_numpy(case["tables"]).to(cuda)
+    lens = torch.from_numpy(case["ctx"]).to(cuda)
+    out = ops.paged_decode_q(q, pools, tables, lens, num_warps=nw, out_dtype=torch.float32)
+    torch.cuda.synchronize()
+    ops.check_device_errors(0)
+    assert attn_err(out, _oracle_decode(case, "bf16")) <= 2e-3
+    for b, c in enumerate(ctx):
+        if c == 0:
+            assert torch.count_nonzero(out[b]) == 0
+
+
+def test_paged_decode_q_tensor_core_matches_mma_sync_kernel(cuda, monkeypatch):
+    """MLXZ_B200_QDECODE_TC selects the form (1: tcgen05, 0: mma.sync): both
+    agree with each other within the attention tolerance on the same inputs."""
+    ctx = [3000, 17, 129, 8000]
+    case = _quant_case(123, ctx, 8, 128, 8, "bf16", G=4)
+    pools = _dev_pools(case["host"], cuda)
+    q = to_dev(case["q"][:, 0], "bf16", cuda)
+    tables = torch.from_numpy(case["tables"]).to(cuda)
+    lens = torch.from_numpy(case["ctx"]).to(cuda)
+    monkeypatch.setenv("MLXZ_B200_QDECODE_TC", "1")
+    tc = ops.paged_decode_q(q, pools, tables, lens, out_dtype=torch.float32)
+    monkeypatch.setenv("MLXZ_B200_QDECODE_TC", "0")
+    legacy = ops.paged_decode_q(q, pools, tables, lens, out_dtype=torch.float32)
+    torch.cuda.synchronize()
+    ops.check_device_errors(0)
+    assert attn_err(tc, legacy.cpu().numpy()) <= 2e-3
+    assert attn_err(tc, _oracle_decode(case, "bf16")[:, 0]) <= 2e-3

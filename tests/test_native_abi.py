@@ -39,7 +39,7 @@ def test_every_declared_symbol_is_exported_and_bound(lib):
 
 
 def test_abi_version(lib):
-    assert lib.mz_abi_version() == 5
+    assert lib.mz_abi_version() == 6
 
 
 def test_argument_errors_do_not_launch(lib):
