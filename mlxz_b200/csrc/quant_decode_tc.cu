@@ -30,18 +30,23 @@
 // (sequence, KV head) pairs is cut into equal contiguous shares, and a pair
 // cut by share boundaries leaves (m, l, O) partials that the last CTA to
 // finish a piece of it merges (per-pair arrival counters in the workspace).
-// Ten warps:
-//   warp 0     copies: per 16-token sub-tile one 2-D bulk tensor copy of the K
-//              and of the V codes (8-bit: 128-byte rows, 128-byte swizzle, the
-//              layout the MMA reads; 4-bit: 64-byte rows, 64-byte swizzle) and
-//              four 64-byte bulk copies of the scales and biases; no multicast
-//   warp 1     TMEM allocation and the MMAs (one elected lane)
-//   warps 2-5  token role: thread = token of the tile (TMEM lane): scores,
-//              online softmax, P' operand; the Q operand of each piece
-//              (thread = head dim); 4-bit: widens the K codes to bytes
-//   warps 6-9  dim role: thread = head dim (TMEM lane): reads PV, accumulates
-//              O in registers, writes outputs / partials, merges; 4-bit:
-//              widens the V codes to bytes
+// Warps:
+//   warp 0     copies: codes by one 2-D bulk tensor copy of K and of V per
+//              16-token sub-tile (8-bit: 128-byte rows, 128-byte swizzle, the
+//              layout the MMA reads; 4-bit: 64-byte rows, 64-byte swizzle; no
+//              multicast), every tile's scales and biases by 16-byte cp.async
+//              (a small bulk copy costs about as much issue time as a 2 KiB
+//              one), all counted on the stage's mbarrier; block ids loaded
+//              four tiles ahead
+//   warp 1     TMEM allocation and the MMAs (one elected lane), each QK / PV
+//              issued as soon as its inputs are in
+//   token groups (one or two warpgroups; two take alternate tiles, each with
+//              its own online-softmax state for the piece): thread = token of
+//              the tile (TMEM lane): scores, exchange of tile maxima, P'
+//   dim role (one warpgroup): thread = head dim (TMEM lane): the Q operand of
+//              each piece, reads PV, accumulates O per token group, combines
+//              the groups' states at a piece's end, writes outputs /
+//              partials, merges; 4-bit: widens the next tile's codes to bytes
 // Every wait is bounded (a wait that gives up sets MZ_DEVERR_TIMEOUT and an
 // abort flag; the roles leave their loops together, the copy warp waits for
 // its copies in flight, the MMA warp drains, warp 1 frees the TMEM).
@@ -60,16 +65,21 @@ namespace qtc {
 
 constexpr int kT = 128;  // tokens per tile
 constexpr int kD = 128;  // head dim
-constexpr int kThreads = 320;
-constexpr int kProdWarp = 0, kMmaWarp = 1, kTokWarp0 = 2, kDimWarp0 = 6;
-constexpr int kBarTok = 2, kBarDim = 3;  // named barriers of the two 128-thread roles
+constexpr int kProdWarp = 0, kMmaWarp = 1, kTokWarp0 = 2;
 
 template <int BITS, int ROWS>
 struct Cfg {
+  // token groups: two (alternate tiles, each with its own online-softmax
+  // state) when the registers allow it, else one
+  static constexpr int TGN = ROWS <= 4 ? 2 : 1;
+  static constexpr int kThreads = 64 + 128 * TGN + 128 + 32;
+  static constexpr int kDimWarp0 = kTokWarp0 + 4 * TGN;
+  static constexpr int kProdWarp2 = kDimWarp0 + 4;  // second copy warp (odd tiles)
+  static constexpr int kBarDim = 2 + TGN;  // named barrier of the dim role (token group g: 2 + g)
+  static constexpr int kBarProd = kBarDim + 1;  // named barrier of the two copy warps
   static constexpr int NB = ((2 * ROWS + 1 + 15) / 16) * 16;  // B operand columns
   static constexpr int kUnits = NB / 16;                      // 16-byte units per B row
   static constexpr int RB = kD * BITS / 8;                    // code bytes per token row
-  static constexpr int kStages = BITS == 8 ? 4 : 3;
   static constexpr int kCodeTile = kT * 128;  // widened codes, 128 rows x 128 bytes
   static constexpr int kRawTile = kT * RB;    // 4-bit rows as stored
   static constexpr int kSub = 16;             // tokens per copy
@@ -78,33 +88,42 @@ struct Cfg {
   static constexpr int kVr = kKr + (BITS == 4 ? kRawTile : 0);
   static constexpr int kSc = kVr + (BITS == 4 ? kRawTile : 0);  // [4 arrays][128 tok][2] fp16
   static constexpr int kStage = kSc + 4 * kT * 4;
-  static constexpr int kSubBytes = 2 * kSub * RB + 4 * kSub * 4;  // bytes one sub-tile brings
-  static constexpr int kBop = kT * NB;                             // one B operand
-  static constexpr int kQb = kStages * kStage;                     // Q operands [2]
-  static constexpr int kPb = kQb + 2 * kBop;                       // P' operands [2 bufs][2 groups]
-  static constexpr int kMisc = kPb + 4 * kBop;
+  static constexpr int kBop = kT * NB;  // one B operand
+  static constexpr int NX4 = (3 * ROWS + 3) / 4;  // int4 words of one exchange slot
   // misc area (offsets from kMisc)
-  static constexpr int kBars = 0;                        // 40 barriers
-  static constexpr int kWords = 320;                     // tmem slot, abort, merge word
-  static constexpr int kXch = 384;                       // [2][4 warps][3 ROWS]
-  static constexpr int kQx = kXch + 2 * 4 * 3 * ROWS * 4;        // [4 warps][ROWS] (x2 uses)
-  static constexpr int kQp = kQx + 4 * ROWS * 4;                 // [2][ROWS] s_q
-  static constexpr int kQs = kQp + 2 * ROWS * 4;                 // [2][2 groups][ROWS]
-  static constexpr int kTp = kQs + 2 * 2 * ROWS * 4;             // [2][3 ROWS]
-  static constexpr int kPe = kTp + 2 * 3 * ROWS * 4;             // [2][4 ROWS]
-  static constexpr int kLx = kPe + 2 * 4 * ROWS * 4;             // [4 warps][3 ROWS]
-  static constexpr int kMiscBytes = kLx + 4 * 3 * ROWS * 4;
+  static constexpr int kBars = 0;                                  // barriers
+  static constexpr int kWords = 512;                               // tmem slot, abort, merge word, stops
+  static constexpr int kXch = 576;                                 // [TGN][2][4 warps][NX4] int4
+  static constexpr int kQx = kXch + TGN * 2 * 4 * NX4 * 16;        // [4 warps][ROWS]
+  static constexpr int kQp = kQx + 4 * ROWS * 4;                   // [2][ROWS] s_q
+  static constexpr int kQs = kQp + 2 * ROWS * 4;                   // [2][2 groups][ROWS]
+  static constexpr int kTp = kQs + 2 * 2 * ROWS * 4;               // [2][3 ROWS]
+  static constexpr int kPe = kTp + 2 * 3 * ROWS * 4;               // [2][TGN][4 ROWS]
+  static constexpr int kLx = kPe + 2 * TGN * 4 * ROWS * 4;         // [TGN][4 warps][3 ROWS]
+  static constexpr int kIds = kLx + TGN * 4 * 3 * ROWS * 4;  // [2 warps][4 tiles][8 sub-tiles] block ids
+  static constexpr int kMiscBytes = kIds + 2 * 4 * 8 * 4;
+  // as many stages as the shared memory holds (up to 8): the copies of
+  // several tiles must be in flight to cover the memory latency under load
+  static constexpr int kFixed = 6 * kBop + kMiscBytes + 1024;
+  static constexpr int kStagesFit = (227 * 1024 - kFixed) / kStage;
+  static constexpr int kStages = kStagesFit > 8 ? 8 : kStagesFit;
+  static constexpr int kWidenAhead = kStages - 2 < 2 ? kStages - 2 : 2;  // 4-bit: tiles widened ahead of their QK
+  static constexpr int kQb = kStages * kStage;  // Q operands [2]
+  static constexpr int kPb = kQb + 2 * kBop;    // P' operands [2 bufs][2 groups]
+  static constexpr int kMisc = kPb + 4 * kBop;
   static constexpr int kSmemBytes = kMisc + kMiscBytes + 1024;
+  static_assert(kStages >= 3, "at least three stages");
+  static_assert(BITS == 8 || kWidenAhead <= kStages - 2, "4-bit widening stays behind the copies");
   static constexpr uint32_t kTmemCols = 8 * NB <= 128 ? 128 : (8 * NB <= 256 ? 256 : 512);
   static_assert(kStage % 1024 == 0, "stages keep the 1024-byte alignment of the swizzled tiles");
   static_assert(kSmemBytes <= 227 * 1024, "shared memory");
 };
 
 // barrier slots
-constexpr int kFull = 0, kKx = 4, kVx = 8, kEmpty = 12, kSFull = 16, kSEmpty = 18, kQFull = 20,
-              kPFull = 22, kTpB = 24, kOFull = 26, kOEmpty = 28, kPeB = 30, kPeEmpty = 32,
-              kDrain = 34, kNumBars = 35;
-static_assert(8 * kNumBars <= 320, "barrier area");
+constexpr int kFull = 0, kKx = 8, kVx = 16, kEmpty = 24, kSFull = 32, kSEmpty = 34, kQFull = 36,
+              kDrainT = 38, kTpB = 40, kOFull = 42, kOEmpty = 44, kPeB = 46, kPeEmpty = 48,
+              kDrain = 50, kNumBars = 51;
+static_assert(8 * kNumBars <= 512, "barrier area");
 
 struct TCur {
   int b, h, t, n, ctx;
@@ -176,6 +195,37 @@ __device__ __forceinline__ TCur next_pair(TCur c, const Params &p) {
   return c;
 }
 
+__device__ __forceinline__ void cp_async4(uint32_t dst, const void *src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+__device__ __forceinline__ void cp_async_wait_group3() {
+  asm volatile("cp.async.wait_group 3;" ::: "memory");
+}
+__device__ __forceinline__ void cp_async16_hint(uint32_t dst, const void *src, uint64_t pol) {
+  asm volatile("cp.async.cg.shared.global.L2::cache_hint [%0], [%1], 16, %2;" ::"r"(dst), "l"(src),
+               "l"(pol)
+               : "memory");
+}
+// The mbarrier gets one arrival (counted in its expected count) once every
+// cp.async this thread issued before has landed.
+__device__ __forceinline__ void cp_async_arrive_noinc(uint32_t bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(bar) : "memory");
+}
+// Non-blocking test of an mbarrier phase.
+__device__ __forceinline__ bool mbar_test(uint32_t bar, uint32_t phase) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(phase)
+      : "memory");
+  return ok != 0;
+}
 __device__ __forceinline__ void mbar_arrive1(uint32_t bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
 }
@@ -270,12 +320,13 @@ __device__ __forceinline__ void widen_row(const uint8_t *raw, uint8_t *dst, int 
 }
 
 template <int BITS, int ROWS>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(Cfg<BITS, ROWS>::kThreads, 1)
     paged_decode_qtc_kernel(const __grid_constant__ CUtensorMap tmK,
                             const __grid_constant__ CUtensorMap tmV, const Params p) {
   using C = Cfg<BITS, ROWS>;
   constexpr int S = C::kStages;
   constexpr int NB = C::NB;
+  constexpr int TGN = C::TGN;
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -293,7 +344,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp == kProdWarp && lane == 0) {
     for (int s = 0; s < S; ++s) {
-      mbar_init(bar(kFull + s), 1);
+      mbar_init(bar(kFull + s), 33);  // lane 0 (+ bulk tensor bytes) and 32 cp.async arrivals
       mbar_init(bar(kKx + s), 128);
       mbar_init(bar(kVx + s), 128);
       mbar_init(bar(kEmpty + s), 1);
@@ -302,11 +353,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(bar(kSFull + j), 1);
       mbar_init(bar(kSEmpty + j), 128);
       mbar_init(bar(kQFull + j), 128);
-      mbar_init(bar(kPFull + j), 128);
+      mbar_init(bar(kDrainT + j), 1);
       mbar_init(bar(kTpB + j), 1);
       mbar_init(bar(kOFull + j), 1);
       mbar_init(bar(kOEmpty + j), 128);
-      mbar_init(bar(kPeB + j), 1);
+      mbar_init(bar(kPeB + j), TGN);
       mbar_init(bar(kPeEmpty + j), 128);
     }
     mbar_init(bar(kDrain), 1);
@@ -331,83 +382,151 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int x0 = static_cast<int>(blockIdx.x) * per;
   const int cnt = max(0, min(per, T - x0));
 
-  if (warp == kProdWarp) {
+  if (warp == kProdWarp || warp == C::kProdWarp2) {
     // ---------------- copies ----------------
+    // Two warps issue the copies, warp kProdWarp the even tiles of the share
+    // and kProdWarp2 the odd ones: one warp's serial issue of a tile (block
+    // ids, sixteen bulk tensor copies, the scales) takes longer than the
+    // period the memory system sustains.
+    const int pw = warp == kProdWarp ? 0 : 1;
     const uint64_t pol = l2_policy_evict_first();
-    int issued = 0;
-    if (cnt > 0) {
+    int stop = cnt;  // first tile of this warp not issued (cnt when all were)
+    if (pw < cnt) {
       TCur c = locate_tc(p, x0, lane);
-      // block id of sub-tile `lane` (< 8) of the tile at cursor cc, or 0
-      auto block_of = [&](const TCur &cc) -> int32_t {
-        const int tok0 = cc.t * kT + lane * C::kSub;
-        if (lane >= kT / C::kSub || tok0 >= cc.ctx) return 0;
-        return p.tables[(int64_t)cc.b * p.max_blocks + tok0 / p.bs];
+      if (pw) adv(c, p);
+      // block ids are copied four own tiles ahead of their use into a ring in
+      // shared memory (cp.async, one group per tile: a table load under full
+      // HBM traffic takes about as long as issuing a tile's copies)
+      int32_t *idring = reinterpret_cast<int32_t *>(misc + C::kIds) + pw * 32;
+      const uint32_t idring_u = sbase + C::kMisc + C::kIds + pw * 128;
+      TCur ca = c;  // cursor of the tile whose ids load next
+      auto load_ids = [&](int slot) {
+        const int tok0 = ca.t * kT + lane * C::kSub;
+        if (lane < kT / C::kSub && tok0 < ca.ctx)
+          cp_async4(idring_u + (slot * 8 + lane) * 4,
+                    p.tables + (int64_t)ca.b * p.max_blocks + tok0 / p.bs);
+        cp_async_commit();
       };
-      int32_t id_cur = block_of(c);
-      for (int i = 0; i < cnt; ++i) {
-        if (__any_sync(0xffffffffu, *abort_flag != 0)) break;
-        TCur cn = c;
-        adv(cn, p);
-        const int32_t id_nxt = (i + 1 < cnt) ? block_of(cn) : 0;
+#pragma unroll
+      for (int a = 0; a < 4; ++a) {
+        if (pw + 2 * a < cnt) {
+          load_ids(a);
+          adv(ca, p);
+          adv(ca, p);
+        } else {
+          cp_async_commit();
+        }
+      }
+      for (int i = pw, j = 0; i < cnt; i += 2, ++j) {
+        if (__any_sync(0xffffffffu, *abort_flag != 0)) {
+          stop = i;
+          break;
+        }
+        cp_async_wait_group3();  // this tile's ids (groups of later tiles may be pending)
+        const int32_t id_cur = lane < 8 ? idring[(j & 3) * 8 + lane] : 0;
         const int s = i % S;
         if (i >= S && !__all_sync(0xffffffffu, wait_b(kEmpty + s, ((i - S) / S) & 1))) {
           if (lane == 0) give_up();
+          stop = i;
           break;
         }
         const int nv = min(kT, c.ctx - c.t * kT);
         const int nsub = (nv + C::kSub - 1) / C::kSub;
-        if (lane == 0) mbar_arrive_expect_tx(bar(kFull + s), static_cast<uint32_t>(nsub * C::kSubBytes));
-        __syncwarp();
+        const uint32_t sb = stage_u(s), fb = bar(kFull + s);
+        // pool row of sub-tile `lane` (lanes < nsub)
+        int64_t row0 = 0;
         if (lane < nsub) {
           int32_t blk = id_cur;
           if (blk < 0 || blk >= p.n_blocks) {
             dev_error(p.err, MZ_DEVERR_BLOCK_ID);
             blk = 0;
           }
-          const int tok0 = c.t * kT + lane * C::kSub;
-          const int64_t row0 = ((int64_t)blk * p.Hkv + c.h) * p.bs + tok0 % p.bs;
-          const uint32_t sb = stage_u(s), fb = bar(kFull + s);
-          if constexpr (BITS == 8) {
-            tma_load_2d(sb + C::kKc + lane * 2048, &tmK, 0, static_cast<int>(row0), fb, pol);
-            tma_load_2d(sb + C::kVc + lane * 2048, &tmV, 0, static_cast<int>(row0), fb, pol);
-          } else {
-            tma_load_2d(sb + C::kKr + lane * 1024, &tmK, 0, static_cast<int>(row0), fb, pol);
-            tma_load_2d(sb + C::kVr + lane * 1024, &tmV, 0, static_cast<int>(row0), fb, pol);
-          }
-          const __half *arr[4] = {p.k_scales, p.k_biases, p.v_scales, p.v_biases};
-#pragma unroll
-          for (int a = 0; a < 4; ++a)
-            bulk_load(sb + C::kSc + a * (kT * 4) + lane * (C::kSub * 4), arr[a] + row0 * 2,
-                      C::kSub * 4, fb, pol);
+          row0 = ((int64_t)blk * p.Hkv + c.h) * p.bs + (c.t * kT + lane * C::kSub) % p.bs;
         }
-        issued = i + 1;
-        id_cur = id_nxt;
-        c = cn;
+        // codes: one 2-D bulk tensor copy of K and of V per sub-tile (8-bit:
+        // 128-byte rows, 128-byte swizzle, the layout the MMA reads; 4-bit:
+        // 64-byte rows, 64-byte swizzle, widened later); the stage's full
+        // barrier counts their bytes (lane 0) and one cp.async arrival of
+        // every lane (the scales)
+        if (lane == 0) mbar_arrive_expect_tx(fb, static_cast<uint32_t>(nsub * 2 * C::kSub * C::RB));
+        __syncwarp();
+        if (lane < nsub) {
+          tma_load_2d(sb + (BITS == 8 ? C::kKc : C::kKr) + lane * C::kSub * C::RB, &tmK, 0,
+                      static_cast<int>(row0), fb, pol);
+          tma_load_2d(sb + (BITS == 8 ? C::kVc : C::kVr) + lane * C::kSub * C::RB, &tmV, 0,
+                      static_cast<int>(row0), fb, pol);
+        }
+        {
+          // scales and biases: 4 arrays x 16 tokens x 4 bytes per sub-tile =
+          // 16 chunks of 16 bytes; lane l copies chunk (l & 3) of sub-tile l / 4
+          // of every array
+          const int j = lane >> 2, part = lane & 3;
+          const int64_t rj = __shfl_sync(0xffffffffu, row0, j);
+          if (j < nsub) {
+            const __half *arr[4] = {p.k_scales, p.k_biases, p.v_scales, p.v_biases};
+#pragma unroll
+            for (int a = 0; a < 4; ++a)
+              cp_async16_hint(sb + C::kSc + a * (kT * 4) + j * (C::kSub * 4) + part * 16,
+                              arr[a] + rj * 2 + part * 8, pol);
+          }
+        }
+        cp_async_arrive_noinc(fb);
+        // the ids of own tile j + 4 into the slot just read
+        if (i + 8 < cnt) {
+          load_ids(j & 3);
+          adv(ca, p);
+          adv(ca, p);
+        } else {
+          cp_async_commit();
+        }
+        adv(c, p);
+        adv(c, p);
       }
     }
-    // copies still in flight land before the CTA leaves
-    if (lane == 0)
-      for (int j = max(0, issued - S); j < issued; ++j)
+    // copies still in flight land before the CTA leaves: the last tile
+    // issued into each stage (a later phase of a stage needs the earlier
+    // one complete first)
+    int *stops = reinterpret_cast<int *>(misc + C::kWords + 16);
+    if (lane == 0) stops[pw] = stop;
+    bar_sync_n(C::kBarProd, 64);
+    if (pw == 0 && lane == 0) {
+      const int st0 = stops[0], st1 = stops[1];
+      int found = 0;
+      for (int j = cnt - 1; j >= 0 && found < S; --j) {
+        if (j >= ((j & 1) ? st1 : st0)) continue;
+        if (j + S < cnt && j + S < (((j + S) & 1) ? st1 : st0)) continue;  // stage reused later
         (void)wait_b(kFull + j % S, (j / S) & 1);
+        ++found;
+      }
+    }
     __syncwarp();
-  } else if (warp == kMmaWarp) {
-    // ---------------- MMAs ----------------
+  }
+  else if (warp == kMmaWarp) {
+    // ---------------- QK MMAs ----------------
+    // QK(j) in tile order, once its codes are in (4-bit: widened), its S
+    // buffer is free (S(j - 2) read) and, for a piece's first tile, the
+    // piece's Q operand is written.  PV(j) is issued by the token group that
+    // wrote P'(j).
     constexpr uint32_t idQK = tc::idesc_u8(kT, NB, false, true);
-    constexpr uint32_t idPV = tc::idesc_u8(kD, NB, true, true);
     bool ok = true;
     if (cnt > 0) {
-      TCur cq = locate_tc(p, x0, lane);  // cursor of the next QK
-      int kq = -1;                        // piece of the next QK
-      auto issue_qk = [&](int j) -> bool {
-        const int s = j % S, buf = j & 1;
-        if (j == 0 || cq.t == 0) {
-          ++kq;
-          if (!wait_b(kQFull + (kq & 1), (kq >> 1) & 1)) return false;
+      TCur cq = locate_tc(p, x0, lane);
+      int kq = -1;  // piece of the last QK
+      for (int nq = 0; nq < cnt; ++nq) {
+        const bool newp = (nq == 0) || (cq.t == 0);
+        const int kk = newp ? kq + 1 : kq;
+        bool r = true;
+        if (lane == 0)
+          r = wait_b((BITS == 8 ? kFull : kKx) + nq % S, (nq / S) & 1) &&
+              (nq < 2 || wait_b(kSEmpty + (nq & 1), ((nq - 2) >> 1) & 1)) &&
+              (!newp || wait_b(kQFull + (kk & 1), (kk >> 1) & 1)) && *abort_flag == 0;
+        if (!__shfl_sync(0xffffffffu, r, 0)) {
+          ok = false;
+          break;
         }
-        if (!wait_b((BITS == 8 ? kFull : kKx) + s, (j / S) & 1)) return false;
-        if (j >= 2 && !wait_b(kSEmpty + buf, ((j - 2) >> 1) & 1)) return false;
         tc::fence_after_sync();
-        const uint32_t qb = sbase + C::kQb + (kq & 1) * C::kBop;
+        const int s = nq % S, buf = nq & 1;
+        const uint32_t qb = sbase + C::kQb + (kk & 1) * C::kBop;
         const uint32_t kc = stage_u(s) + C::kKc;
 #pragma unroll
         for (int g = 0; g < 2; ++g)
@@ -417,40 +536,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                              tc::smem_desc_sw128(kc + 64 * g + 32 * k, 16, 1024),
                              tc::smem_desc_none(qb + 1024 * g + 512 * k, 128, 2048), idQK, k > 0);
         tc::commit_elect(bar(kSFull + buf));
+        kq = kk;
         adv(cq, p);
-        return true;
-      };
-      ok = __all_sync(0xffffffffu, issue_qk(0));
-      for (int i = 0; ok && i < cnt; ++i) {
-        if (__any_sync(0xffffffffu, *abort_flag != 0)) {
-          ok = false;
-          break;
-        }
-        if (i + 1 < cnt && !__all_sync(0xffffffffu, issue_qk(i + 1))) {
-          ok = false;
-          break;
-        }
-        const int s = i % S, buf = i & 1;
-        bool w = wait_b(kPFull + buf, (i >> 1) & 1);
-        if (BITS == 4) w = w && wait_b(kVx + s, (i / S) & 1);
-        if (i >= 2) w = w && wait_b(kOEmpty + buf, ((i - 2) >> 1) & 1);
-        if (!__all_sync(0xffffffffu, w)) {
-          ok = false;
-          break;
-        }
-        tc::fence_after_sync();
-        const uint32_t vc = stage_u(s) + C::kVc;
-#pragma unroll
-        for (int g = 0; g < 2; ++g) {
-          const uint32_t pb = sbase + C::kPb + (buf * 2 + g) * C::kBop;
-#pragma unroll
-          for (int k = 0; k < kT / 32; ++k)
-            tc::mma_i8_elect(tmem + kO0 + buf * 2 * NB + g * NB,
-                             tc::smem_desc_sw128(vc + 4096 * k, 16384, 1024),
-                             tc::smem_desc_none(pb + 512 * k, 128, 2048), idPV, k > 0);
-        }
-        tc::commit_elect(bar(kOFull + buf));
-        tc::commit_elect(bar(kEmpty + s));
       }
     }
     if (!ok && lane == 0) give_up();
@@ -458,235 +545,209 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc::commit_elect(bar(kDrain));
     (void)wait_b(kDrain, 0);
     __syncwarp();
-  } else if (warp < kDimWarp0) {
-    // ---------------- token role ----------------
+  }
+  else if (warp < C::kDimWarp0) {
+    // ---------------- token groups ----------------
+    // Group tg takes the tiles i with i % TGN == tg; thread = token of the
+    // tile (TMEM lane).  Each group keeps its own online-softmax state for the
+    // piece and publishes it at the piece's end; the dim role combines them.
+    const int tg = (warp - kTokWarp0) >> 2;
+    const int bid = 2 + tg;  // the group's named barrier
     const int tok = 32 * (warp & 3) + lane;
+    const int wq = warp & 3;  // the warp's exchange slot
     const uint32_t tl = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
-    float *xch = reinterpret_cast<float *>(misc + C::kXch);
-    int *qx = reinterpret_cast<int *>(misc + C::kQx);
-    float *qp = reinterpret_cast<float *>(misc + C::kQp);
-    float *qs = reinterpret_cast<float *>(misc + C::kQs);
+    int4 *xch = reinterpret_cast<int4 *>(misc + C::kXch) + tg * 2 * 4 * C::NX4;
+    const float *qp = reinterpret_cast<const float *>(misc + C::kQp);
+    const float *qs = reinterpret_cast<const float *>(misc + C::kQs);
     float *tp = reinterpret_cast<float *>(misc + C::kTp);
     float *pe = reinterpret_cast<float *>(misc + C::kPe);
-    float *lx = reinterpret_cast<float *>(misc + C::kLx);
-    const int wq = warp - kTokWarp0;  // 0..3 (exchange slot)
-
-    // Q operand of a piece (pair c), into buffer kk & 1.  Thread = operand
-    // row (head dim dim_of(tok)).  Plain named barriers: no waits inside.
-    auto write_q = [&](int kk, const TCur &c) {
-      const int d = dim_of<BITS>(tok);
-      float qv[ROWS];
-      uint32_t am[ROWS];
-#pragma unroll
-      for (int r = 0; r < ROWS; ++r) {
-        qv[r] = ld_q(p.q, row_offset(p.q_sb, p.q_st, p.q_sh, c.b, c.h, r, p.G) + d, p.q_bf16);
-        am[r] = __reduce_max_sync(0xffffffffu, __float_as_uint(fabsf(qv[r])));
-      }
-      if (lane == 0)
-#pragma unroll
-        for (int r = 0; r < ROWS; ++r) qx[wq * ROWS + r] = static_cast<int>(am[r]);
-      bar_sync_n(kBarTok, 128);
-      float inv[ROWS], sq[ROWS];
-#pragma unroll
-      for (int r = 0; r < ROWS; ++r) {
-        uint32_t m = 0;
-#pragma unroll
-        for (int w = 0; w < 4; ++w) m = max(m, static_cast<uint32_t>(qx[w * ROWS + r]));
-        const float amax = __uint_as_float(m);
-        sq[r] = amax / 32767.f;
-        inv[r] = amax > 0.f ? 32767.f / amax : 0.f;
-      }
-      bar_sync_n(kBarTok, 128);  // every thread has read qx
-      uint32_t u[ROWS];
-      int isum[ROWS];
-#pragma unroll
-      for (int r = 0; r < ROWS; ++r) {
-        const int qi = max(-32767, min(32767, __float2int_rn(qv[r] * inv[r])));
-        u[r] = static_cast<uint32_t>(qi + 32768);
-        isum[r] = __reduce_add_sync(0xffffffffu, qi);
-      }
-      if (lane == 0)
-#pragma unroll
-        for (int r = 0; r < ROWS; ++r) qx[wq * ROWS + r] = isum[r];
-      store_brow<ROWS, C::kUnits>(smem + C::kQb + (kk & 1) * C::kBop, tok, u);
-      fence_proxy_async_smem();
-      mbar_arrive1(bar(kQFull + (kk & 1)));
-      bar_sync_n(kBarTok, 128);
-      if (tok == 0) {
-        // warps 2, 3 hold tokens 64..127 (group 1), warps 4, 5 tokens 0..63
-#pragma unroll
-        for (int r = 0; r < ROWS; ++r) {
-          qp[(kk & 1) * ROWS + r] = sq[r];
-          qs[((kk & 1) * 2 + 0) * ROWS + r] = sq[r] * static_cast<float>(qx[2 * ROWS + r] + qx[3 * ROWS + r]);
-          qs[((kk & 1) * 2 + 1) * ROWS + r] = sq[r] * static_cast<float>(qx[0 * ROWS + r] + qx[1 * ROWS + r]);
-        }
-      }
-      bar_sync_n(kBarTok, 128);  // qp / qs written, qx free again
-    };
-
-    bool bad = false;
+    float *lx = reinterpret_cast<float *>(misc + C::kLx) + tg * 4 * 3 * ROWS;
+    constexpr int NX = 3 * ROWS, NX4 = C::NX4;
+    constexpr uint32_t idPV = tc::idesc_u8(kD, NB, true, true);
+    bool bad = false, pv_issued = false;
     if (cnt > 0) {
       TCur c = locate_tc(p, x0, lane);
-      write_q(0, c);
-      {
-        // the second piece's Q, if the share reaches past the first pair
-        const int pend = x0 + (c.n - c.t);  // flat index one past the first pair
-        if (pend < x0 + cnt) write_q(1, next_pair(c, p));
-      }
-      if constexpr (BITS == 4) {
-        if (!wait_b(kFull + 0, 0)) bad = true;
-        widen_row(stage(0) + C::kKr, stage(0) + C::kKc, tok);
-        fence_proxy_async_smem();
-        mbar_arrive1(bar(kKx + 0));
-      }
       float m[ROWS], l[ROWS], rb[2][ROWS], sq[ROWS], qsum[2][ROWS];
-      int k = -1;
+      int k = -1, kq = -1;
       for (int i = 0; i < cnt; ++i) {
-        const int s = i % S, buf = i & 1;
         const bool first = (i == 0) || (c.t == 0);
         const bool last = (i == cnt - 1) || (c.t == c.n - 1);
-        if (first) ++k;
-        if constexpr (BITS == 4) {
-          if (i + 1 < cnt) {
-            const int s1 = (i + 1) % S;
-            if (!bad && !wait_b(kFull + s1, ((i + 1) / S) & 1)) bad = true;
-            widen_row(stage(s1) + C::kKr, stage(s1) + C::kKc, tok);
-            fence_proxy_async_smem();
-            mbar_arrive1(bar(kKx + s1));
-          }
-        }
-        // scores of this tile
-        uint32_t sr[2 * NB];
-        if (!bad && !wait_b(kSFull + buf, (i >> 1) & 1)) bad = true;
-        tc::fence_after_sync();
-#pragma unroll
-        for (int j = 0; j < 2 * NB; j += 32) {
-          uint32_t r32[32];
-          tc::ld32(tl + kS0 + buf * 2 * NB + j, r32);
-          tc::wait_ld();
-#pragma unroll
-          for (int e = 0; e < 32; ++e)
-            if (j + e < 2 * NB) sr[j + e] = r32[e];
-        }
-        tc::fence_before_sync();
-        mbar_arrive1(bar(kSEmpty + buf));
-        if (BITS == 8 && !bad && !wait_b(kFull + s, (i / S) & 1)) bad = true;
         if (first) {
-          // the piece's Q quantities; the next piece's Q once this piece's
-          // first scores are in (every QK of the piece before is complete)
+          ++k;
 #pragma unroll
           for (int r = 0; r < ROWS; ++r) {
-            sq[r] = qp[(k & 1) * ROWS + r];
-            qsum[0][r] = qs[((k & 1) * 2 + 0) * ROWS + r];
-            qsum[1][r] = qs[((k & 1) * 2 + 1) * ROWS + r];
             m[r] = -INFINITY;
             l[r] = 0.f;
             rb[0][r] = rb[1][r] = 0.f;
           }
         }
-        const uint8_t *sc = stage(s) + C::kSc;
-        const float2 sk = __half22float2(*reinterpret_cast<const __half2 *>(sc + 0 * kT * 4 + tok * 4));
-        const float2 bk = __half22float2(*reinterpret_cast<const __half2 *>(sc + 1 * kT * 4 + tok * 4));
-        const float2 sv = __half22float2(*reinterpret_cast<const __half2 *>(sc + 2 * kT * 4 + tok * 4));
-        const float2 bv = __half22float2(*reinterpret_cast<const __half2 *>(sc + 3 * kT * 4 + tok * 4));
-        const int nv = min(kT, c.ctx - c.t * kT);
-        const bool valid = tok < nv;
-        float x[ROWS];
+        if (i % TGN == tg) {
+          const int s = i % S, buf = i & 1;
+          if (kq != k) {
+            // the piece's Q quantities, published with its Q operand
+            if (!bad && !wait_b(kQFull + (k & 1), (k >> 1) & 1)) bad = true;
 #pragma unroll
-        for (int r = 0; r < ROWS; ++r) {
-          const int d0 = static_cast<int>(sr[r] * 256u + sr[ROWS + r] - (sr[2 * ROWS] << 15));
-          const int d1 = static_cast<int>(sr[NB + r] * 256u + sr[NB + ROWS + r] - (sr[NB + 2 * ROWS] << 15));
-          float v = sq[r] * fmaf(sk.x, static_cast<float>(d0), sk.y * static_cast<float>(d1));
-          v = fmaf(bk.x, qsum[0][r], fmaf(bk.y, qsum[1][r], v));
-          x[r] = valid ? v * p.scale_log2 : -INFINITY;
-        }
-        // tile maxima over the tile's tokens: per row of the score, and per
-        // (group, row) of score + log2 |s_V| (the largest |p s_V| once the
-        // new row maximum is known)
-        constexpr int NX = 3 * ROWS;
-        {
-          const int par = i & 1;
-          const float l2v0 = valid ? __log2f(fabsf(sv.x)) : -INFINITY;
-          const float l2v1 = valid ? __log2f(fabsf(sv.y)) : -INFINITY;
-          int red[NX];
+            for (int r = 0; r < ROWS; ++r) {
+              sq[r] = qp[(k & 1) * ROWS + r];
+              qsum[0][r] = qs[((k & 1) * 2 + 0) * ROWS + r];
+              qsum[1][r] = qs[((k & 1) * 2 + 1) * ROWS + r];
+            }
+            kq = k;
+          }
+          // scores of this tile
+          uint32_t sr[2 * NB];
+          if (!bad && !wait_b(kSFull + buf, (i >> 1) & 1)) bad = true;
+          tc::fence_after_sync();
+#pragma unroll
+          for (int j = 0; j < 2 * NB; j += 32) {
+            uint32_t r32[32];
+            tc::ld32(tl + kS0 + buf * 2 * NB + j, r32);
+            tc::wait_ld();
+#pragma unroll
+            for (int e = 0; e < 32; ++e)
+              if (j + e < 2 * NB) sr[j + e] = r32[e];
+          }
+          tc::fence_before_sync();
+          mbar_arrive1(bar(kSEmpty + buf));
+          if (!bad && !wait_b(kFull + s, (i / S) & 1)) bad = true;  // the tile's scales
+          const uint8_t *sc = stage(s) + C::kSc;
+          const float2 sk = __half22float2(*reinterpret_cast<const __half2 *>(sc + 0 * kT * 4 + tok * 4));
+          const float2 bk = __half22float2(*reinterpret_cast<const __half2 *>(sc + 1 * kT * 4 + tok * 4));
+          const float2 sv = __half22float2(*reinterpret_cast<const __half2 *>(sc + 2 * kT * 4 + tok * 4));
+          const float2 bv = __half22float2(*reinterpret_cast<const __half2 *>(sc + 3 * kT * 4 + tok * 4));
+          const int nv = min(kT, c.ctx - c.t * kT);
+          const bool valid = tok < nv;
+          float x[ROWS];
 #pragma unroll
           for (int r = 0; r < ROWS; ++r) {
-            red[r] = __reduce_max_sync(0xffffffffu, f2ord(x[r]));
-            red[ROWS + r] = __reduce_max_sync(0xffffffffu, f2ord(x[r] + l2v0));
-            red[2 * ROWS + r] = __reduce_max_sync(0xffffffffu, f2ord(x[r] + l2v1));
+            const int d0 = static_cast<int>(sr[r] * 256u + sr[ROWS + r] - (sr[2 * ROWS] << 15));
+            const int d1 = static_cast<int>(sr[NB + r] * 256u + sr[NB + ROWS + r] - (sr[NB + 2 * ROWS] << 15));
+            float v = sq[r] * fmaf(sk.x, static_cast<float>(d0), sk.y * static_cast<float>(d1));
+            v = fmaf(bk.x, qsum[0][r], fmaf(bk.y, qsum[1][r], v));
+            x[r] = valid ? v * p.scale_log2 : -INFINITY;
           }
-          int *xi = reinterpret_cast<int *>(xch) + (par * 4 + wq) * NX;
-          if (lane == 0)
+          // tile maxima over the group's 128 tokens: per row of the score,
+          // and per (group of dims, row) of score + log2 |s_V| (the largest
+          // |p s_V| once the new row maximum is known)
+          const int par = (i / TGN) & 1;
+          {
+            const float l2v0 = valid ? __log2f(fabsf(sv.x)) : -INFINITY;
+            const float l2v1 = valid ? __log2f(fabsf(sv.y)) : -INFINITY;
+            int red[NX4 * 4];
 #pragma unroll
-            for (int e = 0; e < NX; ++e) xi[e] = red[e];
-        }
-        if (bar_or(kBarTok, 128, bad || *abort_flag != 0)) {
-          bad = true;
-          break;
-        }
-        float mnew[ROWS], alpha[ROWS], inv_sp[2][ROWS], sp[2][ROWS];
-        {
-          const int *xi = reinterpret_cast<const int *>(xch) + (i & 1) * 4 * NX;
-          int mx[NX];
+            for (int r = 0; r < ROWS; ++r) {
+              red[r] = __reduce_max_sync(0xffffffffu, f2ord(x[r]));
+              red[ROWS + r] = __reduce_max_sync(0xffffffffu, f2ord(x[r] + l2v0));
+              red[2 * ROWS + r] = __reduce_max_sync(0xffffffffu, f2ord(x[r] + l2v1));
+            }
 #pragma unroll
-          for (int e = 0; e < NX; ++e) {
-            mx[e] = xi[e];
+            for (int e = NX; e < NX4 * 4; ++e) red[e] = 0;
+            if (lane == 0)
 #pragma unroll
-            for (int w = 1; w < 4; ++w) mx[e] = max(mx[e], xi[w * NX + e]);
+              for (int e = 0; e < NX4; ++e)
+                xch[(par * 4 + wq) * NX4 + e] =
+                    make_int4(red[4 * e], red[4 * e + 1], red[4 * e + 2], red[4 * e + 3]);
           }
+          if (bar_or(bid, 128, bad || *abort_flag != 0)) {
+            bad = true;
+            break;
+          }
+          float mnew[ROWS], alpha[ROWS], inv_sp[2][ROWS], sp[2][ROWS];
+          {
+            int mx[NX4 * 4];
+#pragma unroll
+            for (int e = 0; e < NX4; ++e) {
+              int4 a = xch[(par * 4 + 0) * NX4 + e];
+#pragma unroll
+              for (int w = 1; w < 4; ++w) {
+                const int4 b = xch[(par * 4 + w) * NX4 + e];
+                a = make_int4(max(a.x, b.x), max(a.y, b.y), max(a.z, b.z), max(a.w, b.w));
+              }
+              mx[4 * e] = a.x;
+              mx[4 * e + 1] = a.y;
+              mx[4 * e + 2] = a.z;
+              mx[4 * e + 3] = a.w;
+            }
+#pragma unroll
+            for (int r = 0; r < ROWS; ++r) {
+              mnew[r] = fmaxf(m[r], ord2f(mx[r]));
+              alpha[r] = fast_exp2(m[r] - mnew[r]);
+              m[r] = mnew[r];
+#pragma unroll
+              for (int g = 0; g < 2; ++g) {
+                // largest |p s_V| of the tile = 2^(ymax - mnew), taken with a
+                // little headroom for the approximate log / exp: sP = that / 32767
+                const float e = ord2f(mx[(1 + g) * ROWS + r]) - mnew[r];
+                const bool any = e > -INFINITY;
+                sp[g][r] = any ? fast_exp2(e) * (1.000244140625f / 32767.f) : 0.f;
+                inv_sp[g][r] = any ? fast_exp2(-e) * (32767.f / 1.000244140625f) : 0.f;
+              }
+            }
+          }
+          // weights, the running sums, the P' operand of both groups of dims
+          uint32_t u0[ROWS], u1[ROWS];
 #pragma unroll
           for (int r = 0; r < ROWS; ++r) {
-            mnew[r] = fmaxf(m[r], ord2f(mx[r]));
-            alpha[r] = fast_exp2(m[r] - mnew[r]);
-            m[r] = mnew[r];
+            const float pr = valid ? fast_exp2(x[r] - mnew[r]) : 0.f;
+            l[r] = fmaf(l[r], alpha[r], pr);
+            rb[0][r] = fmaf(rb[0][r], alpha[r], valid ? pr * bv.x : 0.f);
+            rb[1][r] = fmaf(rb[1][r], alpha[r], valid ? pr * bv.y : 0.f);
+            const int q0 = valid ? __float2int_rn(pr * sv.x * inv_sp[0][r]) : 0;
+            const int q1 = valid ? __float2int_rn(pr * sv.y * inv_sp[1][r]) : 0;
+            u0[r] = static_cast<uint32_t>(max(-32767, min(32767, q0)) + 32768);
+            u1[r] = static_cast<uint32_t>(max(-32767, min(32767, q1)) + 32768);
+          }
+          // P'[buf] was read by PV(i - 2)
+          if (i >= 2 && !bad && !wait_b(kOFull + buf, ((i - 2) >> 1) & 1)) bad = true;
+          store_brow<ROWS, C::kUnits>(smem + C::kPb + (buf * 2 + 0) * C::kBop, tok, u0);
+          store_brow<ROWS, C::kUnits>(smem + C::kPb + (buf * 2 + 1) * C::kBop, tok, u1);
+          fence_proxy_async_smem();
+          // the group's P' is complete: its first warp issues PV(i) itself
+          // (a polling issuer elsewhere adds its loop time to every tile)
+          if (bar_or(bid, 128, bad || *abort_flag != 0)) {
+            bad = true;
+            break;
+          }
+          if (wq == 0) {
+            // O buffer free (O(i - 2) read by the dim role), 4-bit V widened
+            bool r = true;
+            if (lane == 0)
+              r = (i < 2 || wait_b(kOEmpty + buf, ((i - 2) >> 1) & 1)) &&
+                  (BITS == 8 || wait_b(kVx + i % S, (i / S) & 1));
+            if (__shfl_sync(0xffffffffu, r, 0)) {
+              tc::fence_after_sync();
+              const uint32_t vc = stage_u(i % S) + C::kVc;
 #pragma unroll
-            for (int g = 0; g < 2; ++g) {
-              // bound >= max_t |p s_V| (a little headroom for the approximate log / exp)
-              const float bound = fast_exp2(ord2f(mx[(1 + g) * ROWS + r]) - mnew[r]) * 1.000244140625f;
-              sp[g][r] = bound * (1.f / 32767.f);
-              inv_sp[g][r] = bound > 0.f ? 32767.f / bound : 0.f;
+              for (int g = 0; g < 2; ++g) {
+                const uint32_t pb = sbase + C::kPb + (buf * 2 + g) * C::kBop;
+#pragma unroll
+                for (int kk = 0; kk < kT / 32; ++kk)
+                  tc::mma_i8_elect(tmem + kO0 + buf * 2 * NB + g * NB,
+                                   tc::smem_desc_sw128(vc + 4096 * kk, 16384, 1024),
+                                   tc::smem_desc_none(pb + 512 * kk, 128, 2048), idPV, kk > 0);
+              }
+              tc::commit_elect(bar(kOFull + buf));
+              tc::commit_elect(bar(kEmpty + i % S));
+              pv_issued = true;
+            } else {
+              bad = true;
+              if (lane == 0) give_up();  // the group stops at its next barrier
+            }
+            if (lane == 0) {
+              // the dim role's factors for this tile (tp[buf] was read for tile i - 2)
+#pragma unroll
+              for (int r = 0; r < ROWS; ++r) {
+                tp[buf * 3 * ROWS + r] = alpha[r];
+                tp[buf * 3 * ROWS + ROWS + r] = sp[0][r];
+                tp[buf * 3 * ROWS + 2 * ROWS + r] = sp[1][r];
+              }
+              mbar_arrive1(bar(kTpB + buf));
             }
           }
         }
-        // weights, the running sums, the P' operand of both groups
-        uint32_t u0[ROWS], u1[ROWS];
-#pragma unroll
-        for (int r = 0; r < ROWS; ++r) {
-          const float pr = valid ? fast_exp2(x[r] - mnew[r]) : 0.f;
-          l[r] = fmaf(l[r], alpha[r], pr);
-          rb[0][r] = fmaf(rb[0][r], alpha[r], valid ? pr * bv.x : 0.f);
-          rb[1][r] = fmaf(rb[1][r], alpha[r], valid ? pr * bv.y : 0.f);
-          const int q0 = valid ? __float2int_rn(pr * sv.x * inv_sp[0][r]) : 0;
-          const int q1 = valid ? __float2int_rn(pr * sv.y * inv_sp[1][r]) : 0;
-          u0[r] = static_cast<uint32_t>(max(-32767, min(32767, q0)) + 32768);
-          u1[r] = static_cast<uint32_t>(max(-32767, min(32767, q1)) + 32768);
-        }
-        // P'[buf] was read by PV(i - 2)
-        if (i >= 2 && !bad && !wait_b(kOFull + buf, ((i - 2) >> 1) & 1)) bad = true;
-        store_brow<ROWS, C::kUnits>(smem + C::kPb + (buf * 2 + 0) * C::kBop, tok, u0);
-        store_brow<ROWS, C::kUnits>(smem + C::kPb + (buf * 2 + 1) * C::kBop, tok, u1);
-        fence_proxy_async_smem();
-        mbar_arrive1(bar(kPFull + buf));
-        if (tok == 0) {
-          // the dim role's factors for this tile (tp[buf] was read for tile i - 2)
-          if (i >= 2 && !bad && !wait_b(kOEmpty + buf, ((i - 2) >> 1) & 1)) bad = true;
-#pragma unroll
-          for (int r = 0; r < ROWS; ++r) {
-            tp[buf * 3 * ROWS + r] = alpha[r];
-            tp[buf * 3 * ROWS + ROWS + r] = sp[0][r];
-            tp[buf * 3 * ROWS + 2 * ROWS + r] = sp[1][r];
-          }
-          mbar_arrive1(bar(kTpB + buf));
-        }
-        if (first && i + 1 < cnt) {
-          // prefetch the next piece's Q: its buffer's last QKs (piece k - 1)
-          // completed before this piece's first scores
-          const TCur nx = next_pair(c, p);
-          const int pend = x0 + i + (c.n - c.t);  // one past this pair in the flat list
-          if (k >= 1 && pend < x0 + cnt) write_q(k + 1, nx);
-        }
         if (last) {
-          // the piece's row sums and bias sums over the 128 tokens
+          // the group's row sums and bias sums of the piece over its tokens
+          // (zero, with m = -inf, when it had no tile of the piece)
           float v[3 * ROWS];
 #pragma unroll
           for (int r = 0; r < ROWS; ++r) {
@@ -701,13 +762,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (lane == 0)
 #pragma unroll
             for (int e = 0; e < 3 * ROWS; ++e) lx[wq * 3 * ROWS + e] = v[e];
-          if (bar_or(kBarTok, 128, bad || *abort_flag != 0)) {
+          if (bar_or(bid, 128, bad || *abort_flag != 0)) {
             bad = true;
             break;
           }
           if (tok == 0) {
             if (k >= 2 && !bad && !wait_b(kPeEmpty + (k & 1), ((k - 2) >> 1) & 1)) bad = true;
-            float *pk = pe + (k & 1) * 4 * ROWS;
+            float *pk = pe + ((k & 1) * TGN + tg) * 4 * ROWS;
 #pragma unroll
             for (int e = 0; e < 3 * ROWS; ++e)
               pk[ROWS + e] = (lx[e] + lx[3 * ROWS + e]) + (lx[6 * ROWS + e] + lx[9 * ROWS + e]);
@@ -715,20 +776,83 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int r = 0; r < ROWS; ++r) pk[r] = m[r];
             mbar_arrive1(bar(kPeB + (k & 1)));
           }
-          bar_sync_n(kBarTok, 128);  // lx read before the next piece writes it
+          bar_sync_n(bid, 128);  // lx read before the next piece writes it
         }
         adv(c, p);
       }
     }
+    // this warp's PVs complete before the TMEM is freed
+    if (pv_issued) {
+      tc::commit_elect(bar(kDrainT + tg));
+      (void)wait_b(kDrainT + tg, 0);
+    }
     if (bad && lane == 0) give_up();
-  } else {
+  }
+  else {
     // ---------------- dim role ----------------
     const int q = 32 * (warp & 3) + lane;  // operand row = TMEM lane
     const int dim = dim_of<BITS>(q);
     const int g = q >> 6;
+    const int wq = warp & 3;  // quadrants 0, 1 hold dims of group 0, quadrants 2, 3 group 1
     const uint32_t tl = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
     const float *tp = reinterpret_cast<const float *>(misc + C::kTp);
     const float *pe = reinterpret_cast<const float *>(misc + C::kPe);
+    int *qx = reinterpret_cast<int *>(misc + C::kQx);
+    float *qp = reinterpret_cast<float *>(misc + C::kQp);
+    float *qs = reinterpret_cast<float *>(misc + C::kQs);
+
+    // Q operand of a piece (pair c) into buffer kk & 1, with its scale and
+    // per-group sums for the token groups; thread = operand row (head dim
+    // dim_of(q)).  Plain named barriers: no waits inside.
+    auto write_q = [&](int kk, const TCur &c) {
+      float qv[ROWS];
+      uint32_t am[ROWS];
+#pragma unroll
+      for (int r = 0; r < ROWS; ++r) {
+        qv[r] = ld_q(p.q, row_offset(p.q_sb, p.q_st, p.q_sh, c.b, c.h, r, p.G) + dim, p.q_bf16);
+        am[r] = __reduce_max_sync(0xffffffffu, __float_as_uint(fabsf(qv[r])));
+      }
+      if (lane == 0)
+#pragma unroll
+        for (int r = 0; r < ROWS; ++r) qx[wq * ROWS + r] = static_cast<int>(am[r]);
+      bar_sync_n(C::kBarDim, 128);
+      float inv[ROWS], sq[ROWS];
+#pragma unroll
+      for (int r = 0; r < ROWS; ++r) {
+        uint32_t mxv = 0;
+#pragma unroll
+        for (int w = 0; w < 4; ++w) mxv = max(mxv, static_cast<uint32_t>(qx[w * ROWS + r]));
+        const float amax = __uint_as_float(mxv);
+        sq[r] = amax / 32767.f;
+        inv[r] = amax > 0.f ? 32767.f / amax : 0.f;
+      }
+      bar_sync_n(C::kBarDim, 128);  // every thread has read qx
+      uint32_t u[ROWS];
+      int isum[ROWS];
+#pragma unroll
+      for (int r = 0; r < ROWS; ++r) {
+        const int qi = max(-32767, min(32767, __float2int_rn(qv[r] * inv[r])));
+        u[r] = static_cast<uint32_t>(qi + 32768);
+        isum[r] = __reduce_add_sync(0xffffffffu, qi);
+      }
+      if (lane == 0)
+#pragma unroll
+        for (int r = 0; r < ROWS; ++r) qx[wq * ROWS + r] = isum[r];
+      store_brow<ROWS, C::kUnits>(smem + C::kQb + (kk & 1) * C::kBop, q, u);
+      fence_proxy_async_smem();
+      bar_sync_n(C::kBarDim, 128);
+      if (q == 0) {
+#pragma unroll
+        for (int r = 0; r < ROWS; ++r) {
+          qp[(kk & 1) * ROWS + r] = sq[r];
+          qs[((kk & 1) * 2 + 0) * ROWS + r] = sq[r] * static_cast<float>(qx[0 * ROWS + r] + qx[1 * ROWS + r]);
+          qs[((kk & 1) * 2 + 1) * ROWS + r] = sq[r] * static_cast<float>(qx[2 * ROWS + r] + qx[3 * ROWS + r]);
+        }
+      }
+      bar_sync_n(C::kBarDim, 128);  // qp / qs written, qx free again
+      mbar_arrive1(bar(kQFull + (kk & 1)));
+    };
+
     // sequences without context: zero outputs (CTA b mod grid)
     for (int b = blockIdx.x; b < p.B; b += gridDim.x) {
       if (clamped_ctx(p, b) != 0) continue;
@@ -740,45 +864,52 @@ __global__ void __launch_bounds__(kThreads, 1)
     bool bad = false;
     if (cnt > 0) {
       TCur c = locate_tc(p, x0, lane);
-      float o[ROWS];
+      write_q(0, c);
+      // the second piece's Q, if the share reaches past the first pair
+      if (x0 + (c.n - c.t) < x0 + cnt) write_q(1, next_pair(c, p));
+      float o[TGN][ROWS];
 #pragma unroll
-      for (int r = 0; r < ROWS; ++r) o[r] = 0.f;
-      if constexpr (BITS == 4) {
-        if (!wait_b(kFull + 0, 0)) bad = true;
-        widen_row(stage(0) + C::kVr, stage(0) + C::kVc, q);
+      for (int t = 0; t < TGN; ++t)
+#pragma unroll
+        for (int r = 0; r < ROWS; ++r) o[t][r] = 0.f;
+      // 4-bit: tile j's codes are widened kWidenAhead tiles before the dim
+      // role reaches it (its stage was loaded after PV(j - S), long done)
+      auto widen = [&](int j) {
+        const int sj = j % S;
+        if (!bad && !wait_b(kFull + sj, (j / S) & 1)) bad = true;
+        widen_row(stage(sj) + C::kKr, stage(sj) + C::kKc, q);
+        widen_row(stage(sj) + C::kVr, stage(sj) + C::kVc, q);
         fence_proxy_async_smem();
-        mbar_arrive1(bar(kVx + 0));
-      }
+        mbar_arrive1(bar(kKx + sj));
+        mbar_arrive1(bar(kVx + sj));
+      };
+      if constexpr (BITS == 4)
+        for (int j = 0; j < C::kWidenAhead && j < cnt; ++j) widen(j);
       int k = -1;
       for (int i = 0; i < cnt; ++i) {
         const int buf = i & 1;
         const bool first = (i == 0) || (c.t == 0);
         const bool last = (i == cnt - 1) || (c.t == c.n - 1);
-        if (first) ++k;
+        if (first) {
+          ++k;
+          // the next piece's Q: every QK of the piece before this one is
+          // complete (O of the tile before has been read)
+          if (k >= 1 && x0 + i + (c.n - c.t) < x0 + cnt) write_q(k + 1, next_pair(c, p));
+        }
         if constexpr (BITS == 4) {
-          if (i + 1 < cnt) {
-            const int s1 = (i + 1) % S;
-            if (!bad && !wait_b(kFull + s1, ((i + 1) / S) & 1)) bad = true;
-            widen_row(stage(s1) + C::kVr, stage(s1) + C::kVc, q);
-            fence_proxy_async_smem();
-            mbar_arrive1(bar(kVx + s1));
-          }
+          if (i + C::kWidenAhead < cnt) widen(i + C::kWidenAhead);
         }
         if (!bad && !(wait_b(kOFull + buf, (i >> 1) & 1) && wait_b(kTpB + buf, (i >> 1) & 1)))
           bad = true;
         if (__any_sync(0xffffffffu, bad)) bad = true;
         tc::fence_after_sync();
         uint32_t orr[NB];
-        if constexpr (NB == 16) {
-          tc::ld16(tl + kO0 + buf * 2 * NB + g * NB, orr);
-        } else {
 #pragma unroll
-          for (int j = 0; j < NB; j += 16) {
-            uint32_t r16[16];
-            tc::ld16(tl + kO0 + buf * 2 * NB + g * NB + j, r16);
+        for (int j = 0; j < NB; j += 16) {
+          uint32_t r16[16];
+          tc::ld16(tl + kO0 + buf * 2 * NB + g * NB + j, r16);
 #pragma unroll
-            for (int e = 0; e < 16; ++e) orr[j + e] = r16[e];
-          }
+          for (int e = 0; e < 16; ++e) orr[j + e] = r16[e];
         }
         tc::wait_ld();
         float alpha[ROWS], spg[ROWS];
@@ -789,20 +920,36 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         tc::fence_before_sync();
         mbar_arrive1(bar(kOEmpty + buf));
+        const int gi = i % TGN;
 #pragma unroll
-        for (int r = 0; r < ROWS; ++r) {
-          const int v = static_cast<int>(orr[r] * 256u + orr[ROWS + r] - (orr[2 * ROWS] << 15));
-          o[r] = fmaf(o[r], alpha[r], spg[r] * static_cast<float>(v));
-        }
-        if (last) {
-          if (!bad && !wait_b(kPeB + (k & 1), (k >> 1) & 1)) bad = true;
-          const float *pk = pe + (k & 1) * 4 * ROWS;
-          float mr[ROWS], lr[ROWS], br[ROWS];
+        for (int t = 0; t < TGN; ++t) {
+          if (t != gi) continue;
 #pragma unroll
           for (int r = 0; r < ROWS; ++r) {
-            mr[r] = pk[r];
-            lr[r] = pk[ROWS + r];
-            br[r] = pk[(2 + g) * ROWS + r];
+            const int v = static_cast<int>(orr[r] * 256u + orr[ROWS + r] - (orr[2 * ROWS] << 15));
+            o[t][r] = fmaf(o[t][r], alpha[r], spg[r] * static_cast<float>(v));
+          }
+        }
+        if (last) {
+          // combine the token groups' states: weights 2^(m_g - M)
+          if (!bad && !wait_b(kPeB + (k & 1), (k >> 1) & 1)) bad = true;
+          float mr[ROWS], lr[ROWS], num[ROWS];
+#pragma unroll
+          for (int r = 0; r < ROWS; ++r) {
+            float M = -INFINITY;
+#pragma unroll
+            for (int t = 0; t < TGN; ++t) M = fmaxf(M, pe[((k & 1) * TGN + t) * 4 * ROWS + r]);
+            float L = 0.f, n = 0.f;
+#pragma unroll
+            for (int t = 0; t < TGN; ++t) {
+              const float *pk = pe + ((k & 1) * TGN + t) * 4 * ROWS;
+              const float w = pk[r] > -INFINITY ? fast_exp2(pk[r] - M) : 0.f;
+              L = fmaf(w, pk[ROWS + r], L);
+              n = fmaf(w, o[t][r] + pk[(2 + g) * ROWS + r], n);
+            }
+            mr[r] = M;
+            lr[r] = L;
+            num[r] = n;
           }
           mbar_arrive1(bar(kPeEmpty + (k & 1)));
           const int bh = c.b * p.Hkv + c.h;
@@ -812,27 +959,26 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
             for (int r = 0; r < ROWS; ++r)
               store_one(p, row_offset(p.o_sb, p.o_st, p.o_sh, c.b, c.h, r, p.G) + dim,
-                        (o[r] + br[r]) / lr[r]);
+                        num[r] / lr[r]);
           } else {
             // partial of this piece; the last piece to arrive merges them all
             const int64_t slot = (int64_t)blockIdx.x + bh;
 #pragma unroll
-            for (int r = 0; r < ROWS; ++r)
-              p.part[(slot * ROWS + r) * kD + dim] = o[r] + br[r];
+            for (int r = 0; r < ROWS; ++r) p.part[(slot * ROWS + r) * kD + dim] = num[r];
             if (q == 0)
 #pragma unroll
               for (int r = 0; r < ROWS; ++r)
                 *reinterpret_cast<float2 *>(p.ml + (slot * ROWS + r) * 2) = make_float2(mr[r], lr[r]);
             __threadfence();
-            if (bar_or(kBarDim, 128, bad || *abort_flag != 0)) {
+            if (bar_or(C::kBarDim, 128, bad || *abort_flag != 0)) {
               bad = true;
               break;
             }
             const int nparts = ul - uf + 1;
             if (q == 0) *merge_word = atomicAdd(p.counters + bh, 1);
-            bar_sync_n(kBarDim, 128);
+            bar_sync_n(C::kBarDim, 128);
             const int old = *merge_word;
-            bar_sync_n(kBarDim, 128);  // merge_word read before it is written again
+            bar_sync_n(C::kBarDim, 128);  // merge_word read before it is written again
             if (old == nparts - 1) {
               __threadfence();
 #pragma unroll
@@ -840,21 +986,23 @@ __global__ void __launch_bounds__(kThreads, 1)
                 float M = -INFINITY;
                 for (int u = 0; u < nparts; ++u)
                   M = fmaxf(M, __ldcg(p.ml + (((int64_t)uf + u + bh) * ROWS + r) * 2));
-                float num = 0.f, den = 0.f;
+                float nm = 0.f, den = 0.f;
                 for (int u = 0; u < nparts; ++u) {
                   const int64_t sl = (int64_t)uf + u + bh;
                   const float2 ml = __ldcg(reinterpret_cast<const float2 *>(p.ml + (sl * ROWS + r) * 2));
                   const float w = fast_exp2(ml.x - M);
-                  num = fmaf(__ldcg(p.part + (sl * ROWS + r) * kD + dim), w, num);
+                  nm = fmaf(__ldcg(p.part + (sl * ROWS + r) * kD + dim), w, nm);
                   den = fmaf(ml.y, w, den);
                 }
-                store_one(p, row_offset(p.o_sb, p.o_st, p.o_sh, c.b, c.h, r, p.G) + dim, num / den);
+                store_one(p, row_offset(p.o_sb, p.o_st, p.o_sh, c.b, c.h, r, p.G) + dim, nm / den);
               }
               if (q == 0) p.counters[bh] = 0;
             }
           }
 #pragma unroll
-          for (int r = 0; r < ROWS; ++r) o[r] = 0.f;
+          for (int t = 0; t < TGN; ++t)
+#pragma unroll
+            for (int r = 0; r < ROWS; ++r) o[t][r] = 0.f;
         }
         adv(c, p);
       }
@@ -895,7 +1043,7 @@ int launch_one(const Params &p, const CUtensorMap &tk, const CUtensorMap &tv, in
                                cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<BITS, ROWS>::kSmemBytes);
   });
   if (err != cudaSuccess) return cuda_fail(err, "quantised decode (tcgen05): shared memory attribute");
-  paged_decode_qtc_kernel<BITS, ROWS><<<grid, kThreads, Cfg<BITS, ROWS>::kSmemBytes, s>>>(tk, tv, p);
+  paged_decode_qtc_kernel<BITS, ROWS><<<grid, Cfg<BITS, ROWS>::kThreads, Cfg<BITS, ROWS>::kSmemBytes, s>>>(tk, tv, p);
   MZ_CHECK_LAUNCH("mz_paged_decode_q (tcgen05)");
   return MZ_OK;
 }

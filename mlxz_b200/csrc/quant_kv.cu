@@ -226,6 +226,21 @@ __device__ __forceinline__ uint32_t nib2_biased(uint32_t x) {
   return (x & 0x000F000Fu) | 0x64006400u;
 }
 
+// Codes enter the mma centred on the middle of their range (code - 128 for
+// 8-bit, code - 8 for 4-bit; exact in fp16): with the 1024 of the magic
+// bias left in, a whole context's P.V sums carry 1024 * sum P' and lose the
+// result to cancellation once that is removed.
+template <int BITS>
+constexpr float kCodeCentre = BITS == 8 ? 128.f : 8.f;
+template <int BITS>
+constexpr uint32_t kCentreBits = BITS == 8 ? 0x64806480u : 0x64086408u;  // half2 of 1024 + centre
+template <int BITS>
+__device__ __forceinline__ uint32_t centred(uint32_t biased) {
+  uint32_t r;
+  asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(biased), "r"(kCentreBits<BITS>));
+  return r;
+}
+
 __device__ __forceinline__ float load_q16(const uint16_t *q, int64_t off, bool bf16) {
   const uint16_t b = q[off];
   return bf16 ? __uint_as_float(static_cast<uint32_t>(b) << 16) : __half2float(__ushort_as_half(b));
@@ -233,11 +248,11 @@ __device__ __forceinline__ float load_q16(const uint16_t *q, int64_t off, bool b
 
 // Transposed formulation: tokens (QK) and head dims (PV) are the M = 16 side
 // of mma.m16n8k16, the query rows of a KV head the N = 8 side (NR tiles of 8).
-//   QK:  S^T[tok][row] = sum_k A[tok][k] * B[k][row], A = K codes + 1024 (the
-//        fp16 magic bias, removed through the bias term with sum_k Q) over a
-//        permutation pi of the head dim, B = Q with the same permutation;
-//   PV:  O^T[d][row] = sum_t A[d][t] * B[t][row], A = V codes (+1024, the
-//        fp16 magic bias, removed through sum_t P'), B = P'^T by movmatrix.
+//   QK:  S^T[tok][row] = sum_k A[tok][k] * B[k][row], A = K codes - centre
+//        (restored through the bias term with sum_k Q) over a permutation pi
+//        of the head dim, B = Q with the same permutation;
+//   PV:  O^T[d][row] = sum_t A[d][t] * B[t][row], A = V codes - centre
+//        (restored through sum_t P'), B = P'^T by movmatrix.
 template <int D, int BITS, int NR>
 __global__ void __launch_bounds__(kWarps * 32, QCfg<D, BITS, NR>::kCtas)
     paged_decode_q_kernel(const __grid_constant__ CUtensorMap tmK,
@@ -309,9 +324,9 @@ __global__ void __launch_bounds__(kWarps * 32, QCfg<D, BITS, NR>::kCtas)
 
   uint32_t qb[NR][NG][4][2];  // Q B-fragments: row 8*nr + g, k-step w of group G
   float qs[NR][2][NG];        // sum of Q over group G, rows 8*nr + 2c + {0,1}
-  float oacc[NR][MT][4];      // O^T (biased by 1024 * sum P'), P-scaled
+  float oacc[NR][MT][4];      // O^T (less centre * sum P'), P-scaled
   float rb[NR][2][NG];        // sum_t p * b_v (lane partial over its tokens g, g+8)
-  float cp[NR][2][NG];        // sum_t P' (lane partial) -- removes the +1024 bias
+  float cp[NR][2][NG];        // sum_t P' (lane partial) -- restores the centre
   float mrow[NR][2], lrow[NR][2];
 
   UnitReader ur;
@@ -402,10 +417,10 @@ __global__ void __launch_bounds__(kWarps * 32, QCfg<D, BITS, NR>::kCtas)
 #pragma unroll
         for (int w = 0; w < 4; ++w) {
           uint32_t a[4];
-          a[0] = __byte_perm(w0[w], kMagic, 0x4140);  // 1024 + code
-          a[1] = __byte_perm(w1[w], kMagic, 0x4140);
-          a[2] = __byte_perm(w0[w], kMagic, 0x4342);
-          a[3] = __byte_perm(w1[w], kMagic, 0x4342);
+          a[0] = centred<8>(__byte_perm(w0[w], kMagic, 0x4140));  // code - 128
+          a[1] = centred<8>(__byte_perm(w1[w], kMagic, 0x4140));
+          a[2] = centred<8>(__byte_perm(w0[w], kMagic, 0x4342));
+          a[3] = centred<8>(__byte_perm(w1[w], kMagic, 0x4342));
 #pragma unroll
           for (int nr = 0; nr < NR; ++nr) mma_16816<false>(acc[nr][G], a, qb[nr][G][w][0], qb[nr][G][w][1]);
         }
@@ -417,10 +432,10 @@ __global__ void __launch_bounds__(kWarps * 32, QCfg<D, BITS, NR>::kCtas)
           const uint32_t x0 = (w >> 1) ? k0.y : k0.x, x1 = (w >> 1) ? k1.y : k1.x;
           const int j0 = 2 * (w & 1);
           uint32_t a[4];
-          a[0] = nib2_biased(x0 >> (4 * j0));  // 1024 + code
-          a[1] = nib2_biased(x1 >> (4 * j0));
-          a[2] = nib2_biased(x0 >> (4 * (j0 + 1)));
-          a[3] = nib2_biased(x1 >> (4 * (j0 + 1)));
+          a[0] = centred<4>(nib2_biased(x0 >> (4 * j0)));  // code - 8
+          a[1] = centred<4>(nib2_biased(x1 >> (4 * j0)));
+          a[2] = centred<4>(nib2_biased(x0 >> (4 * (j0 + 1))));
+          a[3] = centred<4>(nib2_biased(x1 >> (4 * (j0 + 1))));
 #pragma unroll
           for (int nr = 0; nr < NR; ++nr) mma_16816<false>(acc[nr][G], a, qb[nr][G][w][0], qb[nr][G][w][1]);
         }
@@ -446,10 +461,10 @@ __global__ void __launch_bounds__(kWarps * 32, QCfg<D, BITS, NR>::kCtas)
             bkv[ts][G] = __half2float(kbi[tok_of<C>(g + 8 * ts) * NG + G]);
           }
         }
-        // the K codes entered the mma as 1024 + code: fold 1024 * s * sum(Q)
-        // into the bias term
+        // the K codes entered the mma centred: fold centre * s * sum(Q) into
+        // the bias term
 #pragma unroll
-        for (int G = 0; G < NG; ++G) bkv[ts][G] = fmaf(-1024.f, skv[ts][G], bkv[ts][G]);
+        for (int G = 0; G < NG; ++G) bkv[ts][G] = fmaf(kCodeCentre<BITS>, skv[ts][G], bkv[ts][G]);
       }
 #pragma unroll
       for (int nr = 0; nr < NR; ++nr)
@@ -506,7 +521,7 @@ __global__ void __launch_bounds__(kWarps * 32, QCfg<D, BITS, NR>::kCtas)
       }
     }
 
-    // ---- O^T += (V codes + 1024) . (p * s_v)^T ; rb += p * b_v ; cp += P' ----
+    // ---- O^T += (V codes - centre) . (p * s_v)^T ; rb += p * b_v ; cp += P' ----
     // V scales (pre-multiplied by the P' scale) and biases of this lane's
     // tokens g, g+8 for every group; 0 past the context
     float svg[2][NG], bvg[2][NG];
@@ -560,10 +575,10 @@ __global__ void __launch_bounds__(kWarps * 32, QCfg<D, BITS, NR>::kCtas)
         for (int v = 0; v < 4; ++v) {
           const uint32_t sel = (v & 1) ? 0x4342u : 0x4140u;
           uint32_t a[4];
-          a[0] = __byte_perm((v < 2) ? lo01a : lo23a, kMagic, sel);  // d = 64G+8g+v, tokens 2c,2c+1
-          a[1] = __byte_perm((v < 2) ? hi01a : hi23a, kMagic, sel);  // d + 4
-          a[2] = __byte_perm((v < 2) ? lo01b : lo23b, kMagic, sel);  // tokens 2c+8, 2c+9
-          a[3] = __byte_perm((v < 2) ? hi01b : hi23b, kMagic, sel);
+          a[0] = centred<8>(__byte_perm((v < 2) ? lo01a : lo23a, kMagic, sel));  // d = 64G+8g+v, tokens 2c,2c+1
+          a[1] = centred<8>(__byte_perm((v < 2) ? hi01a : hi23a, kMagic, sel));  // d + 4
+          a[2] = centred<8>(__byte_perm((v < 2) ? lo01b : lo23b, kMagic, sel));  // tokens 2c+8, 2c+9
+          a[3] = centred<8>(__byte_perm((v < 2) ? hi01b : hi23b, kMagic, sel));
 #pragma unroll
           for (int nr = 0; nr < NR; ++nr) mma_16816<false>(oacc[nr][4 * G + v], a, pb[nr][0], pb[nr][1]);
         }
@@ -579,10 +594,10 @@ __global__ void __launch_bounds__(kWarps * 32, QCfg<D, BITS, NR>::kCtas)
           const uint32_t sh = static_cast<uint32_t>((2 + (v >> 1)) | ((6 + (v >> 1)) << 8));
           const int sft = 4 * (v & 1);
           uint32_t a[4];
-          a[0] = nib2_biased(__byte_perm(v0, v1, sl) >> sft);
-          a[1] = nib2_biased(__byte_perm(v0, v1, sh) >> sft);
-          a[2] = nib2_biased(__byte_perm(v2, v3, sl) >> sft);
-          a[3] = nib2_biased(__byte_perm(v2, v3, sh) >> sft);
+          a[0] = centred<4>(nib2_biased(__byte_perm(v0, v1, sl) >> sft));
+          a[1] = centred<4>(nib2_biased(__byte_perm(v0, v1, sh) >> sft));
+          a[2] = centred<4>(nib2_biased(__byte_perm(v2, v3, sl) >> sft));
+          a[3] = centred<4>(nib2_biased(__byte_perm(v2, v3, sh) >> sft));
 #pragma unroll
           for (int nr = 0; nr < NR; ++nr) mma_16816<false>(oacc[nr][4 * G + v], a, pb[nr][0], pb[nr][1]);
         }
@@ -615,7 +630,7 @@ __global__ void __launch_bounds__(kWarps * 32, QCfg<D, BITS, NR>::kCtas)
               c += __shfl_xor_sync(0xffffffffu, c, o);
             }
             Rg[G] = r;
-            Cg[G] = c * 1024.f;
+            Cg[G] = -c * kCodeCentre<BITS>;  // the V codes entered centred
           }
           const int row = 8 * nr + 2 * cq + rs;
           if (row >= p.rows) continue;
@@ -900,10 +915,10 @@ extern "C" int mz_paged_decode_q(void *out, int32_t out_dtype, int64_t out_seq_s
 
   const int64_t rows_total = n_blocks * n_kv_heads * block_size;
   // The tensor-core form (head_dim 128; 1, 2, 4, 8 or 16 query rows per KV
-  // head) when MLXZ_B200_QDECODE_TC=1, else the mma.sync kernel.  Its grid is
-  // one CTA per SM, or fewer when num_warps caps the launch (its partials then
-  // fit the workspace sized for num_warps).
-  if (qtc_supports(head_dim, rows) && env_int("MLXZ_B200_QDECODE_TC", 0, 0, 1) == 1) {
+  // head) unless MLXZ_B200_QDECODE_TC=0, else the mma.sync kernel.  Its grid
+  // is one CTA per SM, or fewer when num_warps caps the launch (its partials
+  // then fit the workspace sized for num_warps).
+  if (qtc_supports(head_dim, rows) && env_int("MLXZ_B200_QDECODE_TC", 1, 0, 1) == 1) {
     const int sms = sm_count(device);
     if (sms <= 0) return fail(MZ_ERR_CUDA, "%s: cannot query SM count of device %d", fn, device);
     int grid = sms;
