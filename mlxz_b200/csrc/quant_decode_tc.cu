@@ -72,10 +72,15 @@ struct Cfg {
   // token groups: two (alternate tiles, each with its own online-softmax
   // state) when the registers allow it, else one
   static constexpr int TGN = ROWS <= 4 ? 2 : 1;
+  // softmax units per tile (each with its own max, P' scale and PV): one
+  // warp of 32 tokens for up to 4 query rows, two warps for 8, four for 16
+  // (the O columns of the units fill the TMEM)
+  static constexpr int U = ROWS <= 4 ? 4 : (ROWS <= 8 ? 2 : 1);
+  static constexpr int WPU = 4 / U;  // warps per unit
   static constexpr int kThreads = 64 + 128 * TGN + 128 + 32;
   static constexpr int kDimWarp0 = kTokWarp0 + 4 * TGN;
   static constexpr int kProdWarp2 = kDimWarp0 + 4;  // second copy warp (odd tiles)
-  static constexpr int kBarDim = 2 + TGN;  // named barrier of the dim role (token group g: 2 + g)
+  static constexpr int kBarDim = 2 + TGN * U;  // named barrier of the dim role (unit barriers below it)
   static constexpr int kBarProd = kBarDim + 1;  // named barrier of the two copy warps
   static constexpr int NB = ((2 * ROWS + 1 + 15) / 16) * 16;  // B operand columns
   static constexpr int kUnits = NB / 16;                      // 16-byte units per B row
@@ -97,9 +102,9 @@ struct Cfg {
   static constexpr int kQx = kXch + TGN * 2 * 4 * NX4 * 16;        // [4 warps][ROWS]
   static constexpr int kQp = kQx + 4 * ROWS * 4;                   // [2][ROWS] s_q
   static constexpr int kQs = kQp + 2 * ROWS * 4;                   // [2][2 groups][ROWS]
-  static constexpr int kTp = kQs + 2 * 2 * ROWS * 4;               // [2][3 ROWS]
-  static constexpr int kPe = kTp + 2 * 3 * ROWS * 4;               // [2][TGN][4 ROWS]
-  static constexpr int kLx = kPe + 2 * TGN * 4 * ROWS * 4;         // [TGN][4 warps][3 ROWS]
+  static constexpr int kTp = kQs + 2 * 2 * ROWS * 4;               // [2][U][3 ROWS]
+  static constexpr int kPe = kTp + 2 * U * 3 * ROWS * 4;           // [2][TGN][U][4 ROWS]
+  static constexpr int kLx = kPe + 2 * TGN * U * 4 * ROWS * 4;     // [TGN][4 warps][3 ROWS]
   static constexpr int kIds = kLx + TGN * 4 * 3 * ROWS * 4;  // [2 warps][4 tiles][8 sub-tiles] block ids
   static constexpr int kMiscBytes = kIds + 2 * 4 * 8 * 4;
   // as many stages as the shared memory holds (up to 8): the copies of
@@ -114,15 +119,17 @@ struct Cfg {
   static constexpr int kSmemBytes = kMisc + kMiscBytes + 1024;
   static_assert(kStages >= 3, "at least three stages");
   static_assert(BITS == 8 || kWidenAhead <= kStages - 2, "4-bit widening stays behind the copies");
-  static constexpr uint32_t kTmemCols = 8 * NB <= 128 ? 128 : (8 * NB <= 256 ? 256 : 512);
+  static constexpr int kCols = (4 + 4 * U) * NB;  // S [2][2][NB], O [2][U][2][NB]
+  static constexpr uint32_t kTmemCols = kCols <= 128 ? 128 : (kCols <= 256 ? 256 : 512);
+  static_assert(kCols <= 512, "TMEM columns");
   static_assert(kStage % 1024 == 0, "stages keep the 1024-byte alignment of the swizzled tiles");
   static_assert(kSmemBytes <= 227 * 1024, "shared memory");
 };
 
 // barrier slots
 constexpr int kFull = 0, kKx = 8, kVx = 16, kEmpty = 24, kSFull = 32, kSEmpty = 34, kQFull = 36,
-              kDrainT = 38, kTpB = 40, kOFull = 42, kOEmpty = 44, kPeB = 46, kPeEmpty = 48,
-              kDrain = 50, kNumBars = 51;
+              kTpB = 38, kOFull = 40, kOEmpty = 42, kPeB = 44, kPeEmpty = 46, kDrain = 48,
+              kDrainT = 49, kNumBars = 57;  // kDrainT: one per unit
 static_assert(8 * kNumBars <= 512, "barrier area");
 
 struct TCur {
@@ -347,20 +354,20 @@ __global__ void __launch_bounds__(Cfg<BITS, ROWS>::kThreads, 1)
       mbar_init(bar(kFull + s), 33);  // lane 0 (+ bulk tensor bytes) and 32 cp.async arrivals
       mbar_init(bar(kKx + s), 128);
       mbar_init(bar(kVx + s), 128);
-      mbar_init(bar(kEmpty + s), 1);
+      mbar_init(bar(kEmpty + s), C::U);  // the units' PV commits
     }
     for (int j = 0; j < 2; ++j) {
       mbar_init(bar(kSFull + j), 1);
       mbar_init(bar(kSEmpty + j), 128);
       mbar_init(bar(kQFull + j), 128);
-      mbar_init(bar(kDrainT + j), 1);
-      mbar_init(bar(kTpB + j), 1);
-      mbar_init(bar(kOFull + j), 1);
+      mbar_init(bar(kTpB + j), C::U);
+      mbar_init(bar(kOFull + j), C::U);
       mbar_init(bar(kOEmpty + j), 128);
-      mbar_init(bar(kPeB + j), TGN);
+      mbar_init(bar(kPeB + j), TGN * C::U);
       mbar_init(bar(kPeEmpty + j), 128);
     }
     mbar_init(bar(kDrain), 1);
+    for (int j = 0; j < TGN * C::U; ++j) mbar_init(bar(kDrainT + j), 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -369,7 +376,7 @@ __global__ void __launch_bounds__(Cfg<BITS, ROWS>::kThreads, 1)
   __syncthreads();
   tc::fence_after_sync();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t kS0 = 0, kO0 = 4 * NB;  // TMEM columns: S[buf][group], O[buf][group]
+  const uint32_t kS0 = 0, kO0 = 4 * NB;  // TMEM columns: S[buf][group], O[buf][unit][group]
 
   auto give_up = [&]() {
     dev_error(p.err, MZ_DEVERR_TIMEOUT);
@@ -549,21 +556,34 @@ __global__ void __launch_bounds__(Cfg<BITS, ROWS>::kThreads, 1)
   else if (warp < C::kDimWarp0) {
     // ---------------- token groups ----------------
     // Group tg takes the tiles i with i % TGN == tg; thread = token of the
-    // tile (TMEM lane).  Each group keeps its own online-softmax state for the
-    // piece and publishes it at the piece's end; the dim role combines them.
+    // tile (TMEM lane).  The group's tokens form U units (one warp each for
+    // up to 4 query rows, two warps for 8, four for 16), and each unit keeps
+    // its own online-softmax state for the piece, its own P' scale per tile
+    // and issues its own PV: no exchange between the warps of a group on the
+    // way from S to PV.  Units publish their state at the piece's end; the
+    // dim role combines them.
     const int tg = (warp - kTokWarp0) >> 2;
-    const int bid = 2 + tg;  // the group's named barrier
-    const int tok = 32 * (warp & 3) + lane;
-    const int wq = warp & 3;  // the warp's exchange slot
-    const uint32_t tl = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
+    const int wq = warp & 3;                       // warp within the group
+    const int u = wq / C::WPU;                     // unit within the group
+    const int ubar = 2 + tg * C::U + u;            // the unit's named barrier (WPU > 1)
+    const int uslot = tg * C::U + u;               // the unit's slot among all units
+    const bool issuer = (wq % C::WPU) == 0;        // the unit's first warp issues its PV
+    const int tok = 32 * wq + lane;
+    const uint32_t tl = tmem + (static_cast<uint32_t>(wq * 32) << 16);
     int4 *xch = reinterpret_cast<int4 *>(misc + C::kXch) + tg * 2 * 4 * C::NX4;
     const float *qp = reinterpret_cast<const float *>(misc + C::kQp);
     const float *qs = reinterpret_cast<const float *>(misc + C::kQs);
     float *tp = reinterpret_cast<float *>(misc + C::kTp);
     float *pe = reinterpret_cast<float *>(misc + C::kPe);
     float *lx = reinterpret_cast<float *>(misc + C::kLx) + tg * 4 * 3 * ROWS;
-    constexpr int NX = 3 * ROWS, NX4 = C::NX4;
+    constexpr int NX = 3 * ROWS, NX4 = C::NX4, WPU = C::WPU, U = C::U;
     constexpr uint32_t idPV = tc::idesc_u8(kD, NB, true, true);
+    // named barrier over the unit's warps (a warp barrier for one-warp units)
+    // that also ORs a failure flag across them
+    auto unit_or = [&](bool v) -> bool {
+      if constexpr (WPU == 1) return __any_sync(0xffffffffu, v);
+      else return bar_or(ubar, 32 * WPU, v);
+    };
     bool bad = false, pv_issued = false;
     if (cnt > 0) {
       TCur c = locate_tc(p, x0, lane);
@@ -626,41 +646,38 @@ __global__ void __launch_bounds__(Cfg<BITS, ROWS>::kThreads, 1)
             v = fmaf(bk.x, qsum[0][r], fmaf(bk.y, qsum[1][r], v));
             x[r] = valid ? v * p.scale_log2 : -INFINITY;
           }
-          // tile maxima over the group's 128 tokens: per row of the score,
-          // and per (group of dims, row) of score + log2 |s_V| (the largest
-          // |p s_V| once the new row maximum is known)
-          const int par = (i / TGN) & 1;
+          // the unit's tile maxima: per row of the score, and per (group of
+          // dims, row) of score + log2 |s_V| (the largest |p s_V| once the
+          // new row maximum is known)
+          int mx[NX4 * 4];
           {
             const float l2v0 = valid ? __log2f(fabsf(sv.x)) : -INFINITY;
             const float l2v1 = valid ? __log2f(fabsf(sv.y)) : -INFINITY;
-            int red[NX4 * 4];
 #pragma unroll
             for (int r = 0; r < ROWS; ++r) {
-              red[r] = __reduce_max_sync(0xffffffffu, f2ord(x[r]));
-              red[ROWS + r] = __reduce_max_sync(0xffffffffu, f2ord(x[r] + l2v0));
-              red[2 * ROWS + r] = __reduce_max_sync(0xffffffffu, f2ord(x[r] + l2v1));
+              mx[r] = __reduce_max_sync(0xffffffffu, f2ord(x[r]));
+              mx[ROWS + r] = __reduce_max_sync(0xffffffffu, f2ord(x[r] + l2v0));
+              mx[2 * ROWS + r] = __reduce_max_sync(0xffffffffu, f2ord(x[r] + l2v1));
             }
 #pragma unroll
-            for (int e = NX; e < NX4 * 4; ++e) red[e] = 0;
+            for (int e = NX; e < NX4 * 4; ++e) mx[e] = 0;
+          }
+          if constexpr (WPU > 1) {
+            const int par = (i / TGN) & 1;
             if (lane == 0)
 #pragma unroll
               for (int e = 0; e < NX4; ++e)
-                xch[(par * 4 + wq) * NX4 + e] =
-                    make_int4(red[4 * e], red[4 * e + 1], red[4 * e + 2], red[4 * e + 3]);
-          }
-          if (bar_or(bid, 128, bad || *abort_flag != 0)) {
-            bad = true;
-            break;
-          }
-          float mnew[ROWS], alpha[ROWS], inv_sp[2][ROWS], sp[2][ROWS];
-          {
-            int mx[NX4 * 4];
+                xch[(par * 4 + wq) * NX4 + e] = make_int4(mx[4 * e], mx[4 * e + 1], mx[4 * e + 2], mx[4 * e + 3]);
+            if (unit_or(bad || *abort_flag != 0)) {
+              bad = true;
+              break;
+            }
 #pragma unroll
             for (int e = 0; e < NX4; ++e) {
-              int4 a = xch[(par * 4 + 0) * NX4 + e];
+              int4 a = xch[(par * 4 + u * WPU) * NX4 + e];
 #pragma unroll
-              for (int w = 1; w < 4; ++w) {
-                const int4 b = xch[(par * 4 + w) * NX4 + e];
+              for (int w = 1; w < WPU; ++w) {
+                const int4 b = xch[(par * 4 + u * WPU + w) * NX4 + e];
                 a = make_int4(max(a.x, b.x), max(a.y, b.y), max(a.z, b.z), max(a.w, b.w));
               }
               mx[4 * e] = a.x;
@@ -668,20 +685,23 @@ __global__ void __launch_bounds__(Cfg<BITS, ROWS>::kThreads, 1)
               mx[4 * e + 2] = a.z;
               mx[4 * e + 3] = a.w;
             }
+          }
+          float mnew[ROWS], alpha[ROWS], inv_sp[2][ROWS], sp[2][ROWS];
 #pragma unroll
-            for (int r = 0; r < ROWS; ++r) {
-              mnew[r] = fmaxf(m[r], ord2f(mx[r]));
-              alpha[r] = fast_exp2(m[r] - mnew[r]);
-              m[r] = mnew[r];
+          for (int r = 0; r < ROWS; ++r) {
+            mnew[r] = fmaxf(m[r], ord2f(mx[r]));
+            // a unit with no token of the piece yet keeps m = -inf: factor 1
+            alpha[r] = mnew[r] > -INFINITY ? fast_exp2(m[r] - mnew[r]) : 1.f;
+            m[r] = mnew[r];
 #pragma unroll
-              for (int g = 0; g < 2; ++g) {
-                // largest |p s_V| of the tile = 2^(ymax - mnew), taken with a
-                // little headroom for the approximate log / exp: sP = that / 32767
-                const float e = ord2f(mx[(1 + g) * ROWS + r]) - mnew[r];
-                const bool any = e > -INFINITY;
-                sp[g][r] = any ? fast_exp2(e) * (1.000244140625f / 32767.f) : 0.f;
-                inv_sp[g][r] = any ? fast_exp2(-e) * (32767.f / 1.000244140625f) : 0.f;
-              }
+            for (int g = 0; g < 2; ++g) {
+              // largest |p s_V| of the unit's tile = 2^(ymax - mnew), taken
+              // with a little headroom for the approximate log / exp:
+              // sP = that / 32767
+              const float e = ord2f(mx[(1 + g) * ROWS + r]) - mnew[r];
+              const bool any = e > -INFINITY;
+              sp[g][r] = any ? fast_exp2(e) * (1.000244140625f / 32767.f) : 0.f;
+              inv_sp[g][r] = any ? fast_exp2(-e) * (32767.f / 1.000244140625f) : 0.f;
             }
           }
           // weights, the running sums, the P' operand of both groups of dims
@@ -702,52 +722,55 @@ __global__ void __launch_bounds__(Cfg<BITS, ROWS>::kThreads, 1)
           store_brow<ROWS, C::kUnits>(smem + C::kPb + (buf * 2 + 0) * C::kBop, tok, u0);
           store_brow<ROWS, C::kUnits>(smem + C::kPb + (buf * 2 + 1) * C::kBop, tok, u1);
           fence_proxy_async_smem();
-          // the group's P' is complete: its first warp issues PV(i) itself
-          // (a polling issuer elsewhere adds its loop time to every tile)
-          if (bar_or(bid, 128, bad || *abort_flag != 0)) {
+          // the unit's P' is complete: its first warp issues the unit's PV
+          if (unit_or(bad || *abort_flag != 0)) {
             bad = true;
             break;
           }
-          if (wq == 0) {
-            // O buffer free (O(i - 2) read by the dim role), 4-bit V widened
+          if (issuer) {
+            // O columns free (O(i - 2) read by the dim role), 4-bit V widened
             bool r = true;
             if (lane == 0)
               r = (i < 2 || wait_b(kOEmpty + buf, ((i - 2) >> 1) & 1)) &&
-                  (BITS == 8 || wait_b(kVx + i % S, (i / S) & 1));
+                  (BITS == 8 || wait_b(kVx + s, (i / S) & 1));
             if (__shfl_sync(0xffffffffu, r, 0)) {
               tc::fence_after_sync();
-              const uint32_t vc = stage_u(i % S) + C::kVc;
+              const uint32_t vc = stage_u(s) + C::kVc;
 #pragma unroll
               for (int g = 0; g < 2; ++g) {
                 const uint32_t pb = sbase + C::kPb + (buf * 2 + g) * C::kBop;
 #pragma unroll
-                for (int kk = 0; kk < kT / 32; ++kk)
-                  tc::mma_i8_elect(tmem + kO0 + buf * 2 * NB + g * NB,
-                                   tc::smem_desc_sw128(vc + 4096 * kk, 16384, 1024),
-                                   tc::smem_desc_none(pb + 512 * kk, 128, 2048), idPV, kk > 0);
+                for (int kk = 0; kk < WPU; ++kk) {
+                  const int ks = u * WPU + kk;  // 32-token step of the tile
+                  tc::mma_i8_elect(tmem + kO0 + ((buf * U + u) * 2 + g) * NB,
+                                   tc::smem_desc_sw128(vc + 4096 * ks, 16384, 1024),
+                                   tc::smem_desc_none(pb + 512 * ks, 128, 2048), idPV, kk > 0);
+                }
               }
               tc::commit_elect(bar(kOFull + buf));
-              tc::commit_elect(bar(kEmpty + i % S));
+              tc::commit_elect(bar(kEmpty + s));
               pv_issued = true;
             } else {
               bad = true;
               if (lane == 0) give_up();  // the group stops at its next barrier
             }
             if (lane == 0) {
-              // the dim role's factors for this tile (tp[buf] was read for tile i - 2)
+              // the dim role's factors for this tile and unit (tp[buf] was
+              // read for tile i - 2)
+              float *t = tp + (buf * U + u) * 3 * ROWS;
 #pragma unroll
               for (int r = 0; r < ROWS; ++r) {
-                tp[buf * 3 * ROWS + r] = alpha[r];
-                tp[buf * 3 * ROWS + ROWS + r] = sp[0][r];
-                tp[buf * 3 * ROWS + 2 * ROWS + r] = sp[1][r];
+                t[r] = alpha[r];
+                t[ROWS + r] = sp[0][r];
+                t[2 * ROWS + r] = sp[1][r];
               }
               mbar_arrive1(bar(kTpB + buf));
             }
           }
         }
         if (last) {
-          // the group's row sums and bias sums of the piece over its tokens
-          // (zero, with m = -inf, when it had no tile of the piece)
+          // the unit's row sums and bias sums of the piece over its tokens
+          // (zero, with m = -inf, when it had no token of the piece)
           float v[3 * ROWS];
 #pragma unroll
           for (int r = 0; r < ROWS; ++r) {
@@ -759,32 +782,38 @@ __global__ void __launch_bounds__(Cfg<BITS, ROWS>::kThreads, 1)
           for (int e = 0; e < 3 * ROWS; ++e)
 #pragma unroll
             for (int o = 16; o; o >>= 1) v[e] += __shfl_xor_sync(0xffffffffu, v[e], o);
-          if (lane == 0)
+          if constexpr (WPU > 1) {
+            if (lane == 0)
 #pragma unroll
-            for (int e = 0; e < 3 * ROWS; ++e) lx[wq * 3 * ROWS + e] = v[e];
-          if (bar_or(bid, 128, bad || *abort_flag != 0)) {
+              for (int e = 0; e < 3 * ROWS; ++e) lx[wq * 3 * ROWS + e] = v[e];
+          }
+          if (unit_or(bad || *abort_flag != 0)) {
             bad = true;
             break;
           }
-          if (tok == 0) {
+          if (issuer && lane == 0) {
             if (k >= 2 && !bad && !wait_b(kPeEmpty + (k & 1), ((k - 2) >> 1) & 1)) bad = true;
-            float *pk = pe + ((k & 1) * TGN + tg) * 4 * ROWS;
+            float *pk = pe + ((k & 1) * TGN * U + uslot) * 4 * ROWS;
 #pragma unroll
-            for (int e = 0; e < 3 * ROWS; ++e)
-              pk[ROWS + e] = (lx[e] + lx[3 * ROWS + e]) + (lx[6 * ROWS + e] + lx[9 * ROWS + e]);
+            for (int e = 0; e < 3 * ROWS; ++e) {
+              float sum = v[e];
+#pragma unroll
+              for (int w = 1; w < WPU; ++w) sum += lx[(wq + w) * 3 * ROWS + e];
+              pk[ROWS + e] = sum;
+            }
 #pragma unroll
             for (int r = 0; r < ROWS; ++r) pk[r] = m[r];
             mbar_arrive1(bar(kPeB + (k & 1)));
           }
-          bar_sync_n(bid, 128);  // lx read before the next piece writes it
+          if constexpr (WPU > 1) bar_sync_n(ubar, 32 * WPU);  // lx read before the next piece writes it
         }
         adv(c, p);
       }
     }
     // this warp's PVs complete before the TMEM is freed
     if (pv_issued) {
-      tc::commit_elect(bar(kDrainT + tg));
-      (void)wait_b(kDrainT + tg, 0);
+      tc::commit_elect(bar(kDrainT + uslot));
+      (void)wait_b(kDrainT + uslot, 0);
     }
     if (bad && lane == 0) give_up();
   }
@@ -867,9 +896,10 @@ __global__ void __launch_bounds__(Cfg<BITS, ROWS>::kThreads, 1)
       write_q(0, c);
       // the second piece's Q, if the share reaches past the first pair
       if (x0 + (c.n - c.t) < x0 + cnt) write_q(1, next_pair(c, p));
-      float o[TGN][ROWS];
+      constexpr int U = C::U;
+      float o[TGN * U][ROWS];  // per unit (token group t, unit u at t * U + u)
 #pragma unroll
-      for (int t = 0; t < TGN; ++t)
+      for (int t = 0; t < TGN * U; ++t)
 #pragma unroll
         for (int r = 0; r < ROWS; ++r) o[t][r] = 0.f;
       // 4-bit: tile j's codes are widened kWidenAhead tiles before the dim
@@ -903,46 +933,44 @@ __global__ void __launch_bounds__(Cfg<BITS, ROWS>::kThreads, 1)
           bad = true;
         if (__any_sync(0xffffffffu, bad)) bad = true;
         tc::fence_after_sync();
-        uint32_t orr[NB];
+        const int gi = i % TGN;
 #pragma unroll
-        for (int j = 0; j < NB; j += 16) {
-          uint32_t r16[16];
-          tc::ld16(tl + kO0 + buf * 2 * NB + g * NB + j, r16);
+        for (int uu = 0; uu < U; ++uu) {
+          uint32_t orr[NB];
 #pragma unroll
-          for (int e = 0; e < 16; ++e) orr[j + e] = r16[e];
-        }
-        tc::wait_ld();
-        float alpha[ROWS], spg[ROWS];
+          for (int j = 0; j < NB; j += 16) {
+            uint32_t r16[16];
+            tc::ld16(tl + kO0 + ((buf * U + uu) * 2 + g) * NB + j, r16);
 #pragma unroll
-        for (int r = 0; r < ROWS; ++r) {
-          alpha[r] = tp[buf * 3 * ROWS + r];
-          spg[r] = tp[buf * 3 * ROWS + (1 + g) * ROWS + r];
+            for (int e = 0; e < 16; ++e) orr[j + e] = r16[e];
+          }
+          tc::wait_ld();
+          const float *t = tp + (buf * U + uu) * 3 * ROWS;
+#pragma unroll
+          for (int tt = 0; tt < TGN; ++tt) {
+            if (tt != gi) continue;
+#pragma unroll
+            for (int r = 0; r < ROWS; ++r) {
+              const int v = static_cast<int>(orr[r] * 256u + orr[ROWS + r] - (orr[2 * ROWS] << 15));
+              o[tt * U + uu][r] = fmaf(o[tt * U + uu][r], t[r], t[(1 + g) * ROWS + r] * static_cast<float>(v));
+            }
+          }
         }
         tc::fence_before_sync();
         mbar_arrive1(bar(kOEmpty + buf));
-        const int gi = i % TGN;
-#pragma unroll
-        for (int t = 0; t < TGN; ++t) {
-          if (t != gi) continue;
-#pragma unroll
-          for (int r = 0; r < ROWS; ++r) {
-            const int v = static_cast<int>(orr[r] * 256u + orr[ROWS + r] - (orr[2 * ROWS] << 15));
-            o[t][r] = fmaf(o[t][r], alpha[r], spg[r] * static_cast<float>(v));
-          }
-        }
         if (last) {
-          // combine the token groups' states: weights 2^(m_g - M)
+          // combine the units' states: weights 2^(m_u - M)
           if (!bad && !wait_b(kPeB + (k & 1), (k >> 1) & 1)) bad = true;
           float mr[ROWS], lr[ROWS], num[ROWS];
 #pragma unroll
           for (int r = 0; r < ROWS; ++r) {
             float M = -INFINITY;
 #pragma unroll
-            for (int t = 0; t < TGN; ++t) M = fmaxf(M, pe[((k & 1) * TGN + t) * 4 * ROWS + r]);
+            for (int t = 0; t < TGN * U; ++t) M = fmaxf(M, pe[((k & 1) * TGN * U + t) * 4 * ROWS + r]);
             float L = 0.f, n = 0.f;
 #pragma unroll
-            for (int t = 0; t < TGN; ++t) {
-              const float *pk = pe + ((k & 1) * TGN + t) * 4 * ROWS;
+            for (int t = 0; t < TGN * U; ++t) {
+              const float *pk = pe + ((k & 1) * TGN * U + t) * 4 * ROWS;
               const float w = pk[r] > -INFINITY ? fast_exp2(pk[r] - M) : 0.f;
               L = fmaf(w, pk[ROWS + r], L);
               n = fmaf(w, o[t][r] + pk[(2 + g) * ROWS + r], n);
@@ -1000,7 +1028,7 @@ __global__ void __launch_bounds__(Cfg<BITS, ROWS>::kThreads, 1)
             }
           }
 #pragma unroll
-          for (int t = 0; t < TGN; ++t)
+          for (int t = 0; t < TGN * U; ++t)
 #pragma unroll
             for (int r = 0; r < ROWS; ++r) o[t][r] = 0.f;
         }

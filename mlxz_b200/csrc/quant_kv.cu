@@ -914,11 +914,15 @@ extern "C" int mz_paged_decode_q(void *out, int32_t out_dtype, int64_t out_seq_s
   p.err = dev_err;
 
   const int64_t rows_total = n_blocks * n_kv_heads * block_size;
-  // The tensor-core form (head_dim 128; 1, 2, 4, 8 or 16 query rows per KV
-  // head) unless MLXZ_B200_QDECODE_TC=0, else the mma.sync kernel.  Its grid
-  // is one CTA per SM, or fewer when num_warps caps the launch (its partials
-  // then fit the workspace sized for num_warps).
-  if (qtc_supports(head_dim, rows) && env_int("MLXZ_B200_QDECODE_TC", 1, 0, 1) == 1) {
+  // The tcgen05 form (head_dim 128; 1, 2, 4, 8 or 16 query rows per KV head)
+  // or the mma.sync kernel.  MLXZ_B200_QDECODE_TC=1 / 0 forces one; by default
+  // 8-bit stores take the tcgen05 form and 4-bit stores the mma.sync kernel
+  // (faster there: the tcgen05 form widens 4-bit codes to bytes on the way).
+  // The tcgen05 grid is one CTA per SM, or fewer when num_warps caps the
+  // launch (its partials then fit the workspace sized for num_warps).
+  const int tc_mode = env_int("MLXZ_B200_QDECODE_TC", -1, -1, 1);
+  const bool use_tc = qtc_supports(head_dim, rows) && (tc_mode == 1 || (tc_mode == -1 && bits == 8));
+  if (use_tc) {
     const int sms = sm_count(device);
     if (sms <= 0) return fail(MZ_ERR_CUDA, "%s: cannot query SM count of device %d", fn, device);
     int grid = sms;
