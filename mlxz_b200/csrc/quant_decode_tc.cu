@@ -88,11 +88,19 @@ struct Cfg {
   static constexpr int kCodeTile = kT * 128;  // widened codes, 128 rows x 128 bytes
   static constexpr int kRawTile = kT * RB;    // 4-bit rows as stored
   static constexpr int kSub = 16;             // tokens per copy
-  static constexpr int kKc = 0, kVc = kCodeTile;
-  static constexpr int kKr = 2 * kCodeTile;
-  static constexpr int kVr = kKr + (BITS == 4 ? kRawTile : 0);
-  static constexpr int kSc = kVr + (BITS == 4 ? kRawTile : 0);  // [4 arrays][128 tok][2] fp16
-  static constexpr int kStage = kSc + 4 * kT * 4;
+  // A stage holds one tile as copied: 8-bit K and V codes in the layout the
+  // MMAs read, or 4-bit codes as stored; then the scales and biases
+  // [4 arrays][128 tok][2] fp16.  4-bit codes are widened to bytes, and the
+  // scales copied, into one of W separate slots, so a stage is free again
+  // once it is widened, while the slot waits for the tile's PV.
+  static constexpr int kKr = 0, kVr = kRawTile;  // codes within a stage
+  static constexpr int kSc = 2 * kRawTile;
+  static constexpr int kScBytes = 4 * kT * 4;
+  static constexpr int kStage = kSc + kScBytes;
+  static constexpr int W = BITS == 4 ? 3 : 0;     // widened slots
+  static constexpr int kKc = 0, kVc = kCodeTile;  // codes within a widened slot (8-bit: the stage)
+  static constexpr int kWSc = 2 * kCodeTile;      // scales within a widened slot
+  static constexpr int kWide = kWSc + kScBytes;
   static constexpr int kBop = kT * NB;  // one B operand
   static constexpr int NX4 = (3 * ROWS + 3) / 4;  // int4 words of one exchange slot
   // misc area (offsets from kMisc)
@@ -109,27 +117,31 @@ struct Cfg {
   static constexpr int kMiscBytes = kIds + 2 * 4 * 8 * 4;
   // as many stages as the shared memory holds (up to 8): the copies of
   // several tiles must be in flight to cover the memory latency under load
-  static constexpr int kFixed = 6 * kBop + kMiscBytes + 1024;
+  static constexpr int kFixed = W * kWide + 6 * kBop + kMiscBytes + 1024;
   static constexpr int kStagesFit = (227 * 1024 - kFixed) / kStage;
   static constexpr int kStages = kStagesFit > 8 ? 8 : kStagesFit;
-  static constexpr int kWidenAhead = kStages - 2 < 2 ? kStages - 2 : 2;  // 4-bit: tiles widened ahead of their QK
-  static constexpr int kQb = kStages * kStage;  // Q operands [2]
+  static constexpr int kWidenAhead = W - 1;  // 4-bit: tiles widened ahead of the dim role's tile
+  static constexpr int kWideBase = kStages * kStage;  // widened slots [W]
+  static constexpr int kQb = kWideBase + W * kWide;   // Q operands [2]
   static constexpr int kPb = kQb + 2 * kBop;    // P' operands [2 bufs][2 groups]
   static constexpr int kMisc = kPb + 4 * kBop;
   static constexpr int kSmemBytes = kMisc + kMiscBytes + 1024;
   static_assert(kStages >= 3, "at least three stages");
-  static_assert(BITS == 8 || kWidenAhead <= kStages - 2, "4-bit widening stays behind the copies");
+  static_assert(BITS == 8 || kWidenAhead + 2 <= kStages, "4-bit widening stays behind the copies");
+  static_assert(W <= 4, "widened-slot barriers");
   static constexpr int kCols = (4 + 4 * U) * NB;  // S [2][2][NB], O [2][U][2][NB]
   static constexpr uint32_t kTmemCols = kCols <= 128 ? 128 : (kCols <= 256 ? 256 : 512);
   static_assert(kCols <= 512, "TMEM columns");
-  static_assert(kStage % 1024 == 0, "stages keep the 1024-byte alignment of the swizzled tiles");
+  static_assert(kStage % 1024 == 0 && kWide % 1024 == 0, "1024-byte alignment of the swizzled tiles");
   static_assert(kSmemBytes <= 227 * 1024, "shared memory");
 };
 
 // barrier slots
+// (kFull, kEmpty: per stage; kKx, kVx, kWEmpty: per widened slot; kDrainT:
+// per unit)
 constexpr int kFull = 0, kKx = 8, kVx = 16, kEmpty = 24, kSFull = 32, kSEmpty = 34, kQFull = 36,
               kTpB = 38, kOFull = 40, kOEmpty = 42, kPeB = 44, kPeEmpty = 46, kDrain = 48,
-              kDrainT = 49, kNumBars = 57;  // kDrainT: one per unit
+              kDrainT = 49, kWEmpty = 57, kNumBars = 61;
 static_assert(8 * kNumBars <= 512, "barrier area");
 
 struct TCur {
@@ -347,14 +359,17 @@ __global__ void __launch_bounds__(Cfg<BITS, ROWS>::kThreads, 1)
   volatile int *merge_word = reinterpret_cast<volatile int *>(misc + C::kWords + 8);
   auto stage = [&](int s) { return smem + s * C::kStage; };
   auto stage_u = [&](int s) { return sbase + s * C::kStage; };
+  auto wide = [&](int w) { return smem + C::kWideBase + w * C::kWide; };
+  auto wide_u = [&](int w) { return sbase + C::kWideBase + w * C::kWide; };
+  // the codes the MMAs of tile i read (8-bit: its stage; 4-bit: its widened slot)
+  auto codes_u = [&](int i) { return BITS == 8 ? stage_u(i % S) : wide_u(i % C::W); };
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   if (warp == kProdWarp && lane == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(bar(kFull + s), 33);  // lane 0 (+ bulk tensor bytes) and 32 cp.async arrivals
-      mbar_init(bar(kKx + s), 128);
-      mbar_init(bar(kVx + s), 128);
-      mbar_init(bar(kEmpty + s), C::U);  // the units' PV commits
+      // 8-bit: the units' PV commits; 4-bit: the dim role's widening
+      mbar_init(bar(kEmpty + s), BITS == 8 ? C::U : 128);
     }
     for (int j = 0; j < 2; ++j) {
       mbar_init(bar(kSFull + j), 1);
@@ -367,6 +382,11 @@ __global__ void __launch_bounds__(Cfg<BITS, ROWS>::kThreads, 1)
       mbar_init(bar(kPeEmpty + j), 128);
     }
     mbar_init(bar(kDrain), 1);
+    for (int w = 0; w < C::W; ++w) {
+      mbar_init(bar(kKx + w), 128);
+      mbar_init(bar(kVx + w), 128);
+      mbar_init(bar(kWEmpty + w), C::U);  // the units' PV commits
+    }
     for (int j = 0; j < TGN * C::U; ++j) mbar_init(bar(kDrainT + j), 1);
     *abort_flag = 0;
     fence_mbar_init();
@@ -458,9 +478,9 @@ __global__ void __launch_bounds__(Cfg<BITS, ROWS>::kThreads, 1)
         if (lane == 0) mbar_arrive_expect_tx(fb, static_cast<uint32_t>(nsub * 2 * C::kSub * C::RB));
         __syncwarp();
         if (lane < nsub) {
-          tma_load_2d(sb + (BITS == 8 ? C::kKc : C::kKr) + lane * C::kSub * C::RB, &tmK, 0,
+          tma_load_2d(sb + C::kKr + lane * C::kSub * C::RB, &tmK, 0,
                       static_cast<int>(row0), fb, pol);
-          tma_load_2d(sb + (BITS == 8 ? C::kVc : C::kVr) + lane * C::kSub * C::RB, &tmV, 0,
+          tma_load_2d(sb + C::kVr + lane * C::kSub * C::RB, &tmV, 0,
                       static_cast<int>(row0), fb, pol);
         }
         {
@@ -524,7 +544,8 @@ __global__ void __launch_bounds__(Cfg<BITS, ROWS>::kThreads, 1)
         const int kk = newp ? kq + 1 : kq;
         bool r = true;
         if (lane == 0)
-          r = wait_b((BITS == 8 ? kFull : kKx) + nq % S, (nq / S) & 1) &&
+          r = (BITS == 8 ? wait_b(kFull + nq % S, (nq / S) & 1)
+                         : wait_b(kKx + nq % C::W, (nq / C::W) & 1)) &&
               (nq < 2 || wait_b(kSEmpty + (nq & 1), ((nq - 2) >> 1) & 1)) &&
               (!newp || wait_b(kQFull + (kk & 1), (kk >> 1) & 1)) && *abort_flag == 0;
         if (!__shfl_sync(0xffffffffu, r, 0)) {
@@ -534,7 +555,7 @@ __global__ void __launch_bounds__(Cfg<BITS, ROWS>::kThreads, 1)
         tc::fence_after_sync();
         const int s = nq % S, buf = nq & 1;
         const uint32_t qb = sbase + C::kQb + (kk & 1) * C::kBop;
-        const uint32_t kc = stage_u(s) + C::kKc;
+        const uint32_t kc = codes_u(nq) + C::kKc;
 #pragma unroll
         for (int g = 0; g < 2; ++g)
 #pragma unroll
@@ -629,8 +650,13 @@ __global__ void __launch_bounds__(Cfg<BITS, ROWS>::kThreads, 1)
           }
           tc::fence_before_sync();
           mbar_arrive1(bar(kSEmpty + buf));
-          if (!bad && !wait_b(kFull + s, (i / S) & 1)) bad = true;  // the tile's scales
-          const uint8_t *sc = stage(s) + C::kSc;
+          // the tile's scales: in its stage (8-bit) or its widened slot
+          if constexpr (BITS == 8) {
+            if (!bad && !wait_b(kFull + s, (i / S) & 1)) bad = true;
+          } else {
+            if (!bad && !wait_b(kKx + i % C::W, (i / C::W) & 1)) bad = true;
+          }
+          const uint8_t *sc = BITS == 8 ? stage(s) + C::kSc : wide(i % C::W) + C::kWSc;
           const float2 sk = __half22float2(*reinterpret_cast<const __half2 *>(sc + 0 * kT * 4 + tok * 4));
           const float2 bk = __half22float2(*reinterpret_cast<const __half2 *>(sc + 1 * kT * 4 + tok * 4));
           const float2 sv = __half22float2(*reinterpret_cast<const __half2 *>(sc + 2 * kT * 4 + tok * 4));
@@ -732,10 +758,10 @@ __global__ void __launch_bounds__(Cfg<BITS, ROWS>::kThreads, 1)
             bool r = true;
             if (lane == 0)
               r = (i < 2 || wait_b(kOEmpty + buf, ((i - 2) >> 1) & 1)) &&
-                  (BITS == 8 || wait_b(kVx + s, (i / S) & 1));
+                  (BITS == 8 || wait_b(kVx + i % C::W, (i / C::W) & 1));
             if (__shfl_sync(0xffffffffu, r, 0)) {
               tc::fence_after_sync();
-              const uint32_t vc = stage_u(s) + C::kVc;
+              const uint32_t vc = codes_u(i) + C::kVc;
 #pragma unroll
               for (int g = 0; g < 2; ++g) {
                 const uint32_t pb = sbase + C::kPb + (buf * 2 + g) * C::kBop;
@@ -748,7 +774,7 @@ __global__ void __launch_bounds__(Cfg<BITS, ROWS>::kThreads, 1)
                 }
               }
               tc::commit_elect(bar(kOFull + buf));
-              tc::commit_elect(bar(kEmpty + s));
+              tc::commit_elect(bar(BITS == 8 ? kEmpty + s : kWEmpty + i % C::W));
               pv_issued = true;
             } else {
               bad = true;
@@ -902,16 +928,22 @@ __global__ void __launch_bounds__(Cfg<BITS, ROWS>::kThreads, 1)
       for (int t = 0; t < TGN * U; ++t)
 #pragma unroll
         for (int r = 0; r < ROWS; ++r) o[t][r] = 0.f;
-      // 4-bit: tile j's codes are widened kWidenAhead tiles before the dim
-      // role reaches it (its stage was loaded after PV(j - S), long done)
+      // 4-bit: tile j's codes are widened into slot j % W kWidenAhead tiles
+      // before the dim role reaches tile j (the slot's previous tile, j - W,
+      // had its O read already); the stage is released to the copies
       auto widen = [&](int j) {
-        const int sj = j % S;
+        const int sj = j % S, wj = j % C::W;
         if (!bad && !wait_b(kFull + sj, (j / S) & 1)) bad = true;
-        widen_row(stage(sj) + C::kKr, stage(sj) + C::kKc, q);
-        widen_row(stage(sj) + C::kVr, stage(sj) + C::kVc, q);
+        if (j >= C::W && !bad && !wait_b(kWEmpty + wj, ((j - C::W) / C::W) & 1)) bad = true;
+        widen_row(stage(sj) + C::kKr, wide(wj) + C::kKc, q);
+        widen_row(stage(sj) + C::kVr, wide(wj) + C::kVc, q);
+        static_assert(C::kScBytes == 128 * 16, "one 16-byte piece of the scales per thread");
+        *reinterpret_cast<uint4 *>(wide(wj) + C::kWSc + 16 * q) =
+            *reinterpret_cast<const uint4 *>(stage(sj) + C::kSc + 16 * q);
         fence_proxy_async_smem();
-        mbar_arrive1(bar(kKx + sj));
-        mbar_arrive1(bar(kVx + sj));
+        mbar_arrive1(bar(kKx + wj));
+        mbar_arrive1(bar(kVx + wj));
+        mbar_arrive1(bar(kEmpty + sj));
       };
       if constexpr (BITS == 4)
         for (int j = 0; j < C::kWidenAhead && j < cnt; ++j) widen(j);
