@@ -1203,6 +1203,13 @@ def run_quant(args, local_rank: int, bits: int | None = None) -> dict:
     dec_ms = sum(dec) / len(dec)
     peak, peak_kind = peaks()
     value = kv_layer * nl / (ms / 1e3) / 1e9
+    # the form mz_paged_decode_q dispatches to for this shape (head_dim 128,
+    # 4 query rows per KV head): tcgen05 for 8-bit, mma.sync for 4-bit,
+    # unless MLXZ_B200_QDECODE_TC forces one
+    tc_env = os.environ.get("MLXZ_B200_QDECODE_TC", "")
+    use_tc = tc_env == "1" or (tc_env != "0" and bits == 8)
+    qkernel = f"paged_decode_qtc_kernel<{bits},4>" if use_tc else f"paged_decode_q_kernel<128,{bits},1>"
+    qprof = f"paged_decode_qtc{bits}_c4.md" if use_tc else f"paged_decode_q{bits}_c4.md"
     line = {
         "metric": f"quantised ({bits}-bit) paged-decode KV-read GB/s and decode tok/s, 8B shape, batch 32",
         "value": round(value, 2), "unit": "GB/s", "n_gpus": 1, "steps": steps,
@@ -1219,8 +1226,7 @@ def run_quant(args, local_rank: int, bits: int | None = None) -> dict:
         "roofline": {"bound": "hbm", "achieved": round(alg / (dec_ms / 1e3) / 1e9, 1),
                      "peak": peak, "unit": "GB/s",
                      "frac": round(alg / (dec_ms / 1e3) / 1e9 / peak, 4),
-                     "traffic": profile_traffic("paged_decode_q8_c4.md") if bits == 8 else None,
-                     "kernel": f"paged_decode_q_kernel<128,{bits}>", "peak_kind": peak_kind,
+                     "traffic": profile_traffic(qprof), "kernel": qkernel, "peak_kind": peak_kind,
                      "decode_ms_mean": round(dec_ms, 4), "alg_bytes_per_launch": alg},
         "gpu_launches": steps * nl * 2,
         "clocks": clk,
