@@ -74,6 +74,9 @@ def parse_args():
                          "chunked-prefill iteration (append + causal attention per layer); "
                          "kernels: each data-movement kernel timed alone")
     ap.add_argument("--bits", type=int, default=8, choices=[4, 8])
+    ap.add_argument("--kv-bits", type=int, default=16, choices=[4, 8, 16],
+                    help="prefill: the K/V store (16 = bf16; 8 / 4 = quantised, "
+                         "dequantised per layer into a staging pool)")
     ap.add_argument("--gather", default="p2p", choices=["p2p", "nccl"],
                     help="N > 1: p2p = output rows stored into every rank's buffer by the "
                          "decode launch itself (peer memory over NVLink) + bounded signal "
@@ -294,18 +297,30 @@ def run_prefill(args, local_rank: int) -> None:
     import torch
 
     from mlxz_b200 import ops
-    from mlxz_b200.engine import PagedKVStore, PagedPrefillStep
+    from mlxz_b200.engine import PagedKVStore, PagedPrefillStep, QuantizedPagedKVStore
 
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
     nl = args.layers
+    kv_bits = args.kv_bits
     nb_seq = PF_CTX // BS
     n_blocks = int(math.ceil(PF_B * nb_seq * 1.1))
     perm = np.random.default_rng(args.seed + 1).permutation(n_blocks)
-    store = PagedKVStore(nl, n_blocks, HKV, D, BS, torch.bfloat16, dev, init="empty")
     torch.manual_seed(args.seed)
-    for l in range(nl):
-        store.pools[l].normal_()
+    if kv_bits == 16:
+        store = PagedKVStore(nl, n_blocks, HKV, D, BS, torch.bfloat16, dev, init="empty")
+        for l in range(nl):
+            store.pools[l].normal_()
+    else:
+        store = QuantizedPagedKVStore(nl, n_blocks, HKV, D, BS, bits=kv_bits, device=dev,
+                                      init="empty")
+        allsl = torch.arange(n_blocks * BS, dtype=torch.int64, device=dev)
+        for l in range(nl):
+            for lo in range(0, n_blocks * BS, 8192):
+                sl = allsl[lo:lo + 8192]
+                kk = torch.randn(HKV, sl.numel(), D, device=dev).to(torch.bfloat16)
+                vv = torch.randn(HKV, sl.numel(), D, device=dev).to(torch.bfloat16)
+                ops.kv_quant_append(store.qpools(l), kk, vv, sl)
     ids = []
     for b in range(PF_B):
         store.add_sequence(f"s{b}", PF_CTX - PF_CHUNK,
@@ -345,16 +360,25 @@ def run_prefill(args, local_rank: int) -> None:
     ops.check_device_errors(local_rank)
     ms = t0.elapsed_time(t1) / steps
 
-    # the attention kernel alone: events around each launch (one extra pass)
-    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(nl)]
+    # the attention kernel alone: events around each launch (one extra pass);
+    # over a quantised store, the per-layer dequantisation into the staging
+    # pool is timed on its own too
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(nl)]
     for l in range(nl):
-        kp, vp = store.k_pool(l), store.v_pool(l)
+        if kv_bits == 16:
+            kp, vp = store.k_pool(l), store.v_pool(l)
+        else:
+            kp, vp = step._stage
+            evs[l][2].record()
+            ops.kv_dequant_blocks(store.qpools(l), step._ids, kp, vp)
+            evs[l][3].record()
         evs[l][0].record()
         ops.paged_prefill(q[l], kp, vp, step.tables, step.q_start, step.q_len, step.ctx_lens,
                           step.max_q_len, step.scale, out=out[l])
         evs[l][1].record()
     torch.cuda.synchronize()
     pf_ms = statistics.mean(e[0].elapsed_time(e[1]) for e in evs)
+    dq_ms = statistics.mean(e[2].elapsed_time(e[3]) for e in evs) if kv_bits != 16 else None
 
     # end to end: per layer the chunk's q/k/v from pinned host memory and the
     # attention output back, copies pipelined against the layers' launches
@@ -434,7 +458,12 @@ def run_prefill(args, local_rank: int) -> None:
         "data": "synthetic (seeded N(0,1) bf16 K/V/Q, random block tables)",
         "config": {"workload": ("chunked-prefill iteration: 32 layers, 32 q heads, 8 kv heads, "
                                 "head_dim 128, block 16; 8 seqs x 512-token chunk at offset "
-                                "3584 (ctx 4096); per layer kv_append + paged_prefill"),
+                                "3584 (ctx 4096); per layer kv_append + paged_prefill"
+                                + ("" if kv_bits == 16 else
+                                   f"; {kv_bits}-bit store: kv_quant_append, kv_dequant_blocks "
+                                   "of the step's blocks into a bf16 staging pool, paged_prefill "
+                                   "on it")),
+                   "kv_bits": kv_bits,
                    "layers": nl, "global_batch": PF_B, "seq_len": PF_CTX, "chunk": PF_CHUNK,
                    "pool_blocks": n_blocks,
                    "l2": "per layer 134 MB of K/V read > 126 MB L2; layers use distinct pools"},
@@ -443,8 +472,10 @@ def run_prefill(args, local_rank: int) -> None:
                      "unit": "TFLOP/s", "frac": round(achieved / peak, 4),
                      "traffic": profile_traffic("paged_prefill_8b.md"),
                      "kernel": "paged_prefill_tc_kernel<128,bf16>", "peak_kind": peak_kind,
-                     "prefill_ms_mean": round(pf_ms, 4), "alg_flops_per_launch": flops_layer},
-        "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": steps * nl * 2, "clocks": clk,
+                     "prefill_ms_mean": round(pf_ms, 4), "alg_flops_per_launch": flops_layer,
+                     "dequant_ms_mean": None if dq_ms is None else round(dq_ms, 4)},
+        "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": steps * nl * (2 if kv_bits == 16 else 3),
+        "clocks": clk,
     }
     print(json.dumps(line), flush=True)
 

@@ -3,69 +3,87 @@
 // the blocks its sequences use (what a quantised cache's attention over a
 // prompt chunk computes), so the prefill kernel runs on them unchanged.
 //
-// HBM-bound elementwise work: each thread turns 8 codes of one row (one or two
-// code words, one group's scale and bias) into 8 values, f32(scale) * q +
-// f32(bias) with a separate multiply and add (no fused rounding), rounded to
-// the output type, stored as one 16-byte vector.
+// HBM-bound elementwise work.  One CTA per (block id, K or V): the block's
+// codes (H * bs rows) are contiguous, so its threads stream them with vector
+// loads, 16 codes (one 16- or 8-byte piece of a row, inside one group of 64)
+// per step, and turn each into f32(scale) * q + f32(bias) with a separate
+// multiply and add (no fused rounding), rounded to the output type and stored
+// as two 16-byte vectors.
 #include "common.cuh"
 
 namespace mz {
 namespace {
 
+template <int BITS>
+__device__ __forceinline__ void load_codes(const uint8_t *p, bool vec, uint32_t (&w)[BITS / 2]) {
+  // BITS / 2 words hold 16 codes: 4 words at 8-bit, 2 at 4-bit
+  if constexpr (BITS == 8) {
+    if (vec) {
+      const uint4 x = *reinterpret_cast<const uint4 *>(p);
+      w[0] = x.x, w[1] = x.y, w[2] = x.z, w[3] = x.w;
+      return;
+    }
+  } else {
+    if (vec) {
+      const uint2 x = *reinterpret_cast<const uint2 *>(p);
+      w[0] = x.x, w[1] = x.y;
+      return;
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < BITS / 2; ++j) w[j] = reinterpret_cast<const uint32_t *>(p)[j];
+}
+
 template <int BITS, bool BF16>
-__global__ void dequant_blocks_kernel(uint16_t *__restrict__ ko, uint16_t *__restrict__ vo,
-                                      const uint32_t *__restrict__ kc,
-                                      const __half *__restrict__ ks,
-                                      const __half *__restrict__ kb,
-                                      const uint32_t *__restrict__ vc,
-                                      const __half *__restrict__ vs,
-                                      const __half *__restrict__ vb,
-                                      const int32_t *__restrict__ ids, int n_ids, int H, int D,
-                                      int bs, int64_t n_blocks, int32_t *err) {
-  const int oct = D / 8;                                   // 8-element units per row
-  const int64_t rows_per_block = static_cast<int64_t>(H) * bs;
-  const int64_t per_kv = static_cast<int64_t>(n_ids) * rows_per_block * oct;
-  const int words = D * BITS / 32;                          // code words per row
-  for (int64_t x = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; x < 2 * per_kv;
-       x += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const bool isv = x >= per_kv;
-    const int64_t y = isv ? x - per_kv : x;
-    const int u = static_cast<int>(y % oct);
-    const int64_t r = y / oct;                              // output row: i * H * bs + h * bs + t
-    const int i = static_cast<int>(r / rows_per_block);
-    const int64_t rem = r - static_cast<int64_t>(i) * rows_per_block;
-    const int32_t blk = ids[i];
-    if (blk < 0 || blk >= n_blocks) {
-      if (u == 0 && rem == 0 && !isv) dev_error(err, MZ_DEVERR_BLOCK_ID);
-      continue;
-    }
-    const int64_t src = static_cast<int64_t>(blk) * rows_per_block + rem;
-    const uint32_t *cw = (isv ? vc : kc) + src * words;
-    const int64_t gi = src * (D / 64) + (8 * u) / 64;
-    const float s = __half2float((isv ? vs : ks)[gi]);
-    const float b = __half2float((isv ? vb : kb)[gi]);
-    uint32_t q[8];
-    if constexpr (BITS == 8) {
-      const uint32_t w0 = cw[2 * u], w1 = cw[2 * u + 1];
+__global__ void __launch_bounds__(256)
+    dequant_blocks_kernel(uint16_t *__restrict__ ko, uint16_t *__restrict__ vo,
+                          const uint32_t *__restrict__ kc, const __half *__restrict__ ks,
+                          const __half *__restrict__ kb, const uint32_t *__restrict__ vc,
+                          const __half *__restrict__ vs, const __half *__restrict__ vb,
+                          const int32_t *__restrict__ ids, int H, int D, int bs, int64_t n_blocks,
+                          bool vec, int32_t *err) {
+  const int i = static_cast<int>(blockIdx.x >> 1);
+  const bool isv = (blockIdx.x & 1) != 0;
+  const int32_t blk = ids[i];
+  if (blk < 0 || blk >= n_blocks) {
+    if (threadIdx.x == 0 && !isv) dev_error(err, MZ_DEVERR_BLOCK_ID);
+    return;
+  }
+  const int rows = H * bs;       // rows of one block
+  const int per_row = D / 16;    // 16-code pieces per row
+  const int row_bytes = D * BITS / 8;
+  const int groups = D / 64;
+  const uint8_t *codes = reinterpret_cast<const uint8_t *>(isv ? vc : kc) +
+                         static_cast<int64_t>(blk) * rows * row_bytes;
+  const int64_t g0 = static_cast<int64_t>(blk) * rows * groups;
+  const __half *sc = (isv ? vs : ks) + g0;
+  const __half *bi = (isv ? vb : kb) + g0;
+  uint16_t *out = (isv ? vo : ko) + static_cast<int64_t>(i) * rows * D;
+  const int units = rows * per_row;
+  for (int u = threadIdx.x; u < units; u += blockDim.x) {
+    const int row = u / per_row, c = u - row * per_row;
+    const float s = __half2float(sc[row * groups + (c >> 2)]);
+    const float b = __half2float(bi[row * groups + (c >> 2)]);
+    uint32_t w[BITS / 2];
+    load_codes<BITS>(codes + row * row_bytes + c * (16 * BITS / 8), vec, w);
+    uint32_t packed[8];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        q[j] = (w0 >> (8 * j)) & 0xFFu;
-        q[4 + j] = (w1 >> (8 * j)) & 0xFFu;
+    for (int j = 0; j < 8; ++j) {
+      uint32_t q0, q1;  // codes 2j and 2j + 1 (LSB-first fields)
+      if constexpr (BITS == 8) {
+        q0 = (w[j >> 1] >> (16 * (j & 1))) & 0xFFu;
+        q1 = (w[j >> 1] >> (16 * (j & 1) + 8)) & 0xFFu;
+      } else {
+        q0 = (w[j >> 2] >> (8 * (j & 3))) & 0xFu;
+        q1 = (w[j >> 2] >> (8 * (j & 3) + 4)) & 0xFu;
       }
-    } else {
-      const uint32_t w = cw[u];
-#pragma unroll
-      for (int j = 0; j < 8; ++j) q[j] = (w >> (4 * j)) & 0xFu;
+      const float a = __fadd_rn(__fmul_rn(static_cast<float>(q0), s), b);
+      const float e = __fadd_rn(__fmul_rn(static_cast<float>(q1), s), b);
+      packed[j] = pack2<BF16>(a, e);
     }
-    uint32_t packed[4];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const float a = __fadd_rn(__fmul_rn(static_cast<float>(q[2 * j]), s), b);
-      const float c = __fadd_rn(__fmul_rn(static_cast<float>(q[2 * j + 1]), s), b);
-      packed[j] = pack2<BF16>(a, c);
-    }
-    *reinterpret_cast<uint4 *>((isv ? vo : ko) + r * D + 8 * u) =
-        make_uint4(packed[0], packed[1], packed[2], packed[3]);
+    uint4 *o = reinterpret_cast<uint4 *>(out + static_cast<int64_t>(row) * D + 16 * c);
+    o[0] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+    o[1] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
   }
 }
 
@@ -90,6 +108,7 @@ extern "C" int mz_kv_dequant_blocks(void *k_out, void *v_out, int32_t out_dtype,
   if (n_ids < 0 || n_kv_heads <= 0 || block_size <= 0 || n_blocks <= 0)
     return fail(MZ_ERR_INVALID_ARG, "%s: bad sizes", fn);
   if (n_ids == 0) return MZ_OK;
+  if (n_ids > (1 << 30)) return fail(MZ_ERR_UNSUPPORTED, "%s: more than 2^30 block ids", fn);
   if (!k_out || !v_out || !k_codes || !k_scales || !k_biases || !v_codes || !v_scales ||
       !v_biases || !block_ids)
     return fail(MZ_ERR_INVALID_ARG, "%s: null pointer", fn);
@@ -97,13 +116,11 @@ extern "C" int mz_kv_dequant_blocks(void *k_out, void *v_out, int32_t out_dtype,
       !aligned(k_scales, 2) || !aligned(k_biases, 2) || !aligned(v_scales, 2) ||
       !aligned(v_biases, 2))
     return fail(MZ_ERR_ALIGNMENT, "%s: outputs need 16-byte, codes 4-byte alignment", fn);
-  const int64_t units = 2LL * n_ids * n_kv_heads * block_size * (head_dim / 8);
-  // grid-stride kernel: at most 32 blocks of 256 threads per SM
-  const int sms = sm_count(current_device());
-  if (sms <= 0) return fail(MZ_ERR_CUDA, "%s: cannot query the device's SM count", fn);
-  int64_t g = (units + 255) / 256;
-  if (g > 32LL * sms) g = 32LL * sms;
-  const unsigned grid = static_cast<unsigned>(g);
+  // one CTA per (block id, K or V)
+  const unsigned grid = static_cast<unsigned>(2 * static_cast<int64_t>(n_ids));
+  // 16 codes are 16 (8-bit) or 8 (4-bit) bytes: vector loads when the code
+  // pools are aligned to that (row pieces then are too), else word loads
+  const bool vec = aligned(k_codes, bits * 2) && aligned(v_codes, bits * 2);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   auto *ko = static_cast<uint16_t *>(k_out);
   auto *vo = static_cast<uint16_t *>(v_out);
@@ -115,8 +132,8 @@ extern "C" int mz_kv_dequant_blocks(void *k_out, void *v_out, int32_t out_dtype,
   auto *vb = static_cast<const __half *>(v_biases);
 #define MZ_DQ(B_, BF_)                                                                      \
   dequant_blocks_kernel<B_, BF_><<<grid, 256, 0, s>>>(ko, vo, kc, ks, kb, vc, vs, vb,      \
-                                                      block_ids, n_ids, n_kv_heads, head_dim, \
-                                                      block_size, n_blocks, dev_err)
+                                                      block_ids, n_kv_heads, head_dim,      \
+                                                      block_size, n_blocks, vec, dev_err)
   const bool bf16 = out_dtype == MZ_DTYPE_BF16;
   if (bits == 8) {
     if (bf16) MZ_DQ(8, true); else MZ_DQ(8, false);
