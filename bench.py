@@ -1235,10 +1235,9 @@ def run_quant(args, local_rank: int, bits: int | None = None) -> dict:
     peak, peak_kind = peaks()
     value = kv_layer * nl / (ms / 1e3) / 1e9
     # the form mz_paged_decode_q dispatches to for this shape (head_dim 128,
-    # 4 query rows per KV head): tcgen05 for 8-bit, mma.sync for 4-bit,
-    # unless MLXZ_B200_QDECODE_TC forces one
-    tc_env = os.environ.get("MLXZ_B200_QDECODE_TC", "")
-    use_tc = tc_env == "1" or (tc_env != "0" and bits == 8)
+    # 4 query rows per KV head): the mma.sync kernel, unless
+    # MLXZ_B200_QDECODE_TC=1 selects the tcgen05 form
+    use_tc = os.environ.get("MLXZ_B200_QDECODE_TC", "") == "1"
     qkernel = f"paged_decode_qtc_kernel<{bits},4>" if use_tc else f"paged_decode_q_kernel<128,{bits},1>"
     qprof = f"paged_decode_qtc{bits}_c4.md" if use_tc else f"paged_decode_q{bits}_c4.md"
     line = {

@@ -304,6 +304,7 @@ struct Sched {
   Unit *uq;
   Cursor pc;
   int p_left, pushed, issued;
+  int istage;  // issued % S, kept incrementally
   bool p_done, static_taken;
 
   // Returns false (nothing to do, no counter touched) when T == 0.
@@ -326,7 +327,7 @@ struct Sched {
     tot = t * p.Hkv;
     if (tot == 0) return false;
     ticket = p.counters + (int64_t)p.B * p.Hkv;
-    p_left = pushed = issued = 0;
+    p_left = pushed = issued = istage = 0;
     p_done = static_taken = false;
     if (p.batch_invariant) {
       // every (sequence, KV head) pair is cut into pieces of kBiPieceTiles
@@ -483,10 +484,11 @@ struct Sched {
     const int start = wid * per_s;
     push_unit(p, start, min(start + per_s, t_s), wid);
     while (p_left > 0 && issued < S) {
-      issue(issued % S, pc);
+      issue(istage, pc);
       advance(pc, p);
       --p_left;
       ++issued;
+      if (++istage == S) istage = 0;
     }
   }
 
@@ -499,10 +501,11 @@ struct Sched {
         break;
       }
       if (lane == 0 && issued >= S) fence_proxy_async_smem();
-      issue(issued % S, pc);
+      issue(istage, pc);
       advance(pc, p);
       --p_left;
       ++issued;
+      if (++istage == S) istage = 0;
     }
   }
 };

@@ -11,17 +11,19 @@
 //   q = clamp(rint((w - b16) / s16), 0, 2^bits - 1), q = 0 when s16 == 0;
 //   dequantised w' = s16 * q + b16.
 //
-// Decode never materialises dequantised K/V.  The integer codes 0..255 are
-// exact in fp16, so they enter mma.sync directly, and the affine map is applied
-// around the products:
+// Decode never materialises dequantised K/V; the affine map is applied around
+// the products:
 //   S[r][t] = sum_g s_k[t][g] * (Q_g . q_k[t]_g) + b_k[t][g] * sum(Q_g[r])
 //   O[r][d] = sum_t (p[r][t] * s_v[t][g(d)]) * q_v[t][d] + sum_t p[r][t] * b_v[t][g(d)]
-// with Q converted to fp16 once per piece.  The dot products run over a
-// permutation of the head dimension chosen so that each lane's codes are
-// contiguous bytes (Q is loaded with the same permutation; V's output columns
-// are un-permuted when written).  Tiles arrive by 1-D bulk copies (codes,
-// scales and biases of K and V: six copies per 16-token tile) into a per-warp
-// ring, with the same persistent-warp scheduler as the bf16 kernel.
+// Q_g . q_k runs on the integer tensor cores (K codes as stored, u8; Q in
+// 16-bit fixed point per row and group, split into signed bytes); P.V on the
+// fp16 tensor cores (V codes exact in fp16, P' as an fp16 hi + lo pair).  The
+// dot products run over a permutation of the head dimension chosen so that
+// each lane's codes are contiguous bytes (Q is packed with the same
+// permutation; V's output columns are un-permuted when written).  A tile's
+// codes arrive by bulk (tensor) copies and its scales and biases by cp.async
+// into a per-warp ring, with the same persistent-warp scheduler as the bf16
+// kernel; the warp takes two tiles of a pair per step.
 //
 // Roofline: a tile moves 2 * 16 * (D * bits / 8 + 4 * D / 64) bytes; with
 // D = 128 that is 4352 B (8-bit) or 2304 B (4-bit), against 8192 B at bf16.
@@ -159,7 +161,7 @@ int quant_append(const QAppendParams &qp, int D, int bits, cudaStream_t s) {
 // Dequant-fused paged decode.
 // ---------------------------------------------------------------------------
 
-template <int D, int BITS, int NR>
+template <int D, int BITS, int NQ>
 struct QCfg {
   static constexpr int RB = D * BITS / 8;   // code bytes per token row
   static constexpr int NG = D / 64;         // groups per row
@@ -173,11 +175,11 @@ struct QCfg {
   // and the swizzled addresses add to it.)
   static constexpr int kSwz = (RB == 128) ? 128 : 0;
   static constexpr bool kSwizzled = kSwz != 0;
-  static constexpr int kTx = 2 * TD + 4 * TS;
+  static constexpr int kTx = 2 * TD;  // bytes the code copies bring (scales come by cp.async)
   static constexpr int kCodeStage = 2 * TD;          // K + V codes (1024-aligned)
   static constexpr int kScaleStage = 4 * TS;         // K/V scales and biases
   static constexpr int kStageBytes = kCodeStage + kScaleStage;
-  static constexpr int kCtas = NR == 1 ? 3 : 2;  // CTAs per SM the shared memory is sized for
+  static constexpr int kCtas = NQ <= 2 ? 3 : 2;  // CTAs per SM the shared memory is sized for
   static constexpr int kStagesFit = (210 * 1024 / kCtas) / (kWarps * kStageBytes);
   static constexpr int kStages = kStagesFit > 8 ? 8 : (kStagesFit < 3 ? 3 : kStagesFit);
   static constexpr int kSmemCodes = kWarps * kStages * kCodeStage;
@@ -221,15 +223,10 @@ __device__ __forceinline__ int tok_of(int m) {
 
 constexpr uint32_t kMagic = 0x64646464u;  // fp16 0x64xx = 1024 + xx
 
-// two nibbles at bit 0 and bit 16 of x -> half2 of (1024 + nibble)
-__device__ __forceinline__ uint32_t nib2_biased(uint32_t x) {
-  return (x & 0x000F000Fu) | 0x64006400u;
-}
-
-// Codes enter the mma centred on the middle of their range (code - 128 for
-// 8-bit, code - 8 for 4-bit; exact in fp16): with the 1024 of the magic
-// bias left in, a whole context's P.V sums carry 1024 * sum P' and lose the
-// result to cancellation once that is removed.
+// Codes enter the P.V products centred on the middle of their range (code -
+// 128 for 8-bit, code - 8 for 4-bit; exact in fp16): with the 1024 of the
+// magic bias left in, a whole context's P.V sums would carry 1024 * sum P' and
+// lose the result to cancellation once that is removed.
 template <int BITS>
 constexpr float kCodeCentre = BITS == 8 ? 128.f : 8.f;
 template <int BITS>
@@ -240,24 +237,61 @@ __device__ __forceinline__ uint32_t centred(uint32_t biased) {
   asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(biased), "r"(kCentreBits<BITS>));
   return r;
 }
+// half2 of (1024 + 16 n) -> half2 of n - 8 (x / 16 - 72, exact in fp16)
+__device__ __forceinline__ uint32_t centred_hi_nibble(uint32_t biased16) {
+  uint32_t r;
+  asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(r) : "r"(biased16), "r"(0x2C002C00u), "r"(0xD480D480u));
+  return r;
+}
 
 __device__ __forceinline__ float load_q16(const uint16_t *q, int64_t off, bool bf16) {
   const uint16_t b = q[off];
   return bf16 ? __uint_as_float(static_cast<uint32_t>(b) << 16) : __half2float(__ushort_as_half(b));
 }
 
-// Transposed formulation: tokens (QK) and head dims (PV) are the M = 16 side
-// of mma.m16n8k16, the query rows of a KV head the N = 8 side (NR tiles of 8).
-//   QK:  S^T[tok][row] = sum_k A[tok][k] * B[k][row], A = K codes - centre
-//        (restored through the bias term with sum_k Q) over a permutation pi
-//        of the head dim, B = Q with the same permutation;
-//   PV:  O^T[d][row] = sum_t A[d][t] * B[t][row], A = V codes - centre
-//        (restored through sum_t P'), B = P'^T by movmatrix.
-template <int D, int BITS, int NR>
-__global__ void __launch_bounds__(kWarps * 32, QCfg<D, BITS, NR>::kCtas)
+// D(16x8 s32) += A(16x32 u8, row-major) * B(32x8 s8, column-major)
+__device__ __forceinline__ void mma_u8s8(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                         uint32_t a3, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0, %1, %2, %3}, "
+      "{%4, %5, %6, %7}, {%8, %9}, {%0, %1, %2, %3};"
+      : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// x as an fp16 pair (hi, lo) with hi + lo = x to ~22 bits: the two columns of
+// one query in the P.V products.
+__device__ __forceinline__ uint32_t split_hilo(float x) {
+  const __half h = __float2half_rn(x);
+  const __half l = __float2half_rn(x - __half2float(h));
+  return static_cast<uint32_t>(__half_as_ushort(h)) |
+         (static_cast<uint32_t>(__half_as_ushort(l)) << 16);
+}
+
+// The query rows of a KV head go in groups of four (NQ groups, rows <= 4 NQ);
+// lane (g, c) = (lane / 4, lane % 4) carries query row 4 nq + c of every group.
+//
+// QK on integer tensor cores (mma.m16n8k32, u8 x s8 -> s32), exact:
+//   A[tok][k]  = the K codes as stored (8-bit) or split into bytes (4-bit:
+//                x & 0x0F0F0F0F and (x >> 4) & 0x0F0F0F0F), tokens the M side;
+//   B[k][col]  = Q in 16-bit fixed point per (row, group of 64 dims),
+//                q16 = rint(q * 32639 / max|q|) = 256 hi + lo (hi, lo signed
+//                bytes), column 2 i the hi bytes of row i, 2 i + 1 the lo bytes;
+//   S[tok][i]  = sum_g s_k[tok][g] * sq[i][g] * (256 D[tok][2i] + D[tok][2i+1])
+//                + b_k[tok][g] * sum(q~[i]_g),   q~ = q16 * sq (sq = max|q| / 32639)
+// over a permutation of the head dimension within each group (lane c's four
+// k slots of a k-step are its own contiguous code bytes; Q is packed with the
+// same permutation).
+// PV on fp16 tensor cores (mma.m16n8k16): O^T[d][col] = sum_t A[d][t] B[t][col],
+// A = V codes - centre (half2 of two tokens of one dim), B = P'^T by movmatrix,
+// where P' = p * s_v * kPScale goes in as an fp16 pair (hi in column 2 i, lo in
+// 2 i + 1), so the two columns of a row add up to P'.V at ~22 bits of P'.
+// The centre comes back through sum P', the bias through sum p * b_v.
+template <int D, int BITS, int NQ>
+__global__ void __launch_bounds__(kWarps * 32, QCfg<D, BITS, NQ>::kCtas)
     paged_decode_q_kernel(const __grid_constant__ CUtensorMap tmK,
                           const __grid_constant__ CUtensorMap tmV, const Params p) {
-  using C = QCfg<D, BITS, NR>;
+  using C = QCfg<D, BITS, NQ>;
   constexpr int S = C::kStages;
   constexpr int NG = C::NG;
   constexpr int MT = D / 16;  // m-tiles of P.V (4 per group)
@@ -294,48 +328,74 @@ __global__ void __launch_bounds__(kWarps * 32, QCfg<D, BITS, NR>::kCtas)
   if (!sch.init(p, lane, wid, W, uq)) return;
 
   const uint64_t pol = l2_policy_evict_first();
+  // A tile's K and V codes arrive by two bulk (tensor) copies from lanes 0
+  // and 1; its scales and biases (4 x 64 bytes at D = 128) by 16-byte
+  // cp.async pieces from as many lanes, each lane's pieces tracked by the
+  // stage barrier (cp.async.mbarrier.arrive raises the pending count, then
+  // arrives when they land), so the barrier completes when all of it is in
+  // shared memory.  Small bulk copies cost the copy engine as much as large
+  // ones; as cp.async pieces the 64-byte arrays leave it two copies per
+  // tile.  The tile's table entry was loaded when the tile before it was
+  // issued (same pair), so no table load sits on the issue path.
+  int32_t pf_blk = 0;
+  int pf_key = -1;  // table index of pf_blk, -1: none
   auto issue = [&](int s, const Cursor &c) {
-    if (lane == 0) {
-      int32_t blk = p.tables[(int64_t)c.b * p.max_blocks + c.t / p.tpb];
-      if (blk < 0 || blk >= p.n_blocks) {
-        dev_error(p.err, MZ_DEVERR_BLOCK_ID);
-        blk = 0;
-      }
-      const int64_t row0 = ((int64_t)blk * p.Hkv + c.h) * p.bs + (c.t % p.tpb) * kTileTok;
-      const uint32_t bar = bar0 + 8 * s;
-      const uint32_t cs = code0 + s * C::kCodeStage;
-      const uint32_t ss = scale0 + s * C::kScaleStage;
-      mbar_arrive_expect_tx(bar, C::kTx);
+    const int tb = p.tpb == 1 ? c.t : c.t / p.tpb;
+    const int key = c.b * p.max_blocks + tb;
+    int32_t blk = key == pf_key ? pf_blk : __ldg(p.tables + key);
+    if (c.t + 1 < c.n) {
+      pf_key = c.b * p.max_blocks + (p.tpb == 1 ? c.t + 1 : (c.t + 1) / p.tpb);
+      pf_blk = __ldg(p.tables + pf_key);
+    } else {
+      pf_key = -1;
+    }
+    if (blk < 0 || blk >= p.n_blocks) {
+      if (lane == 0) dev_error(p.err, MZ_DEVERR_BLOCK_ID);
+      blk = 0;
+    }
+    const int sub = p.tpb == 1 ? 0 : c.t - tb * p.tpb;
+    const int64_t row0 = ((int64_t)blk * p.Hkv + c.h) * p.bs + sub * kTileTok;
+    const uint32_t bar = bar0 + 8 * s;
+    constexpr int kPer = C::TS / 16, kPieces = 4 * kPer;
+    if (lane < kPieces) {
+      const int arr = lane / kPer, off = (lane - arr * kPer) * 16;
+      const __half *src = arr == 0 ? p.k_scales : arr == 1 ? p.k_biases : arr == 2 ? p.v_scales : p.v_biases;
+      cp_async16(scale0 + s * C::kScaleStage + arr * C::TS + off,
+                 reinterpret_cast<const uint8_t *>(src + row0 * NG) + off);
+      asm volatile("cp.async.mbarrier.arrive.shared::cta.b64 [%0];" ::"r"(bar) : "memory");
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive_expect_tx(bar, C::kTx);
+    __syncwarp();
+    if (lane < 2) {
+      fence_proxy_async_smem();
+      const uint32_t dst = code0 + s * C::kCodeStage + lane * C::TD;
       if constexpr (C::kSwizzled) {
-        tma_load_2d(cs, &tmK, 0, static_cast<int>(row0), bar, pol);
-        tma_load_2d(cs + C::TD, &tmV, 0, static_cast<int>(row0), bar, pol);
+        tma_load_2d(dst, lane ? &tmV : &tmK, 0, static_cast<int>(row0), bar, pol);
       } else {
-        bulk_load(cs, p.kq + row0 * C::RB, C::TD, bar, pol);
-        bulk_load(cs + C::TD, p.vq + row0 * C::RB, C::TD, bar, pol);
+        bulk_load(dst, (lane ? p.vq : p.kq) + row0 * C::RB, C::TD, bar, pol);
       }
-      bulk_load(ss, p.k_scales + row0 * NG, C::TS, bar, pol);
-      bulk_load(ss + C::TS, p.k_biases + row0 * NG, C::TS, bar, pol);
-      bulk_load(ss + 2 * C::TS, p.v_scales + row0 * NG, C::TS, bar, pol);
-      bulk_load(ss + 3 * C::TS, p.v_biases + row0 * NG, C::TS, bar, pol);
     }
   };
 
   const int g = lane >> 2, cq = lane & 3;
 
-  uint32_t qb[NR][NG][4][2];  // Q B-fragments: row 8*nr + g, k-step w of group G
-  float qs[NR][2][NG];        // sum of Q over group G, rows 8*nr + 2c + {0,1}
-  float oacc[NR][MT][4];      // O^T (less centre * sum P'), P-scaled
-  float rb[NR][2][NG];        // sum_t p * b_v (lane partial over its tokens g, g+8)
-  float cp[NR][2][NG];        // sum_t P' (lane partial) -- restores the centre
-  float mrow[NR][2], lrow[NR][2];
+  uint32_t qb[NQ][NG][2][2];  // Q bytes (B fragments), column g of group nq, k-step j of group G
+  float qsc[NQ][NG];          // sq * log2(e) * scale of row 4 nq + cq, group G
+  float qsm[NQ][NG];          // sum(q~) * log2(e) * scale, same row and group
+  float oacc[NQ][MT][4];      // O^T (less centre * sum P'), P-scaled; cols (hi, lo) of one row
+  float rb[NQ][NG];           // sum_t p * b_v (lane partial over its tokens g, g+8)
+  float cp[NQ][NG];           // sum_t P' (lane partial) -- restores the centre
+  float mrow[NQ], lrow[NQ];
 
   UnitReader ur;
   bool seg_first = true;
 
   sch.refill<S>(p, 0, issue);
   bool ring_idle = true;
-  for (int i = 0; i < sch.issued; ++i) {
-    const int s = i % S;
+  int s = 0;           // stage of tile i
+  uint32_t phase = 0;  // its barrier phase
+  for (int i = 0; i < sch.issued;) {
     if (ur.need_pop()) {
       ur.pop(uq);
       seg_first = true;
@@ -347,103 +407,125 @@ __global__ void __launch_bounds__(kWarps * 32, QCfg<D, BITS, NR>::kCtas)
       const auto *q16 = static_cast<const uint16_t *>(p.q);
       const bool qbf = p.q_bf16;
 #pragma unroll
-      for (int nr = 0; nr < NR; ++nr) {
-        const int row = 8 * nr + g;
+      for (int nq = 0; nq < NQ; ++nq) {
+        // B column g holds the hi (g even) or lo (g odd) bytes of row 4 nq + g / 2
+        const int row = 4 * nq + (g >> 1);
         const bool live = row < p.rows;
         const int64_t qo = live ? row_offset(p.q_sb, p.q_st, p.q_sh, cc.b, cc.h, row, p.G) : 0;
-        float part[NG];
 #pragma unroll
         for (int G = 0; G < NG; ++G) {
-          part[G] = 0.f;
+          float f[16];  // head dims 64 G + 16 cq + e
+          float mx = 0.f;
 #pragma unroll
-          for (int w = 0; w < 4; ++w) {
-            int e0, e1, e2, e3;  // head dims of k-slots 2c, 2c+1, 2c+8, 2c+9
-            if constexpr (BITS == 8) {
-              const int d0 = 64 * G + 16 * cq + 4 * w;
-              e0 = d0; e1 = d0 + 1; e2 = d0 + 2; e3 = d0 + 3;
-            } else {
-              const int base = 64 * G + 16 * cq + 8 * (w >> 1), j0 = 2 * (w & 1);
-              e0 = base + j0; e1 = base + j0 + 4; e2 = base + j0 + 1; e3 = base + j0 + 5;
-            }
-            float f0 = 0.f, f1 = 0.f, f2 = 0.f, f3 = 0.f;
-            if (live) {
-              f0 = __half2float(__float2half_rn(load_q16(q16, qo + e0, qbf)));
-              f1 = __half2float(__float2half_rn(load_q16(q16, qo + e1, qbf)));
-              f2 = __half2float(__float2half_rn(load_q16(q16, qo + e2, qbf)));
-              f3 = __half2float(__float2half_rn(load_q16(q16, qo + e3, qbf)));
-            }
-            qb[nr][G][w][0] = pack2<false>(f0, f1);
-            qb[nr][G][w][1] = pack2<false>(f2, f3);
-            part[G] += (f0 + f1) + (f2 + f3);
+          for (int e = 0; e < 16; ++e) {
+            f[e] = live ? load_q16(q16, qo + 64 * G + 16 * cq + e, qbf) : 0.f;
+            mx = fmaxf(mx, fabsf(f[e]));
           }
-          part[G] += __shfl_xor_sync(0xffffffffu, part[G], 1);
-          part[G] += __shfl_xor_sync(0xffffffffu, part[G], 2);
-          // lanes 4r hold row 8*nr + r; this lane needs rows 2c and 2c+1
-          qs[nr][0][G] = __shfl_sync(0xffffffffu, part[G], 8 * cq);
-          qs[nr][1][G] = __shfl_sync(0xffffffffu, part[G], 8 * cq + 4);
-          rb[nr][0][G] = rb[nr][1][G] = cp[nr][0][G] = cp[nr][1][G] = 0.f;
+          mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+          mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+          const float qf = mx > 0.f ? 32639.f / mx : 0.f;
+          int qi[16];
+          int sum = 0;
+#pragma unroll
+          for (int e = 0; e < 16; ++e) {
+            int v = __float2int_rn(f[e] * qf);
+            v = max(-32639, min(32639, v));
+            qi[e] = v;
+            sum += v;
+          }
+          sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+          sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+          uint32_t by[16];
+#pragma unroll
+          for (int e = 0; e < 16; ++e) {
+            const int hi = (qi[e] + 128) >> 8;  // q16 = 256 hi + lo, lo in [-128, 127]
+            by[e] = static_cast<uint32_t>((g & 1) ? qi[e] - (hi << 8) : hi) & 0xFFu;
+          }
+#pragma unroll
+          for (int j = 0; j < 2; ++j) {
+            if constexpr (BITS == 8) {
+              // k slots 4c..4c+3 <-> dims 16c + 8j + 0..3, slots 16+4c.. <-> + 4..7
+              qb[nq][G][j][0] = by[8 * j] | by[8 * j + 1] << 8 | by[8 * j + 2] << 16 | by[8 * j + 3] << 24;
+              qb[nq][G][j][1] = by[8 * j + 4] | by[8 * j + 5] << 8 | by[8 * j + 6] << 16 | by[8 * j + 7] << 24;
+            } else {
+              // k slots 4c..4c+3 <-> dims 16c + 8j + {0,2,4,6}, slots 16+4c.. <-> {1,3,5,7}
+              qb[nq][G][j][0] = by[8 * j] | by[8 * j + 2] << 8 | by[8 * j + 4] << 16 | by[8 * j + 6] << 24;
+              qb[nq][G][j][1] = by[8 * j + 1] | by[8 * j + 3] << 8 | by[8 * j + 5] << 16 | by[8 * j + 7] << 24;
+            }
+          }
+          const float sq = mx * (1.f / 32639.f);
+          const float cs = sq * p.scale_log2, cb = static_cast<float>(sum) * sq * p.scale_log2;
+          // row 4 nq + cq (this lane's scores) was packed by lane 8 cq
+          qsc[nq][G] = __shfl_sync(0xffffffffu, cs, 8 * cq);
+          qsm[nq][G] = __shfl_sync(0xffffffffu, cb, 8 * cq);
+          rb[nq][G] = cp[nq][G] = 0.f;
         }
 #pragma unroll
-        for (int m = 0; m < MT; ++m) oacc[nr][m][0] = oacc[nr][m][1] = oacc[nr][m][2] = oacc[nr][m][3] = 0.f;
-        mrow[nr][0] = mrow[nr][1] = -INFINITY;
-        lrow[nr][0] = lrow[nr][1] = 0.f;
+        for (int m = 0; m < MT; ++m) oacc[nq][m][0] = oacc[nq][m][1] = oacc[nq][m][2] = oacc[nq][m][3] = 0.f;
+        mrow[nq] = -INFINITY;
+        lrow[nq] = 0.f;
       }
     }
 
-    if (!wait_stage<S>(p, bar0, i, sch.issued, lane)) {
+    // Two tiles of the pair per step when the piece has them (u = 0, 1); a
+    // step of one tile runs the same code with tile 1 masked out.
+    const bool has2 = ur.left >= 2 && cc.t + 1 < cc.n && i + 1 < sch.issued;
+    const int nt = has2 ? 2 : 1;
+    const int s1 = s + 1 == S ? 0 : s + 1;
+    const uint32_t phase1 = s + 1 == S ? phase ^ 1u : phase;
+    bool ready = mbar_wait_bounded(bar0 + 8 * s, phase, kTimeoutNs);
+    if (has2) ready = ready && mbar_wait_bounded(bar0 + 8 * s1, phase1, kTimeoutNs);
+    if (!__all_sync(0xffffffffu, ready)) {
+      (void)wait_stage<S>(p, bar0, i, sch.issued, lane);  // records the timeout, drains the copies
       ring_idle = false;
       break;
     }
 
-    const uint8_t *kd = codes + s * C::kCodeStage, *vd = kd + C::TD;
-    const uint8_t *ss = scales + s * C::kScaleStage;
-    const __half *ksc = reinterpret_cast<const __half *>(ss);
-    const __half *kbi = reinterpret_cast<const __half *>(ss + C::TS);
-    const __half *vsc = reinterpret_cast<const __half *>(ss + 2 * C::TS);
-    const __half *vbi = reinterpret_cast<const __half *>(ss + 3 * C::TS);
-    const int nvalid = min(kTileTok, cc.ctx - cc.t * kTileTok);
-    const bool last_tile = (cc.t == cc.n - 1);
+    const int su[2] = {s, has2 ? s1 : s};
+    int nval[2];  // valid tokens of each tile (0: no tile)
+    nval[0] = min(kTileTok, cc.ctx - cc.t * kTileTok);
+    nval[1] = has2 ? min(kTileTok, cc.ctx - (cc.t + 1) * kTileTok) : 0;
 
-    // ---- S^T = K . Q^T per group (tokens g, g+8; rows 2c, 2c+1) ----
-    float acc[NR][NG][4];
+    // ---- S = K . Q^T per group, integer (tokens g, g+8; row 4 nq + cq) ----
+    int acc[2][NQ][NG][4];
 #pragma unroll
-    for (int G = 0; G < NG; ++G) {
+    for (int u = 0; u < 2; ++u) {
+      const uint8_t *kd = codes + su[u] * C::kCodeStage;
 #pragma unroll
-      for (int nr = 0; nr < NR; ++nr) acc[nr][G][0] = acc[nr][G][1] = acc[nr][G][2] = acc[nr][G][3] = 0.f;
-      if constexpr (BITS == 8) {
-        const uint4 k0 = *reinterpret_cast<const uint4 *>(kd + code_off<C>(tok_of<C>(g), 64 * G + 16 * cq));
-        const uint4 k1 = *reinterpret_cast<const uint4 *>(kd + code_off<C>(tok_of<C>(g + 8), 64 * G + 16 * cq));
-        const uint32_t w0[4] = {k0.x, k0.y, k0.z, k0.w}, w1[4] = {k1.x, k1.y, k1.z, k1.w};
+      for (int G = 0; G < NG; ++G) {
 #pragma unroll
-        for (int w = 0; w < 4; ++w) {
-          uint32_t a[4];
-          a[0] = centred<8>(__byte_perm(w0[w], kMagic, 0x4140));  // code - 128
-          a[1] = centred<8>(__byte_perm(w1[w], kMagic, 0x4140));
-          a[2] = centred<8>(__byte_perm(w0[w], kMagic, 0x4342));
-          a[3] = centred<8>(__byte_perm(w1[w], kMagic, 0x4342));
+        for (int nq = 0; nq < NQ; ++nq)
+          acc[u][nq][G][0] = acc[u][nq][G][1] = acc[u][nq][G][2] = acc[u][nq][G][3] = 0;
+        if constexpr (BITS == 8) {
+          const uint4 k0 = *reinterpret_cast<const uint4 *>(kd + code_off<C>(tok_of<C>(g), 64 * G + 16 * cq));
+          const uint4 k1 = *reinterpret_cast<const uint4 *>(kd + code_off<C>(tok_of<C>(g + 8), 64 * G + 16 * cq));
 #pragma unroll
-          for (int nr = 0; nr < NR; ++nr) mma_16816<false>(acc[nr][G], a, qb[nr][G][w][0], qb[nr][G][w][1]);
-        }
-      } else {
-        const uint2 k0 = *reinterpret_cast<const uint2 *>(kd + code_off<C>(tok_of<C>(g), 32 * G + 8 * cq));
-        const uint2 k1 = *reinterpret_cast<const uint2 *>(kd + code_off<C>(tok_of<C>(g + 8), 32 * G + 8 * cq));
+          for (int nq = 0; nq < NQ; ++nq) {
+            mma_u8s8(acc[u][nq][G], k0.x, k1.x, k0.y, k1.y, qb[nq][G][0][0], qb[nq][G][0][1]);
+            mma_u8s8(acc[u][nq][G], k0.z, k1.z, k0.w, k1.w, qb[nq][G][1][0], qb[nq][G][1][1]);
+          }
+        } else {
+          const uint2 k0 = *reinterpret_cast<const uint2 *>(kd + code_off<C>(tok_of<C>(g), 32 * G + 8 * cq));
+          const uint2 k1 = *reinterpret_cast<const uint2 *>(kd + code_off<C>(tok_of<C>(g + 8), 32 * G + 8 * cq));
+          const uint32_t l0 = k0.x & 0x0F0F0F0Fu, h0 = (k0.x >> 4) & 0x0F0F0F0Fu;
+          const uint32_t l1 = k1.x & 0x0F0F0F0Fu, h1 = (k1.x >> 4) & 0x0F0F0F0Fu;
+          const uint32_t l2 = k0.y & 0x0F0F0F0Fu, h2 = (k0.y >> 4) & 0x0F0F0F0Fu;
+          const uint32_t l3 = k1.y & 0x0F0F0F0Fu, h3 = (k1.y >> 4) & 0x0F0F0F0Fu;
 #pragma unroll
-        for (int w = 0; w < 4; ++w) {
-          const uint32_t x0 = (w >> 1) ? k0.y : k0.x, x1 = (w >> 1) ? k1.y : k1.x;
-          const int j0 = 2 * (w & 1);
-          uint32_t a[4];
-          a[0] = centred<4>(nib2_biased(x0 >> (4 * j0)));  // code - 8
-          a[1] = centred<4>(nib2_biased(x1 >> (4 * j0)));
-          a[2] = centred<4>(nib2_biased(x0 >> (4 * (j0 + 1))));
-          a[3] = centred<4>(nib2_biased(x1 >> (4 * (j0 + 1))));
-#pragma unroll
-          for (int nr = 0; nr < NR; ++nr) mma_16816<false>(acc[nr][G], a, qb[nr][G][w][0], qb[nr][G][w][1]);
+          for (int nq = 0; nq < NQ; ++nq) {
+            mma_u8s8(acc[u][nq][G], l0, l1, h0, h1, qb[nq][G][0][0], qb[nq][G][0][1]);
+            mma_u8s8(acc[u][nq][G], l2, l3, h2, h3, qb[nq][G][1][0], qb[nq][G][1][1]);
+          }
         }
       }
     }
-    // scores: reg 2*ts + rs <-> (token tok_of(g + 8*ts), row 2c + rs)
-    float sc[NR][2][2];
-    {
+    // scores: sc[nq][2 u + ts] <-> (token tok_of(g + 8 ts) of tile u, row 4 nq + cq), log2 units
+    float sc[NQ][4];
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      const uint8_t *ss = scales + su[u] * C::kScaleStage;
+      const __half *ksc = reinterpret_cast<const __half *>(ss);
+      const __half *kbi = reinterpret_cast<const __half *>(ss + C::TS);
       float skv[2][NG], bkv[2][NG];
 #pragma unroll
       for (int ts = 0; ts < 2; ++ts) {
@@ -461,151 +543,146 @@ __global__ void __launch_bounds__(kWarps * 32, QCfg<D, BITS, NR>::kCtas)
             bkv[ts][G] = __half2float(kbi[tok_of<C>(g + 8 * ts) * NG + G]);
           }
         }
-        // the K codes entered the mma centred: fold centre * s * sum(Q) into
-        // the bias term
-#pragma unroll
-        for (int G = 0; G < NG; ++G) bkv[ts][G] = fmaf(kCodeCentre<BITS>, skv[ts][G], bkv[ts][G]);
       }
 #pragma unroll
-      for (int nr = 0; nr < NR; ++nr)
+      for (int nq = 0; nq < NQ; ++nq)
 #pragma unroll
-        for (int ts = 0; ts < 2; ++ts)
+        for (int ts = 0; ts < 2; ++ts) {
+          float x = 0.f;
 #pragma unroll
-          for (int rs = 0; rs < 2; ++rs) {
-            float x = 0.f;
-#pragma unroll
-            for (int G = 0; G < NG; ++G)
-              x += skv[ts][G] * acc[nr][G][2 * ts + rs] + bkv[ts][G] * qs[nr][rs][G];
-            x *= p.scale_log2;
-            if (tok_of<C>(g + 8 * ts) >= nvalid) x = -INFINITY;
-            sc[nr][ts][rs] = x;
+          for (int G = 0; G < NG; ++G) {
+            const int si = acc[u][nq][G][2 * ts] * 256 + acc[u][nq][G][2 * ts + 1];
+            x = fmaf(static_cast<float>(si), skv[ts][G] * qsc[nq][G], fmaf(bkv[ts][G], qsm[nq][G], x));
           }
+          if (tok_of<C>(g + 8 * ts) >= nval[u]) x = -INFINITY;
+          sc[nq][2 * u + ts] = x;
+        }
     }
 
-    // ---- online softmax per query row (rows 2c, 2c+1 of each 8-row tile) ----
-    float alpha[NR][2];
+    // ---- online softmax per query row, over the step's 32 tokens ----
+    float alpha[NQ];
     bool moved = false;
 #pragma unroll
-    for (int nr = 0; nr < NR; ++nr)
+    for (int nq = 0; nq < NQ; ++nq) {
+      float mx = fmaxf(fmaxf(sc[nq][0], sc[nq][1]), fmaxf(sc[nq][2], sc[nq][3]));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+      const float mn = fmaxf(mrow[nq], mx);
+      alpha[nq] = fast_exp2(mrow[nq] - mn);
+      moved |= alpha[nq] != 1.f;
+      mrow[nq] = mn;
 #pragma unroll
-      for (int rs = 0; rs < 2; ++rs) {
-        float mx = fmaxf(sc[nr][0][rs], sc[nr][1][rs]);
-        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
-        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
-        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
-        const float mn = fmaxf(mrow[nr][rs], mx);
-        alpha[nr][rs] = fast_exp2(mrow[nr][rs] - mn);
-        moved |= alpha[nr][rs] != 1.f;
-        mrow[nr][rs] = mn;
-        sc[nr][0][rs] = fast_exp2(sc[nr][0][rs] - mn);
-        sc[nr][1][rs] = fast_exp2(sc[nr][1][rs] - mn);
-        lrow[nr][rs] = lrow[nr][rs] * alpha[nr][rs] + sc[nr][0][rs] + sc[nr][1][rs];
-      }
+      for (int k = 0; k < 4; ++k) sc[nq][k] = fast_exp2(sc[nq][k] - mn);
+      lrow[nq] = lrow[nq] * alpha[nq] + ((sc[nq][0] + sc[nq][1]) + (sc[nq][2] + sc[nq][3]));
+    }
     if (__any_sync(0xffffffffu, moved)) {
 #pragma unroll
-      for (int nr = 0; nr < NR; ++nr) {
+      for (int nq = 0; nq < NQ; ++nq) {
 #pragma unroll
         for (int m = 0; m < MT; ++m) {
-          oacc[nr][m][0] *= alpha[nr][0];
-          oacc[nr][m][1] *= alpha[nr][1];
-          oacc[nr][m][2] *= alpha[nr][0];
-          oacc[nr][m][3] *= alpha[nr][1];
+          oacc[nq][m][0] *= alpha[nq];
+          oacc[nq][m][1] *= alpha[nq];
+          oacc[nq][m][2] *= alpha[nq];
+          oacc[nq][m][3] *= alpha[nq];
         }
 #pragma unroll
-        for (int G = 0; G < NG; ++G)
-#pragma unroll
-          for (int rs = 0; rs < 2; ++rs) {
-            rb[nr][rs][G] *= alpha[nr][rs];
-            cp[nr][rs][G] *= alpha[nr][rs];
-          }
+        for (int G = 0; G < NG; ++G) {
+          rb[nq][G] *= alpha[nq];
+          cp[nq][G] *= alpha[nq];
+        }
       }
     }
 
-    // ---- O^T += (V codes - centre) . (p * s_v)^T ; rb += p * b_v ; cp += P' ----
-    // V scales (pre-multiplied by the P' scale) and biases of this lane's
-    // tokens g, g+8 for every group; 0 past the context
-    float svg[2][NG], bvg[2][NG];
+    // ---- O^T += (V codes - centre) . P'^T ; rb += p * b_v ; cp += P' ----
 #pragma unroll
-    for (int ts = 0; ts < 2; ++ts) {
-      const int tok = tok_of<C>(g + 8 * ts);
-      const bool ok = tok < nvalid;
-      if constexpr (NG == 2) {
-        const float2 sv2 = __half22float2(*reinterpret_cast<const __half2 *>(vsc + tok * 2));
-        const float2 bv2 = __half22float2(*reinterpret_cast<const __half2 *>(vbi + tok * 2));
-        svg[ts][0] = ok ? sv2.x * C::kPScale : 0.f;
-        svg[ts][1] = ok ? sv2.y * C::kPScale : 0.f;
-        bvg[ts][0] = ok ? bv2.x : 0.f;
-        bvg[ts][1] = ok ? bv2.y : 0.f;
-      } else {
+    for (int u = 0; u < 2; ++u) {
+      const uint8_t *vd = codes + su[u] * C::kCodeStage + C::TD;
+      const uint8_t *ss = scales + su[u] * C::kScaleStage;
+      const __half *vsc = reinterpret_cast<const __half *>(ss + 2 * C::TS);
+      const __half *vbi = reinterpret_cast<const __half *>(ss + 3 * C::TS);
+      // V scales (times the P' scale) and biases of this lane's tokens g,
+      // g+8 for every group; 0 past the context (and for a missing tile)
+      float svg[2][NG], bvg[2][NG];
 #pragma unroll
-        for (int G = 0; G < NG; ++G) {
-          svg[ts][G] = ok ? __half2float(vsc[tok * NG + G]) * C::kPScale : 0.f;
-          bvg[ts][G] = ok ? __half2float(vbi[tok * NG + G]) : 0.f;
+      for (int ts = 0; ts < 2; ++ts) {
+        const int tok = tok_of<C>(g + 8 * ts);
+        const bool ok = tok < nval[u];
+        if constexpr (NG == 2) {
+          const float2 sv2 = __half22float2(*reinterpret_cast<const __half2 *>(vsc + tok * 2));
+          const float2 bv2 = __half22float2(*reinterpret_cast<const __half2 *>(vbi + tok * 2));
+          svg[ts][0] = ok ? sv2.x * C::kPScale : 0.f;
+          svg[ts][1] = ok ? sv2.y * C::kPScale : 0.f;
+          bvg[ts][0] = ok ? bv2.x : 0.f;
+          bvg[ts][1] = ok ? bv2.y : 0.f;
+        } else {
+#pragma unroll
+          for (int G = 0; G < NG; ++G) {
+            svg[ts][G] = ok ? __half2float(vsc[tok * NG + G]) * C::kPScale : 0.f;
+            bvg[ts][G] = ok ? __half2float(vbi[tok * NG + G]) : 0.f;
+          }
         }
       }
-    }
 #pragma unroll
-    for (int G = 0; G < NG; ++G) {
-      const float sv[2] = {svg[0][G], svg[1][G]}, bv[2] = {bvg[0][G], bvg[1][G]};
-      uint32_t pb[NR][2];
+      for (int G = 0; G < NG; ++G) {
+        uint32_t pb[NQ][2];
 #pragma unroll
-      for (int nr = 0; nr < NR; ++nr) {
-        const __half2 h0 = __floats2half2_rn(sc[nr][0][0] * sv[0], sc[nr][0][1] * sv[0]);
-        const __half2 h1 = __floats2half2_rn(sc[nr][1][0] * sv[1], sc[nr][1][1] * sv[1]);
-        const float2 r0 = __half22float2(h0), r1 = __half22float2(h1);
-        cp[nr][0][G] += r0.x + r1.x;
-        cp[nr][1][G] += r0.y + r1.y;
-#pragma unroll
-        for (int rs = 0; rs < 2; ++rs) rb[nr][rs][G] += sc[nr][0][rs] * bv[0] + sc[nr][1][rs] * bv[1];
-        pb[nr][0] = movmatrix_trans(*reinterpret_cast<const uint32_t *>(&h0));
-        pb[nr][1] = movmatrix_trans(*reinterpret_cast<const uint32_t *>(&h1));
-      }
-      // V codes of k indices 2c, 2c+1, 2c+8, 2c+9 (tokens tok_of(.)) for head dims 64G + 8g + [0, 8)
-      if constexpr (BITS == 8) {
-        const uint2 v0 = *reinterpret_cast<const uint2 *>(vd + code_off<C>(tok_of<C>(2 * cq), 64 * G + 8 * g));
-        const uint2 v1 = *reinterpret_cast<const uint2 *>(vd + code_off<C>(tok_of<C>(2 * cq + 1), 64 * G + 8 * g));
-        const uint2 v2 = *reinterpret_cast<const uint2 *>(vd + code_off<C>(tok_of<C>(2 * cq + 8), 64 * G + 8 * g));
-        const uint2 v3 = *reinterpret_cast<const uint2 *>(vd + code_off<C>(tok_of<C>(2 * cq + 9), 64 * G + 8 * g));
-        // byte interleaves: [ra.bk, rb.bk, ra.bk+1, rb.bk+1]
-        const uint32_t lo01a = __byte_perm(v0.x, v1.x, 0x5140), lo23a = __byte_perm(v0.x, v1.x, 0x7362);
-        const uint32_t hi01a = __byte_perm(v0.y, v1.y, 0x5140), hi23a = __byte_perm(v0.y, v1.y, 0x7362);
-        const uint32_t lo01b = __byte_perm(v2.x, v3.x, 0x5140), lo23b = __byte_perm(v2.x, v3.x, 0x7362);
-        const uint32_t hi01b = __byte_perm(v2.y, v3.y, 0x5140), hi23b = __byte_perm(v2.y, v3.y, 0x7362);
-#pragma unroll
-        for (int v = 0; v < 4; ++v) {
-          const uint32_t sel = (v & 1) ? 0x4342u : 0x4140u;
-          uint32_t a[4];
-          a[0] = centred<8>(__byte_perm((v < 2) ? lo01a : lo23a, kMagic, sel));  // d = 64G+8g+v, tokens 2c,2c+1
-          a[1] = centred<8>(__byte_perm((v < 2) ? hi01a : hi23a, kMagic, sel));  // d + 4
-          a[2] = centred<8>(__byte_perm((v < 2) ? lo01b : lo23b, kMagic, sel));  // tokens 2c+8, 2c+9
-          a[3] = centred<8>(__byte_perm((v < 2) ? hi01b : hi23b, kMagic, sel));
-#pragma unroll
-          for (int nr = 0; nr < NR; ++nr) mma_16816<false>(oacc[nr][4 * G + v], a, pb[nr][0], pb[nr][1]);
+        for (int nq = 0; nq < NQ; ++nq) {
+          const float x0 = sc[nq][2 * u] * svg[0][G], x1 = sc[nq][2 * u + 1] * svg[1][G];
+          cp[nq][G] += x0 + x1;
+          rb[nq][G] = fmaf(sc[nq][2 * u], bvg[0][G], fmaf(sc[nq][2 * u + 1], bvg[1][G], rb[nq][G]));
+          pb[nq][0] = movmatrix_trans(split_hilo(x0));  // k slots 2c, 2c+1 (tokens of rows 0..7)
+          pb[nq][1] = movmatrix_trans(split_hilo(x1));  // k slots 2c+8, 2c+9
         }
-      } else {
-        const uint32_t v0 = *reinterpret_cast<const uint32_t *>(vd + code_off<C>(tok_of<C>(2 * cq), 32 * G + 4 * g));
-        const uint32_t v1 = *reinterpret_cast<const uint32_t *>(vd + code_off<C>(tok_of<C>(2 * cq + 1), 32 * G + 4 * g));
-        const uint32_t v2 = *reinterpret_cast<const uint32_t *>(vd + code_off<C>(tok_of<C>(2 * cq + 8), 32 * G + 4 * g));
-        const uint32_t v3 = *reinterpret_cast<const uint32_t *>(vd + code_off<C>(tok_of<C>(2 * cq + 9), 32 * G + 4 * g));
+        if constexpr (BITS == 8) {
+          // V codes of k slots 2c, 2c+1, 2c+8, 2c+9 (tokens tok_of(.)), head dims 64G + 8g + [0, 8)
+          const uint2 v0 = *reinterpret_cast<const uint2 *>(vd + code_off<C>(tok_of<C>(2 * cq), 64 * G + 8 * g));
+          const uint2 v1 = *reinterpret_cast<const uint2 *>(vd + code_off<C>(tok_of<C>(2 * cq + 1), 64 * G + 8 * g));
+          const uint2 v2 = *reinterpret_cast<const uint2 *>(vd + code_off<C>(tok_of<C>(2 * cq + 8), 64 * G + 8 * g));
+          const uint2 v3 = *reinterpret_cast<const uint2 *>(vd + code_off<C>(tok_of<C>(2 * cq + 9), 64 * G + 8 * g));
+          // byte interleaves: [ra.bk, rb.bk, ra.bk+1, rb.bk+1]
+          const uint32_t lo01a = __byte_perm(v0.x, v1.x, 0x5140), lo23a = __byte_perm(v0.x, v1.x, 0x7362);
+          const uint32_t hi01a = __byte_perm(v0.y, v1.y, 0x5140), hi23a = __byte_perm(v0.y, v1.y, 0x7362);
+          const uint32_t lo01b = __byte_perm(v2.x, v3.x, 0x5140), lo23b = __byte_perm(v2.x, v3.x, 0x7362);
+          const uint32_t hi01b = __byte_perm(v2.y, v3.y, 0x5140), hi23b = __byte_perm(v2.y, v3.y, 0x7362);
 #pragma unroll
-        for (int v = 0; v < 4; ++v) {
-          // nibble v -> byte v/2 (low or high half); nibble 4 + v -> byte 2 + v/2
-          const uint32_t sl = static_cast<uint32_t>((v >> 1) | ((4 + (v >> 1)) << 8));
-          const uint32_t sh = static_cast<uint32_t>((2 + (v >> 1)) | ((6 + (v >> 1)) << 8));
-          const int sft = 4 * (v & 1);
-          uint32_t a[4];
-          a[0] = centred<4>(nib2_biased(__byte_perm(v0, v1, sl) >> sft));
-          a[1] = centred<4>(nib2_biased(__byte_perm(v0, v1, sh) >> sft));
-          a[2] = centred<4>(nib2_biased(__byte_perm(v2, v3, sl) >> sft));
-          a[3] = centred<4>(nib2_biased(__byte_perm(v2, v3, sh) >> sft));
+          for (int v = 0; v < 4; ++v) {
+            // m-tile 4G + v: row g <-> dim 64G + 8g + v, row g + 8 <-> dim 64G + 8g + 4 + v
+            const uint32_t sel = (v & 1) ? 0x4342u : 0x4140u;
+            uint32_t a[4];
+            a[0] = centred<8>(__byte_perm((v < 2) ? lo01a : lo23a, kMagic, sel));
+            a[1] = centred<8>(__byte_perm((v < 2) ? hi01a : hi23a, kMagic, sel));
+            a[2] = centred<8>(__byte_perm((v < 2) ? lo01b : lo23b, kMagic, sel));
+            a[3] = centred<8>(__byte_perm((v < 2) ? hi01b : hi23b, kMagic, sel));
 #pragma unroll
-          for (int nr = 0; nr < NR; ++nr) mma_16816<false>(oacc[nr][4 * G + v], a, pb[nr][0], pb[nr][1]);
+            for (int nq = 0; nq < NQ; ++nq) mma_16816<false>(oacc[nq][4 * G + v], a, pb[nq][0], pb[nq][1]);
+          }
+        } else {
+          // 4-bit: one word per token holds head dims 64G + 8g + [0, 8)
+          const uint32_t v0 = *reinterpret_cast<const uint32_t *>(vd + code_off<C>(tok_of<C>(2 * cq), 32 * G + 4 * g));
+          const uint32_t v1 = *reinterpret_cast<const uint32_t *>(vd + code_off<C>(tok_of<C>(2 * cq + 1), 32 * G + 4 * g));
+          const uint32_t v2 = *reinterpret_cast<const uint32_t *>(vd + code_off<C>(tok_of<C>(2 * cq + 8), 32 * G + 4 * g));
+          const uint32_t v3 = *reinterpret_cast<const uint32_t *>(vd + code_off<C>(tok_of<C>(2 * cq + 9), 32 * G + 4 * g));
+#pragma unroll
+          for (int v = 0; v < 4; ++v) {
+            // m-tile 4G + v: row g <-> dim 64G + 8g + 2v (low nibble of byte v),
+            // row g + 8 <-> dim 64G + 8g + 2v + 1 (high nibble)
+            const uint32_t sel = static_cast<uint32_t>(v | (v << 4) | ((4 + v) << 8) | ((4 + v) << 12));
+            const uint32_t z01 = __byte_perm(v0, v1, sel), z23 = __byte_perm(v2, v3, sel);
+            uint32_t a[4];
+            a[0] = centred<4>((z01 & 0x000F000Fu) | 0x64006400u);
+            a[1] = centred_hi_nibble((z01 & 0x00F000F0u) | 0x64006400u);
+            a[2] = centred<4>((z23 & 0x000F000Fu) | 0x64006400u);
+            a[3] = centred_hi_nibble((z23 & 0x00F000F0u) | 0x64006400u);
+#pragma unroll
+            for (int nq = 0; nq < NQ; ++nq) mma_16816<false>(oacc[nq][4 * G + v], a, pb[nq][0], pb[nq][1]);
+          }
         }
       }
     }
 
     // ---- piece end ----
-    if (last_tile || ur.left == 1) {
+    if (cc.t + nt == cc.n || ur.left == nt) {
       const int bh = cc.b * p.Hkv + cc.h;
       const int pbh = cc.pos - cc.t;
       const int uf = sch.unit_of(pbh), ul = sch.unit_of(pbh + cc.n - 1);
@@ -613,86 +690,98 @@ __global__ void __launch_bounds__(kWarps * 32, QCfg<D, BITS, NR>::kCtas)
       const int64_t slot = (int64_t)ur.unit + bh;
       constexpr float kInvP = 1.f / C::kPScale;
 #pragma unroll
-      for (int nr = 0; nr < NR; ++nr)
+      for (int nq = 0; nq < NQ; ++nq) {
+        float L = lrow[nq];
+        L += __shfl_xor_sync(0xffffffffu, L, 4);
+        L += __shfl_xor_sync(0xffffffffu, L, 8);
+        L += __shfl_xor_sync(0xffffffffu, L, 16);
+        float Rg[NG], Cg[NG];
 #pragma unroll
-        for (int rs = 0; rs < 2; ++rs) {
-          float L = lrow[nr][rs];
-          L += __shfl_xor_sync(0xffffffffu, L, 4);
-          L += __shfl_xor_sync(0xffffffffu, L, 8);
-          L += __shfl_xor_sync(0xffffffffu, L, 16);
-          float Rg[NG], Cg[NG];
+        for (int G = 0; G < NG; ++G) {
+          float r = rb[nq][G], c = cp[nq][G];
 #pragma unroll
-          for (int G = 0; G < NG; ++G) {
-            float r = rb[nr][rs][G], c = cp[nr][rs][G];
-#pragma unroll
-            for (int o = 4; o < 32; o <<= 1) {
-              r += __shfl_xor_sync(0xffffffffu, r, o);
-              c += __shfl_xor_sync(0xffffffffu, c, o);
-            }
-            Rg[G] = r;
-            Cg[G] = -c * kCodeCentre<BITS>;  // the V codes entered centred
+          for (int o = 4; o < 32; o <<= 1) {
+            r += __shfl_xor_sync(0xffffffffu, r, o);
+            c += __shfl_xor_sync(0xffffffffu, c, o);
           }
-          const int row = 8 * nr + 2 * cq + rs;
-          if (row >= p.rows) continue;
-          const float inv = full ? 1.f / L : 1.f;
-          const int64_t o = full ? row_offset(p.o_sb, p.o_st, p.o_sh, cc.b, cc.h, row, p.G) : 0;
-          float *pr = p.part + (slot * p.rows + row) * D;
-#pragma unroll
-          for (int G = 0; G < NG; ++G) {
-            float val[8];  // head dims 64G + 8g + j, j = 0..7
-#pragma unroll
-            for (int v = 0; v < 4; ++v) {
-              val[v] = ((oacc[nr][4 * G + v][rs] - Cg[G]) * kInvP + Rg[G]) * inv;
-              val[4 + v] = ((oacc[nr][4 * G + v][2 + rs] - Cg[G]) * kInvP + Rg[G]) * inv;
-            }
-            const int d0 = 64 * G + 8 * g;
-#pragma unroll
-            for (int j = 0; j < 8; j += 2) {
-              if (full)
-                store_pair(p, o + d0 + j, val[j], val[j + 1]);
-              else
-                *reinterpret_cast<float2 *>(pr + d0 + j) = make_float2(val[j], val[j + 1]);
-            }
-          }
-          if (!full && g == 0)
-            *reinterpret_cast<float2 *>(p.ml + (slot * p.rows + row) * 2) =
-                make_float2(mrow[nr][rs], L);
+          Rg[G] = r;
+          Cg[G] = c * kCodeCentre<BITS>;  // the V codes entered centred
         }
+        const int row = 4 * nq + cq;
+        if (row >= p.rows) continue;
+        const float inv = full ? 1.f / L : 1.f;
+        const int64_t o = full ? row_offset(p.o_sb, p.o_st, p.o_sh, cc.b, cc.h, row, p.G) : 0;
+        float *pr = p.part + (slot * p.rows + row) * D;
+#pragma unroll
+        for (int G = 0; G < NG; ++G) {
+          float val[8];  // head dims 64G + 8g + j, j = 0..7
+#pragma unroll
+          for (int v = 0; v < 4; ++v) {
+            const float x0 = ((oacc[nq][4 * G + v][0] + oacc[nq][4 * G + v][1] + Cg[G]) * kInvP + Rg[G]) * inv;
+            const float x1 = ((oacc[nq][4 * G + v][2] + oacc[nq][4 * G + v][3] + Cg[G]) * kInvP + Rg[G]) * inv;
+            if constexpr (BITS == 8) {
+              val[v] = x0;
+              val[4 + v] = x1;
+            } else {
+              val[2 * v] = x0;
+              val[2 * v + 1] = x1;
+            }
+          }
+          const int d0 = 64 * G + 8 * g;
+#pragma unroll
+          for (int j = 0; j < 8; j += 2) {
+            if (full)
+              store_pair(p, o + d0 + j, val[j], val[j + 1]);
+            else
+              *reinterpret_cast<float2 *>(pr + d0 + j) = make_float2(val[j], val[j + 1]);
+          }
+        }
+        if (!full && g == 0)
+          *reinterpret_cast<float2 *>(p.ml + (slot * p.rows + row) * 2) = make_float2(mrow[nq], L);
+      }
       if (!full) arrive_or_defer<D>(p, cc, bh, uf, ul - uf + 1, lane, dq, nd);
       seg_first = true;
     }
 
     __syncwarp();
-    --ur.left;
-    advance(ur.cc, p);
-    sch.refill<S>(p, i + 1, issue);
+    for (int k = 0; k < nt; ++k) {
+      --ur.left;
+      advance(ur.cc, p);
+      if (++s == S) {
+        s = 0;
+        phase ^= 1u;
+      }
+    }
+    i += nt;
+    sch.refill<S>(p, i, issue);
   }
   run_deferred<D>(p, dq, nd, codes, S * C::kCodeStage, ring_idle, lane);
 }
 
-template <int D, int BITS, int NR>
+template <int D, int BITS, int NQ>
 int q_kernel_ctas_per_sm(int *out) {
   static int cached = -1;
   static std::once_flag once;
   static cudaError_t err = cudaSuccess;
-  return kernel_occupancy(paged_decode_q_kernel<D, BITS, NR>, QCfg<D, BITS, NR>::kSmemBytes,
+  return kernel_occupancy(paged_decode_q_kernel<D, BITS, NQ>, QCfg<D, BITS, NQ>::kSmemBytes,
                           &cached, &once, &err, out);
 }
 
-template <int NR>
-int q_ctas_per_sm_nr(int D, int bits, int *out) {
+template <int NQ>
+int q_ctas_per_sm_nq(int D, int bits, int *out) {
   if (D == 128)
-    return bits == 8 ? q_kernel_ctas_per_sm<128, 8, NR>(out) : q_kernel_ctas_per_sm<128, 4, NR>(out);
-  return bits == 8 ? q_kernel_ctas_per_sm<64, 8, NR>(out) : q_kernel_ctas_per_sm<64, 4, NR>(out);
+    return bits == 8 ? q_kernel_ctas_per_sm<128, 8, NQ>(out) : q_kernel_ctas_per_sm<128, 4, NQ>(out);
+  return bits == 8 ? q_kernel_ctas_per_sm<64, 8, NQ>(out) : q_kernel_ctas_per_sm<64, 4, NQ>(out);
 }
 
-// Occupancy used to size grids and workspaces: the larger of the two query-row
-// instantiations, so one workspace size fits both.
+// Occupancy used to size grids and workspaces: the largest of the query-row
+// instantiations, so one workspace size fits all of them.
 int q_ctas_per_sm(int D, int bits, int *out) {
-  int a = 0, b = 0;
-  if (int rc = q_ctas_per_sm_nr<1>(D, bits, &a)) return rc;
-  if (int rc = q_ctas_per_sm_nr<2>(D, bits, &b)) return rc;
-  *out = a > b ? a : b;
+  int a = 0, b = 0, c = 0;
+  if (int rc = q_ctas_per_sm_nq<1>(D, bits, &a)) return rc;
+  if (int rc = q_ctas_per_sm_nq<2>(D, bits, &b)) return rc;
+  if (int rc = q_ctas_per_sm_nq<4>(D, bits, &c)) return rc;
+  *out = std::max(a, std::max(b, c));
   return MZ_OK;
 }
 
@@ -914,14 +1003,14 @@ extern "C" int mz_paged_decode_q(void *out, int32_t out_dtype, int64_t out_seq_s
   p.err = dev_err;
 
   const int64_t rows_total = n_blocks * n_kv_heads * block_size;
-  // The tcgen05 form (head_dim 128; 1, 2, 4, 8 or 16 query rows per KV head)
-  // or the mma.sync kernel.  MLXZ_B200_QDECODE_TC=1 / 0 forces one; by default
-  // 8-bit stores take the tcgen05 form and 4-bit stores the mma.sync kernel
-  // (faster there: the tcgen05 form widens 4-bit codes to bytes on the way).
-  // The tcgen05 grid is one CTA per SM, or fewer when num_warps caps the
-  // launch (its partials then fit the workspace sized for num_warps).
+  // The mma.sync kernel (the default for both widths: integer Q.K^T on the
+  // tensor cores, two tiles per step, and faster than the tcgen05 form at the
+  // 8B shape) or, with MLXZ_B200_QDECODE_TC=1, the tcgen05 form (head_dim
+  // 128; 1, 2, 4, 8 or 16 query rows per KV head).  The tcgen05 grid is one
+  // CTA per SM, or fewer when num_warps caps the launch (its partials then
+  // fit the workspace sized for num_warps).
   const int tc_mode = env_int("MLXZ_B200_QDECODE_TC", -1, -1, 1);
-  const bool use_tc = qtc_supports(head_dim, rows) && (tc_mode == 1 || (tc_mode == -1 && bits == 8));
+  const bool use_tc = qtc_supports(head_dim, rows) && tc_mode == 1;
   if (use_tc) {
     const int sms = sm_count(device);
     if (sms <= 0) return fail(MZ_ERR_CUDA, "%s: cannot query SM count of device %d", fn, device);
@@ -943,21 +1032,24 @@ extern "C" int mz_paged_decode_q(void *out, int32_t out_dtype, int64_t out_seq_s
   if (int rc = q_ctas_per_sm(head_dim, bits, &per_sm)) return rc;
   const unsigned grid = static_cast<unsigned>(warps / kWarps);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-#define MZ_LQ(D_, B_, NR_)                                                                    \
-  paged_decode_q_kernel<D_, B_, NR_><<<grid, kWarps * 32, QCfg<D_, B_, NR_>::kSmemBytes, s>>>(tk, tv, p)
-  if (rows <= 8) {
-    if (head_dim == 128) {
-      if (bits == 8) MZ_LQ(128, 8, 1); else MZ_LQ(128, 4, 1);
-    } else {
-      if (bits == 8) MZ_LQ(64, 8, 1); else MZ_LQ(64, 4, 1);
-    }
-  } else {
-    if (head_dim == 128) {
-      if (bits == 8) MZ_LQ(128, 8, 2); else MZ_LQ(128, 4, 2);
-    } else {
-      if (bits == 8) MZ_LQ(64, 8, 2); else MZ_LQ(64, 4, 2);
-    }
-  }
+#define MZ_LQ(D_, B_, NQ_)                                                                    \
+  paged_decode_q_kernel<D_, B_, NQ_><<<grid, kWarps * 32, QCfg<D_, B_, NQ_>::kSmemBytes, s>>>(tk, tv, p)
+#define MZ_LQ_NQ(NQ_)                                                \
+  do {                                                               \
+    if (head_dim == 128) {                                           \
+      if (bits == 8) MZ_LQ(128, 8, NQ_); else MZ_LQ(128, 4, NQ_);    \
+    } else {                                                         \
+      if (bits == 8) MZ_LQ(64, 8, NQ_); else MZ_LQ(64, 4, NQ_);      \
+    }                                                                \
+  } while (0)
+  // query rows per KV head in groups of four
+  if (rows <= 4)
+    MZ_LQ_NQ(1);
+  else if (rows <= 8)
+    MZ_LQ_NQ(2);
+  else
+    MZ_LQ_NQ(4);
+#undef MZ_LQ_NQ
 #undef MZ_LQ
   MZ_CHECK_LAUNCH(fn);
   return MZ_OK;

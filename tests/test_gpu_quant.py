@@ -124,7 +124,12 @@ QCASES = [
 
 @pytest.mark.parametrize("bits,D,G,dtype,ctx,nw", QCASES)
 @pytest.mark.parametrize("out32", [True, False])
-def test_paged_decode_q_vs_oracle(cuda, bits, D, G, dtype, ctx, nw, out32):
+@pytest.mark.parametrize("form", ["default", "mma_sync"])
+def test_paged_decode_q_vs_oracle(cuda, bits, D, G, dtype, ctx, nw, out32, form, monkeypatch):
+    """Every case through the default dispatch and through the mma.sync
+    kernel (integer Q.K^T, 1, 2 or 4 groups of four query rows)."""
+    if form == "mma_sync":
+        monkeypatch.setenv("MLXZ_B200_QDECODE_TC", "0")
     Hkv = 2 if G == 16 else 4
     case = _quant_case(40 + bits + D + G, ctx, Hkv, D, bits, dtype, G=G)
     pools = _dev_pools(case["host"], cuda)
