@@ -297,8 +297,10 @@ __global__ void __launch_bounds__(kWarps * 32, QCfg<D, BITS, NQ>::kCtas)
   constexpr int MT = D / 16;  // m-tiles of P.V (4 per group)
 
   extern __shared__ uint8_t smem_raw[];
-  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
-                                              ~static_cast<uintptr_t>(1023));
+  // 1024-byte aligned base, derived from the shared array by pointer
+  // arithmetic so that the compiler keeps every access in the shared window
+  // (a round trip through an integer would turn them into generic accesses)
+  uint8_t *smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int W = gridDim.x * kWarps;
@@ -328,8 +330,8 @@ __global__ void __launch_bounds__(kWarps * 32, QCfg<D, BITS, NQ>::kCtas)
   if (!sch.init(p, lane, wid, W, uq)) return;
 
   const uint64_t pol = l2_policy_evict_first();
-  // A tile's K and V codes arrive by two bulk (tensor) copies from lanes 0
-  // and 1; its scales and biases (4 x 64 bytes at D = 128) by 16-byte
+  // A tile's K and V codes arrive by two bulk (tensor) copies from lane 0;
+  // its scales and biases (4 x 64 bytes at D = 128) by 16-byte
   // cp.async pieces from as many lanes, each lane's pieces tracked by the
   // stage barrier (cp.async.mbarrier.arrive raises the pending count, then
   // arrives when they land), so the barrier completes when all of it is in
@@ -339,6 +341,14 @@ __global__ void __launch_bounds__(kWarps * 32, QCfg<D, BITS, NQ>::kCtas)
   // issued (same pair), so no table load sits on the issue path.
   int32_t pf_blk = 0;
   int pf_key = -1;  // table index of pf_blk, -1: none
+  // this lane's 16-byte piece of the four scale / bias arrays (lanes < kPieces)
+  constexpr int kPer = C::TS / 16, kPieces = 4 * kPer;
+  const int pc_arr = min(lane / kPer, 3);
+  const uint32_t pc_off = static_cast<uint32_t>(lane - pc_arr * kPer) * 16u;
+  const uint32_t pc_dst = pc_arr * C::TS + pc_off;
+  const uint8_t *pc_src =
+      reinterpret_cast<const uint8_t *>(pc_arr == 0 ? p.k_scales : pc_arr == 1 ? p.k_biases
+                                        : pc_arr == 2 ? p.v_scales : p.v_biases) + pc_off;
   auto issue = [&](int s, const Cursor &c) {
     const int tb = p.tpb == 1 ? c.t : c.t / p.tpb;
     const int key = c.b * p.max_blocks + tb;
@@ -356,24 +366,22 @@ __global__ void __launch_bounds__(kWarps * 32, QCfg<D, BITS, NQ>::kCtas)
     const int sub = p.tpb == 1 ? 0 : c.t - tb * p.tpb;
     const int64_t row0 = ((int64_t)blk * p.Hkv + c.h) * p.bs + sub * kTileTok;
     const uint32_t bar = bar0 + 8 * s;
-    constexpr int kPer = C::TS / 16, kPieces = 4 * kPer;
     if (lane < kPieces) {
-      const int arr = lane / kPer, off = (lane - arr * kPer) * 16;
-      const __half *src = arr == 0 ? p.k_scales : arr == 1 ? p.k_biases : arr == 2 ? p.v_scales : p.v_biases;
-      cp_async16(scale0 + s * C::kScaleStage + arr * C::TS + off,
-                 reinterpret_cast<const uint8_t *>(src + row0 * NG) + off);
+      cp_async16(scale0 + s * C::kScaleStage + pc_dst, pc_src + row0 * (NG * 2));
       asm volatile("cp.async.mbarrier.arrive.shared::cta.b64 [%0];" ::"r"(bar) : "memory");
     }
-    __syncwarp();
-    if (lane == 0) mbar_arrive_expect_tx(bar, C::kTx);
-    __syncwarp();
-    if (lane < 2) {
+    __syncwarp();  // every piece's pending count is raised before the barrier can complete
+    if (lane == 0) {
+      // bulk and tensor copies take warp-uniform operands: one lane issues both
       fence_proxy_async_smem();
-      const uint32_t dst = code0 + s * C::kCodeStage + lane * C::TD;
+      mbar_arrive_expect_tx(bar, C::kTx);
+      const uint32_t dst = code0 + s * C::kCodeStage;
       if constexpr (C::kSwizzled) {
-        tma_load_2d(dst, lane ? &tmV : &tmK, 0, static_cast<int>(row0), bar, pol);
+        tma_load_2d(dst, &tmK, 0, static_cast<int>(row0), bar, pol);
+        tma_load_2d(dst + C::TD, &tmV, 0, static_cast<int>(row0), bar, pol);
       } else {
-        bulk_load(dst, (lane ? p.vq : p.kq) + row0 * C::RB, C::TD, bar, pol);
+        bulk_load(dst, p.kq + row0 * C::RB, C::TD, bar, pol);
+        bulk_load(dst + C::TD, p.vq + row0 * C::RB, C::TD, bar, pol);
       }
     }
   };
