@@ -330,59 +330,103 @@ __global__ void __launch_bounds__(kWarps * 32, QCfg<D, BITS, NQ>::kCtas)
   if (!sch.init(p, lane, wid, W, uq)) return;
 
   const uint64_t pol = l2_policy_evict_first();
-  // A tile's K and V codes arrive by two bulk (tensor) copies from lane 0;
-  // its scales and biases (4 x 64 bytes at D = 128) by 16-byte
-  // cp.async pieces from as many lanes, each lane's pieces tracked by the
-  // stage barrier (cp.async.mbarrier.arrive raises the pending count, then
-  // arrives when they land), so the barrier completes when all of it is in
-  // shared memory.  Small bulk copies cost the copy engine as much as large
-  // ones; as cp.async pieces the 64-byte arrays leave it two copies per
-  // tile.  The tile's table entry was loaded when the tile before it was
-  // issued (same pair), so no table load sits on the issue path.
+  // Copies go out for up to two tiles at a time, tile A from lanes 0..15 and
+  // tile B from lanes 16..31.  A tile's K and V codes arrive by two bulk
+  // (tensor) copies, which take warp-uniform operands, so lane 0 issues them
+  // for both tiles; its scales and biases (4 x 64 bytes at D = 128) arrive
+  // as 16-byte cp.async pieces from the lanes of its half, each piece tracked
+  // by the stage barrier (cp.async.mbarrier.arrive raises the pending count,
+  // then arrives when the piece lands), so the barrier completes when all of
+  // the tile is in shared memory.  Small bulk copies cost the copy engine as
+  // much as large ones; as cp.async pieces the 64-byte arrays leave it two
+  // copies per tile.  When a half issues a tile it also loads the table entry
+  // of the tile two on, which it issues next, so no table load sits on the
+  // issue path.
+  const int half = lane >> 4, hl = lane & 15;
   int32_t pf_blk = 0;
   int pf_key = -1;  // table index of pf_blk, -1: none
-  // this lane's 16-byte piece of the four scale / bias arrays (lanes < kPieces)
+  // this lane's 16-byte piece of its tile's four scale / bias arrays (hl < kPieces)
   constexpr int kPer = C::TS / 16, kPieces = 4 * kPer;
-  const int pc_arr = min(lane / kPer, 3);
-  const uint32_t pc_off = static_cast<uint32_t>(lane - pc_arr * kPer) * 16u;
+  static_assert(kPieces <= 16, "scale pieces exceed a half warp");
+  const int pc_arr = min(hl / kPer, 3);
+  const uint32_t pc_off = static_cast<uint32_t>(hl - pc_arr * kPer) * 16u;
   const uint32_t pc_dst = pc_arr * C::TS + pc_off;
   const uint8_t *pc_src =
       reinterpret_cast<const uint8_t *>(pc_arr == 0 ? p.k_scales : pc_arr == 1 ? p.k_biases
                                         : pc_arr == 2 ? p.v_scales : p.v_biases) + pc_off;
-  auto issue = [&](int s, const Cursor &c) {
-    const int tb = p.tpb == 1 ? c.t : c.t / p.tpb;
-    const int key = c.b * p.max_blocks + tb;
-    int32_t blk = key == pf_key ? pf_blk : __ldg(p.tables + key);
-    if (c.t + 1 < c.n) {
-      pf_key = c.b * p.max_blocks + (p.tpb == 1 ? c.t + 1 : (c.t + 1) / p.tpb);
-      pf_blk = __ldg(p.tables + pf_key);
-    } else {
-      pf_key = -1;
-    }
-    if (blk < 0 || blk >= p.n_blocks) {
-      if (lane == 0) dev_error(p.err, MZ_DEVERR_BLOCK_ID);
-      blk = 0;
-    }
-    const int sub = p.tpb == 1 ? 0 : c.t - tb * p.tpb;
-    const int64_t row0 = ((int64_t)blk * p.Hkv + c.h) * p.bs + sub * kTileTok;
-    const uint32_t bar = bar0 + 8 * s;
-    if (lane < kPieces) {
-      cp_async16(scale0 + s * C::kScaleStage + pc_dst, pc_src + row0 * (NG * 2));
-      asm volatile("cp.async.mbarrier.arrive.shared::cta.b64 [%0];" ::"r"(bar) : "memory");
-    }
-    __syncwarp();  // every piece's pending count is raised before the barrier can complete
-    if (lane == 0) {
-      // bulk and tensor copies take warp-uniform operands: one lane issues both
-      fence_proxy_async_smem();
-      mbar_arrive_expect_tx(bar, C::kTx);
-      const uint32_t dst = code0 + s * C::kCodeStage;
-      if constexpr (C::kSwizzled) {
-        tma_load_2d(dst, &tmK, 0, static_cast<int>(row0), bar, pol);
-        tma_load_2d(dst + C::TD, &tmV, 0, static_cast<int>(row0), bar, pol);
+  auto issue2 = [&](bool two, int sa, const Cursor &ca, int sb, const Cursor &cb) {
+    int64_t row0 = 0;
+    if (half == 0 || two) {
+      const Cursor &c = half ? cb : ca;
+      const int s = half ? sb : sa;
+      const int tb = p.tpb == 1 ? c.t : c.t / p.tpb;
+      const int key = c.b * p.max_blocks + tb;
+      int32_t blk = key == pf_key ? pf_blk : __ldg(p.tables + key);
+      if (c.t + 2 < c.n) {
+        pf_key = c.b * p.max_blocks + (p.tpb == 1 ? c.t + 2 : (c.t + 2) / p.tpb);
+        pf_blk = __ldg(p.tables + pf_key);
       } else {
-        bulk_load(dst, p.kq + row0 * C::RB, C::TD, bar, pol);
-        bulk_load(dst + C::TD, p.vq + row0 * C::RB, C::TD, bar, pol);
+        pf_key = -1;
       }
+      if (blk < 0 || blk >= p.n_blocks) {
+        if (hl == 0) dev_error(p.err, MZ_DEVERR_BLOCK_ID);
+        blk = 0;
+      }
+      const int sub = p.tpb == 1 ? 0 : c.t - tb * p.tpb;
+      row0 = ((int64_t)blk * p.Hkv + c.h) * p.bs + sub * kTileTok;
+      if (hl < kPieces) {
+        cp_async16(scale0 + s * C::kScaleStage + pc_dst, pc_src + row0 * (NG * 2));
+        asm volatile("cp.async.mbarrier.arrive.shared::cta.b64 [%0];" ::"r"(bar0 + 8 * s) : "memory");
+      }
+    }
+    __syncwarp();  // every piece's pending count is raised before its barrier can complete
+    const int64_t row_b = __shfl_sync(0xffffffffu, row0, 16);
+    if (lane == 0) {
+      fence_proxy_async_smem();
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        if (u == 1 && !two) break;
+        const int st = u ? sb : sa;
+        const int64_t r = u ? row_b : row0;
+        const uint32_t bar = bar0 + 8 * st;
+        const uint32_t dst = code0 + st * C::kCodeStage;
+        mbar_arrive_expect_tx(bar, C::kTx);
+        if constexpr (C::kSwizzled) {
+          tma_load_2d(dst, &tmK, 0, static_cast<int>(r), bar, pol);
+          tma_load_2d(dst + C::TD, &tmV, 0, static_cast<int>(r), bar, pol);
+        } else {
+          bulk_load(dst, p.kq + r * C::RB, C::TD, bar, pol);
+          bulk_load(dst + C::TD, p.vq + r * C::RB, C::TD, bar, pol);
+        }
+      }
+    }
+  };
+  // keep S tiles in flight, two per round where two stages are free and the
+  // unit has two tiles left
+  auto refill = [&](int consumed) {
+    while (!sch.p_done && sch.issued - consumed < S) {
+      if (sch.p_left == 0 && !sch.next_unit(p)) {
+        sch.p_done = true;
+        break;
+      }
+      const bool two = sch.p_left >= 2 && sch.issued - consumed <= S - 2;
+      const Cursor ca = sch.pc;
+      const int sa = sch.istage;
+      advance(sch.pc, p);
+      --sch.p_left;
+      ++sch.issued;
+      if (++sch.istage == S) sch.istage = 0;
+      Cursor cb = ca;
+      int sb = sa;
+      if (two) {
+        cb = sch.pc;
+        sb = sch.istage;
+        advance(sch.pc, p);
+        --sch.p_left;
+        ++sch.issued;
+        if (++sch.istage == S) sch.istage = 0;
+      }
+      issue2(two, sa, ca, sb, cb);
     }
   };
 
@@ -399,7 +443,7 @@ __global__ void __launch_bounds__(kWarps * 32, QCfg<D, BITS, NQ>::kCtas)
   UnitReader ur;
   bool seg_first = true;
 
-  sch.refill<S>(p, 0, issue);
+  refill(0);
   bool ring_idle = true;
   int s = 0;           // stage of tile i
   uint32_t phase = 0;  // its barrier phase
@@ -761,7 +805,7 @@ __global__ void __launch_bounds__(kWarps * 32, QCfg<D, BITS, NQ>::kCtas)
       }
     }
     i += nt;
-    sch.refill<S>(p, i, issue);
+    refill(i);
   }
   run_deferred<D>(p, dq, nd, codes, S * C::kCodeStage, ring_idle, lane);
 }
