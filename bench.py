@@ -66,13 +66,17 @@ def parse_args():
     ap.add_argument("--batch-invariant", action="store_true",
                     help="decode: MZ_DECODE_BATCH_INVARIANT (whole pairs, batch-independent bytes)")
     ap.add_argument("--config", default="decode",
-                    choices=["decode", "prefix", "quant", "sharded70b", "prefill", "kernels"],
+                    choices=["decode", "prefix", "quant", "sharded70b", "prefill", "kernels",
+                             "peer_pair"],
                     help="decode: the paged decode step (headline); prefix: prefix-cache "
                          "restore / copy-on-write / host-tier eviction and reload; quant: "
                          "4/8-bit quantised KV decode step; sharded70b: 70B-shape decode "
                          "step head-sharded over the ranks (strong scaling); prefill: one "
                          "chunked-prefill iteration (append + causal attention per layer); "
-                         "kernels: each data-movement kernel timed alone")
+                         "kernels: each data-movement kernel timed alone; peer_pair: one "
+                         "process driving two GPUs, the 70B-shape fused decode + all-gather "
+                         "launch of rank 0 of 2 timed on GPU 0 (its output rows stored into "
+                         "GPU 1's buffer over NVLink), for profiling the launch alone")
     ap.add_argument("--bits", type=int, default=8, choices=[4, 8])
     ap.add_argument("--kv-bits", type=int, default=16, choices=[4, 8, 16],
                     help="prefill: the K/V store (16 = bf16; 8 / 4 = quantised, "
@@ -1379,6 +1383,153 @@ def run_kernels(args, local_rank: int) -> dict:
 
 
 
+def run_peer_pair(args) -> dict:
+    """The fused decode + all-gather launch (mz_paged_append_decode_allgather)
+    of a 2-rank KV-head split of the 70B-shape workload (256 sequences,
+    lognormal ctx; rank r holds KV heads [4r, 4r + 4) and q heads
+    [32r, 32r + 32)), both ranks driven from one process: rank r on GPU r, its
+    gathered buffer [B, 64, 128] on GPU r, the peer's buffer reached through
+    peer access.  One model layer is resident per GPU.  Each step launches
+    rank 0 on GPU 0 and rank 1 on GPU 1 (neither waits on the other inside a
+    kernel), synchronises both devices, then runs each rank's bounded signal
+    wait, which finds the peer's signal already set.  CUDA events on GPU 0
+    time rank 0's launches.  Afterwards both gathered buffers must equal,
+    bytewise, the two ranks' ordinary fused append + decode outputs side by
+    side.  The printed line carries the launch time, its KV read rate and the
+    bytes its rows put on NVLink (rows x head_dim x 2 B per pair, to one
+    peer), which an ncu capture of GPU 0 (`--devices 0`) can set against the
+    NVLink counters."""
+    import ctypes
+
+    import numpy as np
+    import torch
+
+    from mlxz_b200 import _native as nat
+    from mlxz_b200 import ops
+
+    if torch.cuda.device_count() < 2:
+        return {"config": "peer_pair", "unavailable": "needs two visible GPUs"}
+    if not (torch.cuda.can_device_access_peer(0, 1) and torch.cuda.can_device_access_peer(1, 0)):
+        return {"config": "peer_pair", "unavailable": "GPUs 0 and 1 have no peer access"}
+    from cuda.bindings import runtime as cudart
+
+    for a, b in ((0, 1), (1, 0)):
+        torch.cuda.set_device(a)
+        torch.cuda.synchronize(a)
+        cudart.cudaSetDevice(a)
+        err = cudart.cudaDeviceEnablePeerAccess(b, 0)[0]
+        if err not in (cudart.cudaError_t.cudaSuccess,
+                       cudart.cudaError_t.cudaErrorPeerAccessAlreadyEnabled):
+            return {"config": "peer_pair", "unavailable": f"cudaDeviceEnablePeerAccess: {err}"}
+    w = Workload(True, 2, 1, 1e9, args.seed, True)
+    N, B, hkv, hq, hq_all = 2, w.B, w.hkv, w.hq, w.hq_all
+    gen = torch.Generator().manual_seed(args.seed)
+    perm = torch.randperm(w.n_blocks, generator=gen).to(torch.int32)
+    width = int(w.need.max())
+    tables = torch.full((B, width), -1, dtype=torch.int32)
+    pos = 0
+    for b in range(B):
+        n = int(w.need[b])
+        tables[b, :n] = perm[pos:pos + n]
+        pos += n
+    lens = torch.from_numpy((w.ctx + 1).astype(np.int32))
+    elem = 2
+    block_bytes = hq * D * elem
+    ranks = []
+    for r in range(N):
+        dev = torch.device("cuda", r)
+        torch.cuda.set_device(r)
+        g = torch.Generator(device=dev).manual_seed(args.seed * 7 + r)
+        pool_shape = (w.n_blocks, hkv, BS, D)
+        rk = {
+            "dev": dev,
+            "k": torch.randn(pool_shape, generator=g, device=dev, dtype=torch.bfloat16),
+            "v": torch.randn(pool_shape, generator=g, device=dev, dtype=torch.bfloat16),
+            "q": torch.randn((B, hq, D), generator=g, device=dev, dtype=torch.bfloat16),
+            "kn": torch.randn((B, hkv, D), generator=g, device=dev, dtype=torch.bfloat16),
+            "vn": torch.randn((B, hkv, D), generator=g, device=dev, dtype=torch.bfloat16),
+            "tables": tables.to(dev), "lens": lens.to(dev),
+            "full": torch.zeros((B, hq_all, D), device=dev, dtype=torch.bfloat16),
+            "sig": torch.zeros(N, device=dev, dtype=torch.int32),
+            "arrivals": torch.zeros(1, device=dev, dtype=torch.int32),
+        }
+        rk["ws"] = ops.decode_workspace(B, hkv, hq // hkv, D, r, 0, shared=False)
+        ranks.append(rk)
+    peers = []
+    for r in range(N):
+        pe = nat.PeerOutputs()
+        pe.n_ranks, pe.rank = N, r
+        for s2 in range(N):
+            pe.out[s2] = ranks[s2]["full"].data_ptr() + r * block_bytes
+            pe.signal[s2] = ranks[s2]["sig"].data_ptr()
+        pe.arrivals = ranks[r]["arrivals"].data_ptr()
+        peers.append(pe)
+    epoch = 0
+
+    def step(timed=None):
+        nonlocal epoch
+        epoch += 1
+        for r in range(N):
+            rk = ranks[r]
+            peers[r].epoch = epoch
+            with torch.cuda.device(r):
+                if r == 0 and timed is not None:
+                    timed[0].record()
+                ops.paged_append_decode_allgather(
+                    peers[r], rk["q"], rk["k"], rk["v"], rk["kn"], rk["vn"], rk["tables"],
+                    rk["lens"], hq_all * D, D, torch.bfloat16, workspace=rk["ws"])
+                if r == 0 and timed is not None:
+                    timed[1].record()
+        for r in range(N):
+            torch.cuda.synchronize(r)
+        for r in range(N):
+            with torch.cuda.device(r):
+                ops.peer_wait(ranks[r]["sig"], N, r, epoch)
+        for r in range(N):
+            torch.cuda.synchronize(r)
+            ops.check_device_errors(r)
+
+    for _ in range(max(1, args.warmup)):
+        step()
+    ms = []
+    for _ in range(max(1, args.steps)):
+        with torch.cuda.device(0):
+            ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+        step(ev)
+        ms.append(ev[0].elapsed_time(ev[1]))
+    # parity: each rank's ordinary fused launch, side by side, bytewise
+    ok = True
+    local = []
+    for r in range(N):
+        rk = ranks[r]
+        with torch.cuda.device(r):
+            local.append(ops.paged_append_decode(rk["q"], rk["k"], rk["v"], rk["kn"], rk["vn"],
+                                                 rk["tables"], rk["lens"]).to("cuda:0"))
+        torch.cuda.synchronize(r)
+    want = torch.cat(local, dim=1)
+    for r in range(N):
+        got = ranks[r]["full"].to("cuda:0")
+        ok = ok and bool(torch.equal(got.view(torch.int16), want.view(torch.int16)))
+    dec_ms = statistics.median(ms)
+    nvlink_bytes = B * hq * D * elem * (N - 1)
+    peak, peak_kind = peaks()
+    return {
+        "config": "peer_pair",
+        "workload": (f"rank 0 of a 2-GPU KV-head split of the 70B KV shape: {B} seqs, ctx "
+                     f"lognormal(median {C5_MEDIAN}, sigma {C5_SIGMA}) in [{C5_LO},{C5_HI}], "
+                     f"{hkv} kv heads and {hq} q heads per GPU, head_dim {D}, block {BS}, bf16; "
+                     "one process driving GPUs 0 and 1"),
+        "kernel": "paged_decode_gather_kernel<128,bf16> (mz_paged_append_decode_allgather)",
+        "steps": len(ms), "launch_ms_median": round(dec_ms, 4),
+        "kv_read_gbs": round(w.decode_alg_bytes / (dec_ms / 1e3) / 1e9, 1),
+        "hbm_frac": round(w.decode_alg_bytes / (dec_ms / 1e3) / 1e9 / peak, 4),
+        "peak": peak, "peak_kind": peak_kind,
+        "alg_bytes_per_launch": w.decode_alg_bytes,
+        "nvlink_store_bytes_per_launch": nvlink_bytes,
+        "parity": {"gathered_equal_to_per_shard_launches": ok},
+    }
+
+
 def main():
     args = parse_args()
     rank = int(os.environ.get("RANK", "0"))
@@ -1403,6 +1554,11 @@ def main():
     elif args.config == "kernels":
         if rank == 0:
             print(json.dumps(run_kernels(args, local_rank)), flush=True)
+    elif args.config == "peer_pair":
+        if world > 1:
+            raise SystemExit("--config peer_pair drives both GPUs from one process: run it "
+                             "without torchrun")
+        print(json.dumps(run_peer_pair(args)), flush=True)
     else:
         run_gpu(args, rank, world, local_rank)
 

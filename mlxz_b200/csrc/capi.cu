@@ -12,7 +12,6 @@ namespace {
 thread_local char t_msg[512] = "";
 thread_local int t_code = MZ_OK;
 
-constexpr int kMaxDevices = 64;
 std::once_flag g_sm_once[kMaxDevices];
 int g_sm_count[kMaxDevices];
 }  // namespace

@@ -7,6 +7,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <mutex>
+
 #include "../../include/mlxz_b200.h"
 
 namespace mz {
@@ -21,6 +23,37 @@ int dtype_bytes(int dtype);
 // Current device and its SM count (cached per device).
 int current_device();
 int sm_count(int device);
+
+constexpr int kMaxDevices = 64;
+
+// One-time set-up per device, e.g. a kernel's shared-memory opt-in: function
+// attributes belong to each device's context, so a process that drives
+// several GPUs needs them set on every device it launches on.  The set-up
+// runs on the current device the first time device_once sees it; its status
+// (and an int it produces, such as an occupancy) is kept for that device.
+struct DeviceOnce {
+  std::once_flag flag[kMaxDevices];
+  cudaError_t err[kMaxDevices] = {};
+  int value[kMaxDevices] = {};
+};
+
+template <class F>
+int device_once(DeviceOnce &o, F &&setup, int *value, const char *what) {
+  const int d = current_device();
+  if (d < 0 || d >= kMaxDevices) return fail(MZ_ERR_CUDA, "%s: no usable current device", what);
+  std::call_once(o.flag[d], [&]() { o.err[d] = setup(&o.value[d]); });
+  if (o.err[d] != cudaSuccess) return cuda_fail(o.err[d], what);
+  if (value) *value = o.value[d];
+  return MZ_OK;
+}
+
+// Dynamic shared-memory opt-in of kernel `k` on the current device (once).
+template <class KernelPtr>
+int smem_optin(KernelPtr k, int smem_bytes, DeviceOnce &o, const char *what) {
+  return device_once(
+      o, [&](int *) { return cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes); },
+      nullptr, what);
+}
 
 inline bool aligned(const void *p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
 

@@ -814,18 +814,15 @@ inline void set_schedule(Params &p, const WsLayout &ws) {
 // Occupancy of a decode kernel instantiation (cached; also sets its shared
 // memory attribute once).
 template <class KernelPtr>
-int kernel_occupancy(KernelPtr k, int smem_bytes, int *cache, std::once_flag *once,
-                     cudaError_t *err, int *out) {
-  std::call_once(*once, [&]() {
-    *err = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes);
-    if (*err != cudaSuccess) return;
-    int n = 0;
-    *err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k, kWarps * 32, smem_bytes);
-    *cache = n;
-  });
-  if (*err != cudaSuccess) return cuda_fail(*err, "paged decode: occupancy query");
-  *out = *cache;
-  return MZ_OK;
+int kernel_occupancy(KernelPtr k, int smem_bytes, DeviceOnce &once, int *out) {
+  return device_once(
+      once,
+      [&](int *n) {
+        cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes);
+        if (e != cudaSuccess) return e;
+        return cudaOccupancyMaxActiveBlocksPerMultiprocessor(n, k, kWarps * 32, smem_bytes);
+      },
+      out, "paged decode: occupancy query");
 }
 
 }  // namespace decode

@@ -382,24 +382,16 @@ int make_pool_map(CUtensorMap *m, const void *pool, int64_t rows, int D, bool bf
 
 template <int D, bool BF16>
 int kernel_ctas_per_sm(int *out) {
-  static int cached = -1;
-  static std::once_flag once;
-  static cudaError_t err = cudaSuccess;
-  return kernel_occupancy(paged_decode_kernel<D, BF16>, Cfg<D>::kSmemBytes, &cached, &once, &err,
-                          out);
+  static DeviceOnce once;
+  return kernel_occupancy(paged_decode_kernel<D, BF16>, Cfg<D>::kSmemBytes, once, out);
 }
 
-// Dynamic shared-memory opt-in for the all-gather instantiation (once).
+// Dynamic shared-memory opt-in for the all-gather instantiation (once per device).
 template <int D, bool BF16>
 int gather_smem_attr() {
-  static std::once_flag once;
-  static cudaError_t err = cudaSuccess;
-  std::call_once(once, []() {
-    err = cudaFuncSetAttribute(paged_decode_gather_kernel<D, BF16>,
-                               cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<D>::kSmemBytes);
-  });
-  if (err != cudaSuccess) return cuda_fail(err, "setting the all-gather kernel's shared memory");
-  return MZ_OK;
+  static DeviceOnce once;
+  return smem_optin(paged_decode_gather_kernel<D, BF16>, Cfg<D>::kSmemBytes, once,
+                    "setting the all-gather kernel's shared memory");
 }
 
 int ctas_per_sm(int D, bool bf16, int *out) {

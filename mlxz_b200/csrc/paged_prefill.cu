@@ -557,15 +557,9 @@ __global__ void __launch_bounds__(tcp::kThreads, 1)
 
 template <int D, bool BF16>
 int smem_attr_tc() {
-  static std::once_flag once;
-  static cudaError_t err = cudaSuccess;
-  std::call_once(once, []() {
-    err = cudaFuncSetAttribute(paged_prefill_tc_kernel<D, BF16>,
-                               cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               tcp::TCfg<D>::kSmemBytes);
-  });
-  if (err != cudaSuccess) return cuda_fail(err, "mz_paged_prefill: shared memory attribute");
-  return MZ_OK;
+  static DeviceOnce once;
+  return smem_optin(paged_prefill_tc_kernel<D, BF16>, tcp::TCfg<D>::kSmemBytes, once,
+                    "mz_paged_prefill: shared memory attribute");
 }
 
 }  // namespace prefill

@@ -1096,13 +1096,10 @@ int make_code_map(CUtensorMap *m, const void *base, int64_t rows, int rb) {
 template <int BITS, int ROWS>
 int launch_one(const Params &p, const CUtensorMap &tk, const CUtensorMap &tv, int grid,
                cudaStream_t s) {
-  static std::once_flag once;
-  static cudaError_t err = cudaSuccess;
-  std::call_once(once, []() {
-    err = cudaFuncSetAttribute(paged_decode_qtc_kernel<BITS, ROWS>,
-                               cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<BITS, ROWS>::kSmemBytes);
-  });
-  if (err != cudaSuccess) return cuda_fail(err, "quantised decode (tcgen05): shared memory attribute");
+  static DeviceOnce once;
+  if (int rc = smem_optin(paged_decode_qtc_kernel<BITS, ROWS>, Cfg<BITS, ROWS>::kSmemBytes, once,
+                          "quantised decode (tcgen05): shared memory attribute"))
+    return rc;
   paged_decode_qtc_kernel<BITS, ROWS><<<grid, Cfg<BITS, ROWS>::kThreads, Cfg<BITS, ROWS>::kSmemBytes, s>>>(tk, tv, p);
   MZ_CHECK_LAUNCH("mz_paged_decode_q (tcgen05)");
   return MZ_OK;

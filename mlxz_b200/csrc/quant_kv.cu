@@ -812,11 +812,9 @@ __global__ void __launch_bounds__(kWarps * 32, QCfg<D, BITS, NQ>::kCtas)
 
 template <int D, int BITS, int NQ>
 int q_kernel_ctas_per_sm(int *out) {
-  static int cached = -1;
-  static std::once_flag once;
-  static cudaError_t err = cudaSuccess;
-  return kernel_occupancy(paged_decode_q_kernel<D, BITS, NQ>, QCfg<D, BITS, NQ>::kSmemBytes,
-                          &cached, &once, &err, out);
+  static DeviceOnce once;
+  return kernel_occupancy(paged_decode_q_kernel<D, BITS, NQ>, QCfg<D, BITS, NQ>::kSmemBytes, once,
+                          out);
 }
 
 template <int NQ>

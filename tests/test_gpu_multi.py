@@ -118,3 +118,77 @@ def test_two_gpu_fused_gather_matches_nccl():
     for r, (equal, same_pools, err, epoch) in got.items():
         assert equal and same_pools, (r, err)
         assert epoch == 2 * L
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_one_process_drives_two_gpus_fused_gather():
+    """One process, two GPUs: each GPU runs its half of the KV heads with the
+    all-gather fused into the launch, its rows stored into the other GPU's
+    buffer through peer access; both gathered buffers equal the two halves'
+    ordinary launches side by side, bytewise.  Kernel shared-memory opt-ins
+    are per device, so the launch on the second GPU also checks that they are
+    set there."""
+    from cuda.bindings import runtime as cudart
+
+    from mlxz_b200 import _native as nat
+    from mlxz_b200 import ops
+
+    if not (torch.cuda.can_device_access_peer(0, 1) and torch.cuda.can_device_access_peer(1, 0)):
+        pytest.skip("GPUs 0 and 1 have no peer access")
+    for a, b in ((0, 1), (1, 0)):
+        torch.cuda.set_device(a)
+        cudart.cudaSetDevice(a)
+        err = cudart.cudaDeviceEnablePeerAccess(b, 0)[0]
+        assert err in (cudart.cudaError_t.cudaSuccess,
+                       cudart.cudaError_t.cudaErrorPeerAccessAlreadyEnabled), err
+    N, hkv, hq = 2, HKV // 2, HKV * G // 2
+    need = [(c + 1 + BS - 1) // BS for c in CTX]
+    n_blocks = sum(need) + 4
+    g = torch.Generator().manual_seed(4321)
+    perm = torch.randperm(n_blocks, generator=g).to(torch.int32)
+    tables = torch.full((B, max(need)), -1, dtype=torch.int32)
+    used = 0
+    for b in range(B):
+        tables[b, :need[b]] = perm[used:used + need[b]]
+        used += need[b]
+    lens = torch.tensor([c + 1 for c in CTX], dtype=torch.int32)
+    ranks = []
+    for r in range(N):
+        dev = torch.device("cuda", r)
+        mk = lambda *shape: torch.randn(shape, generator=g).to(torch.bfloat16).to(dev)  # noqa: E731
+        ranks.append(dict(k=mk(n_blocks, hkv, BS, D), v=mk(n_blocks, hkv, BS, D), q=mk(B, hq, D),
+                          kn=mk(B, hkv, D), vn=mk(B, hkv, D), tables=tables.to(dev),
+                          lens=lens.to(dev),
+                          full=torch.zeros((B, N * hq, D), dtype=torch.bfloat16, device=dev),
+                          sig=torch.zeros(N, dtype=torch.int32, device=dev),
+                          arrivals=torch.zeros(1, dtype=torch.int32, device=dev),
+                          ws=ops.decode_workspace(B, hkv, G, D, r, shared=False)))
+    local = []
+    for r in range(N):
+        rk = ranks[r]
+        with torch.cuda.device(r):
+            local.append(ops.paged_append_decode(rk["q"], rk["k"], rk["v"], rk["kn"], rk["vn"],
+                                                 rk["tables"], rk["lens"]).cpu())
+    for epoch in (1, 2):
+        for r in range(N):
+            rk = ranks[r]
+            pe = nat.PeerOutputs()
+            pe.n_ranks, pe.rank, pe.epoch = N, r, epoch
+            for s in range(N):
+                pe.out[s] = ranks[s]["full"].data_ptr() + r * hq * D * 2
+                pe.signal[s] = ranks[s]["sig"].data_ptr()
+            pe.arrivals = rk["arrivals"].data_ptr()
+            with torch.cuda.device(r):
+                ops.paged_append_decode_allgather(pe, rk["q"], rk["k"], rk["v"], rk["kn"],
+                                                  rk["vn"], rk["tables"], rk["lens"], N * hq * D,
+                                                  D, torch.bfloat16, workspace=rk["ws"])
+        for r in range(N):
+            torch.cuda.synchronize(r)
+        for r in range(N):
+            with torch.cuda.device(r):
+                ops.peer_wait(ranks[r]["sig"], N, r, epoch)
+            torch.cuda.synchronize(r)
+            ops.check_device_errors(r)
+    want = torch.cat(local, dim=1).view(torch.int16)
+    for r in range(N):
+        assert torch.equal(ranks[r]["full"].cpu().view(torch.int16), want)
