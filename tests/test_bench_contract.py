@@ -59,3 +59,20 @@ def test_reference_arm_config_matches_gpu_arm():
     assert w5.B == 256 and w5.hkv == 1 and w5.hq == 8 and w5.nl == 80
     w1 = bench.Workload(True, 1, None, 120.0, 0, True)
     assert 1 <= w1.nl < 80  # 80 layers of the 70B shape do not fit one GPU
+
+
+def test_peer_pair_reports_unavailable_without_two_gpus():
+    """--config peer_pair drives two GPUs from one process; where there are
+    fewer, it prints one JSON line saying so and exits 0."""
+    import torch
+
+    if torch.cuda.device_count() >= 2:
+        return
+    r = subprocess.run([sys.executable, str(ROOT / "bench.py"), "--config", "peer_pair",
+                        "--steps", "1", "--warmup", "1"],
+                       capture_output=True, text=True, timeout=600, cwd=ROOT)
+    assert r.returncode == 0, r.stderr[-2000:]
+    lines = [ln for ln in r.stdout.splitlines() if ln.startswith("{")]
+    assert len(lines) == 1
+    d = json.loads(lines[0])
+    assert d["config"] == "peer_pair" and "unavailable" in d
