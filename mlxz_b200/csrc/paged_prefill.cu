@@ -67,6 +67,33 @@ inline int make_group_map(CUtensorMap *m, const void *base, int64_t rows, int D,
   return MZ_OK;
 }
 
+
+// Two fp32 values in one 64-bit register, for the packed fp32 instructions
+// (fma / add / sub .f32x2): one instruction for both keys of a pair.
+__device__ __forceinline__ uint64_t f2_pack(float x, float y) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(x), "f"(y));
+  return r;
+}
+__device__ __forceinline__ void f2_unpack(uint64_t v, float &x, float &y) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(x), "=f"(y) : "l"(v));
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2_sub(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
 __device__ __forceinline__ void mbar_arrive(uint32_t bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
 }
@@ -452,26 +479,36 @@ __global__ void __launch_bounds__(tcp::kThreads, 1)
       }
       m_used = m_new;
       const float neg_m = -m_used;
-      float l8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      // key pairs through the packed fp32 instructions: scale and shift, the
+      // running sums (four pair accumulators) and the bf16 residual
+      const uint64_t sc2 = f2_pack(p.scale_log2, p.scale_log2), nm2 = f2_pack(neg_m, neg_m);
+      uint64_t l2[4] = {0ull, 0ull, 0ull, 0ull};
 #pragma unroll
       for (int c = 0; c < kH / 32; ++c) {
         uint32_t hi[16], lo[16];
 #pragma unroll
         for (int w = 0; w < 16; ++w) {
-          const float a = fast_exp2(fmaf(sv[32 * c + 2 * w], p.scale_log2, neg_m));
-          const float e = fast_exp2(fmaf(sv[32 * c + 2 * w + 1], p.scale_log2, neg_m));
-          l8[w & 7] += a + e;
+          float xa, xe;
+          f2_unpack(f2_fma(f2_pack(sv[32 * c + 2 * w], sv[32 * c + 2 * w + 1]), sc2, nm2), xa, xe);
+          const float a = fast_exp2(xa), e = fast_exp2(xe);
+          const uint64_t ae = f2_pack(a, e);
+          l2[w & 3] = f2_add(l2[w & 3], ae);
           hi[w] = pack2<BF16>(a, e);
           if constexpr (BF16) {
-            const float ah = __uint_as_float(hi[w] << 16);
-            const float eh = __uint_as_float(hi[w] & 0xffff0000u);
-            lo[w] = pack2<BF16>(a - ah, e - eh);
+            float ra, re;
+            f2_unpack(f2_sub(ae, f2_pack(__uint_as_float(hi[w] << 16),
+                                         __uint_as_float(hi[w] & 0xffff0000u))),
+                      ra, re);
+            lo[w] = pack2<BF16>(ra, re);
           }
         }
         // P over this half's own S columns: hi in the first 32, lo in the last
         tc::st16(scol + 16 * c, hi);
         if constexpr (BF16) tc::st16(scol + 32 + 16 * c, lo);
       }
+      float l8[8];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) f2_unpack(l2[k], l8[2 * k], l8[2 * k + 1]);
       l = l * alpha + (((l8[0] + l8[1]) + (l8[2] + l8[3])) + ((l8[4] + l8[5]) + (l8[6] + l8[7])));
       const int nvalid = kv_len - i * kN;
       if (nvalid < kN) {
