@@ -94,6 +94,13 @@ __device__ __forceinline__ uint64_t f2_sub(uint64_t a, uint64_t b) {
   return d;
 }
 
+// max(a, b, c) in one instruction (three-input max.f32 of sm_100)
+__device__ __forceinline__ float fmax3f(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
 __device__ __forceinline__ void mbar_arrive(uint32_t bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
 }
@@ -436,13 +443,16 @@ __global__ void __launch_bounds__(tcp::kThreads, 1)
       // the other half's through shared memory
       float mx;
       {
-        float m8[8];
+        // four independent chains of three-input maxima over 16 scores each
+        float m4[4];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) m8[j] = sv[j];
+        for (int k = 0; k < 4; ++k) {
+          float m = fmax3f(sv[k], sv[k + 4], sv[k + 8]);
 #pragma unroll
-        for (int j = 8; j < kH; ++j) m8[j & 7] = fmaxf(m8[j & 7], sv[j]);
-        mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])),
-                   fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
+          for (int t = 3; t + 1 < kH / 4; t += 2) m = fmax3f(m, sv[k + 4 * t], sv[k + 4 * (t + 1)]);
+          m4[k] = fmaxf(m, sv[k + kH - 4]);
+        }
+        mx = fmax3f(m4[0], m4[1], fmaxf(m4[2], m4[3]));
         const int par = i & 1;
         xm[(par * 2 + hf) * kM + row] = mx;
         mbar_arrive(bar(kBarXchg + par * 4 + pair));
