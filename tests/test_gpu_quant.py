@@ -124,12 +124,12 @@ QCASES = [
 
 @pytest.mark.parametrize("bits,D,G,dtype,ctx,nw", QCASES)
 @pytest.mark.parametrize("out32", [True, False])
-@pytest.mark.parametrize("form", ["default", "mma_sync"])
+@pytest.mark.parametrize("form", ["mma_sync", "tcgen05"])
 def test_paged_decode_q_vs_oracle(cuda, bits, D, G, dtype, ctx, nw, out32, form, monkeypatch):
-    """Every case through the default dispatch and through the mma.sync
-    kernel (integer Q.K^T, 1, 2 or 4 groups of four query rows)."""
-    if form == "mma_sync":
-        monkeypatch.setenv("MLXZ_B200_QDECODE_TC", "0")
+    """Every case through the default mma.sync kernel (integer Q.K^T, 1, 2 or
+    4 groups of four query rows) and through the opt-in tcgen05 form (head_dim
+    128; other shapes fall back to the mma.sync kernel)."""
+    monkeypatch.setenv("MLXZ_B200_QDECODE_TC", "1" if form == "tcgen05" else "0")
     Hkv = 2 if G == 16 else 4
     case = _quant_case(40 + bits + D + G, ctx, Hkv, D, bits, dtype, G=G)
     pools = _dev_pools(case["host"], cuda)
