@@ -279,9 +279,10 @@ __device__ __forceinline__ uint32_t split_hilo(float x) {
 //                bytes), column 2 i the hi bytes of row i, 2 i + 1 the lo bytes;
 //   S[tok][i]  = sum_g s_k[tok][g] * sq[i][g] * (256 D[tok][2i] + D[tok][2i+1])
 //                + b_k[tok][g] * sum(q~[i]_g),   q~ = q16 * sq (sq = max|q| / 32639)
-// over a permutation of the head dimension within each group (lane c's four
-// k slots of a k-step are its own contiguous code bytes; Q is packed with the
-// same permutation).
+// over a permutation of the head dimension within each group (the k slots of
+// lane c in a k-step come from its own contiguous code words: 8 bytes at
+// 8-bit, one word's low and high nibbles at 4-bit; Q is packed with the same
+// permutation).
 // PV on fp16 tensor cores (mma.m16n8k16): O^T[d][col] = sum_t A[d][t] B[t][col],
 // A = V codes - centre (half2 of two tokens of one dim), B = P'^T by movmatrix,
 // where P' = p * s_v * kPScale goes in as an fp16 pair (hi in column 2 i, lo in
