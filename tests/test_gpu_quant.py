@@ -68,8 +68,7 @@ def test_quant_append_bit_exact(cuda, bits, D, dtype):
         assert np.array_equal(_np(got), exp)
 
 
-def _quant_case(seed, ctx, Hkv, D, bits, dtype, G=4, nq=1):
-    bs = 16
+def _quant_case(seed, ctx, Hkv, D, bits, dtype, G=4, nq=1, bs=16):
     need = [(c + bs - 1) // bs for c in ctx]
     N = max(1, int(sum(need) * 1.1) + 2)
     perm = rng.permutation(seed, N)
@@ -83,7 +82,7 @@ def _quant_case(seed, ctx, Hkv, D, bits, dtype, G=4, nq=1):
     kq, ks, kb = oq.quantize(kraw, dtype, bits)
     vq, vs, vb = oq.quantize(vraw, dtype, bits)
     q = rng.normal(seed, (len(ctx), nq, Hkv * G, D), dtype, stream=3)
-    return dict(N=N, tables=tables, ctx=np.array(ctx, dtype=np.int32), q=q,
+    return dict(N=N, bs=bs, tables=tables, ctx=np.array(ctx, dtype=np.int32), q=q,
                 host=(kq, ks, kb, vq, vs, vb),
                 kdeq=oq.dequantize(kq, ks, kb, bits, D), vdeq=oq.dequantize(vq, vs, vb, bits, D))
 
@@ -100,7 +99,7 @@ def _oracle_decode(case, dtype):
     qf = rng.to_f32(case["q"], dtype)
     B, nq, Hq, D = qf.shape
     out = np.zeros((B, nq, Hq, D))
-    bs = 16
+    bs = case["bs"]
     for b in range(B):
         c = int(case["ctx"][b])
         nb = (c + bs - 1) // bs
@@ -144,6 +143,26 @@ def test_paged_decode_q_vs_oracle(cuda, bits, D, G, dtype, ctx, nw, out32, form,
     for b, c in enumerate(ctx):
         if c == 0:
             assert torch.count_nonzero(out[b]) == 0
+
+
+@pytest.mark.parametrize("bits", [8, 4])
+@pytest.mark.parametrize("bs", [32, 64])
+@pytest.mark.parametrize("form", ["mma_sync", "tcgen05"])
+def test_paged_decode_q_block_sizes(cuda, bits, bs, form, monkeypatch):
+    """Blocks of several 16-token tiles: a tile's pool row is the block's row
+    plus the tile's offset inside the block, and ragged lengths end inside a
+    block."""
+    monkeypatch.setenv("MLXZ_B200_QDECODE_TC", "1" if form == "tcgen05" else "0")
+    ctx = [1, 47, bs, bs + 1, 3 * bs - 5, 700]
+    case = _quant_case(60 + bits + bs, ctx, 4, 128, bits, "bf16", bs=bs)
+    pools = _dev_pools(case["host"], cuda)
+    q = to_dev(case["q"][:, 0], "bf16", cuda)
+    out = ops.paged_decode_q(q, pools, torch.from_numpy(case["tables"]).to(cuda),
+                             torch.from_numpy(case["ctx"]).to(cuda), out_dtype=torch.float32)
+    torch.cuda.synchronize()
+    ops.check_device_errors(0)
+    ref = _oracle_decode(case, "bf16")[:, 0]
+    assert attn_err(out, ref) <= 2e-3
 
 
 def test_paged_decode_q_multi_query_and_paged_append(cuda):
