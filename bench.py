@@ -78,6 +78,9 @@ def parse_args():
                          "launch of rank 0 of 2 timed on GPU 0 (its output rows stored into "
                          "GPU 1's buffer over NVLink), for profiling the launch alone")
     ap.add_argument("--bits", type=int, default=8, choices=[4, 8])
+    ap.add_argument("--prefill-offset", type=int, default=3584,
+                    help="prefill: cached tokens before each 512-token chunk (0 = fresh "
+                         "prompts); the headline prefill workload uses 3584")
     ap.add_argument("--kv-bits", type=int, default=16, choices=[4, 8, 16],
                     help="prefill: the K/V store (16 = bf16; 8 / 4 = quantised, "
                          "dequantised per layer into a staging pool)")
@@ -228,6 +231,16 @@ PF_METRIC = ("chunked-prefill attention TFLOP/s and prefill tok/s, 8B shape, "
              "8 x 512-token chunks at offset 3584")
 
 
+def set_prefill_offset(offset: int) -> None:
+    """Chunks at `offset` cached tokens (the workload constants and metric)."""
+    global PF_CTX, PF_METRIC
+    if offset < 0 or offset % BS:
+        raise SystemExit("--prefill-offset must be a non-negative multiple of 16")
+    PF_CTX = offset + PF_CHUNK
+    PF_METRIC = ("chunked-prefill attention TFLOP/s and prefill tok/s, 8B shape, "
+                 f"8 x 512-token chunks at offset {offset}")
+
+
 def prefill_flops_layer(n_seqs: int = PF_B) -> float:
     """Causal attention FLOPs of one layer: QK^T and PV, 2 per multiply-add,
     over every (query, visible key) pair."""
@@ -270,7 +283,7 @@ def run_reference_prefill(args, world: int) -> None:
     v = statistics.median(x["tflops"] for x in vals)
     ms = statistics.median(x["layer_seq_s"] for x in vals) * 1000.0 * PF_B * args.layers
     sample = (f"1 of {PF_B} sequences x 1 of {args.layers} layers (a 512-token chunk at "
-              f"offset 3584), torch-CPU port of append + causal GQA attention, {threads} "
+              f"offset {PF_CTX - PF_CHUNK}), torch-CPU port of append + causal GQA attention, {threads} "
               f"threads; ms_per_step extrapolated to {PF_B} sequences x {args.layers} layers")
     line = {
         "impl": "reference", "metric": PF_METRIC, "value": round(v, 5), "unit": "TFLOP/s",
@@ -293,7 +306,7 @@ def run_reference_prefill(args, world: int) -> None:
 def run_prefill(args, local_rank: int) -> None:
     """Chunked-prefill iteration, Llama-3.1-8B shape: 32 layers, 32 q heads, 8
     KV heads, head_dim 128, block 16; 8 sequences each prefilling a 512-token
-    chunk on top of 3584 cached tokens.  One step = per layer, through
+    chunk on top of 3584 cached tokens (--prefill-offset; 0 = fresh prompts).  One step = per layer, through
     PagedPrefillStep.layer: mz_kv_append of the chunk's K/V, then
     mz_paged_prefill (causal GQA attention over cache + chunk).  Every step
     rewrites the same slots, so timed steps do identical work."""
@@ -445,7 +458,7 @@ def run_prefill(args, local_rank: int) -> None:
         threads = os.cpu_count() or 1
         r = cpu_prefill_sample(args.seed, threads)
         cpu = {"value": round(r["tflops"], 5), "unit": "TFLOP/s", "cores": threads, "kind": "port",
-               "sample": "1 of 8 sequences x 1 of 32 layers (512-token chunk at offset 3584), "
+               "sample": f"1 of 8 sequences x 1 of 32 layers (512-token chunk at offset {PF_CTX - PF_CHUNK}), "
                          f"torch-CPU port of append + causal GQA attention, {threads} threads"}
     peaks_path = ROOT / "MEASURED_PEAKS.json"
     if peaks_path.exists():
@@ -461,8 +474,8 @@ def run_prefill(args, local_rank: int) -> None:
         "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (seeded N(0,1) bf16 K/V/Q, random block tables)",
         "config": {"workload": ("chunked-prefill iteration: 32 layers, 32 q heads, 8 kv heads, "
-                                "head_dim 128, block 16; 8 seqs x 512-token chunk at offset "
-                                "3584 (ctx 4096); per layer kv_append + paged_prefill"
+                                f"head_dim 128, block 16; 8 seqs x 512-token chunk at offset "
+                                f"{PF_CTX - PF_CHUNK} (ctx {PF_CTX}); per layer kv_append + paged_prefill"
                                 + ("" if kv_bits == 16 else
                                    f"; {kv_bits}-bit store: kv_quant_append, kv_dequant_blocks "
                                    "of the step's blocks into a bf16 staging pool, paged_prefill "
@@ -1540,6 +1553,8 @@ def main():
     sys.path.insert(0, str(ROOT))
     if args.layers is None and args.config != "sharded70b":
         args.layers = L
+    if args.config == "prefill":
+        set_prefill_offset(args.prefill_offset)
     if args.impl == "reference":
         run_reference(args, rank, world)
     elif args.config == "prefix":
