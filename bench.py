@@ -488,7 +488,9 @@ def run_prefill(args, local_rank: int) -> None:
         "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": peak,
                      "unit": "TFLOP/s", "frac": round(achieved / peak, 4),
                      "traffic": profile_traffic("paged_prefill_8b.md"),
-                     "kernel": "paged_prefill_tc_kernel<128,bf16>", "peak_kind": peak_kind,
+                     "kernel": ("paged_prefill_tc_kernel<128,bf16>"
+                                if os.environ.get("MLXZ_B200_PREFILL_PERSIST", "") == "0"
+                                else "paged_prefill_ps_kernel<128,bf16>"), "peak_kind": peak_kind,
                      "prefill_ms_mean": round(pf_ms, 4), "alg_flops_per_launch": flops_layer,
                      "dequant_ms_mean": None if dq_ms is None else round(dq_ms, 4)},
         "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": steps * nl * (2 if kv_bits == 16 else 3),

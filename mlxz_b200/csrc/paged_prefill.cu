@@ -34,6 +34,7 @@ struct PParams {
   float scale_log2;
   int sub_log2;      // rows per bulk copy box: gcd(block_size, 128) = 1 << sub_log2
   int32_t *err;
+  int n_seqs, qblocks;  // persistent form: sequences, query blocks per sequence
 };
 
 // 4-D bulk tensor copy (no multicast): box {64, 8, D / 64, rows / 8} of the
@@ -162,7 +163,9 @@ struct TCfg {
 constexpr int kBarKFull = 0, kBarVFull = 3, kBarSFull = 5, kBarPFull = 8, kBarPvDone = 11,
               kBarDrain = 14, kBarXchg = 15 /* [parity][pair] */, kBarLx = 23 /* [pair] */,
               kNumBars = 27;
-static_assert(8 * kNumBars + 8 <= 256, "barrier area");
+// persistent form only: Q of the next item loaded, O of the last item read
+constexpr int kBarQReady = 27, kBarOFree = 28, kNumBarsPs = 29;
+static_assert(8 * kNumBarsPs + 8 <= 256, "barrier area");
 static_assert(kKRing == kSBufs, "K slots are released through the S barriers");
 }  // namespace tcp
 
@@ -602,6 +605,523 @@ __global__ void __launch_bounds__(tcp::kThreads, 1)
   }
 }
 
+// ---------------------------------------------------------------------------
+// Persistent form: one CTA per SM takes work items -- (sequence, KV head,
+// query block of 128 rows) -- in turn, the query blocks with the most key
+// tiles first, and keeps its barriers, TMEM and copy rings across items.  Tile
+// slots, buffers and barrier phases count the CTA's key tiles over all its
+// items (global tile index g), so the copy warp streams the next item's K/V
+// while the current one finishes.  Per item the softmax warps load Q (once the
+// item before has no S left to issue) and signal it (kBarQReady); the first
+// PV of an item, which starts O afresh, waits until the softmax warps have
+// read the previous item's O (kBarOFree).  Everything else is the one-block
+// kernel above.
+template <int D, bool BF16>
+__global__ void __launch_bounds__(tcp::kThreads, 1)
+    paged_prefill_ps_kernel(const __grid_constant__ CUtensorMap tmK,
+                            const __grid_constant__ CUtensorMap tmV, const PParams p) {
+  using namespace tcp;
+  using C = TCfg<D>;
+  const int tpc = kM / p.G;
+  const int per_q = p.n_seqs * p.Hkv;
+  const int n_items = per_q * p.qblocks;
+
+  // item e: query block qblocks - 1 - e % qblocks (a pair's last, longest
+  // blocks first) of pair e / qblocks = (sequence, KV head): neighbouring
+  // items share their pair's K/V through L2
+  struct Item {
+    int b, h, q0, n, start, q_hi, kv_len, ntiles;
+    bool ok;
+  };
+  auto item_at = [&](int e) {
+    Item it{};
+    const int rem = e / p.qblocks, jr = e - rem * p.qblocks;
+    it.b = rem / p.Hkv;
+    it.h = rem - it.b * p.Hkv;
+    it.q0 = (p.qblocks - 1 - jr) * tpc;
+    it.n = p.q_len[it.b];
+    it.ok = false;
+    if (it.n <= 0 || it.q0 >= it.n) return it;
+    const int ctx = p.ctx[it.b];
+    if (ctx < it.n || ctx > p.max_blocks * p.bs) {
+      if (threadIdx.x == 0) dev_error(p.err, MZ_DEVERR_CONTEXT);
+      return it;
+    }
+    if (p.q_start[it.b] < 0 || (int64_t)p.q_start[it.b] + it.n > p.n_rows) {
+      if (threadIdx.x == 0) dev_error(p.err, MZ_DEVERR_ROWS);
+      return it;
+    }
+    it.start = ctx - it.n;
+    it.q_hi = min(it.q0 + tpc, it.n);
+    it.kv_len = it.start + it.q_hi;
+    it.ntiles = (it.kv_len + kN - 1) / kN;
+    it.ok = true;
+    return it;
+  };
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+  const uint32_t sbase = smem_u32(smem);
+  const uint32_t qs = sbase;
+  auto kst = [&](int s) { return sbase + C::kK0 + s * C::kTile; };
+  auto vst = [&](int s) { return sbase + C::kV0 + s * C::kTile; };
+  const uint32_t bars = sbase + C::kBar;
+  auto bar = [&](int i) { return bars + 8 * i; };
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + C::kBar + 8 * kNumBarsPs);
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + C::kBar + 8 * kNumBarsPs + 4);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  if (warp == kProdWarp && lane == 0) {
+    for (int s = 0; s < kKRing; ++s) mbar_init(bar(kBarKFull + s), 1);
+    for (int s = 0; s < kVRing; ++s) mbar_init(bar(kBarVFull + s), 1);
+    for (int s = 0; s < kSBufs; ++s) {
+      mbar_init(bar(kBarSFull + s), 1);
+      mbar_init(bar(kBarPFull + s), kSoftWarps);
+      mbar_init(bar(kBarPvDone + s), 1);
+    }
+    mbar_init(bar(kBarDrain), 1);
+    for (int x = 0; x < 8; ++x) mbar_init(bar(kBarXchg + x), 64);
+    for (int x = 0; x < 4; ++x) mbar_init(bar(kBarLx + x), 64);
+    mbar_init(bar(kBarQReady), kSoftWarps);
+    mbar_init(bar(kBarOFree), kSoftWarps);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == kProdWarp) {
+    __syncwarp();
+    asm volatile("bar.arrive 1, %0;" ::"n"(kThreads) : "memory");
+  }
+  if (warp == kMmaWarp) tc::tmem_alloc(smem_u32(tmem_slot), kTmemCols);
+  uint32_t tmem = 0;
+  if (warp != kProdWarp) {
+    tc::fence_before_sync();
+    asm volatile("bar.sync 1, %0;" ::"n"(kThreads) : "memory");
+    tc::fence_after_sync();
+    tmem = *tmem_slot;
+  }
+
+  auto give_up = [&]() {
+    dev_error(p.err, MZ_DEVERR_TIMEOUT);
+    *abort_flag = 1;
+  };
+
+  if (warp == kProdWarp) {
+    // ---------------- producer (whole warp) ----------------
+    const uint64_t pol = l2_policy_evict_last();
+    const int sub = 1 << p.sub_log2, nst_log2 = 7 - p.sub_log2, nst = 1 << nst_log2;
+    int tg = 0, k_issued = 0, v_issued = 0;  // global tile counts
+    bool ok = true;
+    for (int e = blockIdx.x; ok && e < n_items; e += gridDim.x) {
+      const Item it = item_at(e);
+      if (!it.ok) continue;
+      const int b = it.b, h = it.h, kv_len = it.kv_len, ntiles = it.ntiles;
+      auto group_key = [&](int g) {
+        return lane < 4 * nst ? (4 * g + (lane >> nst_log2)) * kN + (lane & (nst - 1)) * sub
+                              : kv_len;
+      };
+      auto group_ids = [&](int g) -> int32_t {
+        const int t = group_key(g);
+        return t < kv_len ? p.tables[(int64_t)b * p.max_blocks + t / p.bs] : 0;
+      };
+      auto group_rows = [&](int g, int32_t blk) -> int {
+        const int t = group_key(g);
+        if (t >= kv_len) return 0;
+        if (blk < 0 || blk >= p.n_blocks) {
+          dev_error(p.err, MZ_DEVERR_BLOCK_ID);
+          blk = 0;
+        }
+        return static_cast<int>(((int64_t)blk * p.Hkv + h) * p.bs + t % p.bs);
+      };
+      auto load = [&](const CUtensorMap *tm, uint32_t dst, uint32_t fbar, int j, int y) {
+        const int nsub = min(nst, (kv_len - j * kN + sub - 1) >> p.sub_log2);
+        if (lane == 0)
+          mbar_arrive_expect_tx(fbar, static_cast<uint32_t>(nsub * (D / 64) * sub * 128));
+        __syncwarp();
+        if (lane < nsub) tma_load_4d(dst + lane * (sub / 8) * C::kGroup, tm, y >> 3, fbar, pol);
+      };
+      int y_prv = 0, y_cur = group_rows(0, group_ids(0));
+      int32_t id_nxt = group_ids(1);
+      // step t: K_t, then V_{t-1} (item-local t; slots by the global index)
+      for (int t = 0; t <= ntiles; ++t) {
+        if (__any_sync(0xffffffffu, *abort_flag != 0)) {
+          ok = false;
+          break;
+        }
+        if (t > 0 && (t & 3) == 0) {
+          y_prv = y_cur;
+          y_cur = group_rows(t >> 2, id_nxt);
+          id_nxt = group_ids((t >> 2) + 1);
+        }
+        if (t < ntiles) {
+          const int g = tg + t, s = g % kKRing;
+          const int y = __shfl_sync(0xffffffffu, y_cur, ((t & 3) << nst_log2) + (lane & (nst - 1)));
+          // K slot s frees when S of global tile g - 3 completed (kKRing == kSBufs)
+          if (g >= kKRing &&
+              !__all_sync(0xffffffffu, mbar_wait_bounded(bar(kBarSFull + (g - kKRing) % kSBufs),
+                                                          ((g - kKRing) / kSBufs) & 1, kTimeoutNs))) {
+            if (lane == 0) give_up();
+            ok = false;
+            break;
+          }
+          load(&tmK, kst(s), bar(kBarKFull + s), t, y);
+          k_issued = g + 1;
+        }
+        if (t >= 1) {
+          const int j = t - 1, gj = tg + j, s = gj % kVRing;
+          const int y = __shfl_sync(0xffffffffu, (j >> 2) == (t >> 2) ? y_cur : y_prv,
+                                    ((j & 3) << nst_log2) + (lane & (nst - 1)));
+          // V slot s frees when PV of global tile gj - 2 completed
+          if (gj >= kVRing &&
+              !__all_sync(0xffffffffu, mbar_wait_bounded(bar(kBarPvDone + (gj - kVRing) % kSBufs),
+                                                          ((gj - kVRing) / kSBufs) & 1, kTimeoutNs))) {
+            if (lane == 0) give_up();
+            ok = false;
+            break;
+          }
+          load(&tmV, vst(s), bar(kBarVFull + s), j, y);
+          v_issued = gj + 1;
+        }
+      }
+      tg += ntiles;
+    }
+    // copies still in flight land before the CTA leaves
+    if (lane == 0) {
+      for (int j = max(0, k_issued - kKRing); j < k_issued; ++j)
+        (void)mbar_wait_bounded(bar(kBarKFull + j % kKRing), (j / kKRing) & 1, kTimeoutNs);
+      for (int j = max(0, v_issued - kVRing); j < v_issued; ++j)
+        (void)mbar_wait_bounded(bar(kBarVFull + j % kVRing), (j / kVRing) & 1, kTimeoutNs);
+    }
+    __syncwarp();
+  } else if (warp == kMmaWarp) {
+    // ---------------- MMA issue (whole warp, one elected lane issues) ----------------
+    constexpr uint32_t idS = tc::idesc_f16(BF16, kM, kN, false);
+    constexpr uint32_t idPV = tc::idesc_f16(BF16, kM, D, true);
+    const uint32_t tm0 = __shfl_sync(0xffffffffu, tmem, 0);
+    // S of global tile j
+    auto issue_s = [&](int j) -> bool {
+      const int s = j % kKRing, buf = j % kSBufs;
+      if (!__all_sync(0xffffffffu,
+                      mbar_wait_bounded(bar(kBarKFull + s), (j / kKRing) & 1, kTimeoutNs)))
+        return false;
+      // buffer j % 3 is free once PV of global tile j - 3 (which read P from it) completed
+      if (j >= kSBufs &&
+          !__all_sync(0xffffffffu, mbar_wait_bounded(bar(kBarPvDone + buf),
+                                                      ((j - kSBufs) / kSBufs) & 1, kTimeoutNs)))
+        return false;
+      tc::fence_after_sync();
+      const uint32_t d = tm0 + 128 * (1 + buf);
+#pragma unroll
+      for (int k = 0; k < D / 16; ++k) {
+        const uint32_t ko = (k & 3) * 32;  // 16-column step inside the chunk's atom
+        tc::mma_ss_elect(d, tc::smem_desc_sw128(qs + (k >> 2) * (kM * 128) + ko, 16, 1024),
+                         tc::smem_desc_sw128(kst(s) + (k >> 2) * 1024 + ko, 16, C::kGroup),
+                         idS, k > 0);
+      }
+      tc::commit_elect(bar(kBarSFull + buf));  // also frees K slot s
+      return true;
+    };
+    int tg = 0, nit = 0;
+    bool ok = true;
+    for (int e = blockIdx.x; ok && e < n_items; e += gridDim.x) {
+      const Item it = item_at(e);
+      if (!it.ok) continue;
+      const int ntiles = it.ntiles;
+      // this item's Q is in shared memory
+      if (!__all_sync(0xffffffffu, mbar_wait_bounded(bar(kBarQReady), nit & 1, kTimeoutNs)) ||
+          !issue_s(tg)) {
+        ok = false;
+        break;
+      }
+      for (int i = 0; i < ntiles; ++i) {
+        if (__any_sync(0xffffffffu, *abort_flag != 0)) {
+          ok = false;
+          break;
+        }
+        const int g = tg + i;
+        if (i + 1 < ntiles && !issue_s(g + 1)) {
+          ok = false;
+          break;
+        }
+        const int s = g % kVRing, buf = g % kSBufs;
+        if (!__all_sync(0xffffffffu,
+                        mbar_wait_bounded(bar(kBarPFull + buf), (g / kSBufs) & 1, kTimeoutNs) &&
+                            mbar_wait_bounded(bar(kBarVFull + s), (g / kVRing) & 1, kTimeoutNs))) {
+          ok = false;
+          break;
+        }
+        // the first PV of an item starts O afresh: the previous item's O has been read
+        if (i == 0 && nit > 0 &&
+            !__all_sync(0xffffffffu,
+                        mbar_wait_bounded(bar(kBarOFree), (nit - 1) & 1, kTimeoutNs))) {
+          ok = false;
+          break;
+        }
+        tc::fence_after_sync();
+        const uint32_t pcol = tm0 + 128 * (1 + buf);
+#pragma unroll
+        for (int kk = 0; kk < kN / 16; ++kk) {
+          // keys 16 kk .. : half kk / 4, its hi columns from 64 half, lo 32 further
+          const uint32_t pa = pcol + 64 * (kk >> 2) + 8 * (kk & 3);
+          const uint64_t dv = tc::smem_desc_sw128(vst(s) + kk * 2 * C::kGroup, 1024, C::kGroup);
+          tc::mma_ts_elect(tm0, pa, dv, idPV, (i > 0 || kk > 0) ? 1u : 0u);
+          if constexpr (BF16) tc::mma_ts_elect(tm0, pa + 32, dv, idPV, 1u);
+        }
+        tc::commit_elect(bar(kBarPvDone + buf));  // also frees V slot s
+      }
+      tg += ntiles;
+      ++nit;
+    }
+    if (!ok && lane == 0) give_up();
+    // every MMA issued has completed before the TMEM is freed
+    tc::commit_elect(bar(kBarDrain));
+    (void)mbar_wait_bounded(bar(kBarDrain), 0, kTimeoutNs);
+    __syncwarp();
+  } else {
+    // ---------------- softmax + epilogue (warps 0-7) ----------------
+    constexpr int kH = kN / 2;  // keys of a tile per half
+    const uint32_t tl = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
+    const int pair = warp & 3;
+    float *xm = reinterpret_cast<float *>(smem + C::kXm);  // [parity][half][row]
+    float *xl = reinterpret_cast<float *>(smem + C::kXl);  // [half][row]
+    const int row = threadIdx.x & (kM - 1), hf = threadIdx.x >> 7;
+    int tg = 0, nit = 0;
+    bool ok = true;
+    for (int e = blockIdx.x; ok && e < n_items; e += gridDim.x) {
+      const Item it = item_at(e);
+      if (!it.ok) continue;
+      const int b = it.b, start = it.start, q_hi = it.q_hi, kv_len = it.kv_len, ntiles = it.ntiles;
+      const int tok = it.q0 + row / p.G;
+      const int hq = it.h * p.G + row % p.G;
+      const bool live = tok < q_hi;
+      const int lim = start + min(tok, q_hi - 1);  // last visible key of the row
+      {
+        // half hf of the Q row -> shared memory (128-byte-swizzled K-major
+        // layout); every S of the item before has completed (this thread
+        // waited for each)
+        const uint4 *src = reinterpret_cast<const uint4 *>(
+            static_cast<const uint16_t *>(p.q) + (int64_t)(p.q_start[b] + tok) * p.q_st +
+            (int64_t)hq * p.q_sh);
+#pragma unroll
+        for (int u = hf * (D / 16); u < (hf + 1) * (D / 16); ++u) {
+          const uint4 v = live ? src[u] : make_uint4(0, 0, 0, 0);
+          const int c = u >> 3, uu = u & 7;
+          *reinterpret_cast<uint4 *>(smem + c * (kM * 128) + row * 128 + ((uu ^ (row & 7)) << 4)) = v;
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar(kBarQReady));
+      }
+      float m_used = -INFINITY, l = 0.f;
+      for (int i = 0; i < ntiles; ++i) {
+        const int g = tg + i;
+        if (__any_sync(0xffffffffu, *abort_flag != 0)) {
+          ok = false;
+          break;
+        }
+        const int buf = g % kSBufs;
+        if (!__all_sync(0xffffffffu,
+                        mbar_wait_bounded(bar(kBarSFull + buf), (g / kSBufs) & 1, kTimeoutNs))) {
+          if (lane == 0) give_up();
+          ok = false;
+          break;
+        }
+        tc::fence_after_sync();
+        const uint32_t scol = tl + 128 * (1 + buf) + kH * hf;  // this half's 64 S columns
+        float sv[kH];
+        {
+          uint32_t r[kH / 32][32];
+  #pragma unroll
+          for (int c = 0; c < kH / 32; ++c) tc::ld32(scol + 32 * c, r[c]);
+          tc::wait_ld();
+  #pragma unroll
+          for (int c = 0; c < kH / 32; ++c)
+  #pragma unroll
+            for (int j = 0; j < 32; ++j) sv[32 * c + j] = __uint_as_float(r[c][j]);
+        }
+        const int key0 = i * kN + kH * hf;
+        if (key0 + kH - 1 > lim) {  // this half crosses the row's causal limit
+  #pragma unroll
+          for (int j = 0; j < kH; ++j)
+            if (key0 + j > lim) sv[j] = -INFINITY;
+        }
+        // max over the raw scores (scale > 0), eight independent chains, then
+        // the other half's through shared memory
+        float mx;
+        {
+          // four independent chains of three-input maxima over 16 scores each
+          float m4[4];
+  #pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            float m = fmax3f(sv[k], sv[k + 4], sv[k + 8]);
+  #pragma unroll
+            for (int t = 3; t + 1 < kH / 4; t += 2) m = fmax3f(m, sv[k + 4 * t], sv[k + 4 * (t + 1)]);
+            m4[k] = fmaxf(m, sv[k + kH - 4]);
+          }
+          mx = fmax3f(m4[0], m4[1], fmaxf(m4[2], m4[3]));
+          const int par = g & 1;
+          xm[(par * 2 + hf) * kM + row] = mx;
+          mbar_arrive(bar(kBarXchg + par * 4 + pair));
+          if (!__all_sync(0xffffffffu, mbar_wait_bounded(bar(kBarXchg + par * 4 + pair),
+                                                          (g >> 1) & 1, kTimeoutNs))) {
+            if (lane == 0) give_up();
+            ok = false;
+            break;
+          }
+          mx = fmaxf(xm[(par * 2) * kM + row], xm[(par * 2 + 1) * kM + row]) * p.scale_log2;
+        }
+        const bool need = mx > m_used + kRescaleLog2;
+        const float m_new = need ? mx : m_used;
+        const float alpha = need ? fast_exp2(m_used - m_new) : 1.f;
+        if (i > 0 && __any_sync(0xffffffffu, need)) {
+          const int pb = (g - 1) % kSBufs;
+          if (!__all_sync(0xffffffffu, mbar_wait_bounded(bar(kBarPvDone + pb),
+                                                          ((g - 1) / kSBufs) & 1, kTimeoutNs))) {
+            if (lane == 0) give_up();
+            ok = false;
+            break;
+          }
+          tc::fence_after_sync();
+  #pragma unroll 1
+          for (int c = hf * (D / 64); c < (hf + 1) * (D / 64); ++c) {  // this half's O columns
+            uint32_t r[32];
+            tc::ld32(tl + 32 * c, r);
+            tc::wait_ld();
+  #pragma unroll
+            for (int j = 0; j < 32; ++j) r[j] = __float_as_uint(__uint_as_float(r[j]) * alpha);
+            tc::st32(tl + 32 * c, r);
+          }
+          tc::wait_st();
+        }
+        m_used = m_new;
+        const float neg_m = -m_used;
+        // key pairs through the packed fp32 instructions: scale and shift, the
+        // running sums (four pair accumulators) and the bf16 residual
+        const uint64_t sc2 = f2_pack(p.scale_log2, p.scale_log2), nm2 = f2_pack(neg_m, neg_m);
+        uint64_t l2[4] = {0ull, 0ull, 0ull, 0ull};
+  #pragma unroll
+        for (int c = 0; c < kH / 32; ++c) {
+          uint32_t hi[16], lo[16];
+  #pragma unroll
+          for (int w = 0; w < 16; ++w) {
+            float xa, xe;
+            f2_unpack(f2_fma(f2_pack(sv[32 * c + 2 * w], sv[32 * c + 2 * w + 1]), sc2, nm2), xa, xe);
+            const float a = fast_exp2(xa), e = fast_exp2(xe);
+            const uint64_t ae = f2_pack(a, e);
+            l2[w & 3] = f2_add(l2[w & 3], ae);
+            hi[w] = pack2<BF16>(a, e);
+            if constexpr (BF16) {
+              float ra, re;
+              f2_unpack(f2_sub(ae, f2_pack(__uint_as_float(hi[w] << 16),
+                                           __uint_as_float(hi[w] & 0xffff0000u))),
+                        ra, re);
+              lo[w] = pack2<BF16>(ra, re);
+            }
+          }
+          // P over this half's own S columns: hi in the first 32, lo in the last
+          tc::st16(scol + 16 * c, hi);
+          if constexpr (BF16) tc::st16(scol + 32 + 16 * c, lo);
+        }
+        float l8[8];
+  #pragma unroll
+        for (int k = 0; k < 4; ++k) f2_unpack(l2[k], l8[2 * k], l8[2 * k + 1]);
+        l = l * alpha + (((l8[0] + l8[1]) + (l8[2] + l8[3])) + ((l8[4] + l8[5]) + (l8[6] + l8[7])));
+        const int nvalid = kv_len - i * kN;
+        if (nvalid < kN) {
+          // last tile: keys past kv_len hold stale smem / pool rows; their P is
+          // 0 but 0 * NaN is not, so the V rows become exact zeros first
+          const int s = g % kVRing;
+          if (!__all_sync(0xffffffffu,
+                          mbar_wait_bounded(bar(kBarVFull + s), (g / kVRing) & 1, kTimeoutNs))) {
+            if (lane == 0) give_up();
+            ok = false;
+            break;
+          }
+          const int units = (kN - nvalid) * (D / 8);
+          for (int e = threadIdx.x; e < units; e += 32 * kSoftWarps) {
+            const int r = nvalid + e / (D / 8), u = e % (D / 8);
+            const int c = u >> 3, uu = u & 7;
+            *reinterpret_cast<uint4 *>(smem + C::kV0 + s * C::kTile + (r >> 3) * C::kGroup +
+                                       c * 1024 + (r & 7) * 128 + ((uu ^ (r & 7)) << 4)) =
+                make_uint4(0, 0, 0, 0);
+          }
+          fence_proxy_async_smem();
+        }
+        tc::wait_st();
+        tc::fence_before_sync();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar(kBarPFull + buf));
+      }
+      if (ok) {
+        const int lb = (tg + ntiles - 1) % kSBufs;
+        ok = __all_sync(0xffffffffu, mbar_wait_bounded(bar(kBarPvDone + lb),
+                                                       ((tg + ntiles - 1) / kSBufs) & 1, kTimeoutNs));
+        if (!ok && lane == 0) give_up();
+      }
+      if (ok) {
+        // row sum = the two halves' sums, added in a fixed order
+        xl[hf * kM + row] = l;
+        mbar_arrive(bar(kBarLx + pair));
+        ok = __all_sync(0xffffffffu, mbar_wait_bounded(bar(kBarLx + pair), nit & 1, kTimeoutNs));
+        if (!ok && lane == 0) give_up();
+      }
+      if (ok) {
+        tc::fence_after_sync();
+        const float inv = 1.f / (xl[row] + xl[kM + row]);
+        const int64_t ob = (int64_t)(p.q_start[b] + tok) * p.o_st + (int64_t)hq * p.o_sh;
+  #pragma unroll
+        for (int c = hf * (D / 64); c < (hf + 1) * (D / 64); ++c) {
+          uint32_t r[32];
+          tc::ld32(tl + 32 * c, r);
+          tc::wait_ld();
+          if (live) {
+            if (p.out_f32) {
+              float4 *dst = reinterpret_cast<float4 *>(static_cast<float *>(p.out) + ob + 32 * c);
+  #pragma unroll
+              for (int j = 0; j < 8; ++j)
+                dst[j] = make_float4(__uint_as_float(r[4 * j]) * inv, __uint_as_float(r[4 * j + 1]) * inv,
+                                     __uint_as_float(r[4 * j + 2]) * inv,
+                                     __uint_as_float(r[4 * j + 3]) * inv);
+            } else {
+              uint4 *dst = reinterpret_cast<uint4 *>(static_cast<uint16_t *>(p.out) + ob + 32 * c);
+  #pragma unroll
+              for (int j = 0; j < 4; ++j)
+                dst[j] = make_uint4(pack2<BF16>(__uint_as_float(r[8 * j]) * inv,
+                                                __uint_as_float(r[8 * j + 1]) * inv),
+                                    pack2<BF16>(__uint_as_float(r[8 * j + 2]) * inv,
+                                                __uint_as_float(r[8 * j + 3]) * inv),
+                                    pack2<BF16>(__uint_as_float(r[8 * j + 4]) * inv,
+                                                __uint_as_float(r[8 * j + 5]) * inv),
+                                    pack2<BF16>(__uint_as_float(r[8 * j + 6]) * inv,
+                                                __uint_as_float(r[8 * j + 7]) * inv));
+            }
+          }
+        }
+      }
+      if (!ok) break;
+      // this item's O has been read: the next item's first PV may overwrite it
+      tc::fence_before_sync();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(kBarOFree));
+      tg += ntiles;
+      ++nit;
+    }
+  }
+
+  tc::fence_before_sync();
+  __syncthreads();
+  if (warp == kMmaWarp) {
+    tc::fence_after_sync();
+    tc::tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+template <int D, bool BF16>
+int smem_attr_ps() {
+  static DeviceOnce once;
+  return smem_optin(paged_prefill_ps_kernel<D, BF16>, tcp::TCfg<D>::kSmemBytes, once,
+                    "mz_paged_prefill: shared memory attribute (persistent form)");
+}
+
 template <int D, bool BF16>
 int smem_attr_tc() {
   static DeviceOnce once;
@@ -691,6 +1211,31 @@ extern "C" int mz_paged_prefill(void *out, int32_t out_dtype, int64_t out_tok_st
   if (n_seqs > 65535 || n_kv_heads > 65535)
     return fail(MZ_ERR_UNSUPPORTED, "%s: grid too large", fn);
   const int tpc = tcp::kM / G;
+  // The persistent form (one CTA per SM over all query blocks) by default;
+  // MLXZ_B200_PREFILL_PERSIST=0 launches one CTA per query block instead
+  if (decode::env_int("MLXZ_B200_PREFILL_PERSIST", 1, 0, 1) == 1) {
+    p.n_seqs = n_seqs;
+    p.qblocks = (max_q_len + tpc - 1) / tpc;
+    const int64_t items = (int64_t)n_seqs * n_kv_heads * p.qblocks;
+    if (items >= (int64_t(1) << 31)) return fail(MZ_ERR_UNSUPPORTED, "%s: too many query blocks", fn);
+    const int sms = sm_count(current_device());
+    if (sms <= 0) return fail(MZ_ERR_CUDA, "%s: cannot query the SM count", fn);
+    const dim3 grid_ps(static_cast<unsigned>(std::min<int64_t>(items, sms)));
+#define MZ_PSLAUNCH(D_, BF_)                                                                     \
+  do {                                                                                           \
+    if (int rc = smem_attr_ps<D_, BF_>()) return rc;                                             \
+    paged_prefill_ps_kernel<D_, BF_>                                                             \
+        <<<grid_ps, tcp::kThreads, tcp::TCfg<D_>::kSmemBytes, s>>>(tk, tv, p);                   \
+  } while (0)
+    if (head_dim == 128) {
+      if (bf16) MZ_PSLAUNCH(128, true); else MZ_PSLAUNCH(128, false);
+    } else {
+      if (bf16) MZ_PSLAUNCH(64, true); else MZ_PSLAUNCH(64, false);
+    }
+#undef MZ_PSLAUNCH
+    MZ_CHECK_LAUNCH(fn);
+    return MZ_OK;
+  }
   const dim3 grid((max_q_len + tpc - 1) / tpc, n_kv_heads, n_seqs);
 #define MZ_TCLAUNCH(D_, BF_)                                                                     \
   do {                                                                                           \

@@ -55,7 +55,11 @@ PREFILL_CASES = [
 
 @pytest.mark.parametrize("dtype,D,G,bs,ctx,qlen", PREFILL_CASES)
 @pytest.mark.parametrize("out32", [False, True])
-def test_paged_prefill_vs_oracle(cuda, dtype, D, G, bs, ctx, qlen, out32):
+@pytest.mark.parametrize("form", ["persistent", "per_block"])
+def test_paged_prefill_vs_oracle(cuda, dtype, D, G, bs, ctx, qlen, out32, form, monkeypatch):
+    """Every case through the persistent kernel (the default: one CTA per SM
+    over all query blocks) and the one-CTA-per-block kernel."""
+    monkeypatch.setenv("MLXZ_B200_PREFILL_PERSIST", "1" if form == "persistent" else "0")
     Hkv = 2 if G == 16 else 4
     case = _prefill_case(5 + D + G + len(ctx), ctx, qlen, dtype, D, G, bs, Hkv)
     out = _run(case, dtype, cuda, torch.float32 if out32 else None)
